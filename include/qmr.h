@@ -1,0 +1,184 @@
+/*
+ * qmr.h -- C ABI of the B200 (sm_100a) packed-affine matrix path.
+ *
+ * This library replaces the matrix half of the reference engine's GPU
+ * dispatch layer (rucin93/qwen-mlx-runner v0.7.3, src/gpu.rs).  The reference
+ * engine binds to it through `extern "C"` declarations;
+ * every entry point below names the reference interface it stands in for.
+ *
+ * Conventions shared by all entry points
+ *   - Every pointer argument that names tensor data is a DEVICE pointer of
+ *     the current CUDA device.  Streams are `cudaStream_t` passed as void*
+ *     (NULL = the legacy default stream).  Calls are stream ordered and
+ *     never synchronise the host.
+ *   - Packed weights use the MLX affine layout the reference loads
+ *     (src/weights.rs:292-351): u32 words, row-major, element c of a row at
+ *     bits (c % (32/bits))*bits of word c/(32/bits), little-endian.  Scales
+ *     and biases are one per (row, group): f32, or the high 16 bits of an
+ *     f32 ("bf16 metadata", src/gpu/metadata.rs:6-14).
+ *   - Block operands are token-major: X[b*cols + c], Y[b*rows + r]
+ *     (kernels/matmul_block.metal:1-3).
+ *   - Return value: QMR_OK (0) or a negative QMR_E* code.  All validation
+ *     happens before any launch; on error nothing has been enqueued
+ *     (src/gpu.rs:628-792).  qmr_last_error() gives the message of the last
+ *     failure on the calling thread.
+ */
+#ifndef QMR_H
+#define QMR_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QMR_ABI_VERSION 1
+
+enum {
+    QMR_OK = 0,
+    QMR_EINVAL = -1,       /* bad shape, parameter count, epsilon, batch ...   */
+    QMR_ERANGE = -2,       /* buffer view beyond its allocation, size overflow */
+    QMR_EALIGN = -3,       /* byte offset not 4-aligned (or 16 where required) */
+    QMR_EOVERLAP = -4,     /* an output view overlaps an input view            */
+    QMR_EUNSUPPORTED = -5, /* unknown kernel, no specialisation, mode forbids  */
+    QMR_ECUDA = -6,        /* CUDA runtime error                               */
+    QMR_ETIMEOUT = -7,     /* a bounded device-side wait ran out               */
+    QMR_ENOTINIT = -8      /* qmr_init was not called on this device           */
+};
+
+/* Block-matmul schedules, src/gpu.rs:18-31 (BlockMatmulMode). */
+enum { QMR_BLOCK_LEGACY = 0, QMR_BLOCK_SHARED = 1, QMR_BLOCK_MLP_R2 = 2 };
+
+/* GEMV variants, src/gpu.rs:302-309 (QWEN_METAL_GEMV). */
+enum { QMR_GEMV_PACKED4 = 0, QMR_GEMV_ALIGNED = 1, QMR_GEMV_STREAM = 2 };
+
+/* qmr_init flags. */
+#define QMR_INIT_FROM_ENV 0u  /* read QWEN_METAL_* like Gpu::new (gpu.rs:293-325) */
+#define QMR_INIT_REFERENCE 1u /* force reference kernels, like new_with_reference(true) */
+
+/* One device allocation as the dispatch ABI sees it: base pointer and byte
+ * length.  Stands in for metal::Buffer; two views alias when their bases are
+ * equal (gpu.rs:658-672 compares buffer identity). */
+typedef struct qmr_buffer {
+    void *ptr;
+    uint64_t length;
+} qmr_buffer;
+
+/* ---- lifetime and modes ------------------------------------------------ */
+
+/* Gpu::new / Gpu::new_with_reference (src/gpu.rs:293-437): bind `device`,
+ * parse and validate QWEN_METAL_REFERENCE, QWEN_METAL_GEMV, QWEN_METAL_NORM,
+ * QWEN_METAL_ATTN_VALUES, QWEN_METAL_METADATA, QWEN_METAL_BLOCK_MATMUL and
+ * QWEN_METAL_BLOCK_DELTA with the reference's accepted values.  Safe to call
+ * again; each call re-reads the environment. */
+int qmr_init(int device, uint32_t flags);
+
+/* Gpu::new_with_variant + set_block_kernel_mode (src/gpu.rs:305-309, 449-454):
+ * override the modes.  Any argument may be NULL to keep the current value.
+ * Values are the reference's strings ("aligned", "legacy", "mlp-r2", ...). */
+int qmr_set_modes(const char *gemv, const char *metadata, const char *block_matmul,
+                  const char *block_delta);
+
+/* Current modes as "gemv=..,metadata=..,block_matmul=..,block_delta=..,reference=0|1"
+ * (src/gpu.rs:439-470 kernel_mode/metadata_mode/block_kernel_mode). */
+int qmr_get_modes(char *out, size_t out_len);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char *qmr_last_error(void);
+
+/* Library ABI version (QMR_ABI_VERSION). */
+int qmr_abi_version(void);
+
+/* ---- pure host logic (no GPU needed) ----------------------------------- */
+
+/* BlockKernelMode::parse_for_device (src/gpu.rs:49-61): NULL matmul/delta
+ * mean "unset"; the device default is mlp-r2 only for "Apple M5 Pro". */
+int qmr_parse_block_mode(const char *device_name, const char *matmul, const char *delta,
+                         int *matmul_mode, int *batched_delta);
+
+/* dispatch_layout (src/gpu.rs:1041-1294): validates `params` for kernel
+ * `name`, writes the minimum byte size of each buffer into sizes[0..*count)
+ * and the logical thread count the reference expects.  sizes must hold 8. */
+int qmr_dispatch_layout(const char *name, const uint32_t *params, size_t nparams,
+                        uint64_t *sizes, size_t *count, uint64_t *threads);
+
+/* checked_buffer_range (src/gpu.rs:879-889). */
+int qmr_checked_buffer_range(uint64_t offset, uint64_t minimum, uint64_t length);
+
+/* specialized_matmul / specialized_matvec / specialized_matvec_bf16
+ * (src/gpu.rs:896-1037): the reference's specialised kernel name for
+ * (name, params, aligned, mode), written into out.  QMR_EUNSUPPORTED when the
+ * reference has none.  name is "matmul_affine[_bf16]", "matvec_affine" or
+ * "matvec_affine_bf16"; mode is a QMR_BLOCK_* value. */
+int qmr_select(const char *name, const uint32_t *params, size_t nparams, int aligned,
+               int mode, char *out, size_t out_len);
+
+/* pack_bf16_exact (src/gpu/metadata.rs:6-14): 1 and out filled when every
+ * value is finite with zero low 16 bits, else 0. */
+int qmr_pack_bf16_exact(const float *values, uint64_t n, uint16_t *out);
+
+/* ---- the dispatch ABI -------------------------------------------------- */
+
+/* DispatchEncoder::encode / encode_offsets (src/gpu.rs:120-174, 628-848):
+ * validate and enqueue the named kernel.  offsets may be NULL (all zero).
+ * Supported names: matvec_affine, matvec_affine_bf16, matmul_affine,
+ * matmul_affine_bf16, embed_affine, embed_affine_bf16, copy_f32.  Other names
+ * known to the reference validate and return QMR_EUNSUPPORTED. */
+int qmr_encode(const char *name, const qmr_buffer *buffers, const uint64_t *offsets,
+               size_t nbuffers, const uint32_t *params, size_t nparams, uint64_t threads,
+               uint64_t group_size, void *stream);
+
+/* ---- typed entry points (device pointers, no buffer lengths) ----------- */
+
+/* Matrix::matvec (src/engine.rs:137-164): y[r] = sum_c (q*s+b)*x[c].
+ * meta_bf16: 0 = f32 scales/biases, 1 = bf16 (high-half) scales/biases. */
+int qmr_matvec_affine(const void *w, const void *scales, const void *biases, const float *x,
+                      float *y, uint32_t rows, uint32_t cols, uint32_t bits, uint32_t group,
+                      int meta_bf16, void *stream);
+
+/* Matrix::matmul_block (src/engine/block.rs:191-229): Y[b*rows+r] for
+ * b < batch (1..4), every packed word read once for all batch rows. */
+int qmr_matmul_affine(const void *w, const void *scales, const void *biases, const float *x,
+                      float *y, uint32_t rows, uint32_t cols, uint32_t bits, uint32_t group,
+                      uint32_t batch, int meta_bf16, void *stream);
+
+/* Matrix::embed (src/engine.rs:166-188), kernels embed_affine[_bf16]:
+ * y[c] = float(q)*s + b for one row, bit-exact with the reference. */
+int qmr_embed_affine(const void *w, const void *scales, const void *biases, uint32_t row,
+                     float *y, uint32_t cols, uint32_t bits, uint32_t group, int meta_bf16,
+                     void *stream);
+
+/* The gate/up projections plus swiglu of one MLP (src/engine.rs:755-763,
+ * kernels/qwen.metal:91-94) in one pass: act[b*rows+r] =
+ * silu(gate_b[r]) * up_b[r].  Both matrices share shape and format; x is
+ * read once for both. */
+int qmr_gateup_swiglu(const void *w_gate, const void *s_gate, const void *b_gate,
+                      const void *w_up, const void *s_up, const void *b_up, const float *x,
+                      float *act, uint32_t rows, uint32_t cols, uint32_t bits, uint32_t group,
+                      uint32_t batch, int meta_bf16, void *stream);
+
+/* The head projection (src/engine.rs:777-780) plus greedy argmax
+ * (src/chat.rs:383-390) in one pass: logits[b*rows+r] as qmr_matmul_affine,
+ * and argmax[b] = index of the maximum logit of batch row b under f32 total
+ * order, ties to the lowest index.  row_base is added to every reported index
+ * (a vocabulary shard's first row).  best_key (optional, may be NULL)
+ * receives the packed (total-order key << 32 | ~index) per batch row, the
+ * value a cross-shard argmax reduces with a plain max. */
+int qmr_head_argmax(const void *w, const void *scales, const void *biases, const float *x,
+                    float *logits, int32_t *argmax, uint64_t *best_key, uint32_t rows,
+                    uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch,
+                    int meta_bf16, uint32_t row_base, void *stream);
+
+/* copy_f32 (kernels/matmul_block.metal:315-318): y[i] = x[i], i < n. */
+int qmr_copy_f32(const float *x, float *y, uint32_t n, void *stream);
+
+/* Block until all work this library enqueued on `stream` finished, and
+ * report a device error as QMR_ECUDA (Gpu::finish, src/gpu.rs:849-876). */
+int qmr_stream_sync(void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QMR_H */

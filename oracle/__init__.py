@@ -1,0 +1,157 @@
+"""CPU oracle for the packed-affine matrix path -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU baseline legs may
+import this package; the product (libqmr, qmr) never does.  It wraps
+oracle/liboracle.so, a C restatement of the reference's scalar arithmetic
+(see oracle.c for the file:line each function follows).
+
+Parity pins: the reference's own known-answer tests (src/gpu.rs:1636-1731,
+src/weights.rs:816-870, tests/batch_matrix.rs:357-381, src/gpu/metadata.rs
+tests) are checked against this oracle in tests/test_oracle.py, and the
+reference's Python scalar oracle (scripts/make_fixture.py) output is pinned
+through tests/golden/.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import pathlib
+import subprocess
+
+import numpy as np
+
+HERE = pathlib.Path(__file__).resolve().parent
+LIB = HERE / "liboracle.so"
+SRC = HERE / "oracle.c"
+
+# -ffp-contract=off: Rust never fuses a*b+c, so neither may the restatement.
+CFLAGS = ["-O3", "-march=x86-64-v2", "-fPIC", "-ffp-contract=off", "-fopenmp", "-shared"]
+
+_lib = None
+
+
+def build(force: bool = False) -> pathlib.Path:
+    if force or not LIB.exists() or LIB.stat().st_mtime < SRC.stat().st_mtime:
+        tmp = LIB.with_suffix(".so.tmp")
+        subprocess.run(["gcc", *CFLAGS, "-o", os.fspath(tmp), os.fspath(SRC), "-lm"], check=True)
+        os.replace(tmp, LIB)
+    return LIB
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB.exists() and SRC.exists():
+            build()
+        h = ctypes.CDLL(os.fspath(LIB))
+        vp, u32, u64, i32 = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int
+        h.or_embed.argtypes = [vp, vp, vp, i32, u64, u32, u32, u32, vp]
+        h.or_matmul_f64.argtypes = [vp, vp, vp, i32, vp, u32, u32, u32, u32, u32, u32, u32, vp, vp]
+        h.or_swiglu_f64.argtypes = [vp, vp, vp, vp, vp, vp, i32, vp, u32, u32, u32, u32, u32, vp, vp]
+        h.or_argmax_f32.argtypes = [vp, u64]
+        h.or_argmax_f32.restype = ctypes.c_longlong
+        h.or_argmax_f64.argtypes = [vp, u64]
+        h.or_argmax_f64.restype = ctypes.c_longlong
+        h.or_pack_bf16_exact.argtypes = [vp, u64, vp]
+        h.or_bf16_rne.argtypes = [ctypes.c_float]
+        h.or_bf16_rne.restype = ctypes.c_uint16
+        h.or_num_threads.restype = i32
+        h.or_set_threads.argtypes = [i32]
+        _lib = h
+    return _lib
+
+
+def _c(a, dtype):
+    a = np.ascontiguousarray(a, dtype=dtype)
+    return a, a.ctypes.data
+
+
+def _meta(m):
+    m = np.ascontiguousarray(m)
+    if m.dtype == np.uint16:
+        return m, 1
+    return np.ascontiguousarray(m, dtype=np.float32), 0
+
+
+def matmul_f64(w, s, b, x, rows, cols, bits, group, batch=1, row0=0, nrows=None):
+    """FP64 expansion (tests/quantized.rs:39-51): (y[batch, rows], |w.x| sums).
+
+    Rows outside [row0, row0+nrows) are left as NaN."""
+    nrows = rows - row0 if nrows is None else nrows
+    w, wp = _c(w, np.uint32)
+    s, sb = _meta(s)
+    b, _ = _meta(b)
+    x, xp = _c(x, np.float32)
+    y = np.full(batch * rows, np.nan)
+    mag = np.full(batch * rows, np.nan)
+    lib().or_matmul_f64(wp, s.ctypes.data, b.ctypes.data, sb, xp, rows, cols, bits, group, batch, row0, nrows,
+                        y.ctypes.data, mag.ctypes.data)
+    return y.reshape(batch, rows), mag.reshape(batch, rows)
+
+
+def swiglu_f64(wg, sg, bg, wu, su, bu, x, rows, cols, bits, group, batch=1):
+    """FP64 silu(gate.x)*(up.x) and its first-order error scale."""
+    wg, wgp = _c(wg, np.uint32)
+    wu, wup = _c(wu, np.uint32)
+    sg, sb = _meta(sg)
+    bg, _ = _meta(bg)
+    su, _ = _meta(su)
+    bu, _ = _meta(bu)
+    x, xp = _c(x, np.float32)
+    act = np.empty(batch * rows)
+    mag = np.empty(batch * rows)
+    lib().or_swiglu_f64(wgp, sg.ctypes.data, bg.ctypes.data, wup, su.ctypes.data, bu.ctypes.data, sb, xp, rows,
+                        cols, bits, group, batch, act.ctypes.data, mag.ctypes.data)
+    return act.reshape(batch, rows), mag.reshape(batch, rows)
+
+
+def embed(w, s, b, row, cols, bits, group):
+    """FP32 dequantisation of one row, float(q)*s + b (kernels/qwen.metal:40-47)."""
+    w, wp = _c(w, np.uint32)
+    s, sb = _meta(s)
+    b, _ = _meta(b)
+    y = np.empty(cols, dtype=np.float32)
+    lib().or_embed(wp, s.ctypes.data, b.ctypes.data, sb, row, cols, bits, group, y.ctypes.data)
+    return y
+
+
+def argmax_f32(v) -> int:
+    v, p = _c(v, np.float32)
+    return int(lib().or_argmax_f32(p, v.size))
+
+
+def argmax_f64(v) -> int:
+    v, p = _c(v, np.float64)
+    return int(lib().or_argmax_f64(p, v.size))
+
+
+def pack_bf16_exact(values):
+    v, p = _c(values, np.float32)
+    out = np.empty(v.size, dtype=np.uint16)
+    return out if lib().or_pack_bf16_exact(p, v.size, out.ctypes.data) else None
+
+
+def bf16_rne(v: float) -> int:
+    return int(lib().or_bf16_rne(v))
+
+
+def threads() -> int:
+    return int(lib().or_num_threads())
+
+
+def set_threads(n: int) -> None:
+    lib().or_set_threads(n)
+
+
+def tolerance_ratio(got, want, scale, rtol=2e-5, atol=0.0):
+    """Worst |got - want| / (atol + rtol*scale); <= 1 passes.  NaN fails."""
+    got = np.asarray(got, dtype=np.float64).ravel()
+    want = np.asarray(want, dtype=np.float64).ravel()
+    scale = np.asarray(scale, dtype=np.float64).ravel()
+    err = np.abs(got - want)
+    lim = atol + rtol * scale
+    with np.errstate(divide="ignore", invalid="ignore"):
+        ratio = np.where(err == 0, 0.0, err / lim)
+    ratio = np.where(np.isnan(ratio), np.inf, ratio)
+    i = int(np.argmax(ratio)) if ratio.size else -1
+    return (float(ratio[i]) if ratio.size else 0.0), i
