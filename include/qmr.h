@@ -170,6 +170,32 @@ int qmr_head_argmax(const void *w, const void *scales, const void *biases, const
                     uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch,
                     int meta_bf16, uint32_t row_base, void *stream);
 
+/* ---- prepared activations (caller-owned workspace) ---------------------
+ * The streaming kernels read activations in a pre-scaled, lane-interleaved
+ * form.  The entry points above prepare it in a per-stream library
+ * workspace.  Callers that apply several matrices to the same activations
+ * (q/k/v, gate/up, DeltaNet in-projections), or that own their memory, can
+ * prepare once into their own buffer and stream any number of matrices of
+ * the same bits and cols from it.  These have no single reference
+ * counterpart; they split Matrix::matvec / matmul_block
+ * (src/engine.rs:137-164, src/engine/block.rs:191-229) into its two passes. */
+
+/* Bytes of a prepared-activation buffer for (bits, cols, batch). */
+uint64_t qmr_prepared_bytes(uint32_t bits, uint32_t cols, uint32_t batch);
+
+/* Prepare x [batch, cols] (token-major f32) into `prepared`.  bits 4 or 8;
+ * cols a multiple of 128/bits.  `prepared` must be 256-byte aligned and hold
+ * qmr_prepared_bytes(bits, cols, batch). */
+int qmr_prepare_activations(const float *x, uint32_t cols, uint32_t bits, uint32_t batch, void *prepared,
+                            uint64_t prepared_bytes, void *stream);
+
+/* qmr_matmul_affine from prepared activations (same bits, cols, batch).
+ * Weights must be 16-byte aligned with 16-byte multiple rows and group
+ * 32/64/128; the result equals qmr_matmul_affine bit for bit. */
+int qmr_matmul_prepared(const void *w, const void *scales, const void *biases, const void *prepared, float *y,
+                        uint32_t rows, uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch,
+                        int meta_bf16, void *stream);
+
 /* copy_f32 (kernels/matmul_block.metal:315-318): y[i] = x[i], i < n. */
 int qmr_copy_f32(const float *x, float *y, uint32_t n, void *stream);
 

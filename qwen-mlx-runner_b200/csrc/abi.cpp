@@ -824,6 +824,53 @@ int qmr_head_argmax(const void *w, const void *scales, const void *biases, const
     return run_fast(c, static_cast<cudaStream_t>(stream));
 }
 
+uint64_t qmr_prepared_bytes(uint32_t bits, uint32_t cols, uint32_t batch) {
+    if ((bits != 4 && bits != 8) || batch < 1 || batch > 4 || cols == 0) return 0;
+    return scratch_bytes((int)bits, cols, batch);
+}
+
+int qmr_prepare_activations(const float *x, uint32_t cols, uint32_t bits, uint32_t batch, void *prepared,
+                            uint64_t prepared_bytes, void *stream) {
+    if (bits != 4 && bits != 8) return fail(QMR_EINVAL, "prepared activations support 4 or 8 bits");
+    if (batch < 1 || batch > 4) return fail(QMR_EINVAL, "Matrix blocks support one through four RHS");
+    if (cols == 0 || cols % (128 / bits) != 0)
+        return fail(QMR_EINVAL, "cols must be a nonzero multiple of %u", 128 / bits);
+    if (x == nullptr || prepared == nullptr) return fail(QMR_EINVAL, "null pointer");
+    if (reinterpret_cast<uintptr_t>(prepared) % 256 != 0)
+        return fail(QMR_EALIGN, "prepared activations must be 256-byte aligned");
+    if (prepared_bytes < scratch_bytes((int)bits, cols, batch))
+        return fail(QMR_ERANGE, "prepared buffer of %llu bytes is smaller than %llu", (unsigned long long)prepared_bytes,
+                    (unsigned long long)scratch_bytes((int)bits, cols, batch));
+    return run_prepare(x, cols, bits, batch, prepared, false, static_cast<cudaStream_t>(stream));
+}
+
+int qmr_matmul_prepared(const void *w, const void *scales, const void *biases, const void *prepared, float *y,
+                        uint32_t rows, uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch, int meta_bf16,
+                        void *stream) {
+    int rc = typed_fast_check(w, rows, cols, bits, group, batch, meta_bf16, "qmr_matmul_prepared");
+    if (rc != QMR_OK) return rc;
+    if (prepared == nullptr || reinterpret_cast<uintptr_t>(prepared) % 256 != 0)
+        return fail(QMR_EALIGN, "prepared activations must be 256-byte aligned");
+    const Modes m = modes();
+    const uint32_t p[5] = {rows, cols, bits, group, batch};
+    const char *sel = specialized_matmul(meta_bf16 ? "matmul_affine_bf16" : "matmul_affine", p,
+                                         m.gemv == QMR_GEMV_ALIGNED, m.block);
+    FastCall c = {};
+    c.w = w;
+    c.s = scales;
+    c.b = biases;
+    c.y = y;
+    c.rows = rows;
+    c.cols = cols;
+    c.bits = bits;
+    c.group = group;
+    c.batch = batch;
+    c.bf16 = meta_bf16 != 0;
+    c.r2 = sel != nullptr && strcmp(sel, "matmul_q4_g64_b3_mlp_r2_aligned_bf16") == 0;
+    c.epilogue = 0;
+    return run_stream(c, const_cast<void *>(prepared), static_cast<cudaStream_t>(stream));
+}
+
 int qmr_copy_f32(const float *x, float *y, uint32_t n, void *stream) {
     if (n == 0) return fail(QMR_EINVAL, "copy_f32: dimensions must be nonzero");
     if (x == y) return QMR_OK;

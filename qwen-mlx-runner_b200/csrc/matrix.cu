@@ -180,21 +180,17 @@ int launch_stream(const StreamArgs &a, int bits, bool bf16, uint32_t batch, bool
 
 }  // namespace
 
-int run_fast(const FastCall &c, cudaStream_t stream) {
-    const size_t need = scratch_bytes((int)c.bits, c.cols, c.batch);
-    void *base = c.scratch;
-    if (base == nullptr) {
-        const int rc = acquire_scratch(stream, need, &base);
-        if (rc != QMR_OK) return rc;
-    } else if (c.scratch_bytes < need) {
-        return fail(QMR_ERANGE, "scratch of %zu bytes is smaller than the %zu required", c.scratch_bytes, need);
-    }
+int run_prepare(const float *x, uint32_t cols, uint32_t bits, uint32_t batch, void *base, bool argmax,
+                cudaStream_t stream) {
+    ScratchView sv;
+    scratch_layout(base, (int)bits, cols, batch, &sv);
+    return bits == 4 ? launch_prep<4>(x, cols, batch, sv, argmax, stream)
+                     : launch_prep<8>(x, cols, batch, sv, argmax, stream);
+}
+
+int run_stream(const FastCall &c, void *base, cudaStream_t stream) {
     ScratchView sv;
     scratch_layout(base, (int)c.bits, c.cols, c.batch, &sv);
-    const bool argmax = c.epilogue == 2;
-    int rc = c.bits == 4 ? launch_prep<4>(c.x, c.cols, c.batch, sv, argmax, stream)
-                         : launch_prep<8>(c.x, c.cols, c.batch, sv, argmax, stream);
-    if (rc != QMR_OK) return rc;
     StreamArgs a = {};
     a.w = static_cast<const uint4 *>(c.w);
     a.s = c.s;
@@ -219,6 +215,20 @@ int run_fast(const FastCall &c, cudaStream_t stream) {
         case 1: return launch_stream<1>(a, (int)c.bits, c.bf16, c.batch, c.r2, stream);
         default: return launch_stream<2>(a, (int)c.bits, c.bf16, c.batch, c.r2, stream);
     }
+}
+
+int run_fast(const FastCall &c, cudaStream_t stream) {
+    const size_t need = scratch_bytes((int)c.bits, c.cols, c.batch);
+    void *base = c.scratch;
+    if (base == nullptr) {
+        const int rc = acquire_scratch(stream, need, &base);
+        if (rc != QMR_OK) return rc;
+    } else if (c.scratch_bytes < need) {
+        return fail(QMR_ERANGE, "scratch of %zu bytes is smaller than the %zu required", c.scratch_bytes, need);
+    }
+    const int rc = run_prepare(c.x, c.cols, c.bits, c.batch, base, c.epilogue == 2, stream);
+    if (rc != QMR_OK) return rc;
+    return run_stream(c, base, stream);
 }
 
 int run_generic(const void *w, const void *s, const void *b, const float *x, float *y, uint32_t rows,

@@ -42,6 +42,9 @@ void scratch_layout(void *base, int bits, uint32_t cols, uint32_t batch, Scratch
 int acquire_scratch(cudaStream_t stream, size_t need, void **out);
 
 int run_fast(const FastCall &c, cudaStream_t stream);
+int run_prepare(const float *x, uint32_t cols, uint32_t bits, uint32_t batch, void *base, bool argmax,
+                cudaStream_t stream);
+int run_stream(const FastCall &c, void *base, cudaStream_t stream);
 int run_generic(const void *w, const void *s, const void *b, const float *x, float *y, uint32_t rows,
                 uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch, bool bf16, cudaStream_t stream);
 int run_embed(const void *w, const void *s, const void *b, uint32_t row, float *y, uint32_t cols, uint32_t bits,

@@ -16,12 +16,28 @@ from . import _lib
 from ._lib import QmrError, check
 
 
-def _ptr(t):
+def _ptr(t, min_bytes: int = 0, what: str = "tensor"):
+    """Device address of t after checking it is a contiguous CUDA tensor with
+    at least min_bytes bytes (the C ABI cannot see tensor extents)."""
     if t is None:
         return None
     if not t.is_cuda:
-        raise QmrError(_lib.QMR_EINVAL, "tensors must live on a CUDA device")
+        raise QmrError(_lib.QMR_EINVAL, f"{what} must live on a CUDA device")
+    if not t.is_contiguous():
+        raise QmrError(_lib.QMR_EINVAL, f"{what} must be contiguous")
+    nbytes = t.numel() * t.element_size()
+    if nbytes < min_bytes:
+        raise QmrError(_lib.QMR_ERANGE, f"{what} holds {nbytes} bytes, the call needs {min_bytes}")
     return t.data_ptr()
+
+
+def _mat(m: "PackedMatrix"):
+    """Pointers of a packed matrix after checking its buffers cover the shape."""
+    elems = m.rows * m.cols
+    wbytes = elems * m.bits // 8
+    mbytes = (elems // m.group) * (2 if m.meta_bf16 else 4) if m.group else 0
+    return (_ptr(m.weight, wbytes, "weights"), _ptr(m.scales, mbytes, "scales"),
+            _ptr(m.biases, mbytes, "biases"))
 
 
 def _stream(stream):
@@ -56,40 +72,72 @@ class PackedMatrix:
 
 
 def matvec_affine(m: PackedMatrix, x, y, stream=None) -> None:
-    check(_lib.lib().qmr_matvec_affine(_ptr(m.weight), _ptr(m.scales), _ptr(m.biases), _ptr(x), _ptr(y),
+    w, sc, bi = _mat(m)
+    check(_lib.lib().qmr_matvec_affine(w, sc, bi, _ptr(x, 4 * m.cols, "x"), _ptr(y, 4 * m.rows, "y"),
                                        m.rows, m.cols, m.bits, m.group, int(m.meta_bf16), _stream(stream)))
 
 
 def matmul_affine(m: PackedMatrix, x, y, batch: int, stream=None) -> None:
-    check(_lib.lib().qmr_matmul_affine(_ptr(m.weight), _ptr(m.scales), _ptr(m.biases), _ptr(x), _ptr(y),
-                                       m.rows, m.cols, m.bits, m.group, batch, int(m.meta_bf16),
-                                       _stream(stream)))
+    w, sc, bi = _mat(m)
+    check(_lib.lib().qmr_matmul_affine(w, sc, bi, _ptr(x, 4 * batch * m.cols, "x"),
+                                       _ptr(y, 4 * batch * m.rows, "y"), m.rows, m.cols, m.bits, m.group, batch,
+                                       int(m.meta_bf16), _stream(stream)))
 
 
 def embed_affine(m: PackedMatrix, row: int, y, stream=None) -> None:
-    check(_lib.lib().qmr_embed_affine(_ptr(m.weight), _ptr(m.scales), _ptr(m.biases), row, _ptr(y), m.cols,
-                                      m.bits, m.group, int(m.meta_bf16), _stream(stream)))
+    w, sc, bi = _mat(m)
+    if not 0 <= row < m.rows:
+        raise QmrError(_lib.QMR_ERANGE, f"row {row} outside a {m.rows}-row matrix")
+    check(_lib.lib().qmr_embed_affine(w, sc, bi, row, _ptr(y, 4 * m.cols, "y"), m.cols, m.bits, m.group,
+                                      int(m.meta_bf16), _stream(stream)))
 
 
 def gateup_swiglu(gate: PackedMatrix, up: PackedMatrix, x, act, batch: int, stream=None) -> None:
     if (gate.rows, gate.cols, gate.bits, gate.group, gate.meta_bf16) != (up.rows, up.cols, up.bits, up.group,
                                                                          up.meta_bf16):
         raise QmrError(_lib.QMR_EINVAL, "gate and up matrices must share shape and format")
-    check(_lib.lib().qmr_gateup_swiglu(_ptr(gate.weight), _ptr(gate.scales), _ptr(gate.biases), _ptr(up.weight),
-                                       _ptr(up.scales), _ptr(up.biases), _ptr(x), _ptr(act), gate.rows,
-                                       gate.cols, gate.bits, gate.group, batch, int(gate.meta_bf16),
-                                       _stream(stream)))
+    gw, gs, gb = _mat(gate)
+    uw, us, ub = _mat(up)
+    check(_lib.lib().qmr_gateup_swiglu(gw, gs, gb, uw, us, ub, _ptr(x, 4 * batch * gate.cols, "x"),
+                                       _ptr(act, 4 * batch * gate.rows, "act"), gate.rows, gate.cols, gate.bits,
+                                       gate.group, batch, int(gate.meta_bf16), _stream(stream)))
 
 
 def head_argmax(m: PackedMatrix, x, logits, argmax, batch: int, best_key=None, row_base: int = 0,
                 stream=None) -> None:
-    check(_lib.lib().qmr_head_argmax(_ptr(m.weight), _ptr(m.scales), _ptr(m.biases), _ptr(x), _ptr(logits),
-                                     _ptr(argmax), _ptr(best_key), m.rows, m.cols, m.bits, m.group, batch,
-                                     int(m.meta_bf16), row_base, _stream(stream)))
+    w, sc, bi = _mat(m)
+    check(_lib.lib().qmr_head_argmax(w, sc, bi, _ptr(x, 4 * batch * m.cols, "x"),
+                                     _ptr(logits, 4 * batch * m.rows, "logits"), _ptr(argmax, 4 * batch, "argmax"),
+                                     _ptr(best_key, 8 * batch, "best_key"), m.rows, m.cols, m.bits, m.group,
+                                     batch, int(m.meta_bf16), row_base, _stream(stream)))
+
+
+def prepared_bytes(bits: int, cols: int, batch: int) -> int:
+    return int(_lib.lib().qmr_prepared_bytes(bits, cols, batch))
+
+
+def alloc_prepared(bits: int, cols: int, batch: int, device="cuda"):
+    """A caller-owned prepared-activation buffer (uint8 CUDA tensor, 256-aligned)."""
+    import torch
+    return torch.empty(prepared_bytes(bits, cols, batch), dtype=torch.uint8, device=device)
+
+
+def prepare_activations(x, cols: int, bits: int, batch: int, prepared, stream=None) -> None:
+    check(_lib.lib().qmr_prepare_activations(_ptr(x, 4 * batch * cols, "x"), cols, bits, batch,
+                                             _ptr(prepared, prepared_bytes(bits, cols, batch), "prepared"),
+                                             prepared.numel() * prepared.element_size(), _stream(stream)))
+
+
+def matmul_prepared(m: PackedMatrix, prepared, y, batch: int, stream=None) -> None:
+    w, sc, bi = _mat(m)
+    check(_lib.lib().qmr_matmul_prepared(w, sc, bi, _ptr(prepared, prepared_bytes(m.bits, m.cols, batch),
+                                                         "prepared"),
+                                         _ptr(y, 4 * batch * m.rows, "y"), m.rows, m.cols, m.bits, m.group, batch,
+                                         int(m.meta_bf16), _stream(stream)))
 
 
 def copy_f32(x, y, n: int, stream=None) -> None:
-    check(_lib.lib().qmr_copy_f32(_ptr(x), _ptr(y), n, _stream(stream)))
+    check(_lib.lib().qmr_copy_f32(_ptr(x, 4 * n, "x"), _ptr(y, 4 * n, "y"), n, _stream(stream)))
 
 
 def init(device: int = 0, reference: bool = False) -> None:

@@ -305,7 +305,7 @@ def test_config_shapes_b1_b3_parity_and_block_equals_gemv(cuda, bits):
     mat = synth.affine_matrix(rows, cols, bits, 64, seed=11 + bits)
     m = synth.to_device(mat, rows, cols, bits, 64)
     x = synth.activations(3, cols, seed=7)
-    xd = f32_tensor(x)
+    xd = f32_tensor(x.ravel())
     y3 = torch.empty(3 * rows, dtype=torch.float32, device="cuda")
     qmr.matmul_affine(m, xd, y3, 3)
     y1 = torch.empty((3, rows), dtype=torch.float32, device="cuda")
@@ -442,3 +442,35 @@ def test_extreme_activation_ranges_stay_accurate(cuda):
     torch.cuda.synchronize()
     want, mag = oracle.matmul_f64(mat["weight"], mat["scales"], mat["biases"], x, rows, cols, 4, 64)
     assert_ns_bound(y.cpu().numpy(), want[0], mag[0], "mixed magnitudes")
+
+
+def test_prepared_activations_feed_several_matrices_bit_exactly(cuda):
+    rows, cols = 4096, 5120
+    mats = [synth.affine_matrix(rows, cols, 4, 64, seed=80 + i) for i in range(3)]
+    dm = [synth.to_device(m, rows, cols, 4, 64) for m in mats]
+    for batch in (1, 3):
+        x = f32_tensor(synth.activations(batch, cols, seed=90 + batch).ravel())
+        prepared = qmr.ops.alloc_prepared(4, cols, batch)
+        qmr.ops.prepare_activations(x, cols, 4, batch, prepared)
+        for m in dm:
+            a = torch.empty(batch * rows, dtype=torch.float32, device="cuda")
+            b = torch.empty(batch * rows, dtype=torch.float32, device="cuda")
+            qmr.ops.matmul_prepared(m, prepared, a, batch)
+            qmr.matmul_affine(m, x, b, batch)
+            torch.cuda.synchronize()
+            assert np.array_equal(a.cpu().numpy().view(np.uint32), b.cpu().numpy().view(np.uint32))
+
+
+def test_typed_wrappers_reject_undersized_views_before_launch(cuda):
+    rows, cols = 64, 512
+    m = synth.to_device(synth.affine_matrix(rows, cols, 4, 64, seed=3), rows, cols, 4, 64)
+    x = torch.zeros((3, cols), dtype=torch.float32, device="cuda")
+    y = torch.zeros(3 * rows, dtype=torch.float32, device="cuda")
+    with pytest.raises(QmrError):
+        qmr.matvec_affine(m, x[5:], y)  # empty view
+    with pytest.raises(QmrError):
+        qmr.matmul_affine(m, x[:1], y, 3)
+    with pytest.raises(QmrError):
+        qmr.matmul_affine(m, x, y[:rows], 3)
+    with pytest.raises(QmrError):
+        qmr.embed_affine(m, rows, y)
