@@ -199,6 +199,20 @@ int qmr_matmul_prepared(const void *w, const void *scales, const void *biases, c
 /* copy_f32 (kernels/matmul_block.metal:315-318): y[i] = x[i], i < n. */
 int qmr_copy_f32(const float *x, float *y, uint32_t n, void *stream);
 
+/* Select the streaming kernel of the fast path: "tma" (default; warp-
+ * specialised TMA pipeline, needs 16-byte aligned weights and metadata with
+ * 16-byte multiple metadata rows) or "registers" (register-streaming kernel,
+ * used automatically when those alignments do not hold).  Both give identical
+ * bits; the switch exists for A/B measurement.  No reference counterpart
+ * beyond QWEN_METAL_GEMV's same-binary A/B intent (src/gpu.rs:302-309). */
+int qmr_set_stream_path(const char *path);
+
+/* Read (and optionally clear) the device error word that a kernel sets when
+ * one of its bounded waits runs out (0 = none; 1/2/3 = full-stage,
+ * empty-stage, drain timeout).  Synchronising; call between steps.  Stands in
+ * for the command-status check of Gpu::finish (src/gpu.rs:861-865). */
+int qmr_device_error(int *code, int clear);
+
 /* Block until all work this library enqueued on `stream` finished, and
  * report a device error as QMR_ECUDA (Gpu::finish, src/gpu.rs:849-876). */
 int qmr_stream_sync(void *stream);

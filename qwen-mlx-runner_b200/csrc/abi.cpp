@@ -29,6 +29,7 @@ struct Modes {
     bool batched_delta = true;
     bool parallel_norm = false;
     bool parallel_attention = false;
+    bool register_kernel = false;  // streaming path: false = TMA pipeline, true = register streaming
     bool initialised = false;
 };
 
@@ -467,6 +468,7 @@ static int launch_matrix(const void *w, const void *s, const void *b, const floa
         c.bf16 = bf16;
         c.r2 = r2;
         c.epilogue = 0;
+        c.legacy_kernel = modes().register_kernel;
         return run_fast(c, stream);
     }
     return run_generic(w, s, b, x, y, rows, cols, bits, group, batch, bf16, stream);
@@ -534,6 +536,7 @@ int qmr_init(int device, uint32_t flags) {
     m.batched_delta = batched;
     m.initialised = true;
     std::lock_guard<std::mutex> lock(g_modes_mu);
+    m.register_kernel = g_modes.register_kernel;
     g_modes = m;
     return QMR_OK;
 }
@@ -796,6 +799,7 @@ int qmr_gateup_swiglu(const void *w_gate, const void *s_gate, const void *b_gate
     c.batch = batch;
     c.bf16 = meta_bf16 != 0;
     c.epilogue = 1;
+    c.legacy_kernel = modes().register_kernel;
     return run_fast(c, static_cast<cudaStream_t>(stream));
 }
 
@@ -821,6 +825,7 @@ int qmr_head_argmax(const void *w, const void *scales, const void *biases, const
     c.row_base = row_base;
     c.bf16 = meta_bf16 != 0;
     c.epilogue = 2;
+    c.legacy_kernel = modes().register_kernel;
     return run_fast(c, static_cast<cudaStream_t>(stream));
 }
 
@@ -868,6 +873,7 @@ int qmr_matmul_prepared(const void *w, const void *scales, const void *biases, c
     c.bf16 = meta_bf16 != 0;
     c.r2 = sel != nullptr && strcmp(sel, "matmul_q4_g64_b3_mlp_r2_aligned_bf16") == 0;
     c.epilogue = 0;
+    c.legacy_kernel = m.register_kernel;
     return run_stream(c, const_cast<void *>(prepared), static_cast<cudaStream_t>(stream));
 }
 
@@ -876,6 +882,25 @@ int qmr_copy_f32(const float *x, float *y, uint32_t n, void *stream) {
     if (x == y) return QMR_OK;
     return check_cuda(cudaMemcpyAsync(y, x, (size_t)n * 4, cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream)),
                       "copy_f32");
+}
+
+int qmr_set_stream_path(const char *path) {
+    if (path == nullptr) return fail(QMR_EINVAL, "null path");
+    bool reg;
+    if (strcmp(path, "tma") == 0)
+        reg = false;
+    else if (strcmp(path, "registers") == 0)
+        reg = true;
+    else
+        return fail(QMR_EINVAL, "stream path must be tma or registers");
+    std::lock_guard<std::mutex> lock(g_modes_mu);
+    g_modes.register_kernel = reg;
+    return QMR_OK;
+}
+
+int qmr_device_error(int *code, int clear) {
+    if (code == nullptr) return fail(QMR_EINVAL, "null code");
+    return device_error(code, clear != 0);
 }
 
 int qmr_stream_sync(void *stream) {

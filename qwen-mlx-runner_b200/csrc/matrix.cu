@@ -11,8 +11,10 @@
 
 #include "matrix_kernels.cuh"
 #include "qmr_internal.h"
+#include "tma_stream.cuh"
 
 namespace qmr {
+
 
 namespace {
 
@@ -178,6 +180,84 @@ int launch_stream(const StreamArgs &a, int bits, bool bf16, uint32_t batch, bool
                 : launch_stream_b<8, false, EPI>(a, batch, r2, stream);
 }
 
+constexpr int kTmaConsumers = 8;
+constexpr int kTmaSliceChunks = 64;
+constexpr int kTmaSmemBudget = 200 * 1024;
+
+int sm_count() {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    return n;
+}
+
+template <int BITS, int B, int R, bool BF16, int EPI>
+int launch_tma_t(const TmaArgs &a0, cudaStream_t stream) {
+    constexpr int NM = (EPI == 1) ? 2 : 1;
+    constexpr int TR = kTmaConsumers * R;
+    TmaArgs a = a0;
+    a.slice_chunks = kTmaSliceChunks;
+    const StageLayout L = stage_layout(NM, TR, a.slice_chunks, a.group_shift, a.meta_bytes);
+    int stages = kTmaSmemBudget / (int)L.stage_bytes;
+    if (stages > 8) stages = 8;
+    if (stages < 2) return fail(QMR_EUNSUPPORTED, "stage of %u bytes does not fit shared memory", L.stage_bytes);
+    a.stages = stages;
+    const size_t smem = (size_t)stages * L.stage_bytes + (size_t)stages * 2 * sizeof(uint64_t);
+    auto kern = tma_stream_kernel<BITS, B, R, kTmaConsumers, BF16, EPI>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return fail(QMR_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    int grid = (a.rows + TR - 1) / TR;
+    const int sms = sm_count();
+    if (grid > sms) grid = sms;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(32 * (kTmaConsumers + 1), 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, a);
+    if (e != cudaSuccess) return fail(QMR_ECUDA, "TMA stream kernel launch failed: %s", cudaGetErrorString(e));
+    return QMR_OK;
+}
+
+template <int BITS, bool BF16, int EPI>
+int launch_tma_b(const TmaArgs &a, uint32_t batch, bool r2, cudaStream_t stream) {
+    if constexpr (EPI == 1) {
+        switch (batch) {
+            case 1: return launch_tma_t<BITS, 1, 2, BF16, EPI>(a, stream);
+            case 2: return launch_tma_t<BITS, 2, 2, BF16, EPI>(a, stream);
+            case 3: return launch_tma_t<BITS, 3, 2, BF16, EPI>(a, stream);
+            default: return launch_tma_t<BITS, 4, 2, BF16, EPI>(a, stream);
+        }
+    } else {
+        if (r2 && EPI == 0) {
+            switch (batch) {
+                case 1: return launch_tma_t<BITS, 1, 2, BF16, EPI>(a, stream);
+                case 2: return launch_tma_t<BITS, 2, 2, BF16, EPI>(a, stream);
+                case 3: return launch_tma_t<BITS, 3, 2, BF16, EPI>(a, stream);
+                default: return launch_tma_t<BITS, 4, 2, BF16, EPI>(a, stream);
+            }
+        }
+        switch (batch) {
+            case 1: return launch_tma_t<BITS, 1, 4, BF16, EPI>(a, stream);
+            case 2: return launch_tma_t<BITS, 2, 4, BF16, EPI>(a, stream);
+            case 3: return launch_tma_t<BITS, 3, 4, BF16, EPI>(a, stream);
+            default: return launch_tma_t<BITS, 4, 4, BF16, EPI>(a, stream);
+        }
+    }
+}
+
+template <int EPI>
+int launch_tma(const TmaArgs &a, int bits, bool bf16, uint32_t batch, bool r2, cudaStream_t stream) {
+    if (bits == 4)
+        return bf16 ? launch_tma_b<4, true, EPI>(a, batch, r2, stream) : launch_tma_b<4, false, EPI>(a, batch, r2, stream);
+    return bf16 ? launch_tma_b<8, true, EPI>(a, batch, r2, stream) : launch_tma_b<8, false, EPI>(a, batch, r2, stream);
+}
+
 }  // namespace
 
 int run_prepare(const float *x, uint32_t cols, uint32_t bits, uint32_t batch, void *base, bool argmax,
@@ -188,9 +268,46 @@ int run_prepare(const float *x, uint32_t cols, uint32_t bits, uint32_t batch, vo
                      : launch_prep<8>(x, cols, batch, sv, argmax, stream);
 }
 
+bool tma_eligible(const FastCall &c) {
+    const uint32_t gpc = c.group / (128 / c.bits);
+    const uint64_t meta = c.bf16 ? 2 : 4;
+    const uint64_t nchunks = (uint64_t)c.cols * c.bits / 128;
+    if ((nchunks / gpc) * meta % 16 != 0) return false;            // metadata row bytes
+    if ((kTmaSliceChunks / gpc) * meta % 16 != 0) return false;    // metadata slice bytes
+    auto al = [](const void *p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+    return al(c.w) && al(c.s) && al(c.b) && al(c.w2) && al(c.s2) && al(c.b2);
+}
+
 int run_stream(const FastCall &c, void *base, cudaStream_t stream) {
     ScratchView sv;
     scratch_layout(base, (int)c.bits, c.cols, c.batch, &sv);
+    if (!c.legacy_kernel && tma_eligible(c)) {
+        TmaArgs t = {};
+        t.w = static_cast<const uint8_t *>(c.w);
+        t.s = static_cast<const uint8_t *>(c.s);
+        t.b = static_cast<const uint8_t *>(c.b);
+        t.w2 = static_cast<const uint8_t *>(c.w2);
+        t.s2 = static_cast<const uint8_t *>(c.s2);
+        t.b2 = static_cast<const uint8_t *>(c.b2);
+        t.xp = sv.xp;
+        t.xs = sv.xs;
+        t.y = c.y;
+        t.keys = sv.keys;
+        t.counter = sv.counter;
+        t.argmax = c.argmax;
+        t.best_key_out = reinterpret_cast<unsigned long long *>(c.best_key);
+        t.rows = (int)c.rows;
+        t.nchunks = (int)((uint64_t)c.cols * c.bits / 128);
+        t.group_shift = log2i(c.group / (128 / c.bits));
+        t.meta_bytes = c.bf16 ? 2 : 4;
+        t.ystride = (int)c.rows;
+        t.row_base = (int)c.row_base;
+        switch (c.epilogue) {
+            case 0: return launch_tma<0>(t, (int)c.bits, c.bf16, c.batch, c.r2, stream);
+            case 1: return launch_tma<1>(t, (int)c.bits, c.bf16, c.batch, c.r2, stream);
+            default: return launch_tma<2>(t, (int)c.bits, c.bf16, c.batch, c.r2, stream);
+        }
+    }
     StreamArgs a = {};
     a.w = static_cast<const uint4 *>(c.w);
     a.s = c.s;
@@ -229,6 +346,19 @@ int run_fast(const FastCall &c, cudaStream_t stream) {
     const int rc = run_prepare(c.x, c.cols, c.bits, c.batch, base, c.epilogue == 2, stream);
     if (rc != QMR_OK) return rc;
     return run_stream(c, base, stream);
+}
+
+int device_error(int *code, bool clear) {
+    unsigned int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, g_qmr_device_error, sizeof v);
+    if (e != cudaSuccess) return fail(QMR_ECUDA, "reading the device error word: %s", cudaGetErrorString(e));
+    if (clear && v != 0) {
+        const unsigned int zero = 0;
+        e = cudaMemcpyToSymbol(g_qmr_device_error, &zero, sizeof zero);
+        if (e != cudaSuccess) return fail(QMR_ECUDA, "clearing the device error word: %s", cudaGetErrorString(e));
+    }
+    *code = (int)v;
+    return QMR_OK;
 }
 
 int run_generic(const void *w, const void *s, const void *b, const float *x, float *y, uint32_t rows,

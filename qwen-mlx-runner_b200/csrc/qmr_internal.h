@@ -32,6 +32,7 @@ struct FastCall {
     bool bf16;
     bool r2;                    // two rows per warp (selective R2)
     int epilogue;               // 0 plain, 1 swiglu, 2 head argmax
+    bool legacy_kernel;         // force the register-streaming kernel (tests and A/B runs)
     void *scratch;              // caller scratch or nullptr for the per-stream pool
     size_t scratch_bytes;
 };
@@ -45,6 +46,7 @@ int run_fast(const FastCall &c, cudaStream_t stream);
 int run_prepare(const float *x, uint32_t cols, uint32_t bits, uint32_t batch, void *base, bool argmax,
                 cudaStream_t stream);
 int run_stream(const FastCall &c, void *base, cudaStream_t stream);
+int device_error(int *code, bool clear);
 int run_generic(const void *w, const void *s, const void *b, const float *x, float *y, uint32_t rows,
                 uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch, bool bf16, cudaStream_t stream);
 int run_embed(const void *w, const void *s, const void *b, uint32_t row, float *y, uint32_t cols, uint32_t bits,

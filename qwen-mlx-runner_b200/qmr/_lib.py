@@ -83,6 +83,8 @@ SIGNATURES = {
     "qmr_matmul_prepared": (_int, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _int, _vp]),
     "qmr_copy_f32": (_int, [_vp, _vp, _u32, _vp]),
     "qmr_stream_sync": (_int, [_vp]),
+    "qmr_set_stream_path": (_int, [_cstr]),
+    "qmr_device_error": (_int, [ctypes.POINTER(_int), _int]),
 }
 
 

@@ -144,6 +144,19 @@ def init(device: int = 0, reference: bool = False) -> None:
     check(_lib.lib().qmr_init(device, _lib.INIT_REFERENCE if reference else _lib.INIT_FROM_ENV))
 
 
+def set_stream_path(path: str) -> None:
+    """"tma" (default) or "registers": the streaming kernel of the fast path."""
+    check(_lib.lib().qmr_set_stream_path(path.encode()))
+
+
+def device_error(clear: bool = False) -> int:
+    """Error word of the bounded device waits (0 = none).  Synchronises."""
+    import ctypes
+    code = ctypes.c_int()
+    check(_lib.lib().qmr_device_error(ctypes.byref(code), int(clear)))
+    return code.value
+
+
 def decode_key(key: int):
     """(index, f32 logit) from a packed argmax key (qmr_head_argmax best_key)."""
     import struct

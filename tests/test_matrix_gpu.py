@@ -474,3 +474,44 @@ def test_typed_wrappers_reject_undersized_views_before_launch(cuda):
         qmr.matmul_affine(m, x, y[:rows], 3)
     with pytest.raises(QmrError):
         qmr.embed_affine(m, rows, y)
+
+
+@pytest.mark.parametrize("bits,meta", [(4, "bf16"), (4, "f32"), (8, "bf16")])
+def test_tma_and_register_streaming_paths_agree_bit_for_bit(cuda, bits, meta):
+    """The warp-specialised TMA pipeline and the register-streaming kernel use
+    the same arithmetic: every shape (slices, partial tiles, tails) must give
+    identical bits.  Also checks that no bounded device wait ran out."""
+    shapes = [(17408, 5120), (5120, 17408), (4, 512), (37, 2176), (1000, 3072), (300, 1024)]
+    try:
+        for rows, cols in shapes:
+            mat = synth.affine_matrix(rows, cols, bits, 64, seed=rows + cols, meta=meta)
+            m = synth.to_device(mat, rows, cols, bits, 64)
+            for batch in (1, 2, 3, 4):
+                x = f32_tensor(synth.activations(batch, cols, seed=batch).ravel())
+                outs = []
+                for path in ("tma", "registers"):
+                    qmr.ops.set_stream_path(path)
+                    y = torch.full((batch * rows,), float("nan"), dtype=torch.float32, device="cuda")
+                    qmr.matmul_affine(m, x, y, batch)
+                    outs.append(y.cpu().numpy())
+                assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32)), (rows, cols, batch)
+                assert np.all(np.isfinite(outs[0]))
+            if rows >= 1000 and bits == 4 and meta == "bf16":
+                up = synth.to_device(synth.affine_matrix(rows, cols, bits, 64, seed=7, meta=meta), rows, cols, bits,
+                                     64)
+                x = f32_tensor(synth.activations(3, cols, seed=9).ravel())
+                acts, idxs = [], []
+                for path in ("tma", "registers"):
+                    qmr.ops.set_stream_path(path)
+                    act = torch.empty(3 * rows, dtype=torch.float32, device="cuda")
+                    qmr.gateup_swiglu(m, up, x, act, 3)
+                    lg = torch.empty(3 * rows, dtype=torch.float32, device="cuda")
+                    idx = torch.empty(3, dtype=torch.int32, device="cuda")
+                    qmr.head_argmax(m, x, lg, idx, 3)
+                    acts.append(act.cpu().numpy())
+                    idxs.append(idx.cpu().numpy())
+                assert np.array_equal(acts[0].view(np.uint32), acts[1].view(np.uint32))
+                assert np.array_equal(idxs[0], idxs[1])
+        assert qmr.ops.device_error() == 0
+    finally:
+        qmr.ops.set_stream_path("tma")
