@@ -285,7 +285,7 @@ def kernel_only_ms(wl, stream, steps):
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=stream):
         for i in range(n):
-            qmr.ops.matmul_prepared(wl.mats[i % wl.copies], prepared, wl.y, wl.batch, stream=stream)
+            qmr.ops.matmul_prepared(wl.mats[i % wl.copies], prepared, wl.y, wl.batch, overlap=True, stream=stream)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):

@@ -189,12 +189,21 @@ uint64_t qmr_prepared_bytes(uint32_t bits, uint32_t cols, uint32_t batch);
 int qmr_prepare_activations(const float *x, uint32_t cols, uint32_t bits, uint32_t batch, void *prepared,
                             uint64_t prepared_bytes, void *stream);
 
+/* qmr_matmul_prepared flag: the kernel may start while the previous kernel
+ * on the stream is still running and read the weights and metadata early
+ * (programmatic dependent launch).  Set it only when the previous kernel
+ * does not write this matrix; activations, outputs and the prepared buffer
+ * are always read or written after the previous kernel completed. */
+#define QMR_PREPARED_OVERLAP 1u
+
 /* qmr_matmul_affine from prepared activations (same bits, cols, batch).
  * Weights must be 16-byte aligned with 16-byte multiple rows and group
- * 32/64/128; the result equals qmr_matmul_affine bit for bit. */
+ * 32/64/128; the result equals qmr_matmul_affine bit for bit.  Calls that
+ * share one prepared buffer must not overlap on the GPU (it also holds the
+ * split-K partial sums). */
 int qmr_matmul_prepared(const void *w, const void *scales, const void *biases, const void *prepared, float *y,
                         uint32_t rows, uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch,
-                        int meta_bf16, void *stream);
+                        int meta_bf16, uint32_t flags, void *stream);
 
 /* copy_f32 (kernels/matmul_block.metal:315-318): y[i] = x[i], i < n. */
 int qmr_copy_f32(const float *x, float *y, uint32_t n, void *stream);

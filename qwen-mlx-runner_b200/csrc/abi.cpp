@@ -846,12 +846,12 @@ int qmr_prepare_activations(const float *x, uint32_t cols, uint32_t bits, uint32
     if (prepared_bytes < scratch_bytes((int)bits, cols, batch))
         return fail(QMR_ERANGE, "prepared buffer of %llu bytes is smaller than %llu", (unsigned long long)prepared_bytes,
                     (unsigned long long)scratch_bytes((int)bits, cols, batch));
-    return run_prepare(x, cols, bits, batch, prepared, false, static_cast<cudaStream_t>(stream));
+    return run_prepare(x, cols, bits, batch, prepared, static_cast<cudaStream_t>(stream));
 }
 
 int qmr_matmul_prepared(const void *w, const void *scales, const void *biases, const void *prepared, float *y,
                         uint32_t rows, uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch, int meta_bf16,
-                        void *stream) {
+                        uint32_t flags, void *stream) {
     int rc = typed_fast_check(w, rows, cols, bits, group, batch, meta_bf16, "qmr_matmul_prepared");
     if (rc != QMR_OK) return rc;
     if (prepared == nullptr || reinterpret_cast<uintptr_t>(prepared) % 256 != 0)
@@ -874,6 +874,7 @@ int qmr_matmul_prepared(const void *w, const void *scales, const void *biases, c
     c.r2 = sel != nullptr && strcmp(sel, "matmul_q4_g64_b3_mlp_r2_aligned_bf16") == 0;
     c.epilogue = 0;
     c.legacy_kernel = m.register_kernel;
+    c.overlap = (flags & QMR_PREPARED_OVERLAP) != 0;
     return run_stream(c, const_cast<void *>(prepared), static_cast<cudaStream_t>(stream));
 }
 

@@ -1,6 +1,6 @@
-// Launchers for the packed-affine kernels: kernel choice for B200, the
-// activation scratch, and programmatic dependent launch of the streaming
-// kernel after its prep pass.
+// Launchers for the packed-affine kernels: kernel choice and launch shape for
+// B200, the prepared-activation scratch, and programmatic dependent launch of
+// the streaming kernel behind its prep pass.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -11,10 +11,9 @@
 
 #include "matrix_kernels.cuh"
 #include "qmr_internal.h"
-#include "tma_stream.cuh"
+#include "rowlane.cuh"
 
 namespace qmr {
-
 
 namespace {
 
@@ -26,32 +25,50 @@ struct Scratch {
 std::mutex g_scratch_mu;
 std::map<std::pair<int, cudaStream_t>, Scratch> g_scratch;
 
-constexpr size_t kScratchAlign = 256;
+constexpr size_t kAlign = 256;
+size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
-size_t align_up(size_t v) { return (v + kScratchAlign - 1) / kScratchAlign * kScratchAlign; }
+constexpr int kConsumers = 8;  // consumer warps of the row-lane kernel
+constexpr int kSmemBudget = 220 * 1024;
+constexpr int kMinRowsPerSm = 96;  // below this, split K across CTAs
+
+int log2i(uint32_t v) {
+    int r = 0;
+    while ((1u << r) < v) ++r;
+    return r;
+}
+
+int sm_count() {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    return n;
+}
+
+void scratch_layout(void *base, int bits, uint32_t cols, uint32_t batch, ScratchView *v) {
+    const size_t nchunks = (size_t)cols * bits / 128;
+    char *p = static_cast<char *>(base);
+    v->xp = reinterpret_cast<float *>(p);
+    p += align_up((size_t)batch * cols * sizeof(float));
+    v->xs = reinterpret_cast<float *>(p);
+    p += align_up((size_t)batch * nchunks * sizeof(float));
+    v->cf = reinterpret_cast<float *>(p);
+    p += align_up(8 * sizeof(float));
+    v->keys = reinterpret_cast<unsigned long long *>(p);
+    v->done = reinterpret_cast<unsigned int *>(p + 4 * sizeof(unsigned long long));
+    p += align_up(4 * sizeof(unsigned long long) + sizeof(unsigned int));
+    v->counters = reinterpret_cast<unsigned int *>(p);
+    p += align_up(kCounterCount * sizeof(unsigned int));
+    v->partial = reinterpret_cast<float *>(p);
+}
 
 }  // namespace
 
 size_t scratch_bytes(int bits, uint32_t cols, uint32_t batch) {
-    const size_t elems = 128 / bits;
     const size_t nchunks = (size_t)cols * bits / 128;
-    const size_t nblocks = (nchunks + 31) / 32;
-    const size_t xp = batch * nblocks * 32 * elems * sizeof(float);
-    const size_t xs = batch * nchunks * sizeof(float4);
-    return align_up(xp) + align_up(xs) + align_up(4 * sizeof(unsigned long long) + sizeof(unsigned int));
-}
-
-void scratch_layout(void *base, int bits, uint32_t cols, uint32_t batch, ScratchView *v) {
-    const size_t elems = 128 / bits;
-    const size_t nchunks = (size_t)cols * bits / 128;
-    const size_t nblocks = (nchunks + 31) / 32;
-    const size_t xp = align_up(batch * nblocks * 32 * elems * sizeof(float));
-    const size_t xs = align_up(batch * nchunks * sizeof(float4));
-    char *p = static_cast<char *>(base);
-    v->xp = reinterpret_cast<float4 *>(p);
-    v->xs = reinterpret_cast<float4 *>(p + xp);
-    v->keys = reinterpret_cast<unsigned long long *>(p + xp + xs);
-    v->counter = reinterpret_cast<unsigned int *>(v->keys + 4);
+    return align_up((size_t)batch * cols * sizeof(float)) + align_up((size_t)batch * nchunks * sizeof(float)) +
+           align_up(8 * sizeof(float)) + align_up(4 * sizeof(unsigned long long) + sizeof(unsigned int)) +
+           align_up(kCounterCount * sizeof(unsigned int)) + align_up(kPartialFloats * sizeof(float));
 }
 
 // Per (device, stream) scratch.  The first call on a stream reserves enough
@@ -66,7 +83,8 @@ int acquire_scratch(cudaStream_t stream, size_t need, void **out) {
         *out = s.base;
         return QMR_OK;
     }
-    const size_t want = need > scratch_bytes(4, 65536, 4) ? need : scratch_bytes(4, 65536, 4);
+    const size_t floor_bytes = scratch_bytes(4, 65536, 4);
+    const size_t want = need > floor_bytes ? need : floor_bytes;
     if (s.base != nullptr) {
         cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
         cudaStreamIsCapturing(stream, &cs);
@@ -80,8 +98,10 @@ int acquire_scratch(cudaStream_t stream, size_t need, void **out) {
         s.bytes = 0;
     }
     void *p = nullptr;
-    const cudaError_t e = cudaMalloc(&p, want);
+    cudaError_t e = cudaMalloc(&p, want);
     if (e != cudaSuccess) return fail(QMR_ECUDA, "cudaMalloc of activation scratch failed: %s", cudaGetErrorString(e));
+    e = cudaMemset(p, 0, want);  // counters start at zero
+    if (e != cudaSuccess) return fail(QMR_ECUDA, "cudaMemset of activation scratch failed: %s", cudaGetErrorString(e));
     s.base = p;
     s.bytes = want;
     *out = p;
@@ -99,213 +119,195 @@ bool fast_eligible(const void *w, uint32_t cols, uint32_t bits, uint32_t group) 
 
 namespace {
 
-int log2i(uint32_t v) {
-    int r = 0;
-    while ((1u << r) < v) ++r;
-    return r;
-}
-
 template <int BITS>
-int launch_prep(const float *x, uint32_t cols, uint32_t batch, const ScratchView &sv, bool argmax,
-                cudaStream_t stream) {
-    constexpr int elems = Chunk<BITS>::elems;
+int launch_prep(const float *x, uint32_t cols, uint32_t batch, const ScratchView &sv, cudaStream_t stream) {
     const int nchunks = (int)((uint64_t)cols * BITS / 128);
-    const int tasks = (int)batch * nchunks;
-    const int warps = (tasks * elems + 31) / 32;
-    int blocks = (warps + 7) / 8;
-    if (blocks < 1) blocks = 1;
-    if (blocks > 1184) blocks = 1184;
-    prep_kernel<BITS><<<blocks, 256, 0, stream>>>(x, (int)cols, (int)batch, nchunks, sv.xp, sv.xs,
-                                                  argmax ? sv.keys : nullptr, sv.counter);
+    prep_kernel<BITS><<<batch, 512, 0, stream>>>(x, (int)cols, nchunks, sv);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(QMR_ECUDA, "prep launch failed: %s", cudaGetErrorString(e));
     return QMR_OK;
 }
 
+cudaLaunchAttribute pdl_attr() {
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    return attr;
+}
+
+// ---- register-streaming fallback ------------------------------------------
+
 template <int BITS, int B, int R, bool BF16, int EPI>
-int launch_stream_t(const StreamArgs &a, cudaStream_t stream) {
+int launch_stream_t(const StreamArgs &a, bool overlap, cudaStream_t stream) {
     const int warps = (a.rows + R - 1) / R;
     const int blocks = (warps + 7) / 8;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(blocks, 1, 1);
     cfg.blockDim = dim3(256, 1, 1);
-    cfg.dynamicSmemBytes = 0;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[1] = {pdl_attr()};
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = overlap ? 1 : 0;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, stream_kernel<BITS, B, R, BF16, EPI>, a);
     if (e != cudaSuccess) return fail(QMR_ECUDA, "stream kernel launch failed: %s", cudaGetErrorString(e));
     return QMR_OK;
 }
 
-// Rows per warp for each (block width, epilogue); `r2` forces two rows per
-// warp (the reference's selective R2 schedule).  Results do not depend on it.
 template <int BITS, bool BF16, int EPI>
-int launch_stream_b(const StreamArgs &a, uint32_t batch, bool r2, cudaStream_t stream) {
-    if (r2) {
-        switch (batch) {
-            case 1: return launch_stream_t<BITS, 1, 2, BF16, EPI>(a, stream);
-            case 2: return launch_stream_t<BITS, 2, 2, BF16, EPI>(a, stream);
-            case 3: return launch_stream_t<BITS, 3, 2, BF16, EPI>(a, stream);
-            default: return launch_stream_t<BITS, 4, 2, BF16, EPI>(a, stream);
-        }
-    }
-    if constexpr (EPI == 1) {
-        switch (batch) {
-            case 1: return launch_stream_t<BITS, 1, 2, BF16, EPI>(a, stream);
-            case 2: return launch_stream_t<BITS, 2, 2, BF16, EPI>(a, stream);
-            case 3: return launch_stream_t<BITS, 3, 2, BF16, EPI>(a, stream);
-            default: return launch_stream_t<BITS, 4, 2, BF16, EPI>(a, stream);
-        }
-    } else {
-        switch (batch) {
-            case 1: return launch_stream_t<BITS, 1, 4, BF16, EPI>(a, stream);
-            case 2: return launch_stream_t<BITS, 2, 4, BF16, EPI>(a, stream);
-            case 3: return launch_stream_t<BITS, 3, 4, BF16, EPI>(a, stream);
-            default: return launch_stream_t<BITS, 4, 2, BF16, EPI>(a, stream);
-        }
+int launch_stream_b(const StreamArgs &a, uint32_t batch, bool ov, cudaStream_t stream) {
+    switch (batch) {
+        case 1: return launch_stream_t<BITS, 1, 2, BF16, EPI>(a, ov, stream);
+        case 2: return launch_stream_t<BITS, 2, 2, BF16, EPI>(a, ov, stream);
+        case 3: return launch_stream_t<BITS, 3, 2, BF16, EPI>(a, ov, stream);
+        default: return launch_stream_t<BITS, 4, 2, BF16, EPI>(a, ov, stream);
     }
 }
 
 template <int EPI>
-int launch_stream(const StreamArgs &a, int bits, bool bf16, uint32_t batch, bool r2, cudaStream_t stream) {
-    if (bits == 4) {
-        return bf16 ? launch_stream_b<4, true, EPI>(a, batch, r2, stream)
-                    : launch_stream_b<4, false, EPI>(a, batch, r2, stream);
-    }
-    return bf16 ? launch_stream_b<8, true, EPI>(a, batch, r2, stream)
-                : launch_stream_b<8, false, EPI>(a, batch, r2, stream);
+int launch_stream(const StreamArgs &a, int bits, bool bf16, uint32_t batch, bool ov, cudaStream_t stream) {
+    if (bits == 4)
+        return bf16 ? launch_stream_b<4, true, EPI>(a, batch, ov, stream)
+                    : launch_stream_b<4, false, EPI>(a, batch, ov, stream);
+    return bf16 ? launch_stream_b<8, true, EPI>(a, batch, ov, stream) : launch_stream_b<8, false, EPI>(a, batch, ov, stream);
 }
 
-constexpr int kTmaConsumers = 8;
-constexpr int kTmaSliceChunks = 64;
-constexpr int kTmaSmemBudget = 200 * 1024;
-
-int sm_count() {
-    int dev = 0, n = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    return n;
-}
+// ---- row-lane TMA kernel ----------------------------------------------------
 
 template <int BITS, int B, int R, bool BF16, int EPI>
-int launch_tma_t(const TmaArgs &a0, cudaStream_t stream) {
+int launch_rowlane_t(RowlaneArgs a, bool overlap, cudaStream_t stream) {
     constexpr int NM = (EPI == 1) ? 2 : 1;
-    constexpr int TR = kTmaConsumers * R;
-    TmaArgs a = a0;
-    a.slice_chunks = kTmaSliceChunks;
-    const StageLayout L = stage_layout(NM, TR, a.slice_chunks, a.group_shift, a.meta_bytes);
-    int stages = kTmaSmemBudget / (int)L.stage_bytes;
+    constexpr int TR = 32 * R;
+    constexpr int CE = Chunk<BITS>::elems;
+    const RowlaneLayout L = rowlane_layout(NM, TR, a.slice_chunks, CE, B, a.group_shift, a.meta_bytes);
+    const size_t red = (size_t)(kConsumers + 1) * NM * B * R * 32 * sizeof(float);
+    int stages = (int)((kSmemBudget - red) / (L.stage_bytes + 2 * sizeof(uint64_t)));
     if (stages > 8) stages = 8;
-    if (stages < 2) return fail(QMR_EUNSUPPORTED, "stage of %u bytes does not fit shared memory", L.stage_bytes);
+    if (stages < 2) return fail(QMR_EUNSUPPORTED, "a %u-byte stage does not fit shared memory", L.stage_bytes);
     a.stages = stages;
-    const size_t smem = (size_t)stages * L.stage_bytes + (size_t)stages * 2 * sizeof(uint64_t);
-    auto kern = tma_stream_kernel<BITS, B, R, kTmaConsumers, BF16, EPI>;
+    const size_t smem = (size_t)stages * L.stage_bytes + (size_t)stages * 2 * sizeof(uint64_t) + red;
+    // Split-K bookkeeping: at most 4 tiles per row range use the counters.
+    const int rows_per_range = (a.rows + a.ranges - 1) / a.ranges;
+    if (a.ksplit > 1 && ((rows_per_range + TR - 1) / TR > 4 || a.ranges > 256))
+        return fail(QMR_EUNSUPPORTED, "split-K launch shape exceeds the counter space");
+    auto kern = rowlane_kernel<BITS, B, R, kConsumers, BF16, EPI>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(QMR_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    int grid = (a.rows + TR - 1) / TR;
-    const int sms = sm_count();
-    if (grid > sms) grid = sms;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid, 1, 1);
-    cfg.blockDim = dim3(32 * (kTmaConsumers + 1), 1, 1);
+    cfg.gridDim = dim3(a.ranges * a.ksplit, 1, 1);
+    cfg.blockDim = dim3(32 * (kConsumers + 1), 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[1] = {pdl_attr()};
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = overlap ? 1 : 0;
     e = cudaLaunchKernelEx(&cfg, kern, a);
-    if (e != cudaSuccess) return fail(QMR_ECUDA, "TMA stream kernel launch failed: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess) return fail(QMR_ECUDA, "row-lane kernel launch failed: %s", cudaGetErrorString(e));
     return QMR_OK;
 }
 
 template <int BITS, bool BF16, int EPI>
-int launch_tma_b(const TmaArgs &a, uint32_t batch, bool r2, cudaStream_t stream) {
-    if constexpr (EPI == 1) {
-        switch (batch) {
-            case 1: return launch_tma_t<BITS, 1, 2, BF16, EPI>(a, stream);
-            case 2: return launch_tma_t<BITS, 2, 2, BF16, EPI>(a, stream);
-            case 3: return launch_tma_t<BITS, 3, 2, BF16, EPI>(a, stream);
-            default: return launch_tma_t<BITS, 4, 2, BF16, EPI>(a, stream);
-        }
-    } else {
-        if (r2 && EPI == 0) {
+int launch_rowlane_b(const RowlaneArgs &a, uint32_t batch, int R, bool ov, cudaStream_t stream) {
+    if constexpr (EPI != 1) {
+        if (R == 4) {
             switch (batch) {
-                case 1: return launch_tma_t<BITS, 1, 2, BF16, EPI>(a, stream);
-                case 2: return launch_tma_t<BITS, 2, 2, BF16, EPI>(a, stream);
-                case 3: return launch_tma_t<BITS, 3, 2, BF16, EPI>(a, stream);
-                default: return launch_tma_t<BITS, 4, 2, BF16, EPI>(a, stream);
+                case 1: return launch_rowlane_t<BITS, 1, 4, BF16, EPI>(a, ov, stream);
+                case 2: return launch_rowlane_t<BITS, 2, 4, BF16, EPI>(a, ov, stream);
+                case 3: return launch_rowlane_t<BITS, 3, 4, BF16, EPI>(a, ov, stream);
+                default: return launch_rowlane_t<BITS, 4, 4, BF16, EPI>(a, ov, stream);
             }
         }
-        switch (batch) {
-            case 1: return launch_tma_t<BITS, 1, 4, BF16, EPI>(a, stream);
-            case 2: return launch_tma_t<BITS, 2, 4, BF16, EPI>(a, stream);
-            case 3: return launch_tma_t<BITS, 3, 4, BF16, EPI>(a, stream);
-            default: return launch_tma_t<BITS, 4, 4, BF16, EPI>(a, stream);
-        }
+    }
+    switch (batch) {
+        case 1: return launch_rowlane_t<BITS, 1, 2, BF16, EPI>(a, ov, stream);
+        case 2: return launch_rowlane_t<BITS, 2, 2, BF16, EPI>(a, ov, stream);
+        case 3: return launch_rowlane_t<BITS, 3, 2, BF16, EPI>(a, ov, stream);
+        default: return launch_rowlane_t<BITS, 4, 2, BF16, EPI>(a, ov, stream);
     }
 }
 
 template <int EPI>
-int launch_tma(const TmaArgs &a, int bits, bool bf16, uint32_t batch, bool r2, cudaStream_t stream) {
+int launch_rowlane(const RowlaneArgs &a, int bits, bool bf16, uint32_t batch, int R, bool ov, cudaStream_t stream) {
     if (bits == 4)
-        return bf16 ? launch_tma_b<4, true, EPI>(a, batch, r2, stream) : launch_tma_b<4, false, EPI>(a, batch, r2, stream);
-    return bf16 ? launch_tma_b<8, true, EPI>(a, batch, r2, stream) : launch_tma_b<8, false, EPI>(a, batch, r2, stream);
+        return bf16 ? launch_rowlane_b<4, true, EPI>(a, batch, R, ov, stream)
+                    : launch_rowlane_b<4, false, EPI>(a, batch, R, ov, stream);
+    return bf16 ? launch_rowlane_b<8, true, EPI>(a, batch, R, ov, stream)
+                : launch_rowlane_b<8, false, EPI>(a, batch, R, ov, stream);
+}
+
+bool rowlane_eligible(const FastCall &c, int slice_chunks) {
+    const uint32_t gpc = c.group / (128 / c.bits);
+    const uint64_t meta = c.bf16 ? 2 : 4;
+    const uint64_t nchunks = (uint64_t)c.cols * c.bits / 128;
+    if (nchunks % 4 != 0) return false;                  // chunk-sum slices of 16-byte multiples
+    if ((nchunks / gpc) * meta % 16 != 0) return false;  // metadata row bytes
+    if (((uint64_t)slice_chunks / gpc) * meta % 16 != 0) return false;
+    auto al = [](const void *p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+    return al(c.w) && al(c.s) && al(c.b) && al(c.w2) && al(c.s2) && al(c.b2);
 }
 
 }  // namespace
 
-int run_prepare(const float *x, uint32_t cols, uint32_t bits, uint32_t batch, void *base, bool argmax,
-                cudaStream_t stream) {
+int run_prepare(const float *x, uint32_t cols, uint32_t bits, uint32_t batch, void *base, cudaStream_t stream) {
     ScratchView sv;
     scratch_layout(base, (int)bits, cols, batch, &sv);
-    return bits == 4 ? launch_prep<4>(x, cols, batch, sv, argmax, stream)
-                     : launch_prep<8>(x, cols, batch, sv, argmax, stream);
-}
-
-bool tma_eligible(const FastCall &c) {
-    const uint32_t gpc = c.group / (128 / c.bits);
-    const uint64_t meta = c.bf16 ? 2 : 4;
-    const uint64_t nchunks = (uint64_t)c.cols * c.bits / 128;
-    if ((nchunks / gpc) * meta % 16 != 0) return false;            // metadata row bytes
-    if ((kTmaSliceChunks / gpc) * meta % 16 != 0) return false;    // metadata slice bytes
-    auto al = [](const void *p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; };
-    return al(c.w) && al(c.s) && al(c.b) && al(c.w2) && al(c.s2) && al(c.b2);
+    return bits == 4 ? launch_prep<4>(x, cols, batch, sv, stream) : launch_prep<8>(x, cols, batch, sv, stream);
 }
 
 int run_stream(const FastCall &c, void *base, cudaStream_t stream) {
     ScratchView sv;
     scratch_layout(base, (int)c.bits, c.cols, c.batch, &sv);
-    if (!c.legacy_kernel && tma_eligible(c)) {
-        TmaArgs t = {};
-        t.w = static_cast<const uint8_t *>(c.w);
-        t.s = static_cast<const uint8_t *>(c.s);
-        t.b = static_cast<const uint8_t *>(c.b);
-        t.w2 = static_cast<const uint8_t *>(c.w2);
-        t.s2 = static_cast<const uint8_t *>(c.s2);
-        t.b2 = static_cast<const uint8_t *>(c.b2);
-        t.xp = sv.xp;
-        t.xs = sv.xs;
-        t.y = c.y;
-        t.keys = sv.keys;
-        t.counter = sv.counter;
-        t.argmax = c.argmax;
-        t.best_key_out = reinterpret_cast<unsigned long long *>(c.best_key);
-        t.rows = (int)c.rows;
-        t.nchunks = (int)((uint64_t)c.cols * c.bits / 128);
-        t.group_shift = log2i(c.group / (128 / c.bits));
-        t.meta_bytes = c.bf16 ? 2 : 4;
-        t.ystride = (int)c.rows;
-        t.row_base = (int)c.row_base;
+    const int ce = 128 / (int)c.bits;
+    const int gpc = (int)c.group / ce;
+    const int meta = c.bf16 ? 2 : 4;
+    const int nchunks = (int)((uint64_t)c.cols * c.bits / 128);
+    int slice_chunks = 2 * kConsumers;
+    if (gpc * 16 / meta > slice_chunks) slice_chunks = gpc * 16 / meta;
+    if (!c.legacy_kernel && rowlane_eligible(c, slice_chunks)) {
+        const int NM = c.epilogue == 1 ? 2 : 1;
+        const int sms = sm_count();
+        const int nslices = (nchunks + slice_chunks - 1) / slice_chunks;
+        int ksplit = 1;
+        if ((int)c.rows < kMinRowsPerSm * sms) {
+            ksplit = (kMinRowsPerSm * sms + (int)c.rows - 1) / (int)c.rows;
+            if (ksplit > 4) ksplit = 4;
+            if (ksplit > nslices) ksplit = nslices;
+            while (ksplit > 1 && (size_t)ksplit * NM * c.batch * c.rows > kPartialFloats) --ksplit;
+        }
+        int ranges = sms / ksplit;
+        if (ranges > (int)c.rows) ranges = (int)c.rows;
+        if (ranges < 1) ranges = 1;
+        const int rows_per_range = ((int)c.rows + ranges - 1) / ranges;
+        const int R = (c.r2 || c.epilogue == 1 || rows_per_range <= 64) ? 2 : 4;
+        RowlaneArgs a = {};
+        a.w = static_cast<const uint8_t *>(c.w);
+        a.s = static_cast<const uint8_t *>(c.s);
+        a.b = static_cast<const uint8_t *>(c.b);
+        a.w2 = static_cast<const uint8_t *>(c.w2);
+        a.s2 = static_cast<const uint8_t *>(c.s2);
+        a.b2 = static_cast<const uint8_t *>(c.b2);
+        a.xp = sv.xp;
+        a.xs = sv.xs;
+        a.cf = sv.cf;
+        a.y = c.y;
+        a.partial = sv.partial;
+        a.range_counter = sv.counters;
+        a.done_counter = sv.done;
+        a.keys = sv.keys;
+        a.argmax = c.argmax;
+        a.best_key_out = reinterpret_cast<unsigned long long *>(c.best_key);
+        a.rows = (int)c.rows;
+        a.nchunks = nchunks;
+        a.group_shift = log2i((uint32_t)gpc);
+        a.meta_bytes = meta;
+        a.ystride = (int)c.rows;
+        a.row_base = (int)c.row_base;
+        a.ranges = ranges;
+        a.ksplit = ksplit;
+        a.slice_chunks = slice_chunks;
         switch (c.epilogue) {
-            case 0: return launch_tma<0>(t, (int)c.bits, c.bf16, c.batch, c.r2, stream);
-            case 1: return launch_tma<1>(t, (int)c.bits, c.bf16, c.batch, c.r2, stream);
-            default: return launch_tma<2>(t, (int)c.bits, c.bf16, c.batch, c.r2, stream);
+            case 0: return launch_rowlane<0>(a, (int)c.bits, c.bf16, c.batch, R, c.overlap, stream);
+            case 1: return launch_rowlane<1>(a, (int)c.bits, c.bf16, c.batch, R, c.overlap, stream);
+            default: return launch_rowlane<2>(a, (int)c.bits, c.bf16, c.batch, R, c.overlap, stream);
         }
     }
     StreamArgs a = {};
@@ -317,20 +319,21 @@ int run_stream(const FastCall &c, void *base, cudaStream_t stream) {
     a.bias2 = c.b2;
     a.xp = sv.xp;
     a.xs = sv.xs;
+    a.cf = sv.cf;
     a.y = c.y;
     a.keys = sv.keys;
-    a.counter = sv.counter;
+    a.done = sv.done;
     a.argmax = c.argmax;
     a.best_key_out = reinterpret_cast<unsigned long long *>(c.best_key);
     a.rows = (int)c.rows;
-    a.nchunks = (int)((uint64_t)c.cols * c.bits / 128);
-    a.group_shift = log2i(c.group / (128 / c.bits));
+    a.nchunks = nchunks;
+    a.group_shift = log2i((uint32_t)gpc);
     a.ystride = (int)c.rows;
     a.row_base = (int)c.row_base;
     switch (c.epilogue) {
-        case 0: return launch_stream<0>(a, (int)c.bits, c.bf16, c.batch, c.r2, stream);
-        case 1: return launch_stream<1>(a, (int)c.bits, c.bf16, c.batch, c.r2, stream);
-        default: return launch_stream<2>(a, (int)c.bits, c.bf16, c.batch, c.r2, stream);
+        case 0: return launch_stream<0>(a, (int)c.bits, c.bf16, c.batch, c.overlap, stream);
+        case 1: return launch_stream<1>(a, (int)c.bits, c.bf16, c.batch, c.overlap, stream);
+        default: return launch_stream<2>(a, (int)c.bits, c.bf16, c.batch, c.overlap, stream);
     }
 }
 
@@ -343,9 +346,11 @@ int run_fast(const FastCall &c, cudaStream_t stream) {
     } else if (c.scratch_bytes < need) {
         return fail(QMR_ERANGE, "scratch of %zu bytes is smaller than the %zu required", c.scratch_bytes, need);
     }
-    const int rc = run_prepare(c.x, c.cols, c.bits, c.batch, base, c.epilogue == 2, stream);
+    const int rc = run_prepare(c.x, c.cols, c.bits, c.batch, base, stream);
     if (rc != QMR_OK) return rc;
-    return run_stream(c, base, stream);
+    FastCall behind_prep = c;
+    behind_prep.overlap = true;  // the preceding kernel is our prep, which writes no weights
+    return run_stream(behind_prep, base, stream);
 }
 
 int device_error(int *code, bool clear) {
@@ -361,29 +366,27 @@ int device_error(int *code, bool clear) {
     return QMR_OK;
 }
 
-int run_generic(const void *w, const void *s, const void *b, const float *x, float *y, uint32_t rows,
-                uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch, bool bf16,
-                cudaStream_t stream) {
+int run_generic(const void *w, const void *s, const void *b, const float *x, float *y, uint32_t rows, uint32_t cols,
+                uint32_t bits, uint32_t group, uint32_t batch, bool bf16, cudaStream_t stream) {
     const uint64_t threads = (uint64_t)rows * 32;
     const uint64_t blocks = (threads + 255) / 256;
     if (blocks > 0x7fffffffull) return fail(QMR_EINVAL, "too many rows for one launch");
     if (bf16)
-        generic_kernel<true><<<(unsigned)blocks, 256, 0, stream>>>(static_cast<const uint32_t *>(w), s, b, x, y,
-                                                                   rows, cols, bits, group, batch);
+        generic_kernel<true><<<(unsigned)blocks, 256, 0, stream>>>(static_cast<const uint32_t *>(w), s, b, x, y, rows,
+                                                                   cols, bits, group, batch);
     else
-        generic_kernel<false><<<(unsigned)blocks, 256, 0, stream>>>(static_cast<const uint32_t *>(w), s, b, x, y,
-                                                                    rows, cols, bits, group, batch);
+        generic_kernel<false><<<(unsigned)blocks, 256, 0, stream>>>(static_cast<const uint32_t *>(w), s, b, x, y, rows,
+                                                                    cols, bits, group, batch);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(QMR_ECUDA, "generic launch failed: %s", cudaGetErrorString(e));
     return QMR_OK;
 }
 
-int run_embed(const void *w, const void *s, const void *b, uint32_t row, float *y, uint32_t cols,
-              uint32_t bits, uint32_t group, bool bf16, cudaStream_t stream) {
+int run_embed(const void *w, const void *s, const void *b, uint32_t row, float *y, uint32_t cols, uint32_t bits,
+              uint32_t group, bool bf16, cudaStream_t stream) {
     const unsigned blocks = (cols + 255) / 256;
     if (bf16)
-        embed_kernel<true><<<blocks, 256, 0, stream>>>(static_cast<const uint32_t *>(w), s, b, y, row, cols, bits,
-                                                       group);
+        embed_kernel<true><<<blocks, 256, 0, stream>>>(static_cast<const uint32_t *>(w), s, b, y, row, cols, bits, group);
     else
         embed_kernel<false><<<blocks, 256, 0, stream>>>(static_cast<const uint32_t *>(w), s, b, y, row, cols, bits,
                                                         group);

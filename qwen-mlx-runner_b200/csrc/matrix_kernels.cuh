@@ -1,27 +1,27 @@
-// Packed-affine dequantise-and-multiply kernels for sm_100a.
+// Packed-affine dequantise-and-multiply kernels for sm_100a: shared helpers,
+// the activation prep pass, the register-streaming fallback kernel, the
+// generic per-element kernel and the embed kernel.  The main streaming kernel
+// is rowlane.cuh.
 //
 // Semantics follow the reference's matrix kernels (rucin93/qwen-mlx-runner
 // v0.7.3): y[b*rows+r] = sum_c (q[r,c]*s[r,g]+b[r,g]) * x[b*cols+c], with
 // q little-endian inside each u32 word (kernels/qwen.metal:40-47), f32 or
 // bf16-high-half metadata (kernels/affine_bf16.metal:294-296) and token-major
 // block operands (kernels/matmul_block.metal:1-3).  The arithmetic schedule
-// is this file's own, built for B200:
+// is this build's own:
 //
-//  * Weights stream once from HBM with 16-byte non-allocating loads; one warp
-//    owns R rows and its lane l owns 16-byte chunks l, l+32, ... of each row,
-//    so a warp-wide load is 512 contiguous bytes of one row.
 //  * Dequantisation costs one LOP3 per element.  A nibble (or byte) masked in
 //    place, `w & (0xf << 4k)`, read as an f32 bit pattern is the exact
-//    subnormal q * 2^(4k-149).  The activation was pre-scaled by
-//    2^(E-4k) (prep kernel), so fma(subnormal, x', acc) accumulates
-//    q*x*2^(E-149) with one rounding, exactly like an f32 fma of q*x.  E is
-//    chosen per 32-element activation chunk so that no pre-scaled value
-//    overflows; the chunk result is scaled back by 2^(149-E) (two exact
-//    power-of-two multiplies) before the group scale and bias are applied.
-//    IEEE subnormals are required: this file must not be built with -ftz.
-//  * Products are accumulated with packed f32x2 FMAs (even/odd elements),
-//    every (row, RHS) pair in the same order whatever the block width B or
-//    rows-per-warp R, so a B-wide block equals B GEMVs bit for bit.
+//    subnormal q * 2^(4k-149).  The activation of RHS b was pre-scaled by
+//    2^(E_b - 4k) (prep_kernel), so fma(subnormal, x', acc) accumulates
+//    q*x*2^(E_b-149) with one rounding, exactly as an f32 fma of q*x would.
+//    E_b is chosen per RHS from max|x| so that no pre-scaled value overflows;
+//    outputs are scaled back by 2^(149-E_b) (two exact power-of-two
+//    multiplies).  IEEE subnormals are required: never build with -ftz.
+//  * Products accumulate in packed f32x2 FMAs (even/odd elements).  Each
+//    16-byte chunk (32 Q4 / 16 Q8 elements, inside one group) yields a
+//    partial p that is folded as acc += s*p (f32x2) and acc.x += bias*xsum'
+//    with xsum' the chunk's activation sum scaled by 2^(E_b-149).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -29,13 +29,11 @@
 
 namespace qmr {
 
-constexpr int kWarp = 32;
-
 // Elements per 16-byte chunk for a bit width.
 template <int BITS>
 struct Chunk {
-    static constexpr int elems = 128 / BITS;      // 32 for Q4, 16 for Q8
-    static constexpr int per_word = 32 / BITS;    // 8 for Q4, 4 for Q8
+    static constexpr int elems = 128 / BITS;    // 32 for Q4, 16 for Q8
+    static constexpr int per_word = 32 / BITS;  // 8 for Q4, 4 for Q8
 };
 
 // Pre-scale exponent offset f(k) of element k within its word: the power of
@@ -60,6 +58,15 @@ __device__ __forceinline__ float load_meta(const void *__restrict__ m, size_t i)
     }
 }
 
+template <bool BF16>
+__device__ __forceinline__ float smem_meta(const uint8_t *base, int i) {
+    if constexpr (BF16) {
+        return bf16_bits_to_f32(reinterpret_cast<const unsigned short *>(base)[i]);
+    } else {
+        return reinterpret_cast<const float *>(base)[i];
+    }
+}
+
 __device__ __forceinline__ uint4 ldg_stream(const uint4 *p) {
     uint4 v;
     asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -68,129 +75,13 @@ __device__ __forceinline__ uint4 ldg_stream(const uint4 *p) {
     return v;
 }
 
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-    return __ffma2_rn(a, b, c);
-}
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 
 // Subnormal view of a masked word.
 __device__ __forceinline__ float sub(uint32_t bits) { return __uint_as_float(bits); }
 
-// ---------------------------------------------------------------------------
-// Activation prep.  For every RHS b and 16-byte chunk j of a row (32 Q4 or 16
-// Q8 elements) writes
-//   xp : x[b, c] * 2^(E_j - f(c)) in the lane-interleaved order the streaming
-//        kernel reads (see xp_index), and
-//   xs : {sum_c x[b,c], 2^a, 2^(149-E_j-a), 0} with both factors normal.
-// E_j makes max|x'| < 2^125 inside the chunk.  Also zeroes the argmax
-// reduction slots when `keys` is non-null.
-// ---------------------------------------------------------------------------
-
-// Position, in float4 units, of the 4 pre-scaled values (j, word m, half h)
-// of RHS b: 32 consecutive lanes of a warp read 512 contiguous bytes.
-template <int BITS>
-__host__ __device__ __forceinline__ size_t xp_index(int b, int nblocks, int j, int m, int h) {
-    constexpr int halves = Chunk<BITS>::per_word / 4;  // float4s per word: 2 (Q4) or 1 (Q8)
-    const int jb = j >> 5, lane = j & 31;
-    return ((((size_t)b * nblocks + jb) * 4 + m) * halves + h) * 32 + lane;
-}
-
-template <int BITS>
-__global__ void __launch_bounds__(256) prep_kernel(const float *__restrict__ x, int cols, int batch,
-                                                  int nchunks, float4 *__restrict__ xp,
-                                                  float4 *__restrict__ xs,
-                                                  unsigned long long *__restrict__ keys,
-                                                  unsigned int *__restrict__ counter) {
-    // Let the dependent streaming kernel launch and start its weight loads.
-    asm volatile("griddepcontrol.launch_dependents;");
-    constexpr int E = Chunk<BITS>::elems;  // lanes per chunk: 32 (Q4) or 16 (Q8)
-    constexpr int per_warp = 32 / E;       // chunks per warp pass
-    const int lane = threadIdx.x & 31;
-    const int sub_lane = lane % E;
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int nwarps = (gridDim.x * blockDim.x) >> 5;
-    const int nblocks = (nchunks + 31) >> 5;
-    if (keys != nullptr && blockIdx.x == 0 && threadIdx.x < batch) {
-        keys[threadIdx.x] = 0ull;
-        if (threadIdx.x == 0) *counter = 0u;
-    }
-    const int total = batch * nchunks;
-    for (int t0 = warp * per_warp; t0 < total; t0 += nwarps * per_warp) {
-        const int t = t0 + lane / E;  // (b, j) handled by this lane group
-        const bool valid = t < total;
-        const int b = valid ? t / nchunks : 0;
-        const int j = valid ? t % nchunks : 0;
-        const float v = valid ? x[(size_t)b * cols + (size_t)j * E + sub_lane] : 0.0f;
-        // max |x| and sum x over the chunk, fixed butterfly order.
-        float mx = fabsf(v), sm = v;
-#pragma unroll
-        for (int o = E / 2; o > 0; o >>= 1) {
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            sm = sm + __shfl_xor_sync(0xffffffffu, sm, o);
-        }
-        // exponent of max|x|: max|x| < 2^(e+1).  Zero or subnormal chunks use
-        // e = -127 (any E works: products are exact or zero).
-        const uint32_t mb = __float_as_uint(mx);
-        int e = (int)((mb >> 23) & 0xff) - 127;
-        if (e < -127) e = -127;
-        int Ej = 124 - e;  // max|x| * 2^Ej < 2^125; e <= 128 -> Ej >= -4
-        const int k = sub_lane % Chunk<BITS>::per_word;
-        const float xv = ldexpf(v, Ej - prescale_shift<BITS>(k));
-        if (valid) {
-            const int m = sub_lane / Chunk<BITS>::per_word;
-            const int within = k;  // element inside the word
-            float *dst = reinterpret_cast<float *>(xp + xp_index<BITS>(b, nblocks, j, m, within >> 2));
-            dst[within & 3] = xv;
-            if (sub_lane == 0) {
-                int total_shift = 149 - Ej;  // in [-128, 276]
-                int a = total_shift > 120 ? 120 : (total_shift < -120 ? -120 : total_shift);
-                xs[(size_t)b * nchunks + j] =
-                    make_float4(sm, ldexpf(1.0f, a), ldexpf(1.0f, total_shift - a), 0.0f);
-            }
-        }
-    }
-}
-
-// ---------------------------------------------------------------------------
-// Streaming block kernel.  One warp = R consecutive rows, all B RHS.
-// EPI selects the epilogue:
-//   0: plain, y[b*ystride + row]
-//   1: gate/up SwiGLU: a second matrix (w2,s2,b2) with the same layout;
-//      y = silu(gate)*up
-//   2: head: y written as plain, plus argmax over rows into keys[b].
-// ---------------------------------------------------------------------------
-struct StreamArgs {
-    const uint4 *w;
-    const void *s;
-    const void *bias;
-    const uint4 *w2;  // EPI 1 (up projection)
-    const void *s2;
-    const void *bias2;
-    const float4 *xp;
-    const float4 *xs;
-    float *y;
-    unsigned long long *keys;  // EPI 2
-    unsigned int *counter;     // EPI 2
-    int *argmax;               // EPI 2 (may be null)
-    unsigned long long *best_key_out;  // EPI 2 (may be null)
-    int rows;
-    int nchunks;     // 16-byte chunks per row
-    int group_shift; // log2(chunks per group)
-    int ystride;     // rows of y per RHS
-    int row_base;    // added to argmax indices
-};
-
-__device__ __forceinline__ float silu_f32(float g) {
-    // silu(x) = x * (1 / (1 + exp(-x))), kernels/qwen.metal:32-33.
-    return g * __frcp_rn(__fadd_rn(1.0f, expf(-g)));
-}
-
-__device__ __forceinline__ uint32_t total_order_key(float v) {
-    const uint32_t u = __float_as_uint(v);
-    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-
 // Extract the 8 (Q4) or 4 (Q8) elements of one word as exact subnormals,
-// pairwise, in the element order of the pre-scaled activations.
+// pairwise, in element order.
 template <int BITS>
 __device__ __forceinline__ void extract(uint32_t w, float2 (&d)[Chunk<BITS>::per_word / 2]) {
     if constexpr (BITS == 4) {
@@ -210,44 +101,166 @@ __device__ __forceinline__ uint32_t word_of(const uint4 &v, int m) {
     return m == 0 ? v.x : (m == 1 ? v.y : (m == 2 ? v.z : v.w));
 }
 
-// Fold one chunk's partial into the row accumulator:
-//   acc += s * (p * 2^(149-E)) + bias * xsum.
-__device__ __forceinline__ float fold(float acc, float2 p, float4 xsc, float s, float bias) {
-    const float t = __fmul_rn(__fmul_rn(__fadd_rn(p.x, p.y), xsc.y), xsc.z);
-    acc = __fmaf_rn(s, t, acc);
-    return __fmaf_rn(bias, xsc.x, acc);
-}
-
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
 }
 
+__device__ __forceinline__ float silu_f32(float g) {
+    // silu(x) = x * (1 / (1 + exp(-x))), kernels/qwen.metal:32-33.
+    return __fmul_rn(g, __frcp_rn(__fadd_rn(1.0f, expf(-g))));
+}
+
+// Key ordering f32 like Rust's f32::total_cmp, as an unsigned integer.
+__device__ __forceinline__ uint32_t total_order_key(float v) {
+    const uint32_t u = __float_as_uint(v);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// ---------------------------------------------------------------------------
+// Prepared activations ("scratch"), one buffer per call or caller-owned:
+//   xp [B][K] f32   x[b][k] * 2^(E_b - f(k mod per_word))
+//   xs [B][nchunks] (sum of x over the chunk) * 2^(E_b - 149)
+//   cf [B][2]       2^a, 2^(149 - E_b - a): the output factor, split so both
+//                   halves are normal
+//   keys [4] u64    argmax reduction (zeroed here)
+//   done u32        CTAs finished (zeroed here)
+//   counters        split-K arrivals per (row range, tile) (zeroed here; the
+//                   kernels also leave them at zero)
+//   partial         split-K partial sums
+// ---------------------------------------------------------------------------
+constexpr int kCounterCount = 1024;        // 256 row ranges x 4 tiles
+constexpr size_t kPartialFloats = 262144;  // 1 MiB of split-K partial sums
+
+struct ScratchView {
+    float *xp;
+    float *xs;
+    float *cf;
+    unsigned long long *keys;
+    unsigned int *done;
+    unsigned int *counters;
+    float *partial;
+};
+
+// One CTA per RHS: global max|x| -> E_b, then the pre-scaled activations and
+// the scaled chunk sums.  Block 0 also zeroes the reduction words.
+template <int BITS>
+__global__ void __launch_bounds__(512) prep_kernel(const float *__restrict__ x, int cols, int nchunks,
+                                                  ScratchView sv) {
+    // Let the dependent streaming kernel launch and start its weight loads.
+    asm volatile("griddepcontrol.launch_dependents;");
+    constexpr int CE = Chunk<BITS>::elems;
+    const int b = blockIdx.x;
+    const float *xb = x + (size_t)b * cols;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    __shared__ float wmax[32];
+    __shared__ int s_e;
+
+    if (b == 0) {
+        if (tid < 4) sv.keys[tid] = 0ull;
+        if (tid == 0) *sv.done = 0u;
+        for (int i = tid; i < kCounterCount; i += blockDim.x) sv.counters[i] = 0u;
+    }
+    float mx = 0.0f;
+    bool nonfinite = false;
+    for (int i = tid; i < cols; i += blockDim.x) {
+        const float a = fabsf(xb[i]);
+        nonfinite |= !(a <= 3.402823466e38f);  // inf or NaN
+        mx = fmaxf(mx, a);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    nonfinite = __any_sync(0xffffffffu, nonfinite);
+    if (lane == 0) wmax[warp] = nonfinite ? __int_as_float(0x7f800000) : mx;
+    __syncthreads();
+    if (tid == 0) {
+        float m = 0.0f;
+        for (int w = 0; w < nw; ++w) m = fmaxf(m, wmax[w]);
+        int e = (int)((__float_as_uint(m) >> 23) & 0xff) - 127;  // max|x| < 2^(e+1); inf -> 128
+        if (e < -127) e = -127;  // zero or subnormal: any E keeps products exact
+        s_e = e;
+    }
+    __syncthreads();
+    const int E = 124 - s_e;  // max|x| * 2^E < 2^125
+    if (tid == 0) {
+        const int t = 149 - E;
+        const int a = t > 120 ? 120 : (t < -120 ? -120 : t);
+        sv.cf[2 * b] = ldexpf(1.0f, a);
+        sv.cf[2 * b + 1] = ldexpf(1.0f, t - a);
+    }
+    // One chunk per 32 (Q4) or 16 (Q8) lanes; fixed butterfly for the sums.
+    constexpr int per_warp = 32 / CE;
+    const int sub_lane = lane % CE;
+    for (int j0 = warp * per_warp; j0 < nchunks; j0 += nw * per_warp) {
+        const int j = j0 + lane / CE;
+        const bool valid = j < nchunks;
+        const float v = valid ? xb[(size_t)j * CE + sub_lane] : 0.0f;
+        float sm = v;
+#pragma unroll
+        for (int o = CE / 2; o > 0; o >>= 1) sm = __fadd_rn(sm, __shfl_xor_sync(0xffffffffu, sm, o));
+        if (valid) {
+            const int k = sub_lane % Chunk<BITS>::per_word;
+            sv.xp[(size_t)b * cols + (size_t)j * CE + sub_lane] = ldexpf(v, E - prescale_shift<BITS>(k));
+            if (sub_lane == 0) sv.xs[(size_t)b * nchunks + j] = ldexpf(sm, E - 149);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Register-streaming kernel: the fallback for layouts the TMA kernel cannot
+// copy (metadata rows that are not 16-byte multiples, unaligned metadata).
+// One warp = R consecutive rows; lane l owns chunks l, l+32, ... of each row;
+// the lane partials meet in a butterfly reduction.
+// EPI: 0 plain, 1 gate/up SwiGLU (second matrix w2/s2/b2), 2 head + argmax.
+// ---------------------------------------------------------------------------
+struct StreamArgs {
+    const uint4 *w;
+    const void *s;
+    const void *bias;
+    const uint4 *w2;
+    const void *s2;
+    const void *bias2;
+    const float *xp;
+    const float *xs;
+    const float *cf;
+    float *y;
+    unsigned long long *keys;
+    unsigned int *done;
+    int *argmax;
+    unsigned long long *best_key_out;
+    int rows;
+    int nchunks;
+    int group_shift;
+    int ystride;
+    int row_base;
+};
+
 template <int BITS, int B, int R, bool BF16, int EPI>
 __global__ void __launch_bounds__(256, 2) stream_kernel(const StreamArgs a) {
-    constexpr int XW = Chunk<BITS>::per_word / 2;  // float2 pairs per word
-    constexpr int NM = (EPI == 1) ? 2 : 1;          // matrices streamed
+    constexpr int XW = Chunk<BITS>::per_word / 2;
+    constexpr int CE = Chunk<BITS>::elems;
+    constexpr int NM = (EPI == 1) ? 2 : 1;
     const int lane = threadIdx.x & 31;
     const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int row0 = gwarp * R;
     const int nchunks = a.nchunks;
-    const int nblocks = (nchunks + 31) >> 5;
     const int groups = nchunks >> a.group_shift;
+    const size_t kfloats = (size_t)nchunks * CE;
 
-    float acc[NM][B][R];
+    float2 acc[NM][R][B];
 #pragma unroll
     for (int q = 0; q < NM; ++q)
 #pragma unroll
-        for (int b = 0; b < B; ++b)
+        for (int r = 0; r < R; ++r)
 #pragma unroll
-            for (int r = 0; r < R; ++r) acc[q][b][r] = 0.0f;
+            for (int b = 0; b < B; ++b) acc[q][r][b] = make_float2(0.f, 0.f);
 
     const bool warp_live = row0 < a.rows;
     bool waited = false;
     if (warp_live) {
-        for (int jb = 0; jb < nblocks; ++jb) {
-            const int j = jb * 32 + lane;
+        for (int j0 = 0; j0 < nchunks; j0 += 32) {
+            const int j = j0 + lane;
             const bool valid = j < nchunks;
             uint4 wv[NM][R];
             float sc[NM][R], bi[NM][R];
@@ -272,14 +285,13 @@ __global__ void __launch_bounds__(256, 2) stream_kernel(const StreamArgs a) {
                 }
             }
             if (!waited) {
-                // The first weights are in flight; wait for the prep kernel.
+                // The first weights are in flight; now wait for the prep kernel.
                 asm volatile("griddepcontrol.wait;" ::: "memory");
                 waited = true;
             }
-            float4 xsc[B];
+            float xsv[B];
 #pragma unroll
-            for (int b = 0; b < B; ++b)
-                xsc[b] = valid ? __ldg(a.xs + (size_t)b * nchunks + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int b = 0; b < B; ++b) xsv[b] = valid ? __ldg(a.xs + (size_t)b * nchunks + j) : 0.0f;
             float2 p[NM][R][B];
 #pragma unroll
             for (int q = 0; q < NM; ++q)
@@ -294,8 +306,10 @@ __global__ void __launch_bounds__(256, 2) stream_kernel(const StreamArgs a) {
                 for (int b = 0; b < B; ++b) {
 #pragma unroll
                     for (int h = 0; h < XW / 2; ++h) {
-                        const float4 v = valid ? __ldg(a.xp + xp_index<BITS>(b, nblocks, j, m, h))
-                                               : make_float4(0.f, 0.f, 0.f, 0.f);
+                        const float4 v =
+                            valid ? __ldg(reinterpret_cast<const float4 *>(a.xp + (size_t)b * kfloats + (size_t)j * CE) +
+                                          m * (XW / 2) + h)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
                         xv[b][2 * h] = make_float2(v.x, v.y);
                         xv[b][2 * h + 1] = make_float2(v.z, v.w);
                     }
@@ -316,59 +330,57 @@ __global__ void __launch_bounds__(256, 2) stream_kernel(const StreamArgs a) {
 #pragma unroll
             for (int q = 0; q < NM; ++q)
 #pragma unroll
-                for (int r = 0; r < R; ++r)
+                for (int r = 0; r < R; ++r) {
+                    const float2 ss = make_float2(sc[q][r], sc[q][r]);
 #pragma unroll
-                    for (int b = 0; b < B; ++b)
-                        acc[q][b][r] = fold(acc[q][b][r], p[q][r][b], xsc[b], sc[q][r], bi[q][r]);
+                    for (int b = 0; b < B; ++b) {
+                        acc[q][r][b] = ffma2(ss, p[q][r][b], acc[q][r][b]);
+                        acc[q][r][b].x = __fmaf_rn(bi[q][r], xsv[b], acc[q][r][b].x);
+                    }
+                }
         }
     }
     if (!waited) asm volatile("griddepcontrol.wait;" ::: "memory");
 
-    // Cross-lane reduction, fixed butterfly order: every lane ends with the sum.
+    float tot[NM][R][B];
 #pragma unroll
     for (int q = 0; q < NM; ++q)
 #pragma unroll
-        for (int b = 0; b < B; ++b)
+        for (int r = 0; r < R; ++r)
 #pragma unroll
-            for (int r = 0; r < R; ++r) acc[q][b][r] = warp_sum(acc[q][b][r]);
+            for (int b = 0; b < B; ++b) tot[q][r][b] = warp_sum(__fadd_rn(acc[q][r][b].x, acc[q][r][b].y));
 
-    // Lane r stores row row0 + r.
+    unsigned long long best[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) best[b] = 0ull;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-        if (warp_live && lane == r && row0 + r < a.rows) {
+        const int row = row0 + r;
+        if (warp_live && row < a.rows) {
 #pragma unroll
             for (int b = 0; b < B; ++b) {
-                float v = acc[0][b][r];
-                if constexpr (EPI == 1) v = __fmul_rn(silu_f32(v), acc[NM - 1][b][r]);
-                a.y[(size_t)b * a.ystride + row0 + r] = v;
+                const float c1 = __ldg(a.cf + 2 * b), c2 = __ldg(a.cf + 2 * b + 1);
+                float v = __fmul_rn(__fmul_rn(tot[0][r][b], c1), c2);
+                if constexpr (EPI == 1) v = __fmul_rn(silu_f32(v), __fmul_rn(__fmul_rn(tot[NM - 1][r][b], c1), c2));
+                if (lane == r) a.y[(size_t)b * a.ystride + row] = v;
+                if constexpr (EPI == 2) {
+                    const unsigned long long key = ((unsigned long long)total_order_key(v) << 32) |
+                                                   (unsigned long long)(0xffffffffu - (uint32_t)(a.row_base + row));
+                    best[b] = key > best[b] ? key : best[b];
+                }
             }
         }
     }
-
     if constexpr (EPI == 2) {
-        // Argmax over this warp's rows, one atomicMax per warp and RHS on a
-        // packed (total-order key, ~index) word: the max is order independent.
         __shared__ unsigned int last_block;
 #pragma unroll
-        for (int b = 0; b < B; ++b) {
-            unsigned long long best = 0ull;
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-                const int row = row0 + r;
-                if (row < a.rows) {
-                    const unsigned long long key =
-                        ((unsigned long long)total_order_key(acc[0][b][r]) << 32) |
-                        (unsigned long long)(0xffffffffu - (uint32_t)(a.row_base + row));
-                    best = key > best ? key : best;
-                }
-            }
-            if (lane == 0 && warp_live) atomicMax(a.keys + b, best);
-        }
-        // The last block to finish publishes the winners (fence + counter; no waiting).
+        for (int b = 0; b < B; ++b)
+            if (lane == 0 && warp_live) atomicMax(a.keys + b, best[b]);
         __threadfence();
         __syncthreads();
-        if (threadIdx.x == 0) last_block = (atomicAdd(a.counter, 1u) == gridDim.x - 1) ? 1u : 0u;
+        if (threadIdx.x == 0) last_block = (atomicAdd(a.done, 1u) == gridDim.x - 1) ? 1u : 0u;
         __syncthreads();
+        if (last_block && threadIdx.x == 0) *a.done = 0u;  // ready for the next launch
         if (last_block && threadIdx.x < B) {
             __threadfence();
             const unsigned long long k = atomicAdd(a.keys + threadIdx.x, 0ull);

@@ -128,12 +128,14 @@ def prepare_activations(x, cols: int, bits: int, batch: int, prepared, stream=No
                                              prepared.numel() * prepared.element_size(), _stream(stream)))
 
 
-def matmul_prepared(m: PackedMatrix, prepared, y, batch: int, stream=None) -> None:
+def matmul_prepared(m: PackedMatrix, prepared, y, batch: int, overlap: bool = False, stream=None) -> None:
+    """overlap=True lets the kernel read this matrix while the previous kernel
+    on the stream still runs (it must not write the matrix)."""
     w, sc, bi = _mat(m)
     check(_lib.lib().qmr_matmul_prepared(w, sc, bi, _ptr(prepared, prepared_bytes(m.bits, m.cols, batch),
                                                          "prepared"),
                                          _ptr(y, 4 * batch * m.rows, "y"), m.rows, m.cols, m.bits, m.group, batch,
-                                         int(m.meta_bf16), _stream(stream)))
+                                         int(m.meta_bf16), 1 if overlap else 0, _stream(stream)))
 
 
 def copy_f32(x, y, n: int, stream=None) -> None:

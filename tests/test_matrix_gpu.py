@@ -477,41 +477,53 @@ def test_typed_wrappers_reject_undersized_views_before_launch(cuda):
 
 
 @pytest.mark.parametrize("bits,meta", [(4, "bf16"), (4, "f32"), (8, "bf16")])
-def test_tma_and_register_streaming_paths_agree_bit_for_bit(cuda, bits, meta):
-    """The warp-specialised TMA pipeline and the register-streaming kernel use
-    the same arithmetic: every shape (slices, partial tiles, tails) must give
-    identical bits.  Also checks that no bounded device wait ran out."""
+def test_tma_and_register_streaming_paths_meet_the_bound(cuda, bits, meta):
+    """The TMA row-lane kernel (split-K, partial slices and tiles) and the
+    register-streaming fallback both meet the oracle bound on every shape, and
+    within each path a B-wide block equals B single-RHS calls bit for bit.
+    Also checks that no bounded device wait ran out."""
     shapes = [(17408, 5120), (5120, 17408), (4, 512), (37, 2176), (1000, 3072), (300, 1024)]
     try:
         for rows, cols in shapes:
             mat = synth.affine_matrix(rows, cols, bits, 64, seed=rows + cols, meta=meta)
             m = synth.to_device(mat, rows, cols, bits, 64)
-            for batch in (1, 2, 3, 4):
-                x = f32_tensor(synth.activations(batch, cols, seed=batch).ravel())
-                outs = []
-                for path in ("tma", "registers"):
-                    qmr.ops.set_stream_path(path)
-                    y = torch.full((batch * rows,), float("nan"), dtype=torch.float32, device="cuda")
-                    qmr.matmul_affine(m, x, y, batch)
-                    outs.append(y.cpu().numpy())
-                assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32)), (rows, cols, batch)
-                assert np.all(np.isfinite(outs[0]))
+            x_np = synth.activations(4, cols, seed=rows)
+            x = f32_tensor(x_np.ravel())
+            for path in ("tma", "registers"):
+                qmr.ops.set_stream_path(path)
+                y4 = torch.full((4 * rows,), float("nan"), dtype=torch.float32, device="cuda")
+                qmr.matmul_affine(m, x, y4, 4)
+                y1 = torch.full((rows,), float("nan"), dtype=torch.float32, device="cuda")
+                qmr.matvec_affine(m, x[2 * cols:3 * cols], y1)
+                torch.cuda.synchronize()
+                got = y4.cpu().numpy().reshape(4, rows)
+                assert np.array_equal(got[2].view(np.uint32), y1.cpu().numpy().view(np.uint32)), (path, rows, cols)
+                for r in sampled_rows(rows, 24):
+                    want, mag = oracle.matmul_f64(mat["weight"], mat["scales"], mat["biases"], x_np, rows, cols,
+                                                  bits, 64, batch=4, row0=r, nrows=1)
+                    assert_ns_bound(got[:, r], want[:, r], mag[:, r], f"{path} {rows}x{cols} row {r}")
             if rows >= 1000 and bits == 4 and meta == "bf16":
-                up = synth.to_device(synth.affine_matrix(rows, cols, bits, 64, seed=7, meta=meta), rows, cols, bits,
-                                     64)
-                x = f32_tensor(synth.activations(3, cols, seed=9).ravel())
-                acts, idxs = [], []
+                upm = synth.affine_matrix(rows, cols, bits, 64, seed=7, meta=meta)
+                up = synth.to_device(upm, rows, cols, bits, 64)
+                x3 = x_np[:3]
                 for path in ("tma", "registers"):
                     qmr.ops.set_stream_path(path)
                     act = torch.empty(3 * rows, dtype=torch.float32, device="cuda")
-                    qmr.gateup_swiglu(m, up, x, act, 3)
+                    qmr.gateup_swiglu(m, up, f32_tensor(x3.ravel()), act, 3)
                     lg = torch.empty(3 * rows, dtype=torch.float32, device="cuda")
                     idx = torch.empty(3, dtype=torch.int32, device="cuda")
-                    qmr.head_argmax(m, x, lg, idx, 3)
-                    acts.append(act.cpu().numpy())
-                    idxs.append(idx.cpu().numpy())
-                assert np.array_equal(acts[0].view(np.uint32), acts[1].view(np.uint32))
-                assert np.array_equal(idxs[0], idxs[1])
+                    qmr.head_argmax(m, f32_tensor(x3.ravel()), lg, idx, 3)
+                    torch.cuda.synchronize()
+                    lgh = lg.cpu().numpy().reshape(3, rows)
+                    assert [oracle.argmax_f32(lgh[b]) for b in range(3)] == idx.cpu().numpy().tolist()
+                    a = act.cpu().numpy().reshape(3, rows)
+                    for r in sampled_rows(rows, 12):
+                        want, amag = oracle.swiglu_f64(mat["weight"][r:r + 1], mat["scales"][r:r + 1],
+                                                       mat["biases"][r:r + 1], upm["weight"][r:r + 1],
+                                                       upm["scales"][r:r + 1], upm["biases"][r:r + 1], x3, 1, cols,
+                                                       bits, 64, 3)
+                        assert_ns_bound(a[:, r], want[:, 0], amag[:, 0] + np.abs(want[:, 0]) * 0.1,
+                                        f"{path} swiglu row {r}")
         assert qmr.ops.device_error() == 0
     finally:
         qmr.ops.set_stream_path("tma")
