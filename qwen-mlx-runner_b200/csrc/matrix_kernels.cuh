@@ -120,8 +120,11 @@ __device__ __forceinline__ uint32_t total_order_key(float v) {
 
 // ---------------------------------------------------------------------------
 // Prepared activations ("scratch"), one buffer per call or caller-owned:
-//   xp [B][K] f32   x[b][k] * 2^(E_b - f(k mod per_word))
-//   xs [B][nchunks] (sum of x over the chunk) * 2^(E_b - 149)
+//   xp [B][nblocks][BF] f32: per block of 32 chunks, the values
+//                   x[b][k] * 2^(E_b - f(k mod per_word)) in lane-interleaved
+//                   order (see block_index), then the 32 chunk sums
+//                   (sum of x over the chunk) * 2^(E_b - 149); chunks past
+//                   the row end are zero
 //   cf [B][2]       2^a, 2^(149 - E_b - a): the output factor, split so both
 //                   halves are normal
 //   keys [4] u64    argmax reduction (zeroed here)
@@ -130,12 +133,27 @@ __device__ __forceinline__ uint32_t total_order_key(float v) {
 //                   kernels also leave them at zero)
 //   partial         split-K partial sums
 // ---------------------------------------------------------------------------
+constexpr int kBlockChunks = 32;           // chunks per prepared block (one per lane)
 constexpr int kCounterCount = 1024;        // 256 row ranges x 4 tiles
 constexpr size_t kPartialFloats = 262144;  // 1 MiB of split-K partial sums
 
+template <int BITS>
+__host__ __device__ constexpr int prepared_block_floats() {
+    return kBlockChunks * Chunk<BITS>::elems + kBlockChunks;
+}
+
+// Float index, inside its block, of element k of chunk c (c < 32): the values
+// a lane needs for word m of its chunk are 4*H consecutive floats of a
+// 512-byte row shared by the 32 lanes.
+template <int BITS>
+__host__ __device__ constexpr int block_index(int c, int k) {
+    constexpr int per_word = Chunk<BITS>::per_word;
+    constexpr int H = per_word / 4;  // float4 per word: 2 (Q4) or 1 (Q8)
+    return (((k / per_word) * H + (k % per_word) / 4) * kBlockChunks + c) * 4 + (k & 3);
+}
+
 struct ScratchView {
     float *xp;
-    float *xs;
     float *cf;
     unsigned long long *keys;
     unsigned int *done;
@@ -144,16 +162,19 @@ struct ScratchView {
 };
 
 // One CTA per RHS: global max|x| -> E_b, then the pre-scaled activations and
-// the scaled chunk sums.  Block 0 also zeroes the reduction words.
+// the scaled chunk sums in prepared blocks.  Block 0 also zeroes the
+// reduction words.
 template <int BITS>
 __global__ void __launch_bounds__(512) prep_kernel(const float *__restrict__ x, int cols, int nchunks,
                                                   ScratchView sv) {
     // Let the dependent streaming kernel launch and start its weight loads.
     asm volatile("griddepcontrol.launch_dependents;");
     constexpr int CE = Chunk<BITS>::elems;
+    constexpr int BF = prepared_block_floats<BITS>();
     const int b = blockIdx.x;
     const float *xb = x + (size_t)b * cols;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const int nblocks = (nchunks + kBlockChunks - 1) / kBlockChunks;
     __shared__ float wmax[32];
     __shared__ int s_e;
 
@@ -191,19 +212,18 @@ __global__ void __launch_bounds__(512) prep_kernel(const float *__restrict__ x, 
     }
     // One chunk per 32 (Q4) or 16 (Q8) lanes; fixed butterfly for the sums.
     constexpr int per_warp = 32 / CE;
-    const int sub_lane = lane % CE;
-    for (int j0 = warp * per_warp; j0 < nchunks; j0 += nw * per_warp) {
+    const int k = lane % CE;
+    float *out = sv.xp + (size_t)b * nblocks * BF;
+    for (int j0 = warp * per_warp; j0 < nblocks * kBlockChunks; j0 += nw * per_warp) {
         const int j = j0 + lane / CE;
-        const bool valid = j < nchunks;
-        const float v = valid ? xb[(size_t)j * CE + sub_lane] : 0.0f;
+        const float v = j < nchunks ? xb[(size_t)j * CE + k] : 0.0f;
         float sm = v;
 #pragma unroll
         for (int o = CE / 2; o > 0; o >>= 1) sm = __fadd_rn(sm, __shfl_xor_sync(0xffffffffu, sm, o));
-        if (valid) {
-            const int k = sub_lane % Chunk<BITS>::per_word;
-            sv.xp[(size_t)b * cols + (size_t)j * CE + sub_lane] = ldexpf(v, E - prescale_shift<BITS>(k));
-            if (sub_lane == 0) sv.xs[(size_t)b * nchunks + j] = ldexpf(sm, E - 149);
-        }
+        float *blk = out + (size_t)(j / kBlockChunks) * BF;
+        const int c = j % kBlockChunks;
+        blk[block_index<BITS>(c, k)] = ldexpf(v, E - prescale_shift<BITS>(k % Chunk<BITS>::per_word));
+        if (k == 0) blk[kBlockChunks * CE + c] = ldexpf(sm, E - 149);
     }
 }
 
@@ -222,7 +242,6 @@ struct StreamArgs {
     const void *s2;
     const void *bias2;
     const float *xp;
-    const float *xs;
     const float *cf;
     float *y;
     unsigned long long *keys;
@@ -239,14 +258,16 @@ struct StreamArgs {
 template <int BITS, int B, int R, bool BF16, int EPI>
 __global__ void __launch_bounds__(256, 2) stream_kernel(const StreamArgs a) {
     constexpr int XW = Chunk<BITS>::per_word / 2;
+    constexpr int H = XW / 2;
     constexpr int CE = Chunk<BITS>::elems;
+    constexpr int BF = prepared_block_floats<BITS>();
     constexpr int NM = (EPI == 1) ? 2 : 1;
     const int lane = threadIdx.x & 31;
     const int gwarp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int row0 = gwarp * R;
     const int nchunks = a.nchunks;
     const int groups = nchunks >> a.group_shift;
-    const size_t kfloats = (size_t)nchunks * CE;
+    const int nblocks = (nchunks + kBlockChunks - 1) / kBlockChunks;
 
     float2 acc[NM][R][B];
 #pragma unroll
@@ -291,7 +312,8 @@ __global__ void __launch_bounds__(256, 2) stream_kernel(const StreamArgs a) {
             }
             float xsv[B];
 #pragma unroll
-            for (int b = 0; b < B; ++b) xsv[b] = valid ? __ldg(a.xs + (size_t)b * nchunks + j) : 0.0f;
+            for (int b = 0; b < B; ++b)
+                xsv[b] = __ldcg(a.xp + ((size_t)b * nblocks + j0 / kBlockChunks) * BF + kBlockChunks * CE + lane);
             float2 p[NM][R][B];
 #pragma unroll
             for (int q = 0; q < NM; ++q)
@@ -305,11 +327,11 @@ __global__ void __launch_bounds__(256, 2) stream_kernel(const StreamArgs a) {
 #pragma unroll
                 for (int b = 0; b < B; ++b) {
 #pragma unroll
-                    for (int h = 0; h < XW / 2; ++h) {
-                        const float4 v =
-                            valid ? __ldg(reinterpret_cast<const float4 *>(a.xp + (size_t)b * kfloats + (size_t)j * CE) +
-                                          m * (XW / 2) + h)
-                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int h = 0; h < H; ++h) {
+                        // Chunks past the row end hold zeros in the prepared block.
+                        const float4 v = __ldcg(reinterpret_cast<const float4 *>(
+                                                    a.xp + ((size_t)b * nblocks + j0 / kBlockChunks) * BF) +
+                                                (m * H + h) * kBlockChunks + lane);
                         xv[b][2 * h] = make_float2(v.x, v.y);
                         xv[b][2 * h + 1] = make_float2(v.z, v.w);
                     }
@@ -359,7 +381,7 @@ __global__ void __launch_bounds__(256, 2) stream_kernel(const StreamArgs a) {
         if (warp_live && row < a.rows) {
 #pragma unroll
             for (int b = 0; b < B; ++b) {
-                const float c1 = __ldg(a.cf + 2 * b), c2 = __ldg(a.cf + 2 * b + 1);
+                const float c1 = __ldcg(a.cf + 2 * b), c2 = __ldcg(a.cf + 2 * b + 1);
                 float v = __fmul_rn(__fmul_rn(tot[0][r][b], c1), c2);
                 if constexpr (EPI == 1) v = __fmul_rn(silu_f32(v), __fmul_rn(__fmul_rn(tot[NM - 1][r][b], c1), c2));
                 if (lane == r) a.y[(size_t)b * a.ystride + row] = v;

@@ -19,7 +19,7 @@ LIB_PATH = PKG_ROOT / "libqmr.so"
 REPO_ROOT = PKG_ROOT.parent
 
 SOURCES = ["matrix.cu", "abi.cpp"]
-HEADERS = ["matrix_kernels.cuh", "qmr_internal.h", "rowlane.cuh"]
+HEADERS = ["matrix_kernels.cuh", "qmr_internal.h", "tile.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
