@@ -183,11 +183,14 @@ int qmr_head_argmax(const void *w, const void *scales, const void *biases, const
 /* Bytes of a prepared-activation buffer for (bits, cols, batch). */
 uint64_t qmr_prepared_bytes(uint32_t bits, uint32_t cols, uint32_t batch);
 
-/* Prepare x [batch, cols] (token-major f32) into `prepared`.  bits 4 or 8;
- * cols a multiple of 128/bits.  `prepared` must be 256-byte aligned and hold
- * qmr_prepared_bytes(bits, cols, batch). */
-int qmr_prepare_activations(const float *x, uint32_t cols, uint32_t bits, uint32_t batch, void *prepared,
-                            uint64_t prepared_bytes, void *stream);
+/* Prepare x [batch, cols] (token-major f32) into `prepared` for matrices of
+ * this bits and group (32/64/128); cols a multiple of the group and of
+ * 128/bits.  `prepared` must be 256-byte aligned and hold
+ * qmr_prepared_bytes(bits, cols, batch).  The layout depends on the stream
+ * path (qmr_set_stream_path), which must not change before the matching
+ * qmr_matmul_prepared calls. */
+int qmr_prepare_activations(const float *x, uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch,
+                            void *prepared, uint64_t prepared_bytes, void *stream);
 
 /* qmr_matmul_prepared flag: the kernel may start while the previous kernel
  * on the stream is still running and read the weights and metadata early
@@ -208,12 +211,14 @@ int qmr_matmul_prepared(const void *w, const void *scales, const void *biases, c
 /* copy_f32 (kernels/matmul_block.metal:315-318): y[i] = x[i], i < n. */
 int qmr_copy_f32(const float *x, float *y, uint32_t n, void *stream);
 
-/* Select the streaming kernel of the fast path: "tma" (default; warp-
- * specialised TMA pipeline, needs 16-byte aligned weights and metadata with
- * 16-byte multiple metadata rows) or "registers" (register-streaming kernel,
- * used automatically when those alignments do not hold).  Both give identical
- * bits; the switch exists for A/B measurement.  No reference counterpart
- * beyond QWEN_METAL_GEMV's same-binary A/B intent (src/gpu.rs:302-309). */
+/* Select the streaming kernel of the fast path: "mma" (default; tensor-core
+ * weight streaming, f16 subnormal weights x split-f16 activations, f32
+ * accumulation), "tma" (FP32 warp-specialised TMA pipeline; needs 16-byte
+ * aligned metadata with 16-byte multiple rows, else falls back to
+ * "registers") or "registers" (FP32 register streaming).  All meet the same
+ * oracle bound; each gives the same bits for a B-wide block and B GEMVs.
+ * The switch exists for A/B measurement, in the spirit of QWEN_METAL_GEMV's
+ * same-binary A/B variants (src/gpu.rs:302-309). */
 int qmr_set_stream_path(const char *path);
 
 /* Read (and optionally clear) the device error word that a kernel sets when

@@ -29,7 +29,7 @@ struct Modes {
     bool batched_delta = true;
     bool parallel_norm = false;
     bool parallel_attention = false;
-    bool register_kernel = false;  // streaming path: false = TMA pipeline, true = register streaming
+    int stream_path = kPathMma;  // streaming kernel of the fast path
     bool initialised = false;
 };
 
@@ -468,7 +468,7 @@ static int launch_matrix(const void *w, const void *s, const void *b, const floa
         c.bf16 = bf16;
         c.r2 = r2;
         c.epilogue = 0;
-        c.legacy_kernel = modes().register_kernel;
+        c.path = modes().stream_path;
         return run_fast(c, stream);
     }
     return run_generic(w, s, b, x, y, rows, cols, bits, group, batch, bf16, stream);
@@ -536,7 +536,7 @@ int qmr_init(int device, uint32_t flags) {
     m.batched_delta = batched;
     m.initialised = true;
     std::lock_guard<std::mutex> lock(g_modes_mu);
-    m.register_kernel = g_modes.register_kernel;
+    m.stream_path = g_modes.stream_path;
     g_modes = m;
     return QMR_OK;
 }
@@ -799,7 +799,7 @@ int qmr_gateup_swiglu(const void *w_gate, const void *s_gate, const void *b_gate
     c.batch = batch;
     c.bf16 = meta_bf16 != 0;
     c.epilogue = 1;
-    c.legacy_kernel = modes().register_kernel;
+    c.path = modes().stream_path;
     return run_fast(c, static_cast<cudaStream_t>(stream));
 }
 
@@ -825,7 +825,7 @@ int qmr_head_argmax(const void *w, const void *scales, const void *biases, const
     c.row_base = row_base;
     c.bf16 = meta_bf16 != 0;
     c.epilogue = 2;
-    c.legacy_kernel = modes().register_kernel;
+    c.path = modes().stream_path;
     return run_fast(c, static_cast<cudaStream_t>(stream));
 }
 
@@ -834,9 +834,11 @@ uint64_t qmr_prepared_bytes(uint32_t bits, uint32_t cols, uint32_t batch) {
     return scratch_bytes((int)bits, cols, batch);
 }
 
-int qmr_prepare_activations(const float *x, uint32_t cols, uint32_t bits, uint32_t batch, void *prepared,
-                            uint64_t prepared_bytes, void *stream) {
+int qmr_prepare_activations(const float *x, uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch,
+                            void *prepared, uint64_t prepared_bytes, void *stream) {
     if (bits != 4 && bits != 8) return fail(QMR_EINVAL, "prepared activations support 4 or 8 bits");
+    if (group != 32 && group != 64 && group != 128) return fail(QMR_EINVAL, "group must be 32, 64 or 128");
+    if (cols % group != 0) return fail(QMR_EINVAL, "cols must be a multiple of the group");
     if (batch < 1 || batch > 4) return fail(QMR_EINVAL, "Matrix blocks support one through four RHS");
     if (cols == 0 || cols % (128 / bits) != 0)
         return fail(QMR_EINVAL, "cols must be a nonzero multiple of %u", 128 / bits);
@@ -846,7 +848,7 @@ int qmr_prepare_activations(const float *x, uint32_t cols, uint32_t bits, uint32
     if (prepared_bytes < scratch_bytes((int)bits, cols, batch))
         return fail(QMR_ERANGE, "prepared buffer of %llu bytes is smaller than %llu", (unsigned long long)prepared_bytes,
                     (unsigned long long)scratch_bytes((int)bits, cols, batch));
-    return run_prepare(x, cols, bits, batch, prepared, static_cast<cudaStream_t>(stream));
+    return run_prepare(x, cols, bits, group, batch, prepared, modes().stream_path, static_cast<cudaStream_t>(stream));
 }
 
 int qmr_matmul_prepared(const void *w, const void *scales, const void *biases, const void *prepared, float *y,
@@ -873,7 +875,7 @@ int qmr_matmul_prepared(const void *w, const void *scales, const void *biases, c
     c.bf16 = meta_bf16 != 0;
     c.r2 = sel != nullptr && strcmp(sel, "matmul_q4_g64_b3_mlp_r2_aligned_bf16") == 0;
     c.epilogue = 0;
-    c.legacy_kernel = m.register_kernel;
+    c.path = m.stream_path;
     c.overlap = (flags & QMR_PREPARED_OVERLAP) != 0;
     return run_stream(c, const_cast<void *>(prepared), static_cast<cudaStream_t>(stream));
 }
@@ -887,15 +889,17 @@ int qmr_copy_f32(const float *x, float *y, uint32_t n, void *stream) {
 
 int qmr_set_stream_path(const char *path) {
     if (path == nullptr) return fail(QMR_EINVAL, "null path");
-    bool reg;
-    if (strcmp(path, "tma") == 0)
-        reg = false;
+    int p;
+    if (strcmp(path, "mma") == 0)
+        p = kPathMma;
+    else if (strcmp(path, "tma") == 0)
+        p = kPathTile;
     else if (strcmp(path, "registers") == 0)
-        reg = true;
+        p = kPathRegisters;
     else
-        return fail(QMR_EINVAL, "stream path must be tma or registers");
+        return fail(QMR_EINVAL, "stream path must be mma, tma or registers");
     std::lock_guard<std::mutex> lock(g_modes_mu);
-    g_modes.register_kernel = reg;
+    g_modes.stream_path = p;
     return QMR_OK;
 }
 

@@ -1,8 +1,6 @@
 // Launchers for the packed-affine kernels: kernel choice and launch shape for
 // B200, the prepared-activation scratch, and programmatic dependent launch of
 // the streaming kernel behind its prep pass.
-#include <cuda.h>
-#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -15,9 +13,10 @@
 
 #include "matrix_kernels.cuh"
 #include "qmr_internal.h"
-#include "tile.cuh"
+#include "launch.h"
 
 namespace qmr {
+
 
 namespace {
 
@@ -32,21 +31,7 @@ std::map<std::pair<int, cudaStream_t>, Scratch> g_scratch;
 constexpr size_t kAlign = 256;
 size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
-constexpr int kConsumers = 8;  // consumer warps of the tile kernel
-constexpr int kSmemBudget = 220 * 1024;
 
-int log2i(uint32_t v) {
-    int r = 0;
-    while ((1u << r) < v) ++r;
-    return r;
-}
-
-int sm_count() {
-    int dev = 0, n = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    return n;
-}
 
 size_t prepared_floats(int bits, uint32_t cols, uint32_t batch) {
     const size_t nchunks = (size_t)cols * bits / 128;
@@ -55,11 +40,29 @@ size_t prepared_floats(int bits, uint32_t cols, uint32_t batch) {
     return batch * nblocks * bf;
 }
 
-void scratch_layout(void *base, int bits, uint32_t cols, uint32_t batch, ScratchView *v) {
+// Bytes of the MMA-path activations: 8 RHS-part columns of fp16 per input
+// column, then the group sums (sized for the smallest group, 32).
+size_t mma_prepared_bytes(uint32_t cols, uint32_t batch) {
+    return align_up((size_t)cols * 8 * sizeof(__half)) + align_up((size_t)batch * (cols / 32) * sizeof(float));
+}
+
+// The activation region holds either path's layout.
+size_t prepared_region(int bits, uint32_t cols, uint32_t batch) {
+    const size_t a = align_up(prepared_floats(bits, cols, batch) * sizeof(float));
+    const size_t b = mma_prepared_bytes(cols, batch);
+    return a > b ? a : b;
+}
+
+void scratch_layout(void *base, int bits, uint32_t cols, uint32_t batch, ScratchView *v, MmaPrepView *mv = nullptr) {
     char *p = static_cast<char *>(base);
     v->xp = reinterpret_cast<float *>(p);
-    p += align_up(prepared_floats(bits, cols, batch) * sizeof(float));
+    if (mv != nullptr) {
+        mv->xh = reinterpret_cast<__half *>(p);
+        mv->xs = reinterpret_cast<float *>(p + align_up((size_t)cols * 8 * sizeof(__half)));
+    }
+    p += prepared_region(bits, cols, batch);
     v->cf = reinterpret_cast<float *>(p);
+    if (mv != nullptr) mv->cf = v->cf;
     p += align_up(8 * sizeof(float));
     v->keys = reinterpret_cast<unsigned long long *>(p);
     v->done = reinterpret_cast<unsigned int *>(p + 4 * sizeof(unsigned long long));
@@ -72,7 +75,7 @@ void scratch_layout(void *base, int bits, uint32_t cols, uint32_t batch, Scratch
 }  // namespace
 
 size_t scratch_bytes(int bits, uint32_t cols, uint32_t batch) {
-    return align_up(prepared_floats(bits, cols, batch) * sizeof(float)) + align_up(8 * sizeof(float)) +
+    return prepared_region(bits, cols, batch) + align_up(8 * sizeof(float)) +
            align_up(4 * sizeof(unsigned long long) + sizeof(unsigned int)) +
            align_up(kCounterCount * sizeof(unsigned int)) + align_up(kPartialFloats * sizeof(float));
 }
@@ -123,15 +126,18 @@ bool fast_eligible(const void *w, uint32_t cols, uint32_t bits, uint32_t group) 
     return true;
 }
 
-namespace {
 
-template <int BITS>
-int launch_prep(const float *x, uint32_t cols, uint32_t batch, const ScratchView &sv, cudaStream_t stream) {
-    const int nchunks = (int)((uint64_t)cols * BITS / 128);
-    prep_kernel<BITS><<<batch, 512, 0, stream>>>(x, (int)cols, nchunks, sv);
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return fail(QMR_ECUDA, "prep launch failed: %s", cudaGetErrorString(e));
-    return QMR_OK;
+int log2i(uint32_t v) {
+    int r = 0;
+    while ((1u << r) < v) ++r;
+    return r;
+}
+
+int sm_count() {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    return n;
 }
 
 cudaLaunchAttribute pdl_attr() {
@@ -141,258 +147,66 @@ cudaLaunchAttribute pdl_attr() {
     return attr;
 }
 
-// ---- register-streaming fallback ------------------------------------------
-
-template <int BITS, int B, int R, bool BF16, int EPI>
-int launch_stream_t(const StreamArgs &a, bool overlap, cudaStream_t stream) {
-    const int warps = (a.rows + R - 1) / R;
-    const int blocks = (warps + 7) / 8;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(blocks, 1, 1);
-    cfg.blockDim = dim3(256, 1, 1);
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1] = {pdl_attr()};
-    cfg.attrs = attr;
-    cfg.numAttrs = overlap ? 1 : 0;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, stream_kernel<BITS, B, R, BF16, EPI>, a);
-    if (e != cudaSuccess) return fail(QMR_ECUDA, "stream kernel launch failed: %s", cudaGetErrorString(e));
-    return QMR_OK;
+int launch_mma_prep_bits(int bits, const float *x, uint32_t cols, uint32_t group, uint32_t batch,
+                         const MmaPrepView &v, cudaStream_t stream) {
+    return bits == 4 ? launch_mma_prep4(x, cols, group, batch, v, stream)
+                     : launch_mma_prep8(x, cols, group, batch, v, stream);
 }
 
-template <int BITS, bool BF16, int EPI>
-int launch_stream_b(const StreamArgs &a, uint32_t batch, bool ov, cudaStream_t stream) {
-    switch (batch) {
-        case 1: return launch_stream_t<BITS, 1, 2, BF16, EPI>(a, ov, stream);
-        case 2: return launch_stream_t<BITS, 2, 2, BF16, EPI>(a, ov, stream);
-        case 3: return launch_stream_t<BITS, 3, 2, BF16, EPI>(a, ov, stream);
-        default: return launch_stream_t<BITS, 4, 2, BF16, EPI>(a, ov, stream);
-    }
+int launch_mma_bits(int bits, const MmaArgs &a, bool bf16, uint32_t group, uint32_t batch, int epi, bool overlap,
+                    cudaStream_t stream) {
+    return bits == 4 ? launch_mma4(a, bf16, group, batch, epi, overlap, stream)
+                     : launch_mma8(a, bf16, group, batch, epi, overlap, stream);
 }
 
-template <int EPI>
-int launch_stream(const StreamArgs &a, int bits, bool bf16, uint32_t batch, bool ov, cudaStream_t stream) {
-    if (bits == 4)
-        return bf16 ? launch_stream_b<4, true, EPI>(a, batch, ov, stream)
-                    : launch_stream_b<4, false, EPI>(a, batch, ov, stream);
-    return bf16 ? launch_stream_b<8, true, EPI>(a, batch, ov, stream) : launch_stream_b<8, false, EPI>(a, batch, ov, stream);
-}
-
-// ---- tensor maps -------------------------------------------------------------
-
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    return fn;
-}
-
-// Encoded maps cached by (address, kind, shape, box): the engine and the
-// benchmarks reuse a handful of matrices, so encoding happens once each.
-using MapKey = std::tuple<const void *, int, uint64_t, uint64_t, uint32_t, uint32_t>;
-std::mutex g_map_mu;
-std::map<MapKey, CUtensorMap> g_maps;
-
-// 2-D map over a row-major array of `rows` rows of `row_elems` elements of
-// `esize` bytes, box = box_x elements x box_y rows, zero fill out of range.
-int tensor_map(CUtensorMap *out, const void *base, int esize, uint64_t row_elems, uint64_t rows, uint32_t box_x,
-               uint32_t box_y) {
-    const MapKey key{base, esize, row_elems, rows, box_x, box_y};
-    {
-        std::lock_guard<std::mutex> lock(g_map_mu);
-        auto it = g_maps.find(key);
-        if (it != g_maps.end()) {
-            *out = it->second;
-            return QMR_OK;
-        }
-    }
-    auto fn = encode_fn();
-    if (fn == nullptr) return fail(QMR_ECUDA, "cuTensorMapEncodeTiled is unavailable");
-    const CUtensorMapDataType dt = esize == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32;
-    const cuuint64_t dims[2] = {row_elems, rows};
-    const cuuint64_t strides[1] = {row_elems * (uint64_t)esize};
-    const cuuint32_t box[2] = {box_x, box_y};
-    const cuuint32_t es[2] = {1, 1};
-    CUtensorMap m;
-    const CUresult r = fn(&m, dt, 2, const_cast<void *>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                          CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return fail(QMR_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-    std::lock_guard<std::mutex> lock(g_map_mu);
-    if (g_maps.size() > 4096) g_maps.clear();
-    g_maps[key] = m;
-    *out = m;
-    return QMR_OK;
-}
-
-// ---- tile kernel -------------------------------------------------------------
-
-struct TileMaps {
-    CUtensorMap w, s, b, w2, s2, b2;
-};
-
-template <int BITS, int B, int RW, bool BF16, int EPI>
-int launch_tile_t(const TileMaps &m, TileArgs a, bool overlap, cudaStream_t stream) {
-    constexpr int NM = (EPI == 1) ? 2 : 1;
-    constexpr int TR = kConsumers * RW;
-    const TileLayout L = tile_layout(NM, kConsumers, RW, B, a.group_shift, a.meta_bytes, block_floats<BITS>());
-    int stages = (int)((kSmemBudget - 64) / (L.stage_bytes + 2 * sizeof(uint64_t)));
-    if (stages > 8) stages = 8;
-    if (stages < 2) return fail(QMR_EUNSUPPORTED, "a %u-byte stage does not fit shared memory", L.stage_bytes);
-    a.stages = stages;
-    const size_t smem = (size_t)stages * L.stage_bytes + (size_t)stages * 2 * sizeof(uint64_t);
-    // Split-K bookkeeping: at most 4 tiles per row range use the counters.
-    const int units = (a.rows + RW - 1) / RW;
-    const int rows_per_range = ((units + a.ranges - 1) / a.ranges) * RW;
-    if (a.ksplit > 1 && ((rows_per_range + TR - 1) / TR > 4 || a.ranges > 256))
-        return fail(QMR_EUNSUPPORTED, "split-K launch shape exceeds the counter space");
-    auto kern = tile_kernel<BITS, B, RW, kConsumers, BF16, EPI>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return fail(QMR_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.ranges * a.ksplit, 1, 1);
-    cfg.blockDim = dim3(32 * (kConsumers + 1), 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1] = {pdl_attr()};
-    cfg.attrs = attr;
-    cfg.numAttrs = overlap ? 1 : 0;
-    e = cudaLaunchKernelEx(&cfg, kern, m.w, m.s, m.b, m.w2, m.s2, m.b2, a);
-    if (e != cudaSuccess) return fail(QMR_ECUDA, "tile kernel launch failed: %s", cudaGetErrorString(e));
-    return QMR_OK;
-}
-
-template <int BITS, bool BF16, int EPI>
-int launch_tile_b(const TileMaps &m, const TileArgs &a, uint32_t batch, int RW, bool ov, cudaStream_t stream) {
-    if constexpr (EPI != 1) {
-        if (RW == 8) {
-            switch (batch) {
-                case 1: return launch_tile_t<BITS, 1, 8, BF16, EPI>(m, a, ov, stream);
-                case 2: return launch_tile_t<BITS, 2, 8, BF16, EPI>(m, a, ov, stream);
-                case 3: return launch_tile_t<BITS, 3, 8, BF16, EPI>(m, a, ov, stream);
-                default: return launch_tile_t<BITS, 4, 8, BF16, EPI>(m, a, ov, stream);
-            }
-        }
-    }
-    switch (batch) {
-        case 1: return launch_tile_t<BITS, 1, 4, BF16, EPI>(m, a, ov, stream);
-        case 2: return launch_tile_t<BITS, 2, 4, BF16, EPI>(m, a, ov, stream);
-        case 3: return launch_tile_t<BITS, 3, 4, BF16, EPI>(m, a, ov, stream);
-        default: return launch_tile_t<BITS, 4, 4, BF16, EPI>(m, a, ov, stream);
-    }
-}
-
-template <int EPI>
-int launch_tile(const TileMaps &m, const TileArgs &a, int bits, bool bf16, uint32_t batch, int RW, bool ov,
+int run_prepare(const float *x, uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch, void *base, int path,
                 cudaStream_t stream) {
-    if (bits == 4)
-        return bf16 ? launch_tile_b<4, true, EPI>(m, a, batch, RW, ov, stream)
-                    : launch_tile_b<4, false, EPI>(m, a, batch, RW, ov, stream);
-    return bf16 ? launch_tile_b<8, true, EPI>(m, a, batch, RW, ov, stream)
-                : launch_tile_b<8, false, EPI>(m, a, batch, RW, ov, stream);
-}
-
-bool tile_eligible(const FastCall &c) {
-    const uint32_t gpc = c.group / (128 / c.bits);
-    const uint64_t meta = c.bf16 ? 2 : 4;
-    const uint64_t nchunks = (uint64_t)c.cols * c.bits / 128;
-    if ((nchunks / gpc) * meta % 16 != 0) return false;                    // metadata row stride
-    if (((uint64_t)kSliceChunks / gpc) * meta % 16 != 0) return false;     // metadata box width
-    auto al = [](const void *p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; };
-    return al(c.w) && al(c.s) && al(c.b) && al(c.w2) && al(c.s2) && al(c.b2);
-}
-
-// Column split across CTAs: the share of SM time doing useful rows for
-// ksplit = 1..4, on tiles of 64 rows; the smallest split within 5% of the best.
-int choose_ksplit(int rows, int nslices, int sms, int nm, uint32_t batch) {
-    const int units = (rows + 7) / 8;
-    double best = -1.0;
-    int best_ks = 1;
-    for (int ks = 1; ks <= 4 && ks <= nslices; ++ks) {
-        if ((size_t)ks * nm * batch * rows > kPartialFloats && ks > 1) break;
-        int ranges = sms / ks;
-        if (ranges > units) ranges = units;
-        if (ranges < 1) ranges = 1;
-        const int rpr = ((units + ranges - 1) / ranges) * 8;
-        const int tiles = (rpr + 63) / 64;
-        if (ks > 1 && (tiles > 4 || ranges > 256)) continue;
-        const double eff = (double)rows / ((double)ranges * tiles * 64) * ((double)ranges * ks / sms);
-        if (eff > best * 1.05) {
-            best = eff;
-            best_ks = ks;
-        }
-    }
-    return best_ks;
-}
-
-}  // namespace
-
-int run_prepare(const float *x, uint32_t cols, uint32_t bits, uint32_t batch, void *base, cudaStream_t stream) {
     ScratchView sv;
-    scratch_layout(base, (int)bits, cols, batch, &sv);
-    return bits == 4 ? launch_prep<4>(x, cols, batch, sv, stream) : launch_prep<8>(x, cols, batch, sv, stream);
+    MmaPrepView mv;
+    scratch_layout(base, (int)bits, cols, batch, &sv, &mv);
+    if (path == kPathMma) {
+        // The argmax keys and the CTA counter start each call at zero.
+        const cudaError_t e = cudaMemsetAsync(sv.keys, 0, 4 * sizeof(unsigned long long) + sizeof(unsigned int), stream);
+        if (e != cudaSuccess) return fail(QMR_ECUDA, "clearing argmax keys: %s", cudaGetErrorString(e));
+        return launch_mma_prep_bits((int)bits, x, cols, group, batch, mv, stream);
+    }
+    return launch_prep_fp32(x, cols, bits, batch, sv, stream);
 }
 
 int run_stream(const FastCall &c, void *base, cudaStream_t stream) {
     ScratchView sv;
-    scratch_layout(base, (int)c.bits, c.cols, c.batch, &sv);
+    MmaPrepView mv;
+    scratch_layout(base, (int)c.bits, c.cols, c.batch, &sv, &mv);
     const int ce = 128 / (int)c.bits;
     const int gpc = (int)c.group / ce;
     const int meta = c.bf16 ? 2 : 4;
     const int nchunks = (int)((uint64_t)c.cols * c.bits / 128);
-    if (!c.legacy_kernel && tile_eligible(c)) {
-        const int NM = c.epilogue == 1 ? 2 : 1;
-        const int RW = (c.r2 || c.epilogue == 1) ? 4 : 8;
-        const int sms = sm_count();
-        const int nslices = (nchunks + kSliceChunks - 1) / kSliceChunks;
-        const int ksplit = choose_ksplit((int)c.rows, nslices, sms, NM, c.batch);
-        const int units = ((int)c.rows + RW - 1) / RW;
-        int ranges = sms / ksplit;
-        if (ranges > units) ranges = units;
-        if (ranges < 1) ranges = 1;
-        const int groups = nchunks / gpc;
-        const uint32_t slice_groups = (uint32_t)(kSliceChunks / gpc);
-        const uint32_t tr = (uint32_t)(kConsumers * RW);
-        TileMaps maps;
-        memset(&maps, 0, sizeof maps);
-        int rc = tensor_map(&maps.w, c.w, 4, (uint64_t)nchunks * 4, c.rows, kSliceWords, (uint32_t)RW);
-        if (rc == QMR_OK) rc = tensor_map(&maps.s, c.s, meta, (uint64_t)groups, c.rows, slice_groups, tr);
-        if (rc == QMR_OK) rc = tensor_map(&maps.b, c.b, meta, (uint64_t)groups, c.rows, slice_groups, tr);
-        if (rc == QMR_OK && NM == 2) {
-            rc = tensor_map(&maps.w2, c.w2, 4, (uint64_t)nchunks * 4, c.rows, kSliceWords, (uint32_t)RW);
-            if (rc == QMR_OK) rc = tensor_map(&maps.s2, c.s2, meta, (uint64_t)groups, c.rows, slice_groups, tr);
-            if (rc == QMR_OK) rc = tensor_map(&maps.b2, c.b2, meta, (uint64_t)groups, c.rows, slice_groups, tr);
-        }
-        if (rc != QMR_OK) return rc;
-        TileArgs a = {};
-        a.xp = sv.xp;
-        a.cf = sv.cf;
+    if (c.path == kPathMma) {
+        MmaArgs a = {};
+        a.w = static_cast<const uint32_t *>(c.w);
+        a.w2 = static_cast<const uint32_t *>(c.w2);
+        a.s = c.s;
+        a.b = c.b;
+        a.s2 = c.s2;
+        a.b2 = c.b2;
+        a.xh = mv.xh;
+        a.xs = mv.xs;
+        a.cf = mv.cf;
         a.y = c.y;
-        a.partial = sv.partial;
-        a.range_counter = sv.counters;
-        a.done_counter = sv.done;
         a.keys = sv.keys;
+        a.done = sv.done;
         a.argmax = c.argmax;
         a.best_key_out = reinterpret_cast<unsigned long long *>(c.best_key);
         a.rows = (int)c.rows;
-        a.nchunks = nchunks;
-        a.group_shift = log2i((uint32_t)gpc);
-        a.meta_bytes = meta;
+        a.cols = (int)c.cols;
         a.ystride = (int)c.rows;
         a.row_base = (int)c.row_base;
-        a.ranges = ranges;
-        a.ksplit = ksplit;
-        switch (c.epilogue) {
-            case 0: return launch_tile<0>(maps, a, (int)c.bits, c.bf16, c.batch, RW, c.overlap, stream);
-            case 1: return launch_tile<1>(maps, a, (int)c.bits, c.bf16, c.batch, RW, c.overlap, stream);
-            default: return launch_tile<2>(maps, a, (int)c.bits, c.bf16, c.batch, RW, c.overlap, stream);
-        }
+        const int units = ((int)c.rows + 15) / 16;
+        const int sms = sm_count();
+        a.ranges = units < sms ? units : sms;
+        return launch_mma_bits((int)c.bits, a, c.bf16, c.group, c.batch, c.epilogue, c.overlap, stream);
     }
+    if (c.path == kPathTile && tile_eligible(c)) return launch_tile_call(c, sv, stream);
     StreamArgs a = {};
     a.w = static_cast<const uint4 *>(c.w);
     a.s = c.s;
@@ -412,11 +226,7 @@ int run_stream(const FastCall &c, void *base, cudaStream_t stream) {
     a.group_shift = log2i((uint32_t)gpc);
     a.ystride = (int)c.rows;
     a.row_base = (int)c.row_base;
-    switch (c.epilogue) {
-        case 0: return launch_stream<0>(a, (int)c.bits, c.bf16, c.batch, c.overlap, stream);
-        case 1: return launch_stream<1>(a, (int)c.bits, c.bf16, c.batch, c.overlap, stream);
-        default: return launch_stream<2>(a, (int)c.bits, c.bf16, c.batch, c.overlap, stream);
-    }
+    return launch_reg(a, (int)c.bits, c.bf16, c.batch, c.epilogue, c.overlap, stream);
 }
 
 int run_fast(const FastCall &c, cudaStream_t stream) {
@@ -428,53 +238,11 @@ int run_fast(const FastCall &c, cudaStream_t stream) {
     } else if (c.scratch_bytes < need) {
         return fail(QMR_ERANGE, "scratch of %zu bytes is smaller than the %zu required", c.scratch_bytes, need);
     }
-    const int rc = run_prepare(c.x, c.cols, c.bits, c.batch, base, stream);
+    const int rc = run_prepare(c.x, c.cols, c.bits, c.group, c.batch, base, c.path, stream);
     if (rc != QMR_OK) return rc;
     FastCall behind_prep = c;
     behind_prep.overlap = true;  // the preceding kernel is our prep, which writes no weights
     return run_stream(behind_prep, base, stream);
-}
-
-int device_error(int *code, bool clear) {
-    unsigned int v = 0;
-    cudaError_t e = cudaMemcpyFromSymbol(&v, g_qmr_device_error, sizeof v);
-    if (e != cudaSuccess) return fail(QMR_ECUDA, "reading the device error word: %s", cudaGetErrorString(e));
-    if (clear && v != 0) {
-        const unsigned int zero = 0;
-        e = cudaMemcpyToSymbol(g_qmr_device_error, &zero, sizeof zero);
-        if (e != cudaSuccess) return fail(QMR_ECUDA, "clearing the device error word: %s", cudaGetErrorString(e));
-    }
-    *code = (int)v;
-    return QMR_OK;
-}
-
-int run_generic(const void *w, const void *s, const void *b, const float *x, float *y, uint32_t rows, uint32_t cols,
-                uint32_t bits, uint32_t group, uint32_t batch, bool bf16, cudaStream_t stream) {
-    const uint64_t threads = (uint64_t)rows * 32;
-    const uint64_t blocks = (threads + 255) / 256;
-    if (blocks > 0x7fffffffull) return fail(QMR_EINVAL, "too many rows for one launch");
-    if (bf16)
-        generic_kernel<true><<<(unsigned)blocks, 256, 0, stream>>>(static_cast<const uint32_t *>(w), s, b, x, y, rows,
-                                                                   cols, bits, group, batch);
-    else
-        generic_kernel<false><<<(unsigned)blocks, 256, 0, stream>>>(static_cast<const uint32_t *>(w), s, b, x, y, rows,
-                                                                    cols, bits, group, batch);
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return fail(QMR_ECUDA, "generic launch failed: %s", cudaGetErrorString(e));
-    return QMR_OK;
-}
-
-int run_embed(const void *w, const void *s, const void *b, uint32_t row, float *y, uint32_t cols, uint32_t bits,
-              uint32_t group, bool bf16, cudaStream_t stream) {
-    const unsigned blocks = (cols + 255) / 256;
-    if (bf16)
-        embed_kernel<true><<<blocks, 256, 0, stream>>>(static_cast<const uint32_t *>(w), s, b, y, row, cols, bits, group);
-    else
-        embed_kernel<false><<<blocks, 256, 0, stream>>>(static_cast<const uint32_t *>(w), s, b, y, row, cols, bits,
-                                                        group);
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return fail(QMR_ECUDA, "embed launch failed: %s", cudaGetErrorString(e));
-    return QMR_OK;
 }
 
 }  // namespace qmr

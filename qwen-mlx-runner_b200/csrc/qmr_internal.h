@@ -25,11 +25,16 @@ struct FastCall {
     bool bf16;
     bool r2;                   // two rows per lane (the selective R2 schedule)
     int epilogue;              // 0 plain, 1 swiglu, 2 head argmax
-    bool legacy_kernel;        // force the register-streaming kernel (A/B runs)
+    int path;                  // kPathMma, kPathTile or kPathRegisters
     bool overlap;              // programmatic dependent launch behind the previous kernel
     void *scratch;             // caller scratch or nullptr for the per-stream pool
     size_t scratch_bytes;
 };
+
+// Streaming kernels of the fast path.
+constexpr int kPathMma = 0;        // tensor-core weight streaming (default)
+constexpr int kPathTile = 1;       // FP32 warp-specialised TMA pipeline
+constexpr int kPathRegisters = 2;  // FP32 register streaming
 
 // Fast (prep + streaming) path possible: Q4/Q8, group 32/64/128, 16-byte
 // aligned weights with 16-byte multiple rows.
@@ -39,7 +44,8 @@ size_t scratch_bytes(int bits, uint32_t cols, uint32_t batch);
 int acquire_scratch(cudaStream_t stream, size_t need, void **out);
 
 int run_fast(const FastCall &c, cudaStream_t stream);
-int run_prepare(const float *x, uint32_t cols, uint32_t bits, uint32_t batch, void *base, cudaStream_t stream);
+int run_prepare(const float *x, uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch, void *base, int path,
+                cudaStream_t stream);
 int run_stream(const FastCall &c, void *base, cudaStream_t stream);
 int run_generic(const void *w, const void *s, const void *b, const float *x, float *y, uint32_t rows,
                 uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch, bool bf16, cudaStream_t stream);

@@ -79,7 +79,7 @@ SIGNATURES = {
     "qmr_head_argmax": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32,
                                _int, _u32, _vp]),
     "qmr_prepared_bytes": (_u64, [_u32, _u32, _u32]),
-    "qmr_prepare_activations": (_int, [_vp, _u32, _u32, _u32, _vp, _u64, _vp]),
+    "qmr_prepare_activations": (_int, [_vp, _u32, _u32, _u32, _u32, _vp, _u64, _vp]),
     "qmr_matmul_prepared": (_int, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _int, _u32, _vp]),
     "qmr_copy_f32": (_int, [_vp, _vp, _u32, _vp]),
     "qmr_stream_sync": (_int, [_vp]),

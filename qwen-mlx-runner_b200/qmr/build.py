@@ -18,8 +18,18 @@ CSRC = PKG_ROOT / "csrc"
 LIB_PATH = PKG_ROOT / "libqmr.so"
 REPO_ROOT = PKG_ROOT.parent
 
-SOURCES = ["matrix.cu", "abi.cpp"]
-HEADERS = ["matrix_kernels.cuh", "qmr_internal.h", "tile.cuh"]
+# (source, extra flags, object name): translation units compile in parallel.
+UNITS = [
+    ("matrix.cu", [], "matrix.o"),
+    ("abi.cpp", [], "abi.o"),
+    ("kernels_reg.cu", [], "kernels_reg.o"),
+    ("kernels_tile.cu", [], "kernels_tile.o"),
+    ("kernels_mma.cu", ["-DQMR_MMA_BITS=4"], "kernels_mma4.o"),
+    ("kernels_mma.cu", ["-DQMR_MMA_BITS=8"], "kernels_mma8.o"),
+]
+SOURCES = sorted({u[0] for u in UNITS})
+HEADERS = ["matrix_kernels.cuh", "qmr_internal.h", "tile.cuh", "mma_stream.cuh", "launch.h"]
+OBJ_DIR = PKG_ROOT / "_build"
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -31,7 +41,6 @@ NVCC_FLAGS = [
     "-prec-sqrt=true",
     "-Xcompiler", "-fPIC",
     "-Xcompiler", "-Wall",
-    "-shared",
 ]
 
 
@@ -54,18 +63,33 @@ def build(force: bool = False, verbose: bool = False) -> pathlib.Path:
     """Compile libqmr.so if any source is newer than it (or force)."""
     if not force and not _stale():
         return LIB_PATH
+    from concurrent.futures import ThreadPoolExecutor
+    OBJ_DIR.mkdir(exist_ok=True)
+    tool = nvcc()
+
+    def compile_unit(unit):
+        src, extra, obj = unit
+        cmd = [tool, *NVCC_FLAGS, *extra, "-c"]
+        if verbose:
+            cmd += ["-Xptxas", "-v"]
+        cmd += ["-I", str(REPO_ROOT / "include"), "-o", str(OBJ_DIR / obj), str(CSRC / src)]
+        return subprocess.run(cmd, capture_output=True, text=True)
+
+    with ThreadPoolExecutor(max_workers=min(len(UNITS), os.cpu_count() or 1)) as pool:
+        results = list(pool.map(compile_unit, UNITS))
+    for unit, proc in zip(UNITS, results):
+        if proc.returncode != 0:
+            sys.stderr.write(proc.stdout + proc.stderr)
+            raise RuntimeError(f"nvcc failed on {unit[0]} ({proc.returncode})")
+        if verbose:
+            sys.stderr.write(proc.stderr)
     tmp = LIB_PATH.with_suffix(".so.tmp")
-    cmd = [nvcc(), *NVCC_FLAGS]
-    if verbose:
-        cmd += ["-Xptxas", "-v"]
-    cmd += ["-I", str(REPO_ROOT / "include"), "-o", str(tmp)]
-    cmd += [str(CSRC / s) for s in SOURCES]
-    proc = subprocess.run(cmd, capture_output=True, text=True)
+    link = [tool, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", str(tmp)]
+    link += [str(OBJ_DIR / u[2]) for u in UNITS]
+    proc = subprocess.run(link, capture_output=True, text=True)
     if proc.returncode != 0:
         sys.stderr.write(proc.stdout + proc.stderr)
-        raise RuntimeError(f"nvcc failed building libqmr ({proc.returncode})")
-    if verbose:
-        sys.stderr.write(proc.stderr)
+        raise RuntimeError(f"nvcc failed linking libqmr ({proc.returncode})")
     os.replace(tmp, LIB_PATH)
     return LIB_PATH
 

@@ -122,8 +122,8 @@ def alloc_prepared(bits: int, cols: int, batch: int, device="cuda"):
     return torch.empty(prepared_bytes(bits, cols, batch), dtype=torch.uint8, device=device)
 
 
-def prepare_activations(x, cols: int, bits: int, batch: int, prepared, stream=None) -> None:
-    check(_lib.lib().qmr_prepare_activations(_ptr(x, 4 * batch * cols, "x"), cols, bits, batch,
+def prepare_activations(x, cols: int, bits: int, batch: int, prepared, group: int = 64, stream=None) -> None:
+    check(_lib.lib().qmr_prepare_activations(_ptr(x, 4 * batch * cols, "x"), cols, bits, group, batch,
                                              _ptr(prepared, prepared_bytes(bits, cols, batch), "prepared"),
                                              prepared.numel() * prepared.element_size(), _stream(stream)))
 
@@ -147,7 +147,7 @@ def init(device: int = 0, reference: bool = False) -> None:
 
 
 def set_stream_path(path: str) -> None:
-    """"tma" (default) or "registers": the streaming kernel of the fast path."""
+    """"mma" (default), "tma" or "registers": the streaming kernel of the fast path."""
     check(_lib.lib().qmr_set_stream_path(path.encode()))
 
 

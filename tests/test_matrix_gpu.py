@@ -477,9 +477,10 @@ def test_typed_wrappers_reject_undersized_views_before_launch(cuda):
 
 
 @pytest.mark.parametrize("bits,meta", [(4, "bf16"), (4, "f32"), (8, "bf16")])
-def test_tma_and_register_streaming_paths_meet_the_bound(cuda, bits, meta):
-    """The TMA row-lane kernel (split-K, partial slices and tiles) and the
-    register-streaming fallback both meet the oracle bound on every shape, and
+def test_all_streaming_paths_meet_the_bound(cuda, bits, meta):
+    """The tensor-core kernel, the FP32 TMA tile kernel (split-K, partial
+    slices and tiles) and the FP32 register-streaming kernel all meet the
+    oracle bound on every shape, and
     within each path a B-wide block equals B single-RHS calls bit for bit.
     Also checks that no bounded device wait ran out."""
     shapes = [(17408, 5120), (5120, 17408), (4, 512), (37, 2176), (1000, 3072), (300, 1024)]
@@ -489,7 +490,7 @@ def test_tma_and_register_streaming_paths_meet_the_bound(cuda, bits, meta):
             m = synth.to_device(mat, rows, cols, bits, 64)
             x_np = synth.activations(4, cols, seed=rows)
             x = f32_tensor(x_np.ravel())
-            for path in ("tma", "registers"):
+            for path in ("mma", "tma", "registers"):
                 qmr.ops.set_stream_path(path)
                 y4 = torch.full((4 * rows,), float("nan"), dtype=torch.float32, device="cuda")
                 qmr.matmul_affine(m, x, y4, 4)
@@ -506,7 +507,7 @@ def test_tma_and_register_streaming_paths_meet_the_bound(cuda, bits, meta):
                 upm = synth.affine_matrix(rows, cols, bits, 64, seed=7, meta=meta)
                 up = synth.to_device(upm, rows, cols, bits, 64)
                 x3 = x_np[:3]
-                for path in ("tma", "registers"):
+                for path in ("mma", "tma", "registers"):
                     qmr.ops.set_stream_path(path)
                     act = torch.empty(3 * rows, dtype=torch.float32, device="cuda")
                     qmr.gateup_swiglu(m, up, f32_tensor(x3.ravel()), act, 3)
@@ -526,4 +527,4 @@ def test_tma_and_register_streaming_paths_meet_the_bound(cuda, bits, meta):
                                         f"{path} swiglu row {r}")
         assert qmr.ops.device_error() == 0
     finally:
-        qmr.ops.set_stream_path("tma")
+        qmr.ops.set_stream_path("mma")
