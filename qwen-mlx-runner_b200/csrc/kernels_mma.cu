@@ -1,6 +1,9 @@
 // The tensor-core streaming kernel and its activation prep, built once per
 // bit width (QMR_MMA_BITS = 4 or 8) so the two halves compile in parallel.
+#include <cuda.h>
 #include <cuda_runtime.h>
+
+#include <atomic>
 
 #include "launch.h"
 
@@ -12,50 +15,83 @@ namespace qmr {
 
 namespace {
 
+constexpr int kBits = QMR_MMA_BITS;
+
 template <int G>
-int launch_mma_prep(const float *x, uint32_t cols, uint32_t batch, const MmaPrepView &v, cudaStream_t stream) {
-    mma_prep_kernel<QMR_MMA_BITS, G><<<batch, 512, 0, stream>>>(x, (int)cols, (int)batch, v);
+int launch_prep_g(const float *x, uint32_t cols, uint32_t batch, int ngroups_pad, const MmaImageView &v,
+                  cudaStream_t stream) {
+    mma_prep_kernel<kBits, G><<<batch, 512, 0, stream>>>(x, (int)cols, (int)batch, ngroups_pad, v);
     const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return fail(QMR_ECUDA, "prep launch failed: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess) return fail(QMR_ECUDA, "activation prep launch failed: %s", cudaGetErrorString(e));
+    return QMR_OK;
+}
+
+// The shared-memory opt-in is a per-device function attribute: set it once per
+// device for each instantiation.
+template <typename Kern>
+int opt_in_smem(Kern kern, std::atomic<uint64_t> &done) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return fail(QMR_ECUDA, "cudaGetDevice failed");
+    const uint64_t bit = 1ull << (dev & 63);
+    if (done.load(std::memory_order_acquire) & bit) return QMR_OK;
+    int max_optin = 0;
+    cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, max_optin);
+    if (e != cudaSuccess) return fail(QMR_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    done.fetch_or(bit, std::memory_order_acq_rel);
     return QMR_OK;
 }
 
 template <int G, int B, bool BF16, int EPI>
-int launch_mma_t(const MmaArgs &a, bool overlap, cudaStream_t stream) {
+int launch_t(const CUtensorMap &m1, const CUtensorMap &m2, const MmaArgs &a, const MmaPlan &p, bool overlap,
+             cudaStream_t stream) {
+    auto kern = mma_kernel<kBits, G, B, BF16, EPI>;
+    static std::atomic<uint64_t> opted{0};
+    const int rc = opt_in_smem(kern, opted);
+    if (rc != QMR_OK) return rc;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.ranges, 1, 1);
+    cfg.gridDim = dim3((unsigned)p.ctas, 1, 1);
     cfg.blockDim = dim3(32 * kMmaWarps, 1, 1);
+    cfg.dynamicSmemBytes = p.smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1] = {pdl_attr()};
     cfg.attrs = attr;
     cfg.numAttrs = overlap ? 1 : 0;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, mma_kernel<QMR_MMA_BITS, G, B, BF16, EPI>, a);
-    if (e != cudaSuccess) return fail(QMR_ECUDA, "mma kernel launch failed: %s", cudaGetErrorString(e));
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, m1, m2, a);
+    if (e != cudaSuccess) return fail(QMR_ECUDA, "tensor-core kernel launch failed: %s", cudaGetErrorString(e));
     return QMR_OK;
 }
 
 template <int G, bool BF16, int EPI>
-int launch_mma_b(const MmaArgs &a, uint32_t batch, bool ov, cudaStream_t stream) {
+int launch_b(const CUtensorMap &m1, const CUtensorMap &m2, const MmaArgs &a, const MmaPlan &p, uint32_t batch,
+             bool ov, cudaStream_t stream) {
     switch (batch) {
-        case 1: return launch_mma_t<G, 1, BF16, EPI>(a, ov, stream);
-        case 2: return launch_mma_t<G, 2, BF16, EPI>(a, ov, stream);
-        case 3: return launch_mma_t<G, 3, BF16, EPI>(a, ov, stream);
-        default: return launch_mma_t<G, 4, BF16, EPI>(a, ov, stream);
+        case 1: return launch_t<G, 1, BF16, EPI>(m1, m2, a, p, ov, stream);
+        case 2: return launch_t<G, 2, BF16, EPI>(m1, m2, a, p, ov, stream);
+        case 3: return launch_t<G, 3, BF16, EPI>(m1, m2, a, p, ov, stream);
+        default: return launch_t<G, 4, BF16, EPI>(m1, m2, a, p, ov, stream);
     }
 }
 
 template <bool BF16, int EPI>
-int launch_mma_g(const MmaArgs &a, uint32_t group, uint32_t batch, bool ov, cudaStream_t stream) {
+int launch_g(const CUtensorMap &m1, const CUtensorMap &m2, const MmaArgs &a, const MmaPlan &p, uint32_t group,
+             uint32_t batch, bool ov, cudaStream_t stream) {
     switch (group) {
-        case 32: return launch_mma_b<32, BF16, EPI>(a, batch, ov, stream);
-        case 64: return launch_mma_b<64, BF16, EPI>(a, batch, ov, stream);
-        default: return launch_mma_b<128, BF16, EPI>(a, batch, ov, stream);
+        case 32: return launch_b<32, BF16, EPI>(m1, m2, a, p, batch, ov, stream);
+        case 64: return launch_b<64, BF16, EPI>(m1, m2, a, p, batch, ov, stream);
+        default:
+            // A Q8 window of 1024 columns needs 16 KiB slots, which the plan
+            // never accepts; only Q4 instantiates group 128.
+            if constexpr (kBits == 4) return launch_b<128, BF16, EPI>(m1, m2, a, p, batch, ov, stream);
+            return fail(QMR_EUNSUPPORTED, "the tensor-core kernel does not take Q8 group 128");
     }
 }
 
 template <int EPI>
-int launch_mma_e(const MmaArgs &a, bool bf16, uint32_t group, uint32_t batch, bool ov, cudaStream_t stream) {
-    return bf16 ? launch_mma_g<true, EPI>(a, group, batch, ov, stream) : launch_mma_g<false, EPI>(a, group, batch, ov, stream);
+int launch_e(const CUtensorMap &m1, const CUtensorMap &m2, const MmaArgs &a, const MmaPlan &p, bool bf16,
+             uint32_t group, uint32_t batch, bool ov, cudaStream_t stream) {
+    return bf16 ? launch_g<true, EPI>(m1, m2, a, p, group, batch, ov, stream)
+                : launch_g<false, EPI>(m1, m2, a, p, group, batch, ov, stream);
 }
 
 }  // namespace
@@ -68,21 +104,61 @@ int launch_mma_e(const MmaArgs &a, bool bf16, uint32_t group, uint32_t batch, bo
 #define QMR_MMA_PREP launch_mma_prep8
 #endif
 
-int QMR_MMA_LAUNCH(const MmaArgs &a, bool bf16, uint32_t group, uint32_t batch, int epi, bool overlap,
+int QMR_MMA_LAUNCH(const FastCall &c, const MmaPlan &p, const ScratchView &sv, const MmaImageView &v,
                    cudaStream_t stream) {
-    switch (epi) {
-        case 0: return launch_mma_e<0>(a, bf16, group, batch, overlap, stream);
-        case 1: return launch_mma_e<1>(a, bf16, group, batch, overlap, stream);
-        default: return launch_mma_e<2>(a, bf16, group, batch, overlap, stream);
+    const uint64_t row_words = (uint64_t)c.cols * kBits / 32;
+    CUtensorMap m1, m2;
+    int rc = tensor_map_2d(&m1, c.w, 4, row_words, c.rows, 32, kTileRows, true);
+    if (rc != QMR_OK) return rc;
+    m2 = m1;
+    if (c.epilogue == 1) {
+        rc = tensor_map_2d(&m2, c.w2, 4, row_words, c.rows, 32, kTileRows, true);
+        if (rc != QMR_OK) return rc;
+    }
+    MmaArgs a = {};
+    a.s = static_cast<const unsigned char *>(c.s);
+    a.b = static_cast<const unsigned char *>(c.b);
+    a.s2 = static_cast<const unsigned char *>(c.epilogue == 1 ? c.s2 : c.s);
+    a.b2 = static_cast<const unsigned char *>(c.epilogue == 1 ? c.b2 : c.b);
+    a.image = v.image;
+    a.table = v.table;
+    a.cf = v.cf;
+    a.y = c.y;
+    a.partial = sv.partial;
+    a.counters = sv.counters;
+    a.keys = sv.keys;
+    a.done = sv.done;
+    a.argmax = c.argmax;
+    a.best_key_out = reinterpret_cast<unsigned long long *>(c.best_key);
+    a.err = device_error_word();
+    if (a.err == nullptr) return fail(QMR_ECUDA, "device error word is unavailable");
+    a.rows = (int)c.rows;
+    a.ngroups = (int)(c.cols / c.group);
+    a.ngroups_pad = p.ngroups_pad;
+    a.ystride = (int)c.rows;
+    a.row_base = (int)c.row_base;
+    a.tiles = p.tiles;
+    a.nwin = p.nwin;
+    a.kc = p.kc;
+    a.cps = p.cps;
+    a.slots = p.slots;
+    a.stages = p.stages;
+    a.off_image = p.off_image;
+    a.off_table = p.off_table;
+    a.off_bars = p.off_bars;
+    switch (c.epilogue) {
+        case 0: return launch_e<0>(m1, m2, a, p, c.bf16, c.group, c.batch, c.overlap, stream);
+        case 1: return launch_e<1>(m1, m2, a, p, c.bf16, c.group, c.batch, c.overlap, stream);
+        default: return launch_e<2>(m1, m2, a, p, c.bf16, c.group, c.batch, c.overlap, stream);
     }
 }
 
-int QMR_MMA_PREP(const float *x, uint32_t cols, uint32_t group, uint32_t batch, const MmaPrepView &v,
-                 cudaStream_t stream) {
+int QMR_MMA_PREP(const float *x, uint32_t cols, uint32_t group, uint32_t batch, int ngroups_pad,
+                 const MmaImageView &v, cudaStream_t stream) {
     switch (group) {
-        case 32: return launch_mma_prep<32>(x, cols, batch, v, stream);
-        case 64: return launch_mma_prep<64>(x, cols, batch, v, stream);
-        default: return launch_mma_prep<128>(x, cols, batch, v, stream);
+        case 32: return launch_prep_g<32>(x, cols, batch, ngroups_pad, v, stream);
+        case 64: return launch_prep_g<64>(x, cols, batch, ngroups_pad, v, stream);
+        default: return launch_prep_g<128>(x, cols, batch, ngroups_pad, v, stream);
     }
 }
 

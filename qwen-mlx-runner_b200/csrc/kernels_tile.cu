@@ -34,15 +34,18 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // Encoded maps cached by (address, kind, shape, box): the engine and the
 // benchmarks reuse a handful of matrices, so encoding happens once each.
-using MapKey = std::tuple<const void *, int, uint64_t, uint64_t, uint32_t, uint32_t>;
+using MapKey = std::tuple<const void *, int, uint64_t, uint64_t, uint32_t, uint32_t, bool>;
 std::mutex g_map_mu;
 std::map<MapKey, CUtensorMap> g_maps;
 
+}  // namespace
+
 // 2-D map over a row-major array of `rows` rows of `row_elems` elements of
-// `esize` bytes, box = box_x elements x box_y rows, zero fill out of range.
-int tensor_map(CUtensorMap *out, const void *base, int esize, uint64_t row_elems, uint64_t rows, uint32_t box_x,
-               uint32_t box_y) {
-    const MapKey key{base, esize, row_elems, rows, box_x, box_y};
+// `esize` bytes, box = box_x elements x box_y rows, zero fill out of range,
+// optionally with the 128-byte shared-memory swizzle.
+int tensor_map_2d(CUtensorMap *out, const void *base, int esize, uint64_t row_elems, uint64_t rows, uint32_t box_x,
+                  uint32_t box_y, bool swizzle128) {
+    const MapKey key{base, esize, row_elems, rows, box_x, box_y, swizzle128};
     {
         std::lock_guard<std::mutex> lock(g_map_mu);
         auto it = g_maps.find(key);
@@ -60,14 +63,21 @@ int tensor_map(CUtensorMap *out, const void *base, int esize, uint64_t row_elems
     const cuuint32_t es[2] = {1, 1};
     CUtensorMap m;
     const CUresult r = fn(&m, dt, 2, const_cast<void *>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                          CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                          swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(QMR_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     std::lock_guard<std::mutex> lock(g_map_mu);
     if (g_maps.size() > 4096) g_maps.clear();
     g_maps[key] = m;
     *out = m;
     return QMR_OK;
+}
+
+namespace {
+
+int tensor_map(CUtensorMap *out, const void *base, int esize, uint64_t row_elems, uint64_t rows, uint32_t box_x,
+               uint32_t box_y) {
+    return tensor_map_2d(out, base, esize, row_elems, rows, box_x, box_y, false);
 }
 
 // ---- tile kernel -------------------------------------------------------------
@@ -228,6 +238,17 @@ int launch_tile_call(const FastCall &c, const ScratchView &sv, cudaStream_t stre
             default: return launch_tile<2>(maps, a, (int)c.bits, c.bf16, c.batch, RW, c.overlap, stream);
         }
     }
+
+// Device address of the shared error word on the current device.
+unsigned int *device_error_word() {
+    static std::mutex mu;
+    static void *addr[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (addr[dev] == nullptr && cudaGetSymbolAddress(&addr[dev], g_qmr_device_error) != cudaSuccess) addr[dev] = nullptr;
+    return static_cast<unsigned int *>(addr[dev]);
+}
 
 int device_error(int *code, bool clear) {
     unsigned int v = 0;

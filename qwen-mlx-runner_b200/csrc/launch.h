@@ -4,6 +4,7 @@
 // the tensor-core kernel (kernels_mma.cu, built once per bit width).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -26,19 +27,35 @@ int launch_reg(const StreamArgs &a, int bits, bool bf16, uint32_t batch, int epi
 // kernels_tile.cu
 bool tile_eligible(const FastCall &c);
 int launch_tile_call(const FastCall &c, const ScratchView &sv, cudaStream_t stream);
+int tensor_map_2d(CUtensorMap *out, const void *base, int esize, uint64_t row_elems, uint64_t rows, uint32_t box_x,
+                  uint32_t box_y, bool swizzle128);
+unsigned int *device_error_word();
 
-// kernels_mma.cu
-int launch_mma_prep_bits(int bits, const float *x, uint32_t cols, uint32_t group, uint32_t batch,
-                         const MmaPrepView &v, cudaStream_t stream);
-int launch_mma_bits(int bits, const MmaArgs &a, bool bf16, uint32_t group, uint32_t batch, int epi, bool overlap,
-                    cudaStream_t stream);
-int launch_mma4(const MmaArgs &a, bool bf16, uint32_t group, uint32_t batch, int epi, bool overlap,
+// Launch shape of the tensor-core kernel for one call (matrix.cu).
+struct MmaPlan {
+    int kc;           // column slices
+    int cps;          // CTAs per slice
+    int ctas;
+    int stages;       // ring slots per warp
+    int slots;        // partial-sum slots per warp segment
+    int nwin;         // 512/1024-column windows of the matrix
+    int ngroups_pad;  // groups of the padded activation image
+    int tiles;        // 16-row tiles
+    uint32_t smem, off_image, off_table, off_bars;
+};
+bool mma_plan(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint32_t batch, int epi, bool bf16,
+              MmaPlan *p);
+
+// kernels_mma.cu (one translation unit per bit width)
+int launch_mma_prep_bits(int bits, const float *x, uint32_t cols, uint32_t group, uint32_t batch, int ngroups_pad,
+                         const MmaImageView &v, cudaStream_t stream);
+int launch_mma4(const FastCall &c, const MmaPlan &p, const ScratchView &sv, const MmaImageView &v,
                 cudaStream_t stream);
-int launch_mma8(const MmaArgs &a, bool bf16, uint32_t group, uint32_t batch, int epi, bool overlap,
+int launch_mma8(const FastCall &c, const MmaPlan &p, const ScratchView &sv, const MmaImageView &v,
                 cudaStream_t stream);
-int launch_mma_prep4(const float *x, uint32_t cols, uint32_t group, uint32_t batch, const MmaPrepView &v,
-                     cudaStream_t stream);
-int launch_mma_prep8(const float *x, uint32_t cols, uint32_t group, uint32_t batch, const MmaPrepView &v,
-                     cudaStream_t stream);
+int launch_mma_prep4(const float *x, uint32_t cols, uint32_t group, uint32_t batch, int ngroups_pad,
+                     const MmaImageView &v, cudaStream_t stream);
+int launch_mma_prep8(const float *x, uint32_t cols, uint32_t group, uint32_t batch, int ngroups_pad,
+                     const MmaImageView &v, cudaStream_t stream);
 
 }  // namespace qmr

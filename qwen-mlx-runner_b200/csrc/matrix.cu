@@ -40,10 +40,11 @@ size_t prepared_floats(int bits, uint32_t cols, uint32_t batch) {
     return batch * nblocks * bf;
 }
 
-// Bytes of the MMA-path activations: 8 RHS-part columns of fp16 per input
-// column, then the group sums (sized for the smallest group, 32).
+// Bytes of the tensor-core activation image and its group-sum table, sized
+// for the widest window (1024 columns) and the smallest group (32).
 size_t mma_prepared_bytes(uint32_t cols, uint32_t batch) {
-    return align_up((size_t)cols * 8 * sizeof(__half)) + align_up((size_t)batch * (cols / 32) * sizeof(float));
+    const size_t padded = ((size_t)cols + 1023) / 1024 * 1024;
+    return align_up(padded * 4 * batch) + align_up(padded / 2);
 }
 
 // The activation region holds either path's layout.
@@ -53,12 +54,13 @@ size_t prepared_region(int bits, uint32_t cols, uint32_t batch) {
     return a > b ? a : b;
 }
 
-void scratch_layout(void *base, int bits, uint32_t cols, uint32_t batch, ScratchView *v, MmaPrepView *mv = nullptr) {
+void scratch_layout(void *base, int bits, uint32_t cols, uint32_t batch, ScratchView *v, MmaImageView *mv = nullptr) {
     char *p = static_cast<char *>(base);
     v->xp = reinterpret_cast<float *>(p);
     if (mv != nullptr) {
-        mv->xh = reinterpret_cast<__half *>(p);
-        mv->xs = reinterpret_cast<float *>(p + align_up((size_t)cols * 8 * sizeof(__half)));
+        const size_t padded = ((size_t)cols + 1023) / 1024 * 1024;
+        mv->image = reinterpret_cast<__half *>(p);
+        mv->table = reinterpret_cast<float *>(p + align_up(padded * 4 * batch));
     }
     p += prepared_region(bits, cols, batch);
     v->cf = reinterpret_cast<float *>(p);
@@ -70,7 +72,27 @@ void scratch_layout(void *base, int bits, uint32_t cols, uint32_t batch, Scratch
     v->counters = reinterpret_cast<unsigned int *>(p);
     p += align_up(kCounterCount * sizeof(unsigned int));
     v->partial = reinterpret_cast<float *>(p);
+    if (mv != nullptr) {
+        mv->keys = v->keys;
+        mv->done = v->done;
+        mv->counters = v->counters;
+    }
 }
+
+// Largest opt-in shared memory of one block on the current device.
+int smem_optin() {
+    static int cached[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    if (cached[dev] == 0) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) v = 0;
+        cached[dev] = v;
+    }
+    return cached[dev];
+}
+
+bool aligned16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
 
 }  // namespace
 
@@ -127,6 +149,75 @@ bool fast_eligible(const void *w, uint32_t cols, uint32_t bits, uint32_t group) 
 }
 
 
+// Activation image of one column slice, worst case B = 4, stays within this
+// budget; wider matrices are split into 2 or 4 column slices.
+constexpr size_t kMmaImageBudget = 96 * 1024;
+
+bool mma_plan(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint32_t batch, int epi, bool bf16,
+              MmaPlan *p) {
+    if (bits != 4 && bits != 8) return false;
+    if (group != 32 && group != 64 && group != 128) return false;
+    if (bits == 8 && group == 128) return false;
+    if (rows == 0 || cols == 0 || cols % group != 0 || batch < 1 || batch > 4) return false;
+    const uint32_t ngroups = cols / group;
+    if (ngroups % 8 != 0) return false;  // 16-byte metadata rows for cp.async
+    const uint32_t win_cols = 8 * group > 512 ? 8 * group : 512;
+    const uint32_t wg = win_cols / group;
+    const int nwin = (int)((cols + win_cols - 1) / win_cols);
+    const int tiles = (int)((rows + kTileRows - 1) / kTileRows);
+    const int nm = epi == 1 ? 2 : 1;
+    const int sms = sm_count();
+    int kc = 0;
+    for (int c : {1, 2, 4}) {
+        const size_t nh_max = ((size_t)nwin + c - 1) / c;
+        if (nwin >= c && sms >= c && nh_max * win_cols * 16 <= kMmaImageBudget) {
+            kc = c;
+            break;
+        }
+    }
+    if (kc == 0) return false;
+    const int ctas = sms / kc * kc;
+    const int cps = ctas / kc;
+    const long long K = (long long)cps * kMmaWarps;
+    const int nh_min = nwin / kc, nh_max = (nwin + kc - 1) / kc;
+    int slots = 2;
+    if (kc > 1) {
+        const long long lmax = ((long long)tiles * nh_max + K - 1) / K;
+        slots = (int)(lmax / nh_min) + 2;
+        if (tiles > kCounterCount) return false;
+    } else if (K > kCounterCount) {
+        return false;
+    }
+    if ((size_t)ctas * kMmaWarps * slots * nm * 64 > kPartialFloats) return false;
+    const uint32_t slot = (uint32_t)mma_slot_bytes((int)bits, (int)group, nm, bf16 ? 2 : 4);
+    const uint32_t image = (uint32_t)nh_max * win_cols * 4 * batch;
+    const uint32_t ngroups_pad = (uint32_t)nwin * wg;
+    const uint32_t table = 16 * ngroups_pad;
+    const int limit = smem_optin() - 64;  // room for the kernel's static shared variables
+    for (int st = kMmaMaxStages; st >= 2; --st) {
+        const uint32_t off_image = (uint32_t)kMmaWarps * st * slot;
+        const uint32_t off_table = off_image + (image + 127) / 128 * 128;
+        const uint32_t off_bars = off_table + (table + 127) / 128 * 128;
+        const uint32_t total = 1024 + off_bars + (uint32_t)(kMmaWarps * st + 1) * 8;
+        if ((int)total <= limit) {
+            p->kc = kc;
+            p->cps = cps;
+            p->ctas = ctas;
+            p->stages = st;
+            p->slots = slots;
+            p->nwin = nwin;
+            p->ngroups_pad = (int)ngroups_pad;
+            p->tiles = tiles;
+            p->smem = total;
+            p->off_image = off_image;
+            p->off_table = off_table;
+            p->off_bars = off_bars;
+            return true;
+        }
+    }
+    return false;
+}
+
 int log2i(uint32_t v) {
     int r = 0;
     while ((1u << r) < v) ++r;
@@ -147,66 +238,63 @@ cudaLaunchAttribute pdl_attr() {
     return attr;
 }
 
-int launch_mma_prep_bits(int bits, const float *x, uint32_t cols, uint32_t group, uint32_t batch,
-                         const MmaPrepView &v, cudaStream_t stream) {
-    return bits == 4 ? launch_mma_prep4(x, cols, group, batch, v, stream)
-                     : launch_mma_prep8(x, cols, group, batch, v, stream);
+int launch_mma_prep_bits(int bits, const float *x, uint32_t cols, uint32_t group, uint32_t batch, int ngroups_pad,
+                         const MmaImageView &v, cudaStream_t stream) {
+    return bits == 4 ? launch_mma_prep4(x, cols, group, batch, ngroups_pad, v, stream)
+                     : launch_mma_prep8(x, cols, group, batch, ngroups_pad, v, stream);
 }
 
-int launch_mma_bits(int bits, const MmaArgs &a, bool bf16, uint32_t group, uint32_t batch, int epi, bool overlap,
-                    cudaStream_t stream) {
-    return bits == 4 ? launch_mma4(a, bf16, group, batch, epi, overlap, stream)
-                     : launch_mma8(a, bf16, group, batch, epi, overlap, stream);
+namespace {
+
+// The activation layout the tensor-core kernel would read for this shape
+// (independent of the matrix): its padded group count, or 0 when the shape
+// goes to the FP32 paths.
+int mma_layout_groups(uint32_t bits, uint32_t group, uint32_t cols, uint32_t batch) {
+    MmaPlan p;
+    if (!mma_plan(bits, group, kTileRows, cols, batch, 0, true, &p)) return 0;
+    return p.ngroups_pad;
 }
+
+// The tensor-core kernel takes this call: a launch plan and 16-byte aligned
+// weights and metadata (TMA and cp.async sources).
+bool mma_takes(const FastCall &c, MmaPlan *p) {
+    if (!mma_plan(c.bits, c.group, c.rows, c.cols, c.batch, c.epilogue, c.bf16, p)) return false;
+    if (!aligned16(c.w) || !aligned16(c.s) || !aligned16(c.b)) return false;
+    if (c.epilogue == 1 && (!aligned16(c.w2) || !aligned16(c.s2) || !aligned16(c.b2))) return false;
+    return true;
+}
+
+}  // namespace
 
 int run_prepare(const float *x, uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch, void *base, int path,
                 cudaStream_t stream) {
     ScratchView sv;
-    MmaPrepView mv;
+    MmaImageView mv;
     scratch_layout(base, (int)bits, cols, batch, &sv, &mv);
     if (path == kPathMma) {
-        // The argmax keys and the CTA counter start each call at zero.
-        const cudaError_t e = cudaMemsetAsync(sv.keys, 0, 4 * sizeof(unsigned long long) + sizeof(unsigned int), stream);
-        if (e != cudaSuccess) return fail(QMR_ECUDA, "clearing argmax keys: %s", cudaGetErrorString(e));
-        return launch_mma_prep_bits((int)bits, x, cols, group, batch, mv, stream);
+        const int ngroups_pad = mma_layout_groups(bits, group, cols, batch);
+        if (ngroups_pad > 0) return launch_mma_prep_bits((int)bits, x, cols, group, batch, ngroups_pad, mv, stream);
     }
     return launch_prep_fp32(x, cols, bits, batch, sv, stream);
 }
 
 int run_stream(const FastCall &c, void *base, cudaStream_t stream) {
     ScratchView sv;
-    MmaPrepView mv;
+    MmaImageView mv;
     scratch_layout(base, (int)c.bits, c.cols, c.batch, &sv, &mv);
     const int ce = 128 / (int)c.bits;
     const int gpc = (int)c.group / ce;
-    const int meta = c.bf16 ? 2 : 4;
     const int nchunks = (int)((uint64_t)c.cols * c.bits / 128);
-    if (c.path == kPathMma) {
-        MmaArgs a = {};
-        a.w = static_cast<const uint32_t *>(c.w);
-        a.w2 = static_cast<const uint32_t *>(c.w2);
-        a.s = c.s;
-        a.b = c.b;
-        a.s2 = c.s2;
-        a.b2 = c.b2;
-        a.xh = mv.xh;
-        a.xs = mv.xs;
-        a.cf = mv.cf;
-        a.y = c.y;
-        a.keys = sv.keys;
-        a.done = sv.done;
-        a.argmax = c.argmax;
-        a.best_key_out = reinterpret_cast<unsigned long long *>(c.best_key);
-        a.rows = (int)c.rows;
-        a.cols = (int)c.cols;
-        a.ystride = (int)c.rows;
-        a.row_base = (int)c.row_base;
-        const int units = ((int)c.rows + 15) / 16;
-        const int sms = sm_count();
-        a.ranges = units < sms ? units : sms;
-        return launch_mma_bits((int)c.bits, a, c.bf16, c.group, c.batch, c.epilogue, c.overlap, stream);
+    if (c.path == kPathMma && mma_layout_groups(c.bits, c.group, c.cols, c.batch) > 0) {
+        // The activations were prepared in the tensor-core layout.
+        MmaPlan p;
+        if (!mma_takes(c, &p))
+            return fail(QMR_EUNSUPPORTED,
+                        "activations prepared for the tensor-core kernel, which does not take this matrix "
+                        "(unaligned weights or metadata, or no launch plan)");
+        return c.bits == 4 ? launch_mma4(c, p, sv, mv, stream) : launch_mma8(c, p, sv, mv, stream);
     }
-    if (c.path == kPathTile && tile_eligible(c)) return launch_tile_call(c, sv, stream);
+    if (c.path != kPathRegisters && tile_eligible(c)) return launch_tile_call(c, sv, stream);
     StreamArgs a = {};
     a.w = static_cast<const uint4 *>(c.w);
     a.s = c.s;
@@ -238,11 +326,13 @@ int run_fast(const FastCall &c, cudaStream_t stream) {
     } else if (c.scratch_bytes < need) {
         return fail(QMR_ERANGE, "scratch of %zu bytes is smaller than the %zu required", c.scratch_bytes, need);
     }
-    const int rc = run_prepare(c.x, c.cols, c.bits, c.group, c.batch, base, c.path, stream);
+    FastCall call = c;
+    MmaPlan plan;
+    if (call.path == kPathMma && !mma_takes(call, &plan)) call.path = kPathTile;  // FP32 kernels take the rest
+    const int rc = run_prepare(call.x, call.cols, call.bits, call.group, call.batch, base, call.path, stream);
     if (rc != QMR_OK) return rc;
-    FastCall behind_prep = c;
-    behind_prep.overlap = true;  // the preceding kernel is our prep, which writes no weights
-    return run_stream(behind_prep, base, stream);
+    call.overlap = true;  // the preceding kernel is our prep, which writes no weights
+    return run_stream(call, base, stream);
 }
 
 }  // namespace qmr

@@ -134,8 +134,8 @@ __device__ __forceinline__ uint32_t total_order_key(float v) {
 //   partial         split-K partial sums
 // ---------------------------------------------------------------------------
 constexpr int kBlockChunks = 32;           // chunks per prepared block (one per lane)
-constexpr int kCounterCount = 1024;        // 256 row ranges x 4 tiles
-constexpr size_t kPartialFloats = 262144;  // 1 MiB of split-K partial sums
+constexpr int kCounterCount = 8192;        // arrival counters of split tiles
+constexpr size_t kPartialFloats = 524288;  // 2 MiB of split-K partial sums
 
 template <int BITS>
 __host__ __device__ constexpr int prepared_block_floats() {

@@ -1,62 +1,99 @@
-// Weight-streaming block matmul on the tensor cores (sm_100a, mma.sync
-// m16n8k16, f16 operands, f32 accumulation).
+// Weight-streaming block matmul on the tensor cores (sm_100a: mma.sync
+// m16n8k16 with f16 operands and f32 accumulation, TMA weight tiles,
+// cp.async metadata, mbarrier pipelines).
 //
-// Why tensor cores for M <= 4: on B200 the FP32 formulation needs one LOP3
-// plus B fused multiply-adds per weight element, which issue-limits a B3 block
-// well below HBM speed.  Here each warp instruction multiplies 16 rows x 16
-// columns x 8 RHS columns, so the per-element cost is only the dequantisation
-// (about one instruction per element) whatever the block width.
+// Why tensor cores for a batch of at most 4 right-hand sides: on B200 the FP32
+// formulation needs one LOP3 plus B fused multiply-adds per weight element,
+// which issue-limits a B3 block well below HBM speed.  Here one warp
+// instruction multiplies 16 rows x 16 columns x 8 RHS columns, so the cost per
+// element is the dequantisation alone (5 logic ops per 8 nibbles), whatever B.
 //
 // Operands of one 16-row x 16-column MMA:
 //  * A (weights): `w & 0x000f000f` (Q4) or `w & 0x00ff00ff` (Q8) read as a
-//    half2 is a pair of exact fp16 subnormals q * 2^-24 -- no offset, no
-//    conversion.  The k order inside an MMA is a fixed permutation of the
-//    group's columns (block_perm); activations are stored in the same order.
+//    half2 is a pair of exact fp16 subnormals q * 2^-24.  For Q4 the nibbles
+//    at bits 4..7 are used in place as `w & 0x00f000f0` = 16q * 2^-24, and
+//    the activations paired with them carry a compensating 2^-4; nibbles at
+//    bits 8..15 come from `w >> 8` the same way.  The k order inside an MMA
+//    is a fixed permutation of the group's columns (block_perm); the
+//    activation image is stored in that order.
 //  * B (activations): x[b] * 2^E_b (E_b puts max|x[b]| just below the fp16
-//    maximum) split into an fp16 high part and an fp16 low part; the eight
-//    MMA columns are (RHS b, part) so each thread's accumulator pair holds
-//    both parts of one RHS for two rows.
+//    maximum) split into an fp16 high part and an fp16 low part; the MMA
+//    columns are n = 2b + part, so each thread's accumulator pair holds both
+//    parts of one RHS for two rows.
 //  * Per quantisation group the group's MMAs start from zero; the f32 result
-//    P (q*x*2^(E_b-24) summed over the group) is folded as
-//    acc += s*P + bias*xsum', xsum' = (sum of x over the group)*2^(E_b-24);
-//    the output is acc * 2^(24-E_b) (two exact power-of-two factors).
+//    P = (q*x summed over the group) * 2^(E_b-24) is folded as
+//    acc += s*P (both parts, FFMA2) and acc.hi += bias*xsum' with
+//    xsum' = (sum of x over the group) * 2^(E_b-24); the output is
+//    (acc.hi + acc.lo) * 2^(24-E_b) (two exact power-of-two factors).
 //
-// Work split: CTA c owns the rows [c*rows/G, (c+1)*rows/G) in 16-row units
-// (one persistent CTA per SM).  Its row tiles are shared by its warps: with T
-// tiles and NW warps, KW = NW/T warps split the columns of each tile and add
-// their partial sums in warp order through shared memory; with more tiles
-// than warps each warp walks whole tiles.  Weights stream straight from HBM
-// into registers through a software prefetch ring about 16 words deep per
-// lane (no L1 allocation).
+// Work split (stream-K over (16-row tile, 512-column window) units): with
+// kc column slices, the CTAs are split into kc equal sets and set h owns the
+// windows of slice h for every tile.  A set's units, tile-major, are divided
+// into equal contiguous segments, one per warp.  A warp accumulates each
+// tile piece of its segment in registers; a piece that covers a whole tile
+// (possible only with kc = 1) is written directly, other pieces publish
+// their sums to a partial buffer and the last piece of a tile to arrive
+// (fence + counter, no waiting) adds all pieces in (slice, segment) order.
+// The split depends only on the matrix shape and the SM count, never on B,
+// so a block of B RHS equals B single-RHS calls bit for bit.
+//
+// Data movement per warp: a private ring of `stages` slots; slot = one unit:
+// the tile's 16 rows x window bytes of packed weights as 2-D TMA boxes of
+// 16 rows x 128 bytes with the 128-byte swizzle (conflict-free 8-row reads),
+// plus the tile's scales and biases for the window's groups by 16-byte
+// cp.async (zero-filled out of range), all completing on the slot's
+// mbarrier.  The CTA's activation image (its slice of the prepared image
+// plus the table of group sums) arrives once by bulk copy.  Weight loads are
+// issued before `griddepcontrol.wait`, so they overlap the producer of the
+// activations under programmatic dependent launch.  Every wait is bounded by
+// %globaltimer; on timeout the kernel records an error code and drains the
+// copies it issued (also bounded) before exiting.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include "matrix_kernels.cuh"
+#include "pipe.cuh"
 
 namespace qmr {
 
-constexpr int kMmaWarps = 16;  // warps per CTA
+constexpr int kMmaWarps = 8;     // warps per CTA, each with its own copy ring
+constexpr int kTileRows = 16;    // rows of one MMA tile
+constexpr int kMmaMaxStages = 6;
 
-// Columns each of the 4 lanes of a quad contributes to one group.
-template <int G>
-__host__ __device__ constexpr int cols_per_lane() {
-    return G / 4;
-}
-
-// Words of one row a lane loads per group.
 template <int BITS, int G>
-__host__ __device__ constexpr int words_per_lane() {
-    return cols_per_lane<G>() * BITS / 32;
+struct MmaShape {
+    static constexpr int CPL = G / 4;                               // columns per lane per group
+    static constexpr int WPL = CPL * BITS / 32;                     // words per lane per group and row
+    static constexpr int NMMA = G / 16;                             // MMAs per group
+    static constexpr int NREG = G / 8;                              // half2 registers per lane, row and group
+    static constexpr int NCH = G / 32;                              // 16-byte activation chunks per lane and group
+    static constexpr int WIN_COLS = 8 * G > 512 ? 8 * G : 512;      // columns of one window
+    static constexpr int WG = WIN_COLS / G;                         // groups per window (8 or 16)
+    static constexpr int ROW_BYTES = WIN_COLS * BITS / 8;           // bytes of one row in a window
+    static constexpr int ROW_WORDS = ROW_BYTES / 4;
+    static constexpr int NBOX = ROW_BYTES / 128;                    // 128-byte TMA boxes per window
+    static constexpr int GROUP_BYTES = G * BITS / 8;
+    static constexpr int W_BYTES = kTileRows * ROW_BYTES;           // weights of one unit
+};
+
+// Bytes of one ring slot: the weights of NM matrices, then their metadata
+// (32 lanes x the window's groups of one (row, scale|bias) each).
+__host__ __device__ constexpr int mma_slot_bytes(int bits, int group, int nm, int meta_size) {
+    const int win_cols = 8 * group > 512 ? 8 * group : 512;
+    const int w_bytes = kTileRows * win_cols * bits / 8;
+    const int meta = 32 * (win_cols / group) * meta_size;
+    return (nm * (w_bytes + meta) + 1023) / 1024 * 1024;
 }
 
 // Column (relative to the lane's first column of the group) that feeds half
 // `h` (0/1) of A/B register `reg` of the lane.  Register 2j+i (i = 0, 1) is
 // used by MMA j as its k-slot pair (2t, 2t+1) for i = 0 and (2t+8, 2t+9) for
-// i = 1.  Q4: register m of word w holds nibbles (m, m+4) of that word; Q8:
-// register 2w+m holds bytes (m, m+2) of word w.
+// i = 1.  Q4: register m of word w holds nibbles (m, m+4) of that word
+// (m odd: scaled by 16); Q8: register 2w+m holds bytes (m, m+2) of word w.
 template <int BITS>
 __host__ __device__ constexpr int block_perm(int reg, int h) {
     if (BITS == 4) {
@@ -68,26 +105,39 @@ __host__ __device__ constexpr int block_perm(int reg, int h) {
     }
 }
 
-// Prepared activations for the MMA path, per RHS-part n = 2b + {0: high, 1: low}:
-//   xh [ngroups][8 n][4 lanes][G/4 halves]   (permuted by block_perm)
-//   xs [B][ngroups] f32                       (sum of x over the group) * 2^(E_b - 24)
-//   cf [B][2] f32                             2^a, 2^(24 - E_b - a)
-struct MmaPrepView {
-    __half *xh;
-    float *xs;
+// The prepared activation image, shared by the prep kernel (writer) and the
+// streaming kernel (reader, copied into shared memory verbatim):
+//   image [ngroups_pad][NCH][NB = 2B][4 lanes][8 halves]  (block_perm order;
+//          Q4 odd registers pre-scaled by 2^-4; padding groups are zero)
+//   table [4][ngroups_pad] f32   (sum of x over the group) * 2^(E_b - 24)
+//   cf    [B][2] f32             2^a, 2^(24 - E_b - a)
+struct MmaImageView {
+    __half *image;
+    float *table;
     float *cf;
+    unsigned long long *keys;  // argmax keys, cleared by the prep
+    unsigned int *done;        // CTA counter, cleared by the prep
+    unsigned int *counters;    // split-tile counters, cleared by the prep
 };
 
-// One CTA per RHS: E_b from max|x|, then the split activations.
+// One CTA per RHS: E_b from max|x|, then the group sums and the split halves.
 template <int BITS, int G>
 __global__ void __launch_bounds__(512) mma_prep_kernel(const float *__restrict__ x, int cols, int batch,
-                                                      MmaPrepView v) {
+                                                      int ngroups_pad, MmaImageView v) {
     asm volatile("griddepcontrol.launch_dependents;");
-    constexpr int CPL = cols_per_lane<G>();
+    using S = MmaShape<BITS, G>;
     const int b = blockIdx.x;
     const float *xb = x + (size_t)b * cols;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
     const int ngroups = cols / G;
+    const int NB = 2 * batch;
+    if (b == 0) {
+        // Every call starts with clear argmax and arrival state, even after a
+        // launch that stopped early on a device error.
+        for (int i = tid; i < kCounterCount; i += blockDim.x) v.counters[i] = 0u;
+        if (tid < 4) v.keys[tid] = 0ull;
+        if (tid == 0) *v.done = 0u;
+    }
     __shared__ float wmax[32];
     __shared__ int s_e;
     float mx = 0.0f;
@@ -118,285 +168,416 @@ __global__ void __launch_bounds__(512) mma_prep_kernel(const float *__restrict__
         v.cf[2 * b + 1] = ldexpf(1.0f, t - a);
     }
     // Group sums: one warp per group, fixed order (strided lane sums, butterfly).
-    for (int g = warp; g < ngroups; g += nw) {
+    for (int g = warp; g < ngroups_pad; g += nw) {
         float s = 0.0f;
-        for (int c = lane; c < G; c += 32) s = __fadd_rn(s, xb[(size_t)g * G + c]);
+        if (g < ngroups) {
+            for (int c = lane; c < G; c += 32) s = __fadd_rn(s, xb[(size_t)g * G + c]);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
-        if (lane == 0) v.xs[(size_t)b * ngroups + g] = ldexpf(s, E - 24);
+            for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+        }
+        if (lane == 0) v.table[(size_t)b * ngroups_pad + g] = g < ngroups ? ldexpf(s, E - 24) : 0.0f;
     }
-    // Split halves: element (group g, lane-quad slot t, register r, half h).
-    const int per_group = 4 * CPL;  // = G
-    for (int i = tid; i < ngroups * per_group; i += blockDim.x) {
-        const int g = i / per_group;
-        const int rem = i % per_group;
-        const int t = rem / CPL;
-        const int slot = rem % CPL;  // = 2*reg + h
-        const int reg = slot >> 1, h = slot & 1;
-        const int col = g * G + t * CPL + block_perm<BITS>(reg, h);
-        const float xv = ldexpf(xb[col], E);
+    // Split halves: element (group g, chunk jj, lane slot t, half index k).
+    for (int i = tid; i < ngroups_pad * G; i += blockDim.x) {
+        const int g = i / G, rem = i % G;
+        const int jj = rem >> 5, t = (rem >> 3) & 3, k = rem & 7;
+        const int reg = jj * 4 + (k >> 1), h = k & 1;
+        const int col = g * G + t * S::CPL + block_perm<BITS>(reg, h);
+        const int shift = (BITS == 4 && (reg & 1)) ? 4 : 0;
+        const float xv = col < cols ? ldexpf(xb[col], E - shift) : 0.0f;
         const __half hi = __float2half_rn(xv);
         const __half lo = __float2half_rn(xv - __half2float(hi));
-        __half *base = v.xh + (((size_t)g * 8) * 4 + t) * CPL + slot;
-        base[(size_t)(2 * b) * 4 * CPL] = hi;
-        base[(size_t)(2 * b + 1) * 4 * CPL] = lo;
+        __half *dst = v.image + ((((size_t)g * S::NCH + jj) * NB + 2 * b) * 4 + t) * 8 + k;
+        dst[0] = hi;
+        dst[32] = lo;  // column n + 1
     }
 }
 
-__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// N words of `row` of a 16 x 128-byte TMA box written with the 128-byte
+// swizzle (16-byte unit u of row r sits at unit u ^ (r & 7)), starting at
+// byte `within` of the row.
 template <int N>
-__device__ __forceinline__ void ldg_words(uint32_t (&v)[N], const uint32_t *p) {
+__device__ __forceinline__ void lds_swizzled(uint32_t (&v)[N], const unsigned char *box, int row, int within) {
+    const unsigned char *line = box + row * 128;
+    const int unit = within >> 4, off = within & 15;
     if constexpr (N == 1) {
-        asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v[0]) : "l"(p));
+        v[0] = *reinterpret_cast<const uint32_t *>(line + (((unit ^ (row & 7)) << 4) | off));
     } else if constexpr (N == 2) {
-        asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v[0]), "=r"(v[1]) : "l"(p));
+        const uint2 p = *reinterpret_cast<const uint2 *>(line + (((unit ^ (row & 7)) << 4) | off));
+        v[0] = p.x;
+        v[1] = p.y;
     } else {
 #pragma unroll
-        for (int i = 0; i < N; i += 4)
-            asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                         : "=r"(v[i]), "=r"(v[i + 1]), "=r"(v[i + 2]), "=r"(v[i + 3])
-                         : "l"(p + i));
+        for (int k = 0; k < N / 4; ++k) {
+            const uint4 p = *reinterpret_cast<const uint4 *>(line + (((unit + k) ^ (row & 7)) << 4));
+            v[4 * k] = p.x;
+            v[4 * k + 1] = p.y;
+            v[4 * k + 2] = p.z;
+            v[4 * k + 3] = p.w;
+        }
     }
 }
 
-// A register `reg` of a lane from its words of one row.
-template <int BITS>
-__device__ __forceinline__ uint32_t a_reg(const uint32_t *words, int reg) {
-    if constexpr (BITS == 4) {
-        const uint32_t w = words[reg / 4];
-        return (w >> (4 * (reg % 4))) & 0x000f000fu;
+// A-operand registers of one row from its words (see the file comment).
+template <int BITS, int WPL>
+__device__ __forceinline__ void a_regs(const uint32_t (&w)[WPL], uint32_t (&r)[WPL * 32 / BITS / 2]) {
+#pragma unroll
+    for (int i = 0; i < WPL; ++i) {
+        if constexpr (BITS == 4) {
+            const uint32_t u = w[i] >> 8;
+            r[4 * i] = w[i] & 0x000f000fu;
+            r[4 * i + 1] = w[i] & 0x00f000f0u;
+            r[4 * i + 2] = u & 0x000f000fu;
+            r[4 * i + 3] = u & 0x00f000f0u;
+        } else {
+            r[2 * i] = w[i] & 0x00ff00ffu;
+            r[2 * i + 1] = (w[i] >> 8) & 0x00ff00ffu;
+        }
+    }
+}
+
+// Scales or biases of groups (g, g+1) from the slot's metadata area.
+template <bool BF16>
+__device__ __forceinline__ float2 meta_pair(const unsigned char *p) {
+    if constexpr (BF16) {
+        const uint32_t v = *reinterpret_cast<const uint32_t *>(p);
+        return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
     } else {
-        const uint32_t w = words[reg / 2];
-        return (w >> (8 * (reg % 2))) & 0x00ff00ffu;
+        return *reinterpret_cast<const float2 *>(p);
     }
 }
 
 struct MmaArgs {
-    const uint32_t *w, *w2;   // packed rows (gate/up for EPI 1)
-    const void *s, *b, *s2, *b2;
-    const __half *xh;
-    const float *xs, *cf;
+    const unsigned char *s, *b, *s2, *b2;  // metadata [rows][ngroups] (f32 or bf16 bits)
+    const __half *image;                   // prepared activation image
+    const float *table;                    // group sums [4][ngroups_pad]
+    const float *cf;                       // output factors [B][2]
     float *y;
-    unsigned long long *keys;
-    unsigned int *done;
+    float *partial;                        // [segments][slots][NM][64] piece sums
+    unsigned int *counters;                // arrivals per multi-piece tile
+    unsigned long long *keys;              // [B] packed argmax (EPI 2)
+    unsigned int *done;                    // CTAs finished (EPI 2)
     int *argmax;
     unsigned long long *best_key_out;
-    int rows, cols, ystride, row_base, ranges;
+    unsigned int *err;                     // device error word
+    int rows, ngroups, ngroups_pad, ystride, row_base;
+    int tiles, nwin, kc, cps, slots, stages;
+    uint32_t off_image, off_table, off_bars;  // offsets into the 1024-aligned dynamic shared memory
 };
 
+// Pieces of tile T across the slices and the counter that tracks them.
+__device__ __forceinline__ void tile_pieces(const MmaArgs &a, int T, long long K, int *counter, int *npieces) {
+    int n = 0, c = 0;
+    for (int h = 0; h < a.kc; ++h) {
+        const long long w0 = (long long)h * a.nwin / a.kc, w1 = (long long)(h + 1) * a.nwin / a.kc;
+        const long long nh = w1 - w0, U = (long long)a.tiles * nh;
+        const long long uf = (long long)T * nh, ul = uf + nh - 1;
+        const long long kf = ((uf + 1) * K - 1) / U, kl = ((ul + 1) * K - 1) / U;
+        if (h == 0) c = (int)kf;
+        for (long long k = kf; k <= kl; ++k) n += (U * (k + 1) / K > U * k / K) ? 1 : 0;  // non-empty segments
+    }
+    *counter = a.kc == 1 ? c : T;
+    *npieces = n;
+}
+
 template <int BITS, int G, int B, bool BF16, int EPI>
-__global__ void __launch_bounds__(32 * kMmaWarps, 1) mma_kernel(const MmaArgs a) {
+__global__ void __launch_bounds__(32 * kMmaWarps, 1)
+    mma_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap wmap2, const MmaArgs a) {
+    using S = MmaShape<BITS, G>;
     constexpr int NM = (EPI == 1) ? 2 : 1;
-    constexpr int CPL = cols_per_lane<G>();
-    constexpr int WPL = words_per_lane<BITS, G>();
-    constexpr int NMMA = G / 16;
-    // Groups in flight per lane: about 16 words per lane whatever the format.
-    constexpr int PF = (16 / (WPL * NM)) < 2 ? 2 : 16 / (WPL * NM);
-    __shared__ float red[kMmaWarps][NM][2][B][32];  // per-warp partial sums
+    constexpr int NB = 2 * B;
+    constexpr int MSZ = BF16 ? 2 : 4;
+    constexpr int META_LANE = S::WG * MSZ;
+    constexpr int META_BYTES = 32 * META_LANE;
+    constexpr int SLOT = mma_slot_bytes(BITS, G, NM, MSZ);
+    extern __shared__ unsigned char smem_raw[];
     __shared__ unsigned int flag;
+    unsigned char *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
 
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const int gq = lane >> 2;  // row within the 8-row half tile
-    const int t = lane & 3;    // lane within the quad
-    const int ngroups = a.cols / G;
-    const size_t row_words = (size_t)a.cols * BITS / 32;
-    const size_t row_groups = (size_t)ngroups;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gq = lane >> 2, t = lane & 3;
+    const int nst = a.stages;
+    unsigned char *ring = smem + (size_t)warp * nst * SLOT;
+    const uint4 *ximg = reinterpret_cast<const uint4 *>(smem + a.off_image);
+    const float *xtab = reinterpret_cast<const float *>(smem + a.off_table);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + a.off_bars);
+    uint64_t *full = bars + warp * nst;
+    uint64_t *ibar = bars + kMmaWarps * nst;
 
-    const int units = (a.rows + 15) / 16;
-    const int row_begin = (int)(((long long)blockIdx.x * units) / a.ranges) * 16;
-    const int row_end = min(a.rows, (int)(((long long)(blockIdx.x + 1) * units) / a.ranges) * 16);
-    const int ntiles = row_end > row_begin ? (row_end - row_begin + 15) / 16 : 0;
-    // Warps per tile (column split) when tiles are few; otherwise warps walk tiles.
-    const int kw = ntiles > 0 && ntiles < kMmaWarps ? kMmaWarps / ntiles : 1;
-    const int my_tile0 = warp / kw;
-    const int part = warp % kw;
-    const int tile_step = ntiles >= kMmaWarps ? kMmaWarps : ntiles;  // loop stride over tiles
-    const int g_begin = (part * ngroups) / kw;
-    const int g_end = ((part + 1) * ngroups) / kw;
-    const int ng = g_end - g_begin;
+    // Column slice of this CTA and this warp's segment of (tile, window) units.
+    const int slice = blockIdx.x / a.cps, cl = blockIdx.x % a.cps;
+    const int win0 = (int)((long long)slice * a.nwin / a.kc);
+    const int nh = (int)((long long)(slice + 1) * a.nwin / a.kc) - win0;
+    const long long U = (long long)a.tiles * nh;
+    const long long K = (long long)a.cps * kMmaWarps;
+    const long long kseg = (long long)cl * kMmaWarps + warp;
+    const long long ua = U * kseg / K, ub = U * (kseg + 1) / K;
+    const bool cta_work = U * ((long long)(cl + 1) * kMmaWarps) / K > U * ((long long)cl * kMmaWarps) / K;
+    const int tfirst = (int)(ua / (nh > 0 ? nh : 1));
 
-    // The weights do not depend on the preceding (prep) kernel, so each warp
-    // issues its first weight loads before waiting for the activations.
-    bool waited = false;
+    if (lane == 0)
+        for (int i = 0; i < nst; ++i) mbar_init(&full[i], 33);  // expect_tx arrival + 32 cp.async arrivals
+    if (threadIdx.x == 0) mbar_init(ibar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    __syncthreads();
 
-    unsigned long long best[B];
-#pragma unroll
-    for (int bb = 0; bb < B; ++bb) best[bb] = 0ull;
+    const uint64_t pol_stream = evict_first_policy();
+    const uint64_t pol_keep = evict_normal_policy();
 
-    // Tiles this warp works on: my_tile0, my_tile0 + tile_step, ... (only
-    // my_tile0 when kw > 1).  All warps run the same number of rounds so the
-    // block-wide reductions line up.
-    const int rounds = ntiles > 0 ? (kw > 1 ? 1 : (ntiles + kMmaWarps - 1) / kMmaWarps) : 0;
-    for (int round = 0; round < rounds; ++round) {
-        const int tile = my_tile0 + round * tile_step;
-        const bool active = tile < ntiles && my_tile0 < ntiles && (kw == 1 || warp < ntiles * kw);
-        const int r0 = row_begin + tile * 16;
-        const int rowA = r0 + gq, rowB = r0 + gq + 8;
-        const bool okA = active && rowA < row_end, okB = active && rowB < row_end;
-        float acc[NM][2];
-#pragma unroll
-        for (int q = 0; q < NM; ++q) acc[q][0] = acc[q][1] = 0.0f;
-
-        if (active && ng > 0) {
-            // Base pointers of this lane's words for rows A and B of each matrix.
-            const uint32_t *wp[NM][2];
-#pragma unroll
-            for (int q = 0; q < NM; ++q) {
-                const uint32_t *W = q ? a.w2 : a.w;
-                wp[q][0] = W + (size_t)(okA ? rowA : r0) * row_words + (size_t)g_begin * (G * BITS / 32) + t * WPL;
-                wp[q][1] = W + (size_t)(okB ? rowB : r0) * row_words + (size_t)g_begin * (G * BITS / 32) + t * WPL;
-            }
-            uint32_t ring[PF][NM][2][WPL];
-#pragma unroll
-            for (int s = 0; s < PF; ++s) {
-                if (s < ng) {
-#pragma unroll
-                    for (int q = 0; q < NM; ++q)
-#pragma unroll
-                        for (int h = 0; h < 2; ++h)
-                            ldg_words<WPL>(ring[s][q][h], wp[q][h] + (size_t)s * (G * BITS / 32));
-                }
-            }
-            if (!waited) {
-                asm volatile("griddepcontrol.wait;" ::: "memory");
-                waited = true;
-            }
-            const __half *xg = a.xh + ((size_t)g_begin * 8 + gq) * 4 * CPL + (size_t)t * CPL;
-            for (int i0 = 0; i0 < ng; i0 += PF) {
-#pragma unroll
-                for (int s = 0; s < PF; ++s) {
-                    const int i = i0 + s;
-                    if (i < ng) {
-                        const int grp = g_begin + i;
-                        // Activation fragments for this lane's RHS-part column gq.
-                        uint32_t xb[CPL / 2];
-                        const uint4 *xp4 = reinterpret_cast<const uint4 *>(xg + (size_t)i * 8 * 4 * CPL);
-#pragma unroll
-                        for (int k = 0; k < CPL / 8; ++k) {
-                            const uint4 v = __ldcg(xp4 + k);
-                            xb[4 * k] = v.x;
-                            xb[4 * k + 1] = v.y;
-                            xb[4 * k + 2] = v.z;
-                            xb[4 * k + 3] = v.w;
-                        }
-                        const float xsv = t < B ? __ldcg(a.xs + (size_t)t * row_groups + grp) : 0.0f;
-#pragma unroll
-                        for (int q = 0; q < NM; ++q) {
-                            const void *Sx = q ? a.s2 : a.s;
-                            const void *Bx = q ? a.b2 : a.b;
-                            float d[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                            for (int j = 0; j < NMMA; ++j) {
-                                uint32_t af[4];
-                                af[0] = a_reg<BITS>(ring[s][q][0], 2 * j);
-                                af[1] = a_reg<BITS>(ring[s][q][1], 2 * j);
-                                af[2] = a_reg<BITS>(ring[s][q][0], 2 * j + 1);
-                                af[3] = a_reg<BITS>(ring[s][q][1], 2 * j + 1);
-                                mma_16816(d, af, xb[2 * j], xb[2 * j + 1]);
-                            }
-                            // d: (row A, part hi/lo of RHS t), (row B, ...).
-                            const float pA = __fadd_rn(d[0], d[1]);
-                            const float pB = __fadd_rn(d[2], d[3]);
-                            const size_t giA = (size_t)(okA ? rowA : r0) * row_groups + grp;
-                            const size_t giB = (size_t)(okB ? rowB : r0) * row_groups + grp;
-                            acc[q][0] = __fmaf_rn(load_meta<BF16>(Sx, giA), pA, acc[q][0]);
-                            acc[q][0] = __fmaf_rn(load_meta<BF16>(Bx, giA), xsv, acc[q][0]);
-                            acc[q][1] = __fmaf_rn(load_meta<BF16>(Sx, giB), pB, acc[q][1]);
-                            acc[q][1] = __fmaf_rn(load_meta<BF16>(Bx, giB), xsv, acc[q][1]);
-                        }
-                        // Refill this slot with the group PF ahead.
-                        if (i + PF < ng) {
-#pragma unroll
-                            for (int q = 0; q < NM; ++q)
-#pragma unroll
-                                for (int h = 0; h < 2; ++h)
-                                    ldg_words<WPL>(ring[s][q][h], wp[q][h] + (size_t)(i + PF) * (G * BITS / 32));
-                        }
-                    }
-                }
-            }
-        }
-        // ---- combine the column parts of the tile, in warp order ----
-        if (kw > 1) {
+    // Issue unit (tile T, window wi of the slice) into ring slot sl.
+    auto issue = [&](int T, int wi, int sl) {
+        const int wg = win0 + wi;
+        unsigned char *slot = ring + (size_t)sl * SLOT;
+        uint64_t *bar = &full[sl];
+        if (lane == 0) {
+            fence_proxy_async();
+            mbar_arrive_expect_tx(bar, NM * S::W_BYTES);
 #pragma unroll
             for (int q = 0; q < NM; ++q)
 #pragma unroll
-                for (int bb = 0; bb < B; ++bb) {
-                    red[warp][q][0][bb][lane] = (t == bb) ? acc[q][0] : 0.0f;
-                    red[warp][q][1][bb][lane] = (t == bb) ? acc[q][1] : 0.0f;
-                }
-            __syncthreads();
-            if (part == 0 && active) {
+                for (int c = 0; c < S::NBOX; ++c)
+                    tma_load_2d(slot + q * S::W_BYTES + c * 2048, q ? &wmap2 : &wmap, wg * S::ROW_WORDS + c * 32,
+                                T * kTileRows, bar, pol_stream);
+        }
+        __syncwarp();
+        // Metadata: lane = 2 * row + (0 scale | 1 bias), the window's groups.
+        const int r = lane >> 1, kind = lane & 1;
+        const int row = T * kTileRows + r;
+        const int gbeg = wg * S::WG;
+        int valid = row < a.rows ? (a.ngroups - gbeg) * MSZ : 0;
+        valid = valid < 0 ? 0 : (valid > META_LANE ? META_LANE : valid);
 #pragma unroll
-                for (int q = 0; q < NM; ++q)
+        for (int q = 0; q < NM; ++q) {
+            const unsigned char *base = kind ? (q ? a.b2 : a.b) : (q ? a.s2 : a.s);
+            const unsigned char *src = base + ((size_t)(valid > 0 ? row : 0) * a.ngroups + (valid > 0 ? gbeg : 0)) * MSZ;
+            unsigned char *dst = slot + NM * S::W_BYTES + q * META_BYTES + lane * META_LANE;
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        float v = 0.0f;
-                        for (int p = 0; p < kw; ++p) v = __fadd_rn(v, red[warp + p][q][h][t < B ? t : 0][lane]);
-                        acc[q][h] = v;
-                    }
+            for (int p = 0; p < META_LANE / 16; ++p) {
+                const int n = valid - 16 * p;
+                cp_async16(dst + 16 * p, n > 0 ? src + 16 * p : base, n <= 0 ? 0u : (n > 16 ? 16u : (uint32_t)n));
             }
-            __syncthreads();
         }
-        if (!waited) {
-            asm volatile("griddepcontrol.wait;" ::: "memory");
-            waited = true;
+        cp_async_arrive(bar);
+    };
+
+    // Issue cursor: unit `issued` = (tile it, window iw), ring slot is_.
+    long long issued = ua;
+    int it = nh > 0 ? (int)(ua / nh) : 0, iw = nh > 0 ? (int)(ua % nh) : 0, is_ = 0;
+    auto issue_next = [&]() {
+        issue(it, iw, is_);
+        ++issued;
+        if (++iw == nh) iw = 0, ++it;
+        if (++is_ == nst) is_ = 0;
+    };
+    for (int i = 0; i < nst && issued < ub; ++i) issue_next();
+
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
+    bool ok = true;
+    if (cta_work) {
+        if (threadIdx.x == 0) {
+            const uint32_t img_bytes = (uint32_t)nh * S::WG * G * NB * 2;
+            const uint32_t tab_bytes = 4u * (uint32_t)a.ngroups_pad * 4u;
+            mbar_arrive_expect_tx(ibar, img_bytes + tab_bytes);
+            const unsigned char *src = reinterpret_cast<const unsigned char *>(a.image + (size_t)win0 * S::WG * G * NB);
+            for (uint32_t o = 0; o < img_bytes; o += 32768u) {
+                const uint32_t n = img_bytes - o < 32768u ? img_bytes - o : 32768u;
+                bulk_g2s(smem + a.off_image + o, src + o, n, ibar, pol_keep);
+            }
+            bulk_g2s(smem + a.off_table, a.table, tab_bytes, ibar, pol_keep);
         }
-        if (active && part == 0 && t < B) {
+        if (ua < ub && !__all_sync(0xffffffffu, mbar_wait(ibar, 0))) {
+            ok = false;
+            if (lane == 0) atomicCAS(a.err, 0u, kErrTimeoutFull);
+        }
+    }
+
+    const int n = gq < NB ? gq : NB - 1;  // activation column read by this lane
+    unsigned long long best = 0ull;
+    float2 acc[NM][2];
+    bool piece_whole = false;  // the current piece started at window 0 of its tile
+    long long u = ua;
+    int T = tfirst, wi = nh > 0 ? (int)(ua % nh) : 0, sl = 0;
+    uint32_t phase = 0;
+    for (; ok && u < ub; ++u, wi = (wi + 1 == nh) ? 0 : wi + 1, T += (wi == 0) ? 1 : 0) {
+        if (u == ua || wi == 0) {
+#pragma unroll
+            for (int q = 0; q < NM; ++q) acc[q][0] = acc[q][1] = make_float2(0.0f, 0.0f);
+            piece_whole = wi == 0;
+        }
+        const int cur = sl;
+        const uint32_t cur_phase = phase;
+        if (++sl == nst) {
+            sl = 0;
+            phase ^= 1u;
+        }
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[cur], cur_phase))) {  // warp-uniform outcome
+            ok = false;
+            if (lane == 0) atomicCAS(a.err, 0u, kErrTimeoutFull);
+            break;
+        }
+        const unsigned char *slot = ring + (size_t)cur * SLOT;
+        const int lg0 = wi * S::WG;               // slice-local group of the window
+        const int gg0 = (win0 + wi) * S::WG;      // global group of the window
+#pragma unroll
+        for (int gl = 0; gl < S::WG; gl += 2) {
+            uint32_t xb[2][S::NREG];
+#pragma unroll
+            for (int e = 0; e < 2; ++e)
+#pragma unroll
+                for (int jj = 0; jj < S::NCH; ++jj) {
+                    const uint4 v = ximg[((((size_t)(lg0 + gl + e) * S::NCH + jj) * NB + n) * 4) + t];
+                    xb[e][4 * jj] = v.x;
+                    xb[e][4 * jj + 1] = v.y;
+                    xb[e][4 * jj + 2] = v.z;
+                    xb[e][4 * jj + 3] = v.w;
+                }
+            const float2 xs = *reinterpret_cast<const float2 *>(xtab + (size_t)t * a.ngroups_pad + gg0 + gl);
+#pragma unroll
+            for (int q = 0; q < NM; ++q) {
+                const unsigned char *wq = slot + q * S::W_BYTES;
+                const unsigned char *mq = slot + NM * S::W_BYTES + q * META_BYTES + gl * MSZ;
+                const float2 sA = meta_pair<BF16>(mq + (2 * gq) * META_LANE);
+                const float2 bA = meta_pair<BF16>(mq + (2 * gq + 1) * META_LANE);
+                const float2 sB = meta_pair<BF16>(mq + (2 * gq + 16) * META_LANE);
+                const float2 bB = meta_pair<BF16>(mq + (2 * gq + 17) * META_LANE);
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int off = (gl + e) * S::GROUP_BYTES + t * S::WPL * 4;
+                    const unsigned char *box = wq + (off >> 7) * 2048;
+                    uint32_t wa[S::WPL], wb[S::WPL];
+                    lds_swizzled<S::WPL>(wa, box, gq, off & 127);
+                    lds_swizzled<S::WPL>(wb, box, gq + 8, off & 127);
+                    uint32_t ra[S::NREG], rb[S::NREG];
+                    a_regs<BITS, S::WPL>(wa, ra);
+                    a_regs<BITS, S::WPL>(wb, rb);
+                    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                    for (int mj = 0; mj < S::NMMA; ++mj)
+                        mma_16816(d, ra[2 * mj], rb[2 * mj], ra[2 * mj + 1], rb[2 * mj + 1], xb[e][2 * mj],
+                                  xb[e][2 * mj + 1]);
+                    const float s_a = e ? sA.y : sA.x, b_a = e ? bA.y : bA.x;
+                    const float s_b = e ? sB.y : sB.x, b_b = e ? bB.y : bB.x;
+                    const float xsum = e ? xs.y : xs.x;
+                    acc[q][0] = ffma2(make_float2(s_a, s_a), make_float2(d[0], d[1]), acc[q][0]);
+                    acc[q][0].x = __fmaf_rn(b_a, xsum, acc[q][0].x);
+                    acc[q][1] = ffma2(make_float2(s_b, s_b), make_float2(d[2], d[3]), acc[q][1]);
+                    acc[q][1].x = __fmaf_rn(b_b, xsum, acc[q][1].x);
+                }
+            }
+        }
+        __syncwarp();
+        if (issued < ub) issue_next();  // refills the slot just read
+
+        if (wi != nh - 1 && u + 1 != ub) continue;
+        // ---- a tile piece ends here ----
+        float v[NM][2];
+#pragma unroll
+        for (int q = 0; q < NM; ++q) {
+            v[q][0] = __fadd_rn(acc[q][0].x, acc[q][0].y);
+            v[q][1] = __fadd_rn(acc[q][1].x, acc[q][1].y);
+        }
+        const bool whole = a.kc == 1 && piece_whole && wi == nh - 1;
+        if (!whole) {
+            const int sidx = a.kc == 1 ? (T == tfirst ? 0 : 1) : T - tfirst;
+            float *p = a.partial + (((size_t)slice * K + kseg) * a.slots + sidx) * (NM * 64);
+#pragma unroll
+            for (int q = 0; q < NM; ++q) {
+                p[q * 64 + lane] = v[q][0];
+                p[q * 64 + 32 + lane] = v[q][1];
+            }
+            __threadfence();
+            __syncwarp();
+            unsigned int last = 0;
+            if (lane == 0) {
+                int cidx, np;
+                tile_pieces(a, T, K, &cidx, &np);
+                last = atomicAdd(a.counters + cidx, 1u) == (unsigned int)(np - 1) ? 1u : 0u;
+                if (last) a.counters[cidx] = 0u;  // ready for the next launch
+            }
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (!last) continue;
+            __threadfence();
+            // Add every piece of the tile in (slice, segment) order.
+#pragma unroll
+            for (int q = 0; q < NM; ++q) v[q][0] = v[q][1] = 0.0f;
+            for (int h = 0; h < a.kc; ++h) {
+                const long long w0 = (long long)h * a.nwin / a.kc, w1 = (long long)(h + 1) * a.nwin / a.kc;
+                const long long nhh = w1 - w0, Uh = (long long)a.tiles * nhh;
+                const long long uf = (long long)T * nhh, ul = uf + nhh - 1;
+                const long long kf = ((uf + 1) * K - 1) / Uh, kl = ((ul + 1) * K - 1) / Uh;
+                for (long long k = kf; k <= kl; ++k) {
+                    if (Uh * (k + 1) / K == Uh * k / K) continue;  // empty segment
+                    const int tf = (int)((Uh * k / K) / nhh);
+                    const int si = a.kc == 1 ? (T == tf ? 0 : 1) : T - tf;
+                    const float *pp = a.partial + (((size_t)h * K + k) * a.slots + si) * (NM * 64);
+#pragma unroll
+                    for (int q = 0; q < NM; ++q) {
+                        v[q][0] = __fadd_rn(v[q][0], __ldcg(pp + q * 64 + lane));
+                        v[q][1] = __fadd_rn(v[q][1], __ldcg(pp + q * 64 + 32 + lane));
+                    }
+                }
+            }
+        }
+        // ---- epilogue: scale, activation, store, argmax keys ----
+        if (t < B) {
             const float c1 = __ldcg(a.cf + 2 * t), c2 = __ldcg(a.cf + 2 * t + 1);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-                const int row = h ? rowB : rowA;
-                if (row < row_end) {
-                    float v = __fmul_rn(__fmul_rn(acc[0][h], c1), c2);
-                    if constexpr (EPI == 1)
-                        v = __fmul_rn(silu_f32(v), __fmul_rn(__fmul_rn(acc[NM - 1][h], c1), c2));
-                    a.y[(size_t)t * a.ystride + row] = v;
+                const int row = T * kTileRows + gq + 8 * h;
+                if (row < a.rows) {
+                    float val = __fmul_rn(__fmul_rn(v[0][h], c1), c2);
+                    if constexpr (EPI == 1) val = __fmul_rn(silu_f32(val), __fmul_rn(__fmul_rn(v[NM - 1][h], c1), c2));
+                    a.y[(size_t)t * a.ystride + row] = val;
                     if constexpr (EPI == 2) {
-                        const unsigned long long key = ((unsigned long long)total_order_key(v) << 32) |
+                        const unsigned long long key = ((unsigned long long)total_order_key(val) << 32) |
                                                        (unsigned long long)(0xffffffffu - (uint32_t)(a.row_base + row));
-#pragma unroll
-                        for (int bb = 0; bb < B; ++bb)
-                            if (bb == t) best[bb] = key > best[bb] ? key : best[bb];
+                        best = key > best ? key : best;
                     }
                 }
             }
         }
     }
-
-    if (!waited) asm volatile("griddepcontrol.wait;" ::: "memory");
-    if constexpr (EPI == 2) {
-        // Per-warp maximum per RHS, one atomic per warp, then the last CTA
-        // to finish publishes the winners (fence + counter, no waiting).
-#pragma unroll
-        for (int bb = 0; bb < B; ++bb) {
-            unsigned long long k = best[bb];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const unsigned long long other = __shfl_xor_sync(0xffffffffu, k, o);
-                k = other > k ? other : k;
-            }
-            if (lane == 0 && k != 0ull) atomicMax(a.keys + bb, k);
+    // Drain copies issued but not consumed (only after a failed wait).
+    for (long long d = u; d < issued; ++d) {
+        const long long j = d - ua;
+        if (!mbar_wait(&full[(int)(j % nst)], (uint32_t)((j / nst) & 1))) {
+            if (lane == 0) atomicCAS(a.err, 0u, kErrTimeoutDrain);
+            break;
         }
+    }
+    (void)best;
+
+    if constexpr (EPI == 2) {
+        // Maximum per RHS over the lanes that share it, one atomic per RHS and
+        // warp, then the last CTA publishes the winners and clears the keys.
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+            best = other > best ? other : best;
+        }
+        if (lane < B && best != 0ull) atomicMax(a.keys + lane, best);
         __threadfence();
         __syncthreads();
         if (threadIdx.x == 0) flag = (atomicAdd(a.done, 1u) == gridDim.x - 1) ? 1u : 0u;
         __syncthreads();
-        if (flag && threadIdx.x == 0) *a.done = 0u;  // ready for the next launch
         if (flag && threadIdx.x < B) {
             __threadfence();
-            const unsigned long long k = atomicAdd(a.keys + threadIdx.x, 0ull);
+            const unsigned long long k = atomicExch(a.keys + threadIdx.x, 0ull);
             if (a.argmax) a.argmax[threadIdx.x] = (int)(0xffffffffu - (uint32_t)(k & 0xffffffffu));
             if (a.best_key_out) a.best_key_out[threadIdx.x] = k;
         }
+        if (flag && threadIdx.x == 0) *a.done = 0u;
     }
 }
 
