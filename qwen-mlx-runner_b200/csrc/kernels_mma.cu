@@ -36,22 +36,25 @@ int opt_in_smem(Kern kern, std::atomic<uint64_t> &done) {
     if (done.load(std::memory_order_acquire) & bit) return QMR_OK;
     int max_optin = 0;
     cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, max_optin);
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, kern);
+    if (e != cudaSuccess) return fail(QMR_ECUDA, "cudaFuncGetAttributes: %s", cudaGetErrorString(e));
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, max_optin - (int)fa.sharedSizeBytes);
     if (e != cudaSuccess) return fail(QMR_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     done.fetch_or(bit, std::memory_order_acq_rel);
     return QMR_OK;
 }
 
-template <int G, int B, bool BF16, int EPI>
-int launch_t(const CUtensorMap &m1, const CUtensorMap &m2, const MmaArgs &a, const MmaPlan &p, bool overlap,
+template <int G, int B, bool BF16, int EPI, int NW>
+int launch_w(const CUtensorMap &m1, const CUtensorMap &m2, const MmaArgs &a, const MmaPlan &p, bool overlap,
              cudaStream_t stream) {
-    auto kern = mma_kernel<kBits, G, B, BF16, EPI>;
+    auto kern = mma_kernel<kBits, G, B, BF16, EPI, NW>;
     static std::atomic<uint64_t> opted{0};
     const int rc = opt_in_smem(kern, opted);
     if (rc != QMR_OK) return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)p.ctas, 1, 1);
-    cfg.blockDim = dim3(32 * kMmaWarps, 1, 1);
+    cfg.blockDim = dim3(32 * NW, 1, 1);
     cfg.dynamicSmemBytes = p.smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1] = {pdl_attr()};
@@ -60,6 +63,15 @@ int launch_t(const CUtensorMap &m1, const CUtensorMap &m2, const MmaArgs &a, con
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, m1, m2, a);
     if (e != cudaSuccess) return fail(QMR_ECUDA, "tensor-core kernel launch failed: %s", cudaGetErrorString(e));
     return QMR_OK;
+}
+
+template <int G, int B, bool BF16, int EPI>
+int launch_t(const CUtensorMap &m1, const CUtensorMap &m2, const MmaArgs &a, const MmaPlan &p, bool overlap,
+             cudaStream_t stream) {
+    // 16 warps for Q4 single-matrix calls, 8 otherwise (the plan's rule).
+    constexpr int NW = (kBits == 4 && EPI != 1) ? 16 : 8;
+    if (p.warps != NW) return fail(QMR_EUNSUPPORTED, "no tensor-core kernel with %d warps", p.warps);
+    return launch_w<G, B, BF16, EPI, NW>(m1, m2, a, p, overlap, stream);
 }
 
 template <int G, bool BF16, int EPI>

@@ -41,6 +41,7 @@ struct MmaPlan {
     int nwin;         // 512/1024-column windows of the matrix
     int ngroups_pad;  // groups of the padded activation image
     int tiles;        // 16-row tiles
+    int warps;        // warps per CTA (8 or 16)
     uint32_t smem, off_image, off_table, off_bars;
 };
 bool mma_plan(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint32_t batch, int epi, bool bf16,

@@ -150,11 +150,30 @@ bool fast_eligible(const void *w, uint32_t cols, uint32_t bits, uint32_t group) 
 
 
 // Activation image of one column slice, worst case B = 4, stays within this
-// budget; wider matrices are split into 2 or 4 column slices.
+// budget (5120 columns take one slice, 17408 columns 4).
 constexpr size_t kMmaImageBudget = 96 * 1024;
 
+namespace {
+
+bool mma_plan_b(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint32_t batch, int epi, bool bf16,
+                MmaPlan *p);
+
+}  // namespace
+
+// The launch plan for this call.  Whether the kernel takes a shape is decided
+// at B = 4, and the column slicing does not depend on B, so every block width
+// of one matrix runs the same kernel with the same summation order.
 bool mma_plan(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint32_t batch, int epi, bool bf16,
               MmaPlan *p) {
+    MmaPlan widest;
+    if (!mma_plan_b(bits, group, rows, cols, 4, epi, bf16, &widest)) return false;
+    return mma_plan_b(bits, group, rows, cols, batch, epi, bf16, p);
+}
+
+namespace {
+
+bool mma_plan_b(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint32_t batch, int epi, bool bf16,
+                MmaPlan *p) {
     if (bits != 4 && bits != 8) return false;
     if (group != 32 && group != 64 && group != 128) return false;
     if (bits == 8 && group == 128) return false;
@@ -166,6 +185,9 @@ bool mma_plan(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint3
     const int nwin = (int)((cols + win_cols - 1) / win_cols);
     const int tiles = (int)((rows + kTileRows - 1) / kTileRows);
     const int nm = epi == 1 ? 2 : 1;
+    // Q4 single-matrix units are light on shared memory: 16 warps hide more
+    // latency; the heavier slots of Q8 and gate/up pairs fit 8.
+    const int warps = (bits == 4 && nm == 1) ? 16 : 8;
     const int sms = sm_count();
     int kc = 0;
     for (int c : {1, 2, 4}) {
@@ -178,27 +200,28 @@ bool mma_plan(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint3
     if (kc == 0) return false;
     const int ctas = sms / kc * kc;
     const int cps = ctas / kc;
-    const long long K = (long long)cps * kMmaWarps;
+    const long long K = (long long)cps * warps;
     const int nh_min = nwin / kc, nh_max = (nwin + kc - 1) / kc;
     int slots = 2;
     if (kc > 1) {
         const long long lmax = ((long long)tiles * nh_max + K - 1) / K;
         slots = (int)(lmax / nh_min) + 2;
-        if (tiles > kCounterCount) return false;
+        if (tiles > kCounterCount || slots > kMaxPending) return false;
     } else if (K > kCounterCount) {
         return false;
     }
-    if ((size_t)ctas * kMmaWarps * slots * nm * 64 > kPartialFloats) return false;
-    const uint32_t slot = (uint32_t)mma_slot_bytes((int)bits, (int)group, nm, bf16 ? 2 : 4);
+    if ((size_t)ctas * warps * slots * nm * 64 > kPartialFloats) return false;
+    const uint32_t slot = (uint32_t)(mma_slot_weight_bytes((int)bits, (int)group, nm) +
+                                     mma_slot_meta_bytes((int)group, nm, bf16 ? 2 : 4));
     const uint32_t image = (uint32_t)nh_max * win_cols * 4 * batch;
     const uint32_t ngroups_pad = (uint32_t)nwin * wg;
     const uint32_t table = 16 * ngroups_pad;
-    const int limit = smem_optin() - 64;  // room for the kernel's static shared variables
+    const int limit = smem_optin() - 128;  // room for the kernel's static shared variables (16 bytes)
     for (int st = kMmaMaxStages; st >= 2; --st) {
-        const uint32_t off_image = (uint32_t)kMmaWarps * st * slot;
+        const uint32_t off_image = (uint32_t)warps * st * slot;
         const uint32_t off_table = off_image + (image + 127) / 128 * 128;
         const uint32_t off_bars = off_table + (table + 127) / 128 * 128;
-        const uint32_t total = 1024 + off_bars + (uint32_t)(kMmaWarps * st + 1) * 8;
+        const uint32_t total = 1024 + off_bars + (uint32_t)(warps * st + 1) * 8;
         if ((int)total <= limit) {
             p->kc = kc;
             p->cps = cps;
@@ -208,6 +231,7 @@ bool mma_plan(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint3
             p->nwin = nwin;
             p->ngroups_pad = (int)ngroups_pad;
             p->tiles = tiles;
+            p->warps = warps;
             p->smem = total;
             p->off_image = off_image;
             p->off_table = off_table;
@@ -217,6 +241,8 @@ bool mma_plan(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint3
     }
     return false;
 }
+
+}  // namespace
 
 int log2i(uint32_t v) {
     int r = 0;

@@ -60,8 +60,8 @@
 
 namespace qmr {
 
-constexpr int kMmaWarps = 8;     // warps per CTA, each with its own copy ring
 constexpr int kTileRows = 16;    // rows of one MMA tile
+constexpr int kMaxPending = 4;   // split pieces one warp may publish
 constexpr int kMmaMaxStages = 6;
 
 template <int BITS, int G>
@@ -80,13 +80,15 @@ struct MmaShape {
     static constexpr int W_BYTES = kTileRows * ROW_BYTES;           // weights of one unit
 };
 
-// Bytes of one ring slot: the weights of NM matrices, then their metadata
-// (32 lanes x the window's groups of one (row, scale|bias) each).
-__host__ __device__ constexpr int mma_slot_bytes(int bits, int group, int nm, int meta_size) {
-    const int win_cols = 8 * group > 512 ? 8 * group : 512;
-    const int w_bytes = kTileRows * win_cols * bits / 8;
-    const int meta = 32 * (win_cols / group) * meta_size;
-    return (nm * (w_bytes + meta) + 1023) / 1024 * 1024;
+// Bytes of one ring slot: the weights of NM matrices (a multiple of 2 KiB, so
+// every slot stays 1024-byte aligned for the swizzle) and, in a separate
+// region, their metadata (32 lanes x the window's groups of one
+// (row, scale|bias) each).
+__host__ __device__ constexpr int mma_slot_weight_bytes(int bits, int group, int nm) {
+    return nm * kTileRows * (8 * group > 512 ? 8 * group : 512) * bits / 8;
+}
+__host__ __device__ constexpr int mma_slot_meta_bytes(int group, int nm, int meta_size) {
+    return nm * 32 * ((8 * group > 512 ? 8 * group : 512) / group) * meta_size;
 }
 
 // Column (relative to the lane's first column of the group) that feeds half
@@ -193,66 +195,80 @@ __global__ void __launch_bounds__(512) mma_prep_kernel(const float *__restrict__
     }
 }
 
+// D = A * B + D and D = A * B (zero accumulator) for m16n8k16 f16 -> f32.
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                           uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// N words of `row` of a 16 x 128-byte TMA box written with the 128-byte
-// swizzle (16-byte unit u of row r sits at unit u ^ (r & 7)), starting at
-// byte `within` of the row.
+__device__ __forceinline__ void mma_16816_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                            uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
+}
+
+// Shared-memory loads at 32-bit shared addresses.  Volatile keeps them after
+// the mbarrier wait that publishes the data.
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+
+// The N = 1, 2 or 4 words a lane reads from one row of a group.
 template <int N>
-__device__ __forceinline__ void lds_swizzled(uint32_t (&v)[N], const unsigned char *box, int row, int within) {
-    const unsigned char *line = box + row * 128;
-    const int unit = within >> 4, off = within & 15;
+__device__ __forceinline__ void lds_words(uint32_t (&w)[N], uint32_t a) {
     if constexpr (N == 1) {
-        v[0] = *reinterpret_cast<const uint32_t *>(line + (((unit ^ (row & 7)) << 4) | off));
+        w[0] = lds32(a);
     } else if constexpr (N == 2) {
-        const uint2 p = *reinterpret_cast<const uint2 *>(line + (((unit ^ (row & 7)) << 4) | off));
-        v[0] = p.x;
-        v[1] = p.y;
+        const uint2 v = lds64(a);
+        w[0] = v.x;
+        w[1] = v.y;
     } else {
-#pragma unroll
-        for (int k = 0; k < N / 4; ++k) {
-            const uint4 p = *reinterpret_cast<const uint4 *>(line + (((unit + k) ^ (row & 7)) << 4));
-            v[4 * k] = p.x;
-            v[4 * k + 1] = p.y;
-            v[4 * k + 2] = p.z;
-            v[4 * k + 3] = p.w;
-        }
+        const uint4 v = lds128(a);
+        w[0] = v.x;
+        w[1] = v.y;
+        w[2] = v.z;
+        w[3] = v.w;
     }
 }
 
-// A-operand registers of one row from its words (see the file comment).
-template <int BITS, int WPL>
-__device__ __forceinline__ void a_regs(const uint32_t (&w)[WPL], uint32_t (&r)[WPL * 32 / BITS / 2]) {
-#pragma unroll
-    for (int i = 0; i < WPL; ++i) {
-        if constexpr (BITS == 4) {
-            const uint32_t u = w[i] >> 8;
-            r[4 * i] = w[i] & 0x000f000fu;
-            r[4 * i + 1] = w[i] & 0x00f000f0u;
-            r[4 * i + 2] = u & 0x000f000fu;
-            r[4 * i + 3] = u & 0x00f000f0u;
-        } else {
-            r[2 * i] = w[i] & 0x00ff00ffu;
-            r[2 * i + 1] = (w[i] >> 8) & 0x00ff00ffu;
-        }
+// A-operand register `r` of a row from its words (see the file comment).
+template <int BITS>
+__device__ __forceinline__ uint32_t a_reg(const uint32_t *w, int r) {
+    if constexpr (BITS == 4) {
+        const uint32_t v = (r & 2) ? (w[r >> 2] >> 8) : w[r >> 2];
+        return v & ((r & 1) ? 0x00f000f0u : 0x000f000fu);
+    } else {
+        const uint32_t v = (r & 1) ? (w[r >> 1] >> 8) : w[r >> 1];
+        return v & 0x00ff00ffu;
     }
 }
 
-// Scales or biases of groups (g, g+1) from the slot's metadata area.
+// Scales or biases of groups (g, g+1) of one row from the metadata ring.
 template <bool BF16>
-__device__ __forceinline__ float2 meta_pair(const unsigned char *p) {
+__device__ __forceinline__ float2 meta_pair(uint32_t a) {
     if constexpr (BF16) {
-        const uint32_t v = *reinterpret_cast<const uint32_t *>(p);
+        const uint32_t v = lds32(a);
         return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
     } else {
-        return *reinterpret_cast<const float2 *>(p);
+        const uint2 v = lds64(a);
+        return make_float2(__uint_as_float(v.x), __uint_as_float(v.y));
     }
 }
 
@@ -263,7 +279,7 @@ struct MmaArgs {
     const float *cf;                       // output factors [B][2]
     float *y;
     float *partial;                        // [segments][slots][NM][64] piece sums
-    unsigned int *counters;                // arrivals per multi-piece tile
+    unsigned int *counters;                // arrivals per split tile
     unsigned long long *keys;              // [B] packed argmax (EPI 2)
     unsigned int *done;                    // CTAs finished (EPI 2)
     int *argmax;
@@ -274,7 +290,8 @@ struct MmaArgs {
     uint32_t off_image, off_table, off_bars;  // offsets into the 1024-aligned dynamic shared memory
 };
 
-// Pieces of tile T across the slices and the counter that tracks them.
+// Pieces of tile T across the slices (non-empty segments only) and the
+// counter that tracks them.
 __device__ __forceinline__ void tile_pieces(const MmaArgs &a, int T, long long K, int *counter, int *npieces) {
     int n = 0, c = 0;
     for (int h = 0; h < a.kc; ++h) {
@@ -283,14 +300,14 @@ __device__ __forceinline__ void tile_pieces(const MmaArgs &a, int T, long long K
         const long long uf = (long long)T * nh, ul = uf + nh - 1;
         const long long kf = ((uf + 1) * K - 1) / U, kl = ((ul + 1) * K - 1) / U;
         if (h == 0) c = (int)kf;
-        for (long long k = kf; k <= kl; ++k) n += (U * (k + 1) / K > U * k / K) ? 1 : 0;  // non-empty segments
+        for (long long k = kf; k <= kl; ++k) n += (U * (k + 1) / K > U * k / K) ? 1 : 0;
     }
     *counter = a.kc == 1 ? c : T;
     *npieces = n;
 }
 
-template <int BITS, int G, int B, bool BF16, int EPI>
-__global__ void __launch_bounds__(32 * kMmaWarps, 1)
+template <int BITS, int G, int B, bool BF16, int EPI, int NW>
+__global__ void __launch_bounds__(32 * NW, 1)
     mma_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap wmap2, const MmaArgs a) {
     using S = MmaShape<BITS, G>;
     constexpr int NM = (EPI == 1) ? 2 : 1;
@@ -298,30 +315,36 @@ __global__ void __launch_bounds__(32 * kMmaWarps, 1)
     constexpr int MSZ = BF16 ? 2 : 4;
     constexpr int META_LANE = S::WG * MSZ;
     constexpr int META_BYTES = 32 * META_LANE;
-    constexpr int SLOT = mma_slot_bytes(BITS, G, NM, MSZ);
+    constexpr int SLOT_W = mma_slot_weight_bytes(BITS, G, NM);
+    constexpr int SLOT_M = mma_slot_meta_bytes(G, NM, MSZ);
+    constexpr int GPB = 128 / S::GROUP_BYTES;  // groups per 128-byte line of a box
+    constexpr int LANE_BYTES = S::WPL * 4;      // bytes of one row a lane reads per group
+    constexpr int XG = S::NCH * NB * 64;        // activation image bytes per group
+    static_assert(LANE_BYTES <= 16 && GPB >= 1, "one 16-byte unit per lane and row");
     extern __shared__ unsigned char smem_raw[];
     __shared__ unsigned int flag;
-    unsigned char *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const uint32_t sraw = smem_u32(smem_raw);
+    const uint32_t sbase = (sraw + 1023u) & ~1023u;
+    unsigned char *smem = smem_raw + (sbase - sraw);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gq = lane >> 2, t = lane & 3;
     const int nst = a.stages;
-    unsigned char *ring = smem + (size_t)warp * nst * SLOT;
-    const uint4 *ximg = reinterpret_cast<const uint4 *>(smem + a.off_image);
-    const float *xtab = reinterpret_cast<const float *>(smem + a.off_table);
+    const uint32_t ring_w = sbase + (uint32_t)(warp * nst * SLOT_W);
+    const uint32_t ring_m = sbase + (uint32_t)(NW * nst * SLOT_W + warp * nst * SLOT_M);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + a.off_bars);
     uint64_t *full = bars + warp * nst;
-    uint64_t *ibar = bars + kMmaWarps * nst;
+    uint64_t *ibar = bars + NW * nst;
 
     // Column slice of this CTA and this warp's segment of (tile, window) units.
     const int slice = blockIdx.x / a.cps, cl = blockIdx.x % a.cps;
     const int win0 = (int)((long long)slice * a.nwin / a.kc);
     const int nh = (int)((long long)(slice + 1) * a.nwin / a.kc) - win0;
     const long long U = (long long)a.tiles * nh;
-    const long long K = (long long)a.cps * kMmaWarps;
-    const long long kseg = (long long)cl * kMmaWarps + warp;
+    const long long K = (long long)a.cps * NW;
+    const long long kseg = (long long)cl * NW + warp;
     const long long ua = U * kseg / K, ub = U * (kseg + 1) / K;
-    const bool cta_work = U * ((long long)(cl + 1) * kMmaWarps) / K > U * ((long long)cl * kMmaWarps) / K;
+    const bool cta_work = U * ((long long)(cl + 1) * NW) / K > U * ((long long)cl * NW) / K;
     const int tfirst = (int)(ua / (nh > 0 ? nh : 1));
 
     if (lane == 0)
@@ -336,17 +359,18 @@ __global__ void __launch_bounds__(32 * kMmaWarps, 1)
     // Issue unit (tile T, window wi of the slice) into ring slot sl.
     auto issue = [&](int T, int wi, int sl) {
         const int wg = win0 + wi;
-        unsigned char *slot = ring + (size_t)sl * SLOT;
+        const uint32_t slot = ring_w + (uint32_t)(sl * SLOT_W);
+        const uint32_t mslot = ring_m + (uint32_t)(sl * SLOT_M);
         uint64_t *bar = &full[sl];
         if (lane == 0) {
             fence_proxy_async();
-            mbar_arrive_expect_tx(bar, NM * S::W_BYTES);
+            mbar_arrive_expect_tx(bar, SLOT_W);
 #pragma unroll
             for (int q = 0; q < NM; ++q)
 #pragma unroll
                 for (int c = 0; c < S::NBOX; ++c)
-                    tma_load_2d(slot + q * S::W_BYTES + c * 2048, q ? &wmap2 : &wmap, wg * S::ROW_WORDS + c * 32,
-                                T * kTileRows, bar, pol_stream);
+                    tma_load_2d_s(slot + q * S::W_BYTES + c * 2048, q ? &wmap2 : &wmap, wg * S::ROW_WORDS + c * 32,
+                                  T * kTileRows, bar, pol_stream);
         }
         __syncwarp();
         // Metadata: lane = 2 * row + (0 scale | 1 bias), the window's groups.
@@ -359,11 +383,11 @@ __global__ void __launch_bounds__(32 * kMmaWarps, 1)
         for (int q = 0; q < NM; ++q) {
             const unsigned char *base = kind ? (q ? a.b2 : a.b) : (q ? a.s2 : a.s);
             const unsigned char *src = base + ((size_t)(valid > 0 ? row : 0) * a.ngroups + (valid > 0 ? gbeg : 0)) * MSZ;
-            unsigned char *dst = slot + NM * S::W_BYTES + q * META_BYTES + lane * META_LANE;
+            const uint32_t dst = mslot + (uint32_t)(q * META_BYTES + lane * META_LANE);
 #pragma unroll
             for (int p = 0; p < META_LANE / 16; ++p) {
                 const int n = valid - 16 * p;
-                cp_async16(dst + 16 * p, n > 0 ? src + 16 * p : base, n <= 0 ? 0u : (n > 16 ? 16u : (uint32_t)n));
+                cp_async16_s(dst + 16 * p, n > 0 ? src + 16 * p : base, n <= 0 ? 0u : (n > 16 ? 16u : (uint32_t)n));
             }
         }
         cp_async_arrive(bar);
@@ -386,10 +410,10 @@ __global__ void __launch_bounds__(32 * kMmaWarps, 1)
     bool ok = true;
     if (cta_work) {
         if (threadIdx.x == 0) {
-            const uint32_t img_bytes = (uint32_t)nh * S::WG * G * NB * 2;
+            const uint32_t img_bytes = (uint32_t)nh * S::WG * XG;
             const uint32_t tab_bytes = 4u * (uint32_t)a.ngroups_pad * 4u;
             mbar_arrive_expect_tx(ibar, img_bytes + tab_bytes);
-            const unsigned char *src = reinterpret_cast<const unsigned char *>(a.image + (size_t)win0 * S::WG * G * NB);
+            const unsigned char *src = reinterpret_cast<const unsigned char *>(a.image) + (size_t)win0 * S::WG * XG;
             for (uint32_t o = 0; o < img_bytes; o += 32768u) {
                 const uint32_t n = img_bytes - o < 32768u ? img_bytes - o : 32768u;
                 bulk_g2s(smem + a.off_image + o, src + o, n, ibar, pol_keep);
@@ -402,17 +426,55 @@ __global__ void __launch_bounds__(32 * kMmaWarps, 1)
         }
     }
 
-    const int n = gq < NB ? gq : NB - 1;  // activation column read by this lane
+    // Per-lane byte offsets: A words of row gq for the GPB groups of a box
+    // line (128-byte swizzle: 16-byte unit u of row r at u ^ (r & 7)), the
+    // activation column this lane reads, its RHS row of the group-sum table
+    // and its rows' metadata.
+    uint32_t a_off[GPB];
+#pragma unroll
+    for (int m = 0; m < GPB; ++m) {
+        const int byte = m * S::GROUP_BYTES + t * LANE_BYTES;
+        a_off[m] = (uint32_t)(gq * 128 + ((((byte >> 4) ^ gq) & 7) << 4) + (byte & 15));
+    }
+    const int n = gq < NB ? gq : NB - 1;
+    const uint32_t x_lane = sbase + a.off_image + (uint32_t)((n * 4 + t) * 16);
+    const uint32_t t_lane = sbase + a.off_table + (uint32_t)(t * a.ngroups_pad * 4);
+    const uint32_t m_lane = (uint32_t)(2 * gq * META_LANE);
+
     unsigned long long best = 0ull;
-    float2 acc[NM][2];
+    // The epilogue of one finished tile: scale, activation, store, argmax key.
+    auto finish_tile = [&](int T, const float (&v)[NM][2]) {
+        if (t < B) {
+            const float c1 = __ldcg(a.cf + 2 * t), c2 = __ldcg(a.cf + 2 * t + 1);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int row = T * kTileRows + gq + 8 * h;
+                if (row < a.rows) {
+                    float val = __fmul_rn(__fmul_rn(v[0][h], c1), c2);
+                    if constexpr (EPI == 1)
+                        val = __fmul_rn(silu_f32(val), __fmul_rn(__fmul_rn(v[NM - 1][h], c1), c2));
+                    a.y[(size_t)t * a.ystride + row] = val;
+                    if constexpr (EPI == 2) {
+                        const unsigned long long key = ((unsigned long long)total_order_key(val) << 32) |
+                                                       (unsigned long long)(0xffffffffu - (uint32_t)(a.row_base + row));
+                        best = key > best ? key : best;
+                    }
+                }
+            }
+        }
+    };
+
+    float acc[NM][2][2];  // [matrix][row A|B][part hi|lo]
     bool piece_whole = false;  // the current piece started at window 0 of its tile
+    int pend[kMaxPending];     // split pieces written, published after the segment
+    int npend = 0;
     long long u = ua;
     int T = tfirst, wi = nh > 0 ? (int)(ua % nh) : 0, sl = 0;
     uint32_t phase = 0;
     for (; ok && u < ub; ++u, wi = (wi + 1 == nh) ? 0 : wi + 1, T += (wi == 0) ? 1 : 0) {
         if (u == ua || wi == 0) {
 #pragma unroll
-            for (int q = 0; q < NM; ++q) acc[q][0] = acc[q][1] = make_float2(0.0f, 0.0f);
+            for (int q = 0; q < NM; ++q) acc[q][0][0] = acc[q][0][1] = acc[q][1][0] = acc[q][1][1] = 0.0f;
             piece_whole = wi == 0;
         }
         const int cur = sl;
@@ -426,9 +488,10 @@ __global__ void __launch_bounds__(32 * kMmaWarps, 1)
             if (lane == 0) atomicCAS(a.err, 0u, kErrTimeoutFull);
             break;
         }
-        const unsigned char *slot = ring + (size_t)cur * SLOT;
-        const int lg0 = wi * S::WG;               // slice-local group of the window
-        const int gg0 = (win0 + wi) * S::WG;      // global group of the window
+        const uint32_t wslot = ring_w + (uint32_t)(cur * SLOT_W);
+        const uint32_t mw = ring_m + (uint32_t)(cur * SLOT_M) + m_lane;
+        const uint32_t xw = x_lane + (uint32_t)(wi * S::WG * XG);
+        const uint32_t tw = t_lane + (uint32_t)((win0 + wi) * S::WG * 4);
 #pragma unroll
         for (int gl = 0; gl < S::WG; gl += 2) {
             uint32_t xb[2][S::NREG];
@@ -436,43 +499,46 @@ __global__ void __launch_bounds__(32 * kMmaWarps, 1)
             for (int e = 0; e < 2; ++e)
 #pragma unroll
                 for (int jj = 0; jj < S::NCH; ++jj) {
-                    const uint4 v = ximg[((((size_t)(lg0 + gl + e) * S::NCH + jj) * NB + n) * 4) + t];
+                    const uint4 v = lds128(xw + (uint32_t)((gl + e) * XG + jj * NB * 64));
                     xb[e][4 * jj] = v.x;
                     xb[e][4 * jj + 1] = v.y;
                     xb[e][4 * jj + 2] = v.z;
                     xb[e][4 * jj + 3] = v.w;
                 }
-            const float2 xs = *reinterpret_cast<const float2 *>(xtab + (size_t)t * a.ngroups_pad + gg0 + gl);
+            const uint2 xsv = lds64(tw + (uint32_t)(gl * 4));
+            const float xs[2] = {__uint_as_float(xsv.x), __uint_as_float(xsv.y)};
 #pragma unroll
             for (int q = 0; q < NM; ++q) {
-                const unsigned char *wq = slot + q * S::W_BYTES;
-                const unsigned char *mq = slot + NM * S::W_BYTES + q * META_BYTES + gl * MSZ;
-                const float2 sA = meta_pair<BF16>(mq + (2 * gq) * META_LANE);
-                const float2 bA = meta_pair<BF16>(mq + (2 * gq + 1) * META_LANE);
-                const float2 sB = meta_pair<BF16>(mq + (2 * gq + 16) * META_LANE);
-                const float2 bB = meta_pair<BF16>(mq + (2 * gq + 17) * META_LANE);
+                const uint32_t mq = mw + (uint32_t)(q * META_BYTES + gl * MSZ);
+                const float2 sA = meta_pair<BF16>(mq);
+                const float2 bA = meta_pair<BF16>(mq + META_LANE);
+                const float2 sB = meta_pair<BF16>(mq + 16 * META_LANE);
+                const float2 bB = meta_pair<BF16>(mq + 17 * META_LANE);
+                float d[2][4];
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
-                    const int off = (gl + e) * S::GROUP_BYTES + t * S::WPL * 4;
-                    const unsigned char *box = wq + (off >> 7) * 2048;
+                    const int gi = gl + e;
+                    const uint32_t aa = wslot + (uint32_t)(q * S::W_BYTES + (gi / GPB) * 2048) + a_off[gi % GPB];
                     uint32_t wa[S::WPL], wb[S::WPL];
-                    lds_swizzled<S::WPL>(wa, box, gq, off & 127);
-                    lds_swizzled<S::WPL>(wb, box, gq + 8, off & 127);
-                    uint32_t ra[S::NREG], rb[S::NREG];
-                    a_regs<BITS, S::WPL>(wa, ra);
-                    a_regs<BITS, S::WPL>(wb, rb);
-                    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    lds_words<S::WPL>(wa, aa);
+                    lds_words<S::WPL>(wb, aa + 1024u);
+                    mma_16816_z(d[e], a_reg<BITS>(wa, 0), a_reg<BITS>(wb, 0), a_reg<BITS>(wa, 1), a_reg<BITS>(wb, 1),
+                                xb[e][0], xb[e][1]);
 #pragma unroll
-                    for (int mj = 0; mj < S::NMMA; ++mj)
-                        mma_16816(d, ra[2 * mj], rb[2 * mj], ra[2 * mj + 1], rb[2 * mj + 1], xb[e][2 * mj],
-                                  xb[e][2 * mj + 1]);
+                    for (int mj = 1; mj < S::NMMA; ++mj)
+                        mma_16816(d[e], a_reg<BITS>(wa, 2 * mj), a_reg<BITS>(wb, 2 * mj), a_reg<BITS>(wa, 2 * mj + 1),
+                                  a_reg<BITS>(wb, 2 * mj + 1), xb[e][2 * mj], xb[e][2 * mj + 1]);
+                }
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
                     const float s_a = e ? sA.y : sA.x, b_a = e ? bA.y : bA.x;
                     const float s_b = e ? sB.y : sB.x, b_b = e ? bB.y : bB.x;
-                    const float xsum = e ? xs.y : xs.x;
-                    acc[q][0] = ffma2(make_float2(s_a, s_a), make_float2(d[0], d[1]), acc[q][0]);
-                    acc[q][0].x = __fmaf_rn(b_a, xsum, acc[q][0].x);
-                    acc[q][1] = ffma2(make_float2(s_b, s_b), make_float2(d[2], d[3]), acc[q][1]);
-                    acc[q][1].x = __fmaf_rn(b_b, xsum, acc[q][1].x);
+                    acc[q][0][0] = __fmaf_rn(s_a, d[e][0], acc[q][0][0]);
+                    acc[q][0][1] = __fmaf_rn(s_a, d[e][1], acc[q][0][1]);
+                    acc[q][0][0] = __fmaf_rn(b_a, xs[e], acc[q][0][0]);
+                    acc[q][1][0] = __fmaf_rn(s_b, d[e][2], acc[q][1][0]);
+                    acc[q][1][1] = __fmaf_rn(s_b, d[e][3], acc[q][1][1]);
+                    acc[q][1][0] = __fmaf_rn(b_b, xs[e], acc[q][1][0]);
                 }
             }
         }
@@ -484,69 +550,24 @@ __global__ void __launch_bounds__(32 * kMmaWarps, 1)
         float v[NM][2];
 #pragma unroll
         for (int q = 0; q < NM; ++q) {
-            v[q][0] = __fadd_rn(acc[q][0].x, acc[q][0].y);
-            v[q][1] = __fadd_rn(acc[q][1].x, acc[q][1].y);
+            v[q][0] = __fadd_rn(acc[q][0][0], acc[q][0][1]);
+            v[q][1] = __fadd_rn(acc[q][1][0], acc[q][1][1]);
         }
-        const bool whole = a.kc == 1 && piece_whole && wi == nh - 1;
-        if (!whole) {
-            const int sidx = a.kc == 1 ? (T == tfirst ? 0 : 1) : T - tfirst;
-            float *p = a.partial + (((size_t)slice * K + kseg) * a.slots + sidx) * (NM * 64);
-#pragma unroll
-            for (int q = 0; q < NM; ++q) {
-                p[q * 64 + lane] = v[q][0];
-                p[q * 64 + 32 + lane] = v[q][1];
-            }
-            __threadfence();
-            __syncwarp();
-            unsigned int last = 0;
-            if (lane == 0) {
-                int cidx, np;
-                tile_pieces(a, T, K, &cidx, &np);
-                last = atomicAdd(a.counters + cidx, 1u) == (unsigned int)(np - 1) ? 1u : 0u;
-                if (last) a.counters[cidx] = 0u;  // ready for the next launch
-            }
-            last = __shfl_sync(0xffffffffu, last, 0);
-            if (!last) continue;
-            __threadfence();
-            // Add every piece of the tile in (slice, segment) order.
-#pragma unroll
-            for (int q = 0; q < NM; ++q) v[q][0] = v[q][1] = 0.0f;
-            for (int h = 0; h < a.kc; ++h) {
-                const long long w0 = (long long)h * a.nwin / a.kc, w1 = (long long)(h + 1) * a.nwin / a.kc;
-                const long long nhh = w1 - w0, Uh = (long long)a.tiles * nhh;
-                const long long uf = (long long)T * nhh, ul = uf + nhh - 1;
-                const long long kf = ((uf + 1) * K - 1) / Uh, kl = ((ul + 1) * K - 1) / Uh;
-                for (long long k = kf; k <= kl; ++k) {
-                    if (Uh * (k + 1) / K == Uh * k / K) continue;  // empty segment
-                    const int tf = (int)((Uh * k / K) / nhh);
-                    const int si = a.kc == 1 ? (T == tf ? 0 : 1) : T - tf;
-                    const float *pp = a.partial + (((size_t)h * K + k) * a.slots + si) * (NM * 64);
-#pragma unroll
-                    for (int q = 0; q < NM; ++q) {
-                        v[q][0] = __fadd_rn(v[q][0], __ldcg(pp + q * 64 + lane));
-                        v[q][1] = __fadd_rn(v[q][1], __ldcg(pp + q * 64 + 32 + lane));
-                    }
-                }
-            }
+        if (a.kc == 1 && piece_whole && wi == nh - 1) {
+            finish_tile(T, v);
+            continue;
         }
-        // ---- epilogue: scale, activation, store, argmax keys ----
-        if (t < B) {
-            const float c1 = __ldcg(a.cf + 2 * t), c2 = __ldcg(a.cf + 2 * t + 1);
+        const int sidx = a.kc == 1 ? (T == tfirst ? 0 : 1) : T - tfirst;
+        float *p = a.partial + (((size_t)slice * K + kseg) * a.slots + sidx) * (NM * 64);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int row = T * kTileRows + gq + 8 * h;
-                if (row < a.rows) {
-                    float val = __fmul_rn(__fmul_rn(v[0][h], c1), c2);
-                    if constexpr (EPI == 1) val = __fmul_rn(silu_f32(val), __fmul_rn(__fmul_rn(v[NM - 1][h], c1), c2));
-                    a.y[(size_t)t * a.ystride + row] = val;
-                    if constexpr (EPI == 2) {
-                        const unsigned long long key = ((unsigned long long)total_order_key(val) << 32) |
-                                                       (unsigned long long)(0xffffffffu - (uint32_t)(a.row_base + row));
-                        best = key > best ? key : best;
-                    }
-                }
-            }
+        for (int q = 0; q < NM; ++q) {
+            p[q * 64 + lane] = v[q][0];
+            p[q * 64 + 32 + lane] = v[q][1];
         }
+#pragma unroll
+        for (int i = 0; i < kMaxPending; ++i)
+            if (i == npend) pend[i] = T;
+        ++npend;
     }
     // Drain copies issued but not consumed (only after a failed wait).
     for (long long d = u; d < issued; ++d) {
@@ -556,7 +577,49 @@ __global__ void __launch_bounds__(32 * kMmaWarps, 1)
             break;
         }
     }
-    (void)best;
+
+    // Publish the split pieces (one fence for all of them); the last piece of
+    // a tile to arrive adds every piece in (slice, segment) order.
+    if (ok && npend > 0) {
+        __threadfence();
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < kMaxPending; ++i) {
+            if (i >= npend) break;
+            const int Tp = pend[i];
+            unsigned int last = 0;
+            if (lane == 0) {
+                int cidx, np;
+                tile_pieces(a, Tp, K, &cidx, &np);
+                last = atomicAdd(a.counters + cidx, 1u) == (unsigned int)(np - 1) ? 1u : 0u;
+                if (last) a.counters[cidx] = 0u;  // ready for the next launch
+            }
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (!last) continue;
+            __threadfence();
+            float v[NM][2];
+#pragma unroll
+            for (int q = 0; q < NM; ++q) v[q][0] = v[q][1] = 0.0f;
+            for (int h = 0; h < a.kc; ++h) {
+                const long long w0 = (long long)h * a.nwin / a.kc, w1 = (long long)(h + 1) * a.nwin / a.kc;
+                const long long nhh = w1 - w0, Uh = (long long)a.tiles * nhh;
+                const long long uf = (long long)Tp * nhh, ul = uf + nhh - 1;
+                const long long kf = ((uf + 1) * K - 1) / Uh, kl = ((ul + 1) * K - 1) / Uh;
+                for (long long k = kf; k <= kl; ++k) {
+                    if (Uh * (k + 1) / K == Uh * k / K) continue;  // empty segment
+                    const int tf = (int)((Uh * k / K) / nhh);
+                    const int si = a.kc == 1 ? (Tp == tf ? 0 : 1) : Tp - tf;
+                    const float *pp = a.partial + (((size_t)h * K + k) * a.slots + si) * (NM * 64);
+#pragma unroll
+                    for (int q = 0; q < NM; ++q) {
+                        v[q][0] = __fadd_rn(v[q][0], __ldcg(pp + q * 64 + lane));
+                        v[q][1] = __fadd_rn(v[q][1], __ldcg(pp + q * 64 + 32 + lane));
+                    }
+                }
+            }
+            finish_tile(Tp, v);
+        }
+    }
 
     if constexpr (EPI == 2) {
         // Maximum per RHS over the lanes that share it, one atomic per RHS and
@@ -579,6 +642,7 @@ __global__ void __launch_bounds__(32 * kMmaWarps, 1)
         }
         if (flag && threadIdx.x == 0) *a.done = 0u;
     }
+    (void)best;
 }
 
 }  // namespace qmr

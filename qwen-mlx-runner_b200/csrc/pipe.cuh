@@ -95,6 +95,21 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
+// 2-D tensor copy to a 32-bit shared address.
+__device__ __forceinline__ void tma_load_2d_s(uint32_t dst, const CUtensorMap *map, int x, int y, uint64_t *bar,
+                                              uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+
+// 16-byte cp.async to a 32-bit shared address (see cp_async16).
+__device__ __forceinline__ void cp_async16_s(uint32_t dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+
 // 16-byte cp.async (L1 bypass) that reads `src_bytes` (0..16) bytes and
 // zero-fills the rest; with src_bytes == 0 nothing is read.
 __device__ __forceinline__ void cp_async16(void *dst, const void *src, uint32_t src_bytes) {
