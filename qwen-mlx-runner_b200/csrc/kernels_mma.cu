@@ -68,8 +68,7 @@ int launch_w(const CUtensorMap &m1, const CUtensorMap &m2, const MmaArgs &a, con
 template <int G, int B, bool BF16, int EPI>
 int launch_t(const CUtensorMap &m1, const CUtensorMap &m2, const MmaArgs &a, const MmaPlan &p, bool overlap,
              cudaStream_t stream) {
-    // 16 warps for Q4 single-matrix calls, 8 otherwise (the plan's rule).
-    constexpr int NW = (kBits == 4 && EPI != 1) ? 16 : 8;
+    constexpr int NW = kMmaWarps;
     if (p.warps != NW) return fail(QMR_EUNSUPPORTED, "no tensor-core kernel with %d warps", p.warps);
     return launch_w<G, B, BF16, EPI, NW>(m1, m2, a, p, overlap, stream);
 }

@@ -185,9 +185,7 @@ bool mma_plan_b(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uin
     const int nwin = (int)((cols + win_cols - 1) / win_cols);
     const int tiles = (int)((rows + kTileRows - 1) / kTileRows);
     const int nm = epi == 1 ? 2 : 1;
-    // Q4 single-matrix units are light on shared memory: 16 warps hide more
-    // latency; the heavier slots of Q8 and gate/up pairs fit 8.
-    const int warps = (bits == 4 && nm == 1) ? 16 : 8;
+    const int warps = kMmaWarps;
     const int sms = sm_count();
     int kc = 0;
     for (int c : {1, 2, 4}) {

@@ -60,6 +60,7 @@
 
 namespace qmr {
 
+constexpr int kMmaWarps = 8;     // warps per CTA, each with its own copy ring
 constexpr int kTileRows = 16;    // rows of one MMA tile
 constexpr int kMaxPending = 4;   // split pieces one warp may publish
 constexpr int kMmaMaxStages = 6;
@@ -483,13 +484,45 @@ __global__ void __launch_bounds__(32 * NW, 1)
             sl = 0;
             phase ^= 1u;
         }
-        if (!__all_sync(0xffffffffu, mbar_wait(&full[cur], cur_phase))) {  // warp-uniform outcome
+        if (!__all_sync(0xffffffffu, mbar_wait_sleep(&full[cur], cur_phase))) {  // warp-uniform outcome
             ok = false;
             if (lane == 0) atomicCAS(a.err, 0u, kErrTimeoutFull);
             break;
         }
         const uint32_t wslot = ring_w + (uint32_t)(cur * SLOT_W);
         const uint32_t mw = ring_m + (uint32_t)(cur * SLOT_M) + m_lane;
+        // Stage the unit's weight words and metadata in registers, then hand
+        // the slot straight back to the copy engine: every slot but the one
+        // being read stays in flight, which is what keeps HBM busy.
+        uint32_t wr[NM][S::WG][2][S::WPL];
+        uint32_t mr[NM][S::WG / 2][4][BF16 ? 1 : 2];
+#pragma unroll
+        for (int q = 0; q < NM; ++q) {
+#pragma unroll
+            for (int gi = 0; gi < S::WG; ++gi) {
+                const uint32_t aa = wslot + (uint32_t)(q * S::W_BYTES + (gi / GPB) * 2048) + a_off[gi % GPB];
+                lds_words<S::WPL>(wr[q][gi][0], aa);
+                lds_words<S::WPL>(wr[q][gi][1], aa + 1024u);
+            }
+#pragma unroll
+            for (int pr = 0; pr < S::WG / 2; ++pr) {
+                const uint32_t mq = mw + (uint32_t)(q * META_BYTES + 2 * pr * MSZ);
+                const uint32_t offs[4] = {0u, (uint32_t)META_LANE, (uint32_t)(16 * META_LANE), (uint32_t)(17 * META_LANE)};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    if constexpr (BF16) {
+                        mr[q][pr][k][0] = lds32(mq + offs[k]);
+                    } else {
+                        const uint2 v = lds64(mq + offs[k]);
+                        mr[q][pr][k][0] = v.x;
+                        mr[q][pr][k][BF16 ? 0 : 1] = v.y;
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (issued < ub) issue_next();  // refills the slot just staged
+
         const uint32_t xw = x_lane + (uint32_t)(wi * S::WG * XG);
         const uint32_t tw = t_lane + (uint32_t)((win0 + wi) * S::WG * 4);
 #pragma unroll
@@ -509,19 +542,11 @@ __global__ void __launch_bounds__(32 * NW, 1)
             const float xs[2] = {__uint_as_float(xsv.x), __uint_as_float(xsv.y)};
 #pragma unroll
             for (int q = 0; q < NM; ++q) {
-                const uint32_t mq = mw + (uint32_t)(q * META_BYTES + gl * MSZ);
-                const float2 sA = meta_pair<BF16>(mq);
-                const float2 bA = meta_pair<BF16>(mq + META_LANE);
-                const float2 sB = meta_pair<BF16>(mq + 16 * META_LANE);
-                const float2 bB = meta_pair<BF16>(mq + 17 * META_LANE);
                 float d[2][4];
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
-                    const int gi = gl + e;
-                    const uint32_t aa = wslot + (uint32_t)(q * S::W_BYTES + (gi / GPB) * 2048) + a_off[gi % GPB];
-                    uint32_t wa[S::WPL], wb[S::WPL];
-                    lds_words<S::WPL>(wa, aa);
-                    lds_words<S::WPL>(wb, aa + 1024u);
+                    const uint32_t *wa = wr[q][gl + e][0];
+                    const uint32_t *wb = wr[q][gl + e][1];
                     mma_16816_z(d[e], a_reg<BITS>(wa, 0), a_reg<BITS>(wb, 0), a_reg<BITS>(wa, 1), a_reg<BITS>(wb, 1),
                                 xb[e][0], xb[e][1]);
 #pragma unroll
@@ -531,19 +556,25 @@ __global__ void __launch_bounds__(32 * NW, 1)
                 }
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
-                    const float s_a = e ? sA.y : sA.x, b_a = e ? bA.y : bA.x;
-                    const float s_b = e ? sB.y : sB.x, b_b = e ? bB.y : bB.x;
-                    acc[q][0][0] = __fmaf_rn(s_a, d[e][0], acc[q][0][0]);
-                    acc[q][0][1] = __fmaf_rn(s_a, d[e][1], acc[q][0][1]);
-                    acc[q][0][0] = __fmaf_rn(b_a, xs[e], acc[q][0][0]);
-                    acc[q][1][0] = __fmaf_rn(s_b, d[e][2], acc[q][1][0]);
-                    acc[q][1][1] = __fmaf_rn(s_b, d[e][3], acc[q][1][1]);
-                    acc[q][1][0] = __fmaf_rn(b_b, xs[e], acc[q][1][0]);
+                    float m4[4];  // scale A, bias A, scale B, bias B of group gl + e
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        if constexpr (BF16) {
+                            const uint32_t v = mr[q][gl / 2][k][0];
+                            m4[k] = __uint_as_float(e ? (v & 0xffff0000u) : (v << 16));
+                        } else {
+                            m4[k] = __uint_as_float(mr[q][gl / 2][k][e]);
+                        }
+                    }
+                    acc[q][0][0] = __fmaf_rn(m4[0], d[e][0], acc[q][0][0]);
+                    acc[q][0][1] = __fmaf_rn(m4[0], d[e][1], acc[q][0][1]);
+                    acc[q][0][0] = __fmaf_rn(m4[1], xs[e], acc[q][0][0]);
+                    acc[q][1][0] = __fmaf_rn(m4[2], d[e][2], acc[q][1][0]);
+                    acc[q][1][1] = __fmaf_rn(m4[2], d[e][3], acc[q][1][1]);
+                    acc[q][1][0] = __fmaf_rn(m4[3], xs[e], acc[q][1][0]);
                 }
             }
         }
-        __syncwarp();
-        if (issued < ub) issue_next();  // refills the slot just read
 
         if (wi != nh - 1 && u + 1 != ub) continue;
         // ---- a tile piece ends here ----

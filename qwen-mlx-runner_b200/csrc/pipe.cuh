@@ -52,6 +52,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait that lets the thread sleep up to `hint_ns` for the phase instead
+// of returning at once, so waiting warps leave the issue slots to others.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// mbar_wait with sleeping polls (same bound).
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long start = global_ns();
+    for (;;) {
+        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+        if (global_ns() - start > kWaitLimitNs) return false;
+    }
+}
+
 // Wait for the phase with the given parity, bounded by kWaitLimitNs of
 // wall-clock time; false on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {

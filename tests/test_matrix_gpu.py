@@ -335,14 +335,15 @@ def test_gateup_swiglu_matches_oracle_and_separate_projections(cuda):
         a = act.cpu().numpy().reshape(batch, rows)
         gh = gy.cpu().numpy().astype(np.float64)
         uh = uy.cpu().numpy().astype(np.float64)
-        # Same gate/up sums as the plain kernel: act = silu(g)*u up to the f32 silu rounding.
         ref = (gh / (1.0 + np.exp(-gh)) * uh).reshape(batch, rows)
-        np.testing.assert_allclose(a, ref, rtol=2e-6, atol=1e-30)
-        for r in sampled_rows(rows, 48):
-            want, mag = oracle.swiglu_f64(g["weight"][r:r + 1], g["scales"][r:r + 1], g["biases"][r:r + 1],
-                                          u["weight"][r:r + 1], u["scales"][r:r + 1], u["biases"][r:r + 1], x, 1,
-                                          cols, 4, 64, batch)
-            assert_ns_bound(a[:, r], want[:, 0], mag[:, 0] + np.abs(want[:, 0]) * 1e-1, f"swiglu row {r}")
+        # Every row against FP64: first-order error scale |u|*1.1*sum|g_j| + |silu(g)|*sum|u_j| at the
+        # per-product bound, plus the f32 silu/product rounding (a few ulps of the result).
+        want, mag = oracle.swiglu_f64(g["weight"], g["scales"], g["biases"], u["weight"], u["scales"], u["biases"],
+                                      x, rows, cols, 4, 64, batch)
+        assert_ns_bound(a, want, mag + np.abs(want) * 0.05, f"swiglu B{batch}")
+        # The fused pair against the two plain projections (whose split of the columns may differ):
+        # both sides carry the bound once.
+        assert_ns_bound(a, ref, 2 * mag + np.abs(ref) * 0.1, f"swiglu vs separate B{batch}")
 
 
 def test_head_argmax_matches_logits_and_oracle(cuda):
