@@ -57,9 +57,18 @@ int launch_w(const CUtensorMap &m1, const CUtensorMap &m2, const MmaArgs &a, con
     cfg.blockDim = dim3(32 * NW, 1, 1);
     cfg.dynamicSmemBytes = p.smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1] = {pdl_attr()};
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (p.kc > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = (unsigned)p.kc;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    if (overlap) attr[na++] = pdl_attr();
     cfg.attrs = attr;
-    cfg.numAttrs = overlap ? 1 : 0;
+    cfg.numAttrs = na;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, m1, m2, a);
     if (e != cudaSuccess) return fail(QMR_ECUDA, "tensor-core kernel launch failed: %s", cudaGetErrorString(e));
     return QMR_OK;
@@ -135,8 +144,6 @@ int QMR_MMA_LAUNCH(const FastCall &c, const MmaPlan &p, const ScratchView &sv, c
     a.table = v.table;
     a.cf = v.cf;
     a.y = c.y;
-    a.partial = sv.partial;
-    a.counters = sv.counters;
     a.keys = sv.keys;
     a.done = sv.done;
     a.argmax = c.argmax;
@@ -151,11 +158,13 @@ int QMR_MMA_LAUNCH(const FastCall &c, const MmaPlan &p, const ScratchView &sv, c
     a.tiles = p.tiles;
     a.nwin = p.nwin;
     a.kc = p.kc;
-    a.cps = p.cps;
-    a.slots = p.slots;
+    a.clusters = p.clusters;
+    a.pieces = p.pieces;
     a.stages = p.stages;
     a.off_image = p.off_image;
     a.off_table = p.off_table;
+    a.off_pieces = p.off_pieces;
+    a.off_part = p.off_part;
     a.off_bars = p.off_bars;
     switch (c.epilogue) {
         case 0: return launch_e<0>(m1, m2, a, p, c.bf16, c.group, c.batch, c.overlap, stream);

@@ -33,16 +33,16 @@ unsigned int *device_error_word();
 
 // Launch shape of the tensor-core kernel for one call (matrix.cu).
 struct MmaPlan {
-    int kc;           // column slices
-    int cps;          // CTAs per slice
+    int kc;           // column slices = CTAs per cluster
+    int clusters;
     int ctas;
     int stages;       // ring slots per warp
-    int slots;        // partial-sum slots per warp segment
+    int pieces;       // shared-memory piece slots per warp
     int nwin;         // 512/1024-column windows of the matrix
     int ngroups_pad;  // groups of the padded activation image
     int tiles;        // 16-row tiles
-    int warps;        // warps per CTA (8 or 16)
-    uint32_t smem, off_image, off_table, off_bars;
+    int warps;        // warps per CTA
+    uint32_t smem, off_image, off_table, off_pieces, off_part, off_bars;
 };
 bool mma_plan(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint32_t batch, int epi, bool bf16,
               MmaPlan *p);

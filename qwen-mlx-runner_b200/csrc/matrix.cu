@@ -75,7 +75,6 @@ void scratch_layout(void *base, int bits, uint32_t cols, uint32_t batch, Scratch
     if (mv != nullptr) {
         mv->keys = v->keys;
         mv->done = v->done;
-        mv->counters = v->counters;
     }
 }
 
@@ -187,45 +186,60 @@ bool mma_plan_b(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uin
     const int nm = epi == 1 ? 2 : 1;
     const int warps = kMmaWarps;
     const int sms = sm_count();
+    // Column slices (= cluster size): the first kc whose activation slice fits
+    // the budget and whose clusters get within 4% of an even share of tiles;
+    // otherwise the fitting kc with the best balance.
     int kc = 0;
+    double best_imb = 1e30;
     for (int c : {1, 2, 4}) {
         const size_t nh_max = ((size_t)nwin + c - 1) / c;
-        if (nwin >= c && sms >= c && nh_max * win_cols * 16 <= kMmaImageBudget) {
+        if (nwin < c || sms < c || nh_max * win_cols * 16 > kMmaImageBudget) continue;
+        const int nc = sms / c;
+        const double share = (double)tiles / nc;
+        const double imb = (double)((tiles + nc - 1) / nc) / (share > 1.0 ? share : 1.0);
+        if (imb <= 1.04) {
             kc = c;
             break;
         }
+        if (imb < best_imb) {
+            best_imb = imb;
+            kc = c;
+        }
     }
     if (kc == 0) return false;
-    const int ctas = sms / kc * kc;
-    const int cps = ctas / kc;
-    const long long K = (long long)cps * warps;
+    const int clusters = sms / kc;
+    const int ctas = clusters * kc;
     const int nh_min = nwin / kc, nh_max = (nwin + kc - 1) / kc;
-    int slots = 2;
+    const int tmax = (tiles + clusters - 1) / clusters;
+    if ((long long)tmax * nh_max * warps >= (1ll << 31)) return false;  // 32-bit unit arithmetic
+    int pieces = 2;
     if (kc > 1) {
-        const long long lmax = ((long long)tiles * nh_max + K - 1) / K;
-        slots = (int)(lmax / nh_min) + 2;
-        if (tiles > kCounterCount || slots > kMaxPending) return false;
-    } else if (K > kCounterCount) {
-        return false;
+        const int lmax = (tmax * nh_max + warps - 1) / warps;
+        pieces = (lmax + nh_min - 1) / nh_min + 1;
+        if (pieces > kMaxPieces) return false;
     }
-    if ((size_t)ctas * warps * slots * nm * 64 > kPartialFloats) return false;
+    const uint32_t piece_bytes = (uint32_t)nm * 64 * 4;
     const uint32_t slot = (uint32_t)(mma_slot_weight_bytes((int)bits, (int)group, nm) +
                                      mma_slot_meta_bytes((int)group, nm, bf16 ? 2 : 4));
     const uint32_t image = (uint32_t)nh_max * win_cols * 4 * batch;
     const uint32_t ngroups_pad = (uint32_t)nwin * wg;
     const uint32_t table = 16 * ngroups_pad;
+    const uint32_t pieces_bytes = (uint32_t)warps * pieces * piece_bytes;
+    const uint32_t part_bytes = kc > 1 ? (uint32_t)tmax * piece_bytes : 0u;
     const int limit = smem_optin() - 128;  // room for the kernel's static shared variables (16 bytes)
     for (int st = kMmaMaxStages; st >= 2; --st) {
         const uint32_t off_image = (uint32_t)warps * st * slot;
         const uint32_t off_table = off_image + (image + 127) / 128 * 128;
-        const uint32_t off_bars = off_table + (table + 127) / 128 * 128;
+        const uint32_t off_pieces = off_table + (table + 127) / 128 * 128;
+        const uint32_t off_part = off_pieces + pieces_bytes;
+        const uint32_t off_bars = off_part + part_bytes;
         const uint32_t total = 1024 + off_bars + (uint32_t)(warps * st + 1) * 8;
         if ((int)total <= limit) {
             p->kc = kc;
-            p->cps = cps;
+            p->clusters = clusters;
             p->ctas = ctas;
             p->stages = st;
-            p->slots = slots;
+            p->pieces = pieces;
             p->nwin = nwin;
             p->ngroups_pad = (int)ngroups_pad;
             p->tiles = tiles;
@@ -233,6 +247,8 @@ bool mma_plan_b(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uin
             p->smem = total;
             p->off_image = off_image;
             p->off_table = off_table;
+            p->off_pieces = off_pieces;
+            p->off_part = off_part;
             p->off_bars = off_bars;
             return true;
         }

@@ -26,16 +26,18 @@
 //    xsum' = (sum of x over the group) * 2^(E_b-24); the output is
 //    (acc.hi + acc.lo) * 2^(24-E_b) (two exact power-of-two factors).
 //
-// Work split (stream-K over (16-row tile, 512-column window) units): with
-// kc column slices, the CTAs are split into kc equal sets and set h owns the
-// windows of slice h for every tile.  A set's units, tile-major, are divided
-// into equal contiguous segments, one per warp.  A warp accumulates each
-// tile piece of its segment in registers; a piece that covers a whole tile
-// (possible only with kc = 1) is written directly, other pieces publish
-// their sums to a partial buffer and the last piece of a tile to arrive
-// (fence + counter, no waiting) adds all pieces in (slice, segment) order.
-// The split depends only on the matrix shape and the SM count, never on B,
-// so a block of B RHS equals B single-RHS calls bit for bit.
+// Work split: the CTAs form clusters of kc CTAs (kc = 1, 2 or 4 column
+// slices).  Cluster i owns the 16-row tiles [i*T/C, (i+1)*T/C) of the matrix
+// and its CTA of rank h owns the 512/1024-column windows of slice h.  A CTA's
+// (tile, window) units, tile-major, are divided into equal contiguous segments,
+// one per warp.  A warp accumulates each tile piece of its segment in
+// registers; a piece covering a whole tile (kc = 1) is written directly, the
+// others go to shared memory and are added in warp order after the loop; with
+// kc > 1 the CTAs' per-tile sums are then added in rank order through
+// distributed shared memory.  No partial sum leaves the chip and nothing
+// waits on another CTA outside the cluster barrier.  The split depends only
+// on the matrix shape and the SM count, never on B, so a block of B RHS equals
+// B single-RHS calls bit for bit.
 //
 // Data movement per warp: a private ring of `stages` slots; slot = one unit:
 // the tile's 16 rows x window bytes of packed weights as 2-D TMA boxes of
@@ -62,7 +64,7 @@ namespace qmr {
 
 constexpr int kMmaWarps = 8;     // warps per CTA, each with its own copy ring
 constexpr int kTileRows = 16;    // rows of one MMA tile
-constexpr int kMaxPending = 4;   // split pieces one warp may publish
+constexpr int kMaxPieces = 4;    // tile pieces one warp may leave in shared memory
 constexpr int kMmaMaxStages = 6;
 
 template <int BITS, int G>
@@ -120,7 +122,6 @@ struct MmaImageView {
     float *cf;
     unsigned long long *keys;  // argmax keys, cleared by the prep
     unsigned int *done;        // CTA counter, cleared by the prep
-    unsigned int *counters;    // split-tile counters, cleared by the prep
 };
 
 // One CTA per RHS: E_b from max|x|, then the group sums and the split halves.
@@ -135,9 +136,8 @@ __global__ void __launch_bounds__(512) mma_prep_kernel(const float *__restrict__
     const int ngroups = cols / G;
     const int NB = 2 * batch;
     if (b == 0) {
-        // Every call starts with clear argmax and arrival state, even after a
-        // launch that stopped early on a device error.
-        for (int i = tid; i < kCounterCount; i += blockDim.x) v.counters[i] = 0u;
+        // Every call starts with clear argmax state, even after a launch that
+        // stopped early on a device error.
         if (tid < 4) v.keys[tid] = 0ull;
         if (tid == 0) *v.done = 0u;
     }
@@ -273,39 +273,37 @@ __device__ __forceinline__ float2 meta_pair(uint32_t a) {
     }
 }
 
+// Distributed shared memory of the cluster: map a local shared address to
+// rank `rank`'s copy, load from it, and the full cluster barrier.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 struct MmaArgs {
     const unsigned char *s, *b, *s2, *b2;  // metadata [rows][ngroups] (f32 or bf16 bits)
     const __half *image;                   // prepared activation image
     const float *table;                    // group sums [4][ngroups_pad]
     const float *cf;                       // output factors [B][2]
     float *y;
-    float *partial;                        // [segments][slots][NM][64] piece sums
-    unsigned int *counters;                // arrivals per split tile
     unsigned long long *keys;              // [B] packed argmax (EPI 2)
     unsigned int *done;                    // CTAs finished (EPI 2)
     int *argmax;
     unsigned long long *best_key_out;
     unsigned int *err;                     // device error word
     int rows, ngroups, ngroups_pad, ystride, row_base;
-    int tiles, nwin, kc, cps, slots, stages;
-    uint32_t off_image, off_table, off_bars;  // offsets into the 1024-aligned dynamic shared memory
+    int tiles, nwin, kc, clusters, pieces, stages;
+    uint32_t off_image, off_table, off_pieces, off_part, off_bars;  // offsets into the 1024-aligned dynamic smem
 };
-
-// Pieces of tile T across the slices (non-empty segments only) and the
-// counter that tracks them.
-__device__ __forceinline__ void tile_pieces(const MmaArgs &a, int T, long long K, int *counter, int *npieces) {
-    int n = 0, c = 0;
-    for (int h = 0; h < a.kc; ++h) {
-        const long long w0 = (long long)h * a.nwin / a.kc, w1 = (long long)(h + 1) * a.nwin / a.kc;
-        const long long nh = w1 - w0, U = (long long)a.tiles * nh;
-        const long long uf = (long long)T * nh, ul = uf + nh - 1;
-        const long long kf = ((uf + 1) * K - 1) / U, kl = ((ul + 1) * K - 1) / U;
-        if (h == 0) c = (int)kf;
-        for (long long k = kf; k <= kl; ++k) n += (U * (k + 1) / K > U * k / K) ? 1 : 0;
-    }
-    *counter = a.kc == 1 ? c : T;
-    *npieces = n;
-}
 
 template <int BITS, int G, int B, bool BF16, int EPI, int NW>
 __global__ void __launch_bounds__(32 * NW, 1)
@@ -321,6 +319,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
     constexpr int GPB = 128 / S::GROUP_BYTES;  // groups per 128-byte line of a box
     constexpr int LANE_BYTES = S::WPL * 4;      // bytes of one row a lane reads per group
     constexpr int XG = S::NCH * NB * 64;        // activation image bytes per group
+    constexpr int PIECE = NM * 64 * 4;          // bytes of one tile piece (64 values per matrix)
     static_assert(LANE_BYTES <= 16 && GPB >= 1, "one 16-byte unit per lane and row");
     extern __shared__ unsigned char smem_raw[];
     __shared__ unsigned int flag;
@@ -330,6 +329,10 @@ __global__ void __launch_bounds__(32 * NW, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gq = lane >> 2, t = lane & 3;
+    if (threadIdx.x == 0) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
+        if (NM == 2) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap2)) : "memory");
+    }
     const int nst = a.stages;
     const uint32_t ring_w = sbase + (uint32_t)(warp * nst * SLOT_W);
     const uint32_t ring_m = sbase + (uint32_t)(NW * nst * SLOT_W + warp * nst * SLOT_M);
@@ -337,16 +340,16 @@ __global__ void __launch_bounds__(32 * NW, 1)
     uint64_t *full = bars + warp * nst;
     uint64_t *ibar = bars + NW * nst;
 
-    // Column slice of this CTA and this warp's segment of (tile, window) units.
-    const int slice = blockIdx.x / a.cps, cl = blockIdx.x % a.cps;
-    const int win0 = (int)((long long)slice * a.nwin / a.kc);
-    const int nh = (int)((long long)(slice + 1) * a.nwin / a.kc) - win0;
-    const long long U = (long long)a.tiles * nh;
-    const long long K = (long long)a.cps * NW;
-    const long long kseg = (long long)cl * NW + warp;
-    const long long ua = U * kseg / K, ub = U * (kseg + 1) / K;
-    const bool cta_work = U * ((long long)(cl + 1) * NW) / K > U * ((long long)cl * NW) / K;
-    const int tfirst = (int)(ua / (nh > 0 ? nh : 1));
+    // Cluster tiles, this CTA's column slice and this warp's segment of
+    // (tile, window) units.
+    const int rank = (int)(blockIdx.x % (unsigned)a.kc), ci = (int)(blockIdx.x / (unsigned)a.kc);
+    const int win0 = rank * a.nwin / a.kc;
+    const int nh = (rank + 1) * a.nwin / a.kc - win0;
+    const int t0 = ci * a.tiles / a.clusters;
+    const int ntl = (ci + 1) * a.tiles / a.clusters - t0;
+    const uint32_t U = (uint32_t)(ntl * nh);
+    const uint32_t ua = U * (uint32_t)warp / NW, ub = U * (uint32_t)(warp + 1) / NW;
+    const int tfirst = nh > 0 ? (int)(ua / (uint32_t)nh) : 0;
 
     if (lane == 0)
         for (int i = 0; i < nst; ++i) mbar_init(&full[i], 33);  // expect_tx arrival + 32 cp.async arrivals
@@ -357,46 +360,60 @@ __global__ void __launch_bounds__(32 * NW, 1)
     const uint64_t pol_stream = evict_first_policy();
     const uint64_t pol_keep = evict_normal_policy();
 
-    // Issue unit (tile T, window wi of the slice) into ring slot sl.
-    auto issue = [&](int T, int wi, int sl) {
-        const int wg = win0 + wi;
+    // Metadata source of this lane (row 2r + kind of a unit's 16 rows) for the
+    // CTA's first tile and the slice's first window.
+    const int mrow = lane >> 1, mkind = lane & 1;
+    const unsigned char *msrc[NM];
+#pragma unroll
+    for (int q = 0; q < NM; ++q) {
+        const unsigned char *base = mkind ? (q ? a.b2 : a.b) : (q ? a.s2 : a.s);
+        msrc[q] = base + ((size_t)(t0 * kTileRows + mrow) * a.ngroups + (size_t)win0 * S::WG) * MSZ;
+    }
+
+    // Issue unit (local tile tl, window wi of the slice) into ring slot sl.
+    auto issue = [&](int tl, int wi, int sl) {
+        const int T = t0 + tl;
         const uint32_t slot = ring_w + (uint32_t)(sl * SLOT_W);
         const uint32_t mslot = ring_m + (uint32_t)(sl * SLOT_M);
         uint64_t *bar = &full[sl];
         if (lane == 0) {
-            fence_proxy_async();
             mbar_arrive_expect_tx(bar, SLOT_W);
 #pragma unroll
             for (int q = 0; q < NM; ++q)
 #pragma unroll
                 for (int c = 0; c < S::NBOX; ++c)
-                    tma_load_2d_s(slot + q * S::W_BYTES + c * 2048, q ? &wmap2 : &wmap, wg * S::ROW_WORDS + c * 32,
-                                  T * kTileRows, bar, pol_stream);
+                    tma_load_2d_s(slot + q * S::W_BYTES + c * 2048, q ? &wmap2 : &wmap,
+                                  (win0 + wi) * S::ROW_WORDS + c * 32, T * kTileRows, bar, pol_stream);
         }
         __syncwarp();
-        // Metadata: lane = 2 * row + (0 scale | 1 bias), the window's groups.
-        const int r = lane >> 1, kind = lane & 1;
-        const int row = T * kTileRows + r;
-        const int gbeg = wg * S::WG;
-        int valid = row < a.rows ? (a.ngroups - gbeg) * MSZ : 0;
-        valid = valid < 0 ? 0 : (valid > META_LANE ? META_LANE : valid);
+        const int row = T * kTileRows + mrow;
+        const int gbeg = (win0 + wi) * S::WG;
+        const size_t moff = ((size_t)tl * kTileRows * a.ngroups + (size_t)wi * S::WG) * MSZ;
+        const bool inside = row < a.rows && gbeg + S::WG <= a.ngroups;
 #pragma unroll
         for (int q = 0; q < NM; ++q) {
-            const unsigned char *base = kind ? (q ? a.b2 : a.b) : (q ? a.s2 : a.s);
-            const unsigned char *src = base + ((size_t)(valid > 0 ? row : 0) * a.ngroups + (valid > 0 ? gbeg : 0)) * MSZ;
             const uint32_t dst = mslot + (uint32_t)(q * META_BYTES + lane * META_LANE);
+            if (inside) {
 #pragma unroll
-            for (int p = 0; p < META_LANE / 16; ++p) {
-                const int n = valid - 16 * p;
-                cp_async16_s(dst + 16 * p, n > 0 ? src + 16 * p : base, n <= 0 ? 0u : (n > 16 ? 16u : (uint32_t)n));
+                for (int p = 0; p < META_LANE / 16; ++p) cp_async16_s(dst + 16 * p, msrc[q] + moff + 16 * p, 16u);
+            } else {
+                // Rows past the matrix and groups past the row read nothing.
+                int valid = row < a.rows ? (a.ngroups - gbeg) * MSZ : 0;
+                valid = valid < 0 ? 0 : (valid > META_LANE ? META_LANE : valid);
+#pragma unroll
+                for (int p = 0; p < META_LANE / 16; ++p) {
+                    const int n = valid - 16 * p;
+                    const unsigned char *src = n > 0 ? msrc[q] + moff + 16 * p : (q ? a.s2 : a.s);
+                    cp_async16_s(dst + 16 * p, src, n <= 0 ? 0u : (n > 16 ? 16u : (uint32_t)n));
+                }
             }
         }
         cp_async_arrive(bar);
     };
 
-    // Issue cursor: unit `issued` = (tile it, window iw), ring slot is_.
-    long long issued = ua;
-    int it = nh > 0 ? (int)(ua / nh) : 0, iw = nh > 0 ? (int)(ua % nh) : 0, is_ = 0;
+    // Issue cursor: unit `issued` = (local tile it, window iw), ring slot is_.
+    uint32_t issued = ua;
+    int it = tfirst, iw = nh > 0 ? (int)(ua % (uint32_t)nh) : 0, is_ = 0;
     auto issue_next = [&]() {
         issue(it, iw, is_);
         ++issued;
@@ -409,7 +426,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
     bool ok = true;
-    if (cta_work) {
+    if (U > 0) {
         if (threadIdx.x == 0) {
             const uint32_t img_bytes = (uint32_t)nh * S::WG * XG;
             const uint32_t tab_bytes = 4u * (uint32_t)a.ngroups_pad * 4u;
@@ -421,7 +438,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
             }
             bulk_g2s(smem + a.off_table, a.table, tab_bytes, ibar, pol_keep);
         }
-        if (ua < ub && !__all_sync(0xffffffffu, mbar_wait(ibar, 0))) {
+        if (ua < ub && !__all_sync(0xffffffffu, mbar_wait_sleep(ibar, 0))) {
             ok = false;
             if (lane == 0) atomicCAS(a.err, 0u, kErrTimeoutFull);
         }
@@ -441,6 +458,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
     const uint32_t x_lane = sbase + a.off_image + (uint32_t)((n * 4 + t) * 16);
     const uint32_t t_lane = sbase + a.off_table + (uint32_t)(t * a.ngroups_pad * 4);
     const uint32_t m_lane = (uint32_t)(2 * gq * META_LANE);
+    const uint32_t piece_base = sbase + a.off_pieces + (uint32_t)(warp * a.pieces * PIECE);
 
     unsigned long long best = 0ull;
     // The epilogue of one finished tile: scale, activation, store, argmax key.
@@ -467,12 +485,10 @@ __global__ void __launch_bounds__(32 * NW, 1)
 
     float acc[NM][2][2];  // [matrix][row A|B][part hi|lo]
     bool piece_whole = false;  // the current piece started at window 0 of its tile
-    int pend[kMaxPending];     // split pieces written, published after the segment
-    int npend = 0;
-    long long u = ua;
-    int T = tfirst, wi = nh > 0 ? (int)(ua % nh) : 0, sl = 0;
+    uint32_t u = ua;
+    int tl = tfirst, wi = nh > 0 ? (int)(ua % (uint32_t)nh) : 0, sl = 0;
     uint32_t phase = 0;
-    for (; ok && u < ub; ++u, wi = (wi + 1 == nh) ? 0 : wi + 1, T += (wi == 0) ? 1 : 0) {
+    while (ok && u < ub) {
         if (u == ua || wi == 0) {
 #pragma unroll
             for (int q = 0; q < NM; ++q) acc[q][0][0] = acc[q][0][1] = acc[q][1][0] = acc[q][1][1] = 0.0f;
@@ -576,80 +592,94 @@ __global__ void __launch_bounds__(32 * NW, 1)
             }
         }
 
-        if (wi != nh - 1 && u + 1 != ub) continue;
-        // ---- a tile piece ends here ----
-        float v[NM][2];
+        const bool piece_end = wi == nh - 1 || u + 1 == ub;
+        if (piece_end) {
+            float v[NM][2];
 #pragma unroll
-        for (int q = 0; q < NM; ++q) {
-            v[q][0] = __fadd_rn(acc[q][0][0], acc[q][0][1]);
-            v[q][1] = __fadd_rn(acc[q][1][0], acc[q][1][1]);
-        }
-        if (a.kc == 1 && piece_whole && wi == nh - 1) {
-            finish_tile(T, v);
-            continue;
-        }
-        const int sidx = a.kc == 1 ? (T == tfirst ? 0 : 1) : T - tfirst;
-        float *p = a.partial + (((size_t)slice * K + kseg) * a.slots + sidx) * (NM * 64);
+            for (int q = 0; q < NM; ++q) {
+                v[q][0] = __fadd_rn(acc[q][0][0], acc[q][0][1]);
+                v[q][1] = __fadd_rn(acc[q][1][0], acc[q][1][1]);
+            }
+            if (a.kc == 1 && piece_whole && wi == nh - 1) {
+                finish_tile(t0 + tl, v);
+            } else {
+                // kc = 1: only a segment's first and last pieces can be split.
+                const int slot_i = a.kc == 1 ? (tl == tfirst ? 0 : 1) : tl - tfirst;
+                const uint32_t pb = piece_base + (uint32_t)(slot_i * PIECE);
 #pragma unroll
-        for (int q = 0; q < NM; ++q) {
-            p[q * 64 + lane] = v[q][0];
-            p[q * 64 + 32 + lane] = v[q][1];
+                for (int q = 0; q < NM; ++q) {
+                    asm volatile("st.shared.f32 [%0], %1;" ::"r"(pb + (uint32_t)(q * 256 + lane * 4)), "f"(v[q][0]) : "memory");
+                    asm volatile("st.shared.f32 [%0], %1;" ::"r"(pb + (uint32_t)(q * 256 + 128 + lane * 4)), "f"(v[q][1])
+                                 : "memory");
+                }
+            }
         }
-#pragma unroll
-        for (int i = 0; i < kMaxPending; ++i)
-            if (i == npend) pend[i] = T;
-        ++npend;
+        ++u;
+        if (++wi == nh) wi = 0, ++tl;
     }
     // Drain copies issued but not consumed (only after a failed wait).
-    for (long long d = u; d < issued; ++d) {
-        const long long j = d - ua;
-        if (!mbar_wait(&full[(int)(j % nst)], (uint32_t)((j / nst) & 1))) {
+    for (uint32_t d = u; d < issued; ++d) {
+        const uint32_t j = d - ua;
+        if (!mbar_wait(&full[(int)(j % (uint32_t)nst)], (j / (uint32_t)nst) & 1u)) {
             if (lane == 0) atomicCAS(a.err, 0u, kErrTimeoutDrain);
             break;
         }
     }
 
-    // Publish the split pieces (one fence for all of them); the last piece of
-    // a tile to arrive adds every piece in (slice, segment) order.
-    if (ok && npend > 0) {
-        __threadfence();
-        __syncwarp();
+    // Tiles split between warps: add the pieces in warp order.  With column
+    // slices the CTA's sum of a tile goes to its part buffer for the cluster.
+    __syncthreads();
+    for (int T = warp; T < ntl; T += NW) {
+        const uint32_t uf = (uint32_t)(T * nh), ul = uf + (uint32_t)nh - 1u;
+        const int wf = (int)(((uf + 1u) * NW - 1u) / U), wl = (int)(((ul + 1u) * NW - 1u) / U);
+        if (a.kc == 1 && wf == wl) continue;  // one warp held the whole tile and wrote it
+        float v[NM][2];
 #pragma unroll
-        for (int i = 0; i < kMaxPending; ++i) {
-            if (i >= npend) break;
-            const int Tp = pend[i];
-            unsigned int last = 0;
-            if (lane == 0) {
-                int cidx, np;
-                tile_pieces(a, Tp, K, &cidx, &np);
-                last = atomicAdd(a.counters + cidx, 1u) == (unsigned int)(np - 1) ? 1u : 0u;
-                if (last) a.counters[cidx] = 0u;  // ready for the next launch
+        for (int q = 0; q < NM; ++q) v[q][0] = v[q][1] = 0.0f;
+        for (int w = wf; w <= wl; ++w) {
+            const uint32_t wa = U * (uint32_t)w / NW, wb = U * (uint32_t)(w + 1) / NW;
+            if (wb == wa) continue;  // empty segment
+            const int tf = (int)(wa / (uint32_t)nh);
+            const int slot_i = a.kc == 1 ? (T == tf ? 0 : 1) : T - tf;
+            const uint32_t pb = sbase + a.off_pieces + (uint32_t)((w * a.pieces + slot_i) * PIECE);
+#pragma unroll
+            for (int q = 0; q < NM; ++q) {
+                v[q][0] = __fadd_rn(v[q][0], __uint_as_float(lds32(pb + (uint32_t)(q * 256 + lane * 4))));
+                v[q][1] = __fadd_rn(v[q][1], __uint_as_float(lds32(pb + (uint32_t)(q * 256 + 128 + lane * 4))));
             }
-            last = __shfl_sync(0xffffffffu, last, 0);
-            if (!last) continue;
-            __threadfence();
+        }
+        if (a.kc == 1) {
+            finish_tile(t0 + T, v);
+        } else {
+            const uint32_t pp = sbase + a.off_part + (uint32_t)(T * PIECE);
+#pragma unroll
+            for (int q = 0; q < NM; ++q) {
+                asm volatile("st.shared.f32 [%0], %1;" ::"r"(pp + (uint32_t)(q * 256 + lane * 4)), "f"(v[q][0]) : "memory");
+                asm volatile("st.shared.f32 [%0], %1;" ::"r"(pp + (uint32_t)(q * 256 + 128 + lane * 4)), "f"(v[q][1])
+                             : "memory");
+            }
+        }
+    }
+    if (a.kc > 1) {
+        // Every CTA of the cluster has its per-tile sums; rank r finalises the
+        // tiles T with T % kc == r, adding the ranks' sums in rank order.
+        cluster_sync();
+        for (int T = rank + warp * a.kc; T < ntl; T += NW * a.kc) {
             float v[NM][2];
 #pragma unroll
             for (int q = 0; q < NM; ++q) v[q][0] = v[q][1] = 0.0f;
-            for (int h = 0; h < a.kc; ++h) {
-                const long long w0 = (long long)h * a.nwin / a.kc, w1 = (long long)(h + 1) * a.nwin / a.kc;
-                const long long nhh = w1 - w0, Uh = (long long)a.tiles * nhh;
-                const long long uf = (long long)Tp * nhh, ul = uf + nhh - 1;
-                const long long kf = ((uf + 1) * K - 1) / Uh, kl = ((ul + 1) * K - 1) / Uh;
-                for (long long k = kf; k <= kl; ++k) {
-                    if (Uh * (k + 1) / K == Uh * k / K) continue;  // empty segment
-                    const int tf = (int)((Uh * k / K) / nhh);
-                    const int si = a.kc == 1 ? (Tp == tf ? 0 : 1) : Tp - tf;
-                    const float *pp = a.partial + (((size_t)h * K + k) * a.slots + si) * (NM * 64);
+            const uint32_t pp = sbase + a.off_part + (uint32_t)(T * PIECE);
+            for (int r = 0; r < a.kc; ++r) {
 #pragma unroll
-                    for (int q = 0; q < NM; ++q) {
-                        v[q][0] = __fadd_rn(v[q][0], __ldcg(pp + q * 64 + lane));
-                        v[q][1] = __fadd_rn(v[q][1], __ldcg(pp + q * 64 + 32 + lane));
-                    }
+                for (int q = 0; q < NM; ++q) {
+                    v[q][0] = __fadd_rn(v[q][0], ld_cluster_f32(cluster_map(pp + (uint32_t)(q * 256 + lane * 4), (uint32_t)r)));
+                    v[q][1] = __fadd_rn(v[q][1],
+                                        ld_cluster_f32(cluster_map(pp + (uint32_t)(q * 256 + 128 + lane * 4), (uint32_t)r)));
                 }
             }
-            finish_tile(Tp, v);
+            finish_tile(t0 + T, v);
         }
+        cluster_sync();  // no CTA leaves while others read its shared memory
     }
 
     if constexpr (EPI == 2) {
