@@ -20,8 +20,14 @@ constexpr int kBits = QMR_MMA_BITS;
 template <int G>
 int launch_prep_g(const float *x, uint32_t cols, uint32_t batch, int ngroups_pad, const MmaImageView &v,
                   cudaStream_t stream) {
-    mma_prep_kernel<kBits, G><<<batch, 512, 0, stream>>>(x, (int)cols, (int)batch, ngroups_pad, v);
-    const cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(batch, 1, 1);
+    cfg.blockDim = dim3(512, 1, 1);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1] = {pdl_attr()};
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, mma_prep_kernel<kBits, G>, x, (int)cols, (int)batch, ngroups_pad, v);
     if (e != cudaSuccess) return fail(QMR_ECUDA, "activation prep launch failed: %s", cudaGetErrorString(e));
     return QMR_OK;
 }

@@ -186,24 +186,14 @@ bool mma_plan_b(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uin
     const int nm = epi == 1 ? 2 : 1;
     const int warps = kMmaWarps;
     const int sms = sm_count();
-    // Column slices (= cluster size): the first kc whose activation slice fits
-    // the budget and whose clusters get within 4% of an even share of tiles;
-    // otherwise the fitting kc with the best balance.
+    // Column slices (= cluster size): the smallest kc whose activation slice
+    // fits the budget.
     int kc = 0;
-    double best_imb = 1e30;
     for (int c : {1, 2, 4}) {
         const size_t nh_max = ((size_t)nwin + c - 1) / c;
-        if (nwin < c || sms < c || nh_max * win_cols * 16 > kMmaImageBudget) continue;
-        const int nc = sms / c;
-        const double share = (double)tiles / nc;
-        const double imb = (double)((tiles + nc - 1) / nc) / (share > 1.0 ? share : 1.0);
-        if (imb <= 1.04) {
+        if (nwin >= c && sms >= c && nh_max * win_cols * 16 <= kMmaImageBudget) {
             kc = c;
             break;
-        }
-        if (imb < best_imb) {
-            best_imb = imb;
-            kc = c;
         }
     }
     if (kc == 0) return false;
@@ -225,7 +215,8 @@ bool mma_plan_b(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uin
     const uint32_t ngroups_pad = (uint32_t)nwin * wg;
     const uint32_t table = 16 * ngroups_pad;
     const uint32_t pieces_bytes = (uint32_t)warps * pieces * piece_bytes;
-    const uint32_t part_bytes = kc > 1 ? (uint32_t)tmax * piece_bytes : 0u;
+    const uint32_t part_bytes = kc > 1 ? (uint32_t)((tmax + kc - 1) / kc * kc) * piece_bytes : 0u;
+    if (nh_max > 32) return false;  // image-window barriers and the per-warp ready mask
     const int limit = smem_optin() - 128;  // room for the kernel's static shared variables (16 bytes)
     for (int st = kMmaMaxStages; st >= 2; --st) {
         const uint32_t off_image = (uint32_t)warps * st * slot;
@@ -233,7 +224,7 @@ bool mma_plan_b(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uin
         const uint32_t off_pieces = off_table + (table + 127) / 128 * 128;
         const uint32_t off_part = off_pieces + pieces_bytes;
         const uint32_t off_bars = off_part + part_bytes;
-        const uint32_t total = 1024 + off_bars + (uint32_t)(warps * st + 1) * 8;
+        const uint32_t total = 1024 + off_bars + (uint32_t)(warps * st + nh_max) * 8;
         if ((int)total <= limit) {
             p->kc = kc;
             p->clusters = clusters;

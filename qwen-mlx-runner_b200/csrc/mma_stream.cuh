@@ -128,7 +128,11 @@ struct MmaImageView {
 template <int BITS, int G>
 __global__ void __launch_bounds__(512) mma_prep_kernel(const float *__restrict__ x, int cols, int batch,
                                                       int ngroups_pad, MmaImageView v) {
+    // Launched behind the previous kernel (programmatic dependent launch): let
+    // the streaming kernel launch now, then wait for x and for the previous
+    // user of this scratch before touching either.
     asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     using S = MmaShape<BITS, G>;
     const int b = blockIdx.x;
     const float *xb = x + (size_t)b * cols;
@@ -274,7 +278,7 @@ __device__ __forceinline__ float2 meta_pair(uint32_t a) {
 }
 
 // Distributed shared memory of the cluster: map a local shared address to
-// rank `rank`'s copy, load from it, and the full cluster barrier.
+// rank `rank`'s copy, load from or store to it, and the full cluster barrier.
 __device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
     uint32_t r;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
@@ -284,6 +288,9 @@ __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
     float v;
     asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
     return v;
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -338,7 +345,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
     const uint32_t ring_m = sbase + (uint32_t)(NW * nst * SLOT_W + warp * nst * SLOT_M);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + a.off_bars);
     uint64_t *full = bars + warp * nst;
-    uint64_t *ibar = bars + NW * nst;
+    uint64_t *ibar = bars + NW * nst;  // one per window of the slice
 
     // Cluster tiles, this CTA's column slice and this warp's segment of
     // (tile, window) units.
@@ -353,7 +360,8 @@ __global__ void __launch_bounds__(32 * NW, 1)
 
     if (lane == 0)
         for (int i = 0; i < nst; ++i) mbar_init(&full[i], 33);  // expect_tx arrival + 32 cp.async arrivals
-    if (threadIdx.x == 0) mbar_init(ibar, 1);
+    if (threadIdx.x == 0)
+        for (int i = 0; i < nh; ++i) mbar_init(&ibar[i], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     __syncthreads();
 
@@ -425,24 +433,20 @@ __global__ void __launch_bounds__(32 * NW, 1)
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
+    // The activation image arrives window by window (the group-sum table with
+    // the first), so each warp starts as soon as its first window is in.
     bool ok = true;
-    if (U > 0) {
-        if (threadIdx.x == 0) {
-            const uint32_t img_bytes = (uint32_t)nh * S::WG * XG;
-            const uint32_t tab_bytes = 4u * (uint32_t)a.ngroups_pad * 4u;
-            mbar_arrive_expect_tx(ibar, img_bytes + tab_bytes);
-            const unsigned char *src = reinterpret_cast<const unsigned char *>(a.image) + (size_t)win0 * S::WG * XG;
-            for (uint32_t o = 0; o < img_bytes; o += 32768u) {
-                const uint32_t n = img_bytes - o < 32768u ? img_bytes - o : 32768u;
-                bulk_g2s(smem + a.off_image + o, src + o, n, ibar, pol_keep);
-            }
-            bulk_g2s(smem + a.off_table, a.table, tab_bytes, ibar, pol_keep);
-        }
-        if (ua < ub && !__all_sync(0xffffffffu, mbar_wait_sleep(ibar, 0))) {
-            ok = false;
-            if (lane == 0) atomicCAS(a.err, 0u, kErrTimeoutFull);
+    if (U > 0 && threadIdx.x == 0) {
+        const uint32_t chunk = (uint32_t)S::WG * XG;
+        const uint32_t tab_bytes = 4u * (uint32_t)a.ngroups_pad * 4u;
+        const unsigned char *src = reinterpret_cast<const unsigned char *>(a.image) + (size_t)win0 * chunk;
+        for (int i = 0; i < nh; ++i) {
+            mbar_arrive_expect_tx(&ibar[i], chunk + (i == 0 ? tab_bytes : 0u));
+            if (i == 0) bulk_g2s(smem + a.off_table, a.table, tab_bytes, &ibar[0], pol_keep);
+            bulk_g2s(smem + a.off_image + (size_t)i * chunk, src + (size_t)i * chunk, chunk, &ibar[i], pol_keep);
         }
     }
+    uint32_t img_ready = 0;  // windows of the image this warp has waited for (bit 0 also covers the table)
 
     // Per-lane byte offsets: A words of row gq for the GPB groups of a box
     // line (128-byte swizzle: 16-byte unit u of row r at u ^ (r & 7)), the
@@ -539,6 +543,15 @@ __global__ void __launch_bounds__(32 * NW, 1)
         __syncwarp();
         if (issued < ub) issue_next();  // refills the slot just staged
 
+        if (!((img_ready >> wi) & 1u) || !(img_ready & 1u)) {
+            const bool got = __all_sync(0xffffffffu, mbar_wait_sleep(&ibar[0], 0) && mbar_wait_sleep(&ibar[wi], 0));
+            if (!got) {
+                ok = false;
+                if (lane == 0) atomicCAS(a.err, 0u, kErrTimeoutFull);
+                break;
+            }
+            img_ready |= 1u | (1u << wi);
+        }
         const uint32_t xw = x_lane + (uint32_t)(wi * S::WG * XG);
         const uint32_t tw = t_lane + (uint32_t)((win0 + wi) * S::WG * 4);
 #pragma unroll
@@ -626,6 +639,15 @@ __global__ void __launch_bounds__(32 * NW, 1)
         }
     }
 
+    // Every image copy has landed before the CTA can exit (normally already
+    // waited for by the warps that read the window).
+    if (U > 0 && threadIdx.x == 0)
+        for (int i = 0; i < nh; ++i)
+            if (!mbar_wait(&ibar[i], 0)) {
+                atomicCAS(a.err, 0u, kErrTimeoutDrain);
+                break;
+            }
+
     // Tiles split between warps: add the pieces in warp order.  With column
     // slices the CTA's sum of a tile goes to its part buffer for the cluster.
     __syncthreads();
@@ -651,35 +673,35 @@ __global__ void __launch_bounds__(32 * NW, 1)
         if (a.kc == 1) {
             finish_tile(t0 + T, v);
         } else {
-            const uint32_t pp = sbase + a.off_part + (uint32_t)(T * PIECE);
+            // Tile T belongs to rank T % kc: store this slice's sum into the
+            // owner's part buffer, row T / kc, column = this rank.
+            const uint32_t pp = sbase + a.off_part + (uint32_t)(((T / a.kc) * a.kc + rank) * PIECE);
+            const uint32_t owner = (uint32_t)(T % a.kc);
 #pragma unroll
             for (int q = 0; q < NM; ++q) {
-                asm volatile("st.shared.f32 [%0], %1;" ::"r"(pp + (uint32_t)(q * 256 + lane * 4)), "f"(v[q][0]) : "memory");
-                asm volatile("st.shared.f32 [%0], %1;" ::"r"(pp + (uint32_t)(q * 256 + 128 + lane * 4)), "f"(v[q][1])
-                             : "memory");
+                st_cluster_f32(cluster_map(pp + (uint32_t)(q * 256 + lane * 4), owner), v[q][0]);
+                st_cluster_f32(cluster_map(pp + (uint32_t)(q * 256 + 128 + lane * 4), owner), v[q][1]);
             }
         }
     }
     if (a.kc > 1) {
-        // Every CTA of the cluster has its per-tile sums; rank r finalises the
-        // tiles T with T % kc == r, adding the ranks' sums in rank order.
+        // One cluster barrier publishes the remote stores; each rank then adds
+        // the slices of its own tiles in rank order from local shared memory.
         cluster_sync();
         for (int T = rank + warp * a.kc; T < ntl; T += NW * a.kc) {
             float v[NM][2];
 #pragma unroll
             for (int q = 0; q < NM; ++q) v[q][0] = v[q][1] = 0.0f;
-            const uint32_t pp = sbase + a.off_part + (uint32_t)(T * PIECE);
             for (int r = 0; r < a.kc; ++r) {
+                const uint32_t pp = sbase + a.off_part + (uint32_t)(((T / a.kc) * a.kc + r) * PIECE);
 #pragma unroll
                 for (int q = 0; q < NM; ++q) {
-                    v[q][0] = __fadd_rn(v[q][0], ld_cluster_f32(cluster_map(pp + (uint32_t)(q * 256 + lane * 4), (uint32_t)r)));
-                    v[q][1] = __fadd_rn(v[q][1],
-                                        ld_cluster_f32(cluster_map(pp + (uint32_t)(q * 256 + 128 + lane * 4), (uint32_t)r)));
+                    v[q][0] = __fadd_rn(v[q][0], __uint_as_float(lds32(pp + (uint32_t)(q * 256 + lane * 4))));
+                    v[q][1] = __fadd_rn(v[q][1], __uint_as_float(lds32(pp + (uint32_t)(q * 256 + 128 + lane * 4))));
                 }
             }
             finish_tile(t0 + T, v);
         }
-        cluster_sync();  // no CTA leaves while others read its shared memory
     }
 
     if constexpr (EPI == 2) {
