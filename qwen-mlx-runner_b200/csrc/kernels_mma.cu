@@ -172,6 +172,7 @@ int QMR_MMA_LAUNCH(const FastCall &c, const MmaPlan &p, const ScratchView &sv, c
     a.off_pieces = p.off_pieces;
     a.off_part = p.off_part;
     a.off_bars = p.off_bars;
+    a.zero = 0u;
     switch (c.epilogue) {
         case 0: return launch_e<0>(m1, m2, a, p, c.bf16, c.group, c.batch, c.overlap, stream);
         case 1: return launch_e<1>(m1, m2, a, p, c.bf16, c.group, c.batch, c.overlap, stream);

@@ -42,9 +42,10 @@
 // Data movement per warp: a private ring of `stages` slots; slot = one unit:
 // the tile's 16 rows x window bytes of packed weights as 2-D TMA boxes of
 // 16 rows x 128 bytes with the 128-byte swizzle (conflict-free 8-row reads),
-// plus the tile's scales and biases for the window's groups by 16-byte
-// cp.async (zero-filled out of range), all completing on the slot's
-// mbarrier.  The CTA's activation image (its slice of the prepared image
+// completing on the slot's mbarrier, plus the tile's scales and biases for
+// the window's groups by 16-byte cp.async (zero-filled out of range) in one
+// commit group per unit, waited for with cp.async.wait_group and a warp
+// barrier.  The CTA's activation image (its slice of the prepared image
 // plus the table of group sums) arrives once by bulk copy.  Weight loads are
 // issued before `griddepcontrol.wait`, so they overlap the producer of the
 // activations under programmatic dependent launch.  Every wait is bounded by
@@ -309,6 +310,7 @@ struct MmaArgs {
     unsigned int *err;                     // device error word
     int rows, ngroups, ngroups_pad, ystride, row_base;
     int tiles, nwin, kc, clusters, pieces, stages;
+    uint32_t zero;                         // always 0 (an opaque operand, see the slot refill)
     uint32_t off_image, off_table, off_pieces, off_part, off_bars;  // offsets into the 1024-aligned dynamic smem
 };
 
@@ -359,7 +361,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
     const int tfirst = nh > 0 ? (int)(ua / (uint32_t)nh) : 0;
 
     if (lane == 0)
-        for (int i = 0; i < nst; ++i) mbar_init(&full[i], 33);  // expect_tx arrival + 32 cp.async arrivals
+        for (int i = 0; i < nst; ++i) mbar_init(&full[i], 1);  // the expect_tx arrival; TMA bytes complete it
     if (threadIdx.x == 0)
         for (int i = 0; i < nh; ++i) mbar_init(&ibar[i], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -416,7 +418,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
                 }
             }
         }
-        cp_async_arrive(bar);
+        cp_async_commit();  // one cp.async group per unit
     };
 
     // Issue cursor: unit `issued` = (local tile it, window iw), ring slot is_.
@@ -509,6 +511,11 @@ __global__ void __launch_bounds__(32 * NW, 1)
             if (lane == 0) atomicCAS(a.err, 0u, kErrTimeoutFull);
             break;
         }
+        // This unit's metadata group is complete once at most the groups of
+        // the units issued after it are pending; the warp barrier makes every
+        // lane's copies visible to the warp.
+        cp_async_wait_pending(issued - u - 1u);
+        __syncwarp();
         const uint32_t wslot = ring_w + (uint32_t)(cur * SLOT_W);
         const uint32_t mw = ring_m + (uint32_t)(cur * SLOT_M) + m_lane;
         // Stage the unit's weight words and metadata in registers, then hand
@@ -540,7 +547,21 @@ __global__ void __launch_bounds__(32 * NW, 1)
                 }
             }
         }
-        __syncwarp();
+        // The slot is refilled next, by TMA and cp.async.  Every staged load
+        // must have returned first: fold one word of each load into a value
+        // the warp barrier's mask depends on (a.zero is 0, but opaque to the
+        // compiler), so each lane passes the barrier only with all its loads
+        // complete.
+        uint32_t dep = 0;
+#pragma unroll
+        for (int q = 0; q < NM; ++q) {
+#pragma unroll
+            for (int gi = 0; gi < S::WG; ++gi) dep ^= wr[q][gi][0][0] ^ wr[q][gi][1][0];
+#pragma unroll
+            for (int pr = 0; pr < S::WG / 2; ++pr)
+                dep ^= mr[q][pr][0][0] ^ mr[q][pr][1][0] ^ mr[q][pr][2][0] ^ mr[q][pr][3][0];
+        }
+        __syncwarp(0xffffffffu | (dep & a.zero));
         if (issued < ub) issue_next();  // refills the slot just staged
 
         if (!((img_ready >> wi) & 1u) || !(img_ready & 1u)) {
@@ -630,6 +651,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
         ++u;
         if (++wi == nh) wi = 0, ++tl;
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");  // no metadata copy outlives the CTA
     // Drain copies issued but not consumed (only after a failed wait).
     for (uint32_t d = u; d < issued; ++d) {
         const uint32_t j = d - ua;

@@ -477,6 +477,31 @@ def test_typed_wrappers_reject_undersized_views_before_launch(cuda):
         qmr.embed_affine(m, rows, y)
 
 
+@pytest.mark.parametrize("meta", ["f32", "bf16"])
+def test_fresh_matrices_keep_blocks_equal_to_gemv(cuda, meta):
+    """Freshly uploaded matrices (cold L2, metadata arriving late) still give a
+    B4 block equal to the single-RHS call and within the oracle bound: every
+    metadata copy is complete and visible before any lane reads it."""
+    rows, cols = 17408, 5120
+    for it in range(6):
+        mat = synth.affine_matrix(rows, cols, 4, 64, seed=900 + it, meta=meta)
+        m = synth.to_device(mat, rows, cols, 4, 64)
+        x_np = synth.activations(4, cols, seed=950 + it)
+        x = f32_tensor(x_np.ravel())
+        y4 = torch.full((4 * rows,), float("nan"), dtype=torch.float32, device="cuda")
+        qmr.matmul_affine(m, x, y4, 4)
+        y1 = torch.full((rows,), float("nan"), dtype=torch.float32, device="cuda")
+        qmr.matvec_affine(m, x[2 * cols:3 * cols], y1)
+        torch.cuda.synchronize()
+        got = y4.cpu().numpy().reshape(4, rows)
+        assert np.array_equal(got[2].view(np.uint32), y1.cpu().numpy().view(np.uint32)), f"iteration {it}"
+        for r in sampled_rows(rows, 16):
+            want, mag = oracle.matmul_f64(mat["weight"], mat["scales"], mat["biases"], x_np, rows, cols, 4, 64,
+                                          batch=4, row0=r, nrows=1)
+            assert_ns_bound(got[:, r], want[:, 0], mag[:, 0], f"fresh {meta} it {it} row {r}")
+        del m
+
+
 @pytest.mark.parametrize("bits,meta", [(4, "bf16"), (4, "f32"), (8, "bf16")])
 def test_all_streaming_paths_meet_the_bound(cuda, bits, meta):
     """The tensor-core kernel, the FP32 TMA tile kernel (split-K, partial
