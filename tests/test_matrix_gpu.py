@@ -498,7 +498,7 @@ def test_fresh_matrices_keep_blocks_equal_to_gemv(cuda, meta):
         for r in sampled_rows(rows, 16):
             want, mag = oracle.matmul_f64(mat["weight"], mat["scales"], mat["biases"], x_np, rows, cols, 4, 64,
                                           batch=4, row0=r, nrows=1)
-            assert_ns_bound(got[:, r], want[:, 0], mag[:, 0], f"fresh {meta} it {it} row {r}")
+            assert_ns_bound(got[:, r], want[:, r], mag[:, r], f"fresh {meta} it {it} row {r}")
         del m
 
 
