@@ -149,6 +149,21 @@ int qmr_embed_affine(const void *w, const void *scales, const void *biases, uint
                      float *y, uint32_t cols, uint32_t bits, uint32_t group, int meta_bf16,
                      void *stream);
 
+/* qmr_matmul_affine that allocates no device memory (no reference
+ * counterpart: the reference's Metal encoder never allocates per call).
+ * For callers that must not allocate once running, e.g. an engine that
+ * reserves its HBM budget at start-up (cudaMalloc would also synchronise the
+ * device mid-step) or a binding that cannot own a scratch buffer.  Uses one
+ * fixed 3 MiB device array per device: cols up to 32768 at batch <= 4,
+ * larger shapes fail with QMR_ERANGE before any launch.  The array is shared
+ * by all streams and threads, so calls that overlap in time race and must be
+ * serialised by the caller.  The first call on each device does the set-up
+ * (symbol lookup with the device current, clearing the array, which
+ * synchronises the device) and should come before any stream capture. */
+int qmr_matmul_affine_static(const void *w, const void *scales, const void *biases, const float *x,
+                             float *y, uint32_t rows, uint32_t cols, uint32_t bits, uint32_t group,
+                             uint32_t batch, int meta_bf16, void *stream);
+
 /* The gate/up projections plus swiglu of one MLP (src/engine.rs:755-763,
  * kernels/qwen.metal:91-94) in one pass: act[b*rows+r] =
  * silu(gate_b[r]) * up_b[r].  Both matrices share shape and format; x is

@@ -758,6 +758,21 @@ int qmr_matmul_affine(const void *w, const void *scales, const void *biases, con
                          static_cast<cudaStream_t>(stream));
 }
 
+int qmr_matmul_affine_static(const void *w, const void *scales, const void *biases, const float *x, float *y,
+                             uint32_t rows, uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch,
+                             int meta_bf16, void *stream) {
+    const uint32_t p[5] = {rows, cols, bits, group, batch};
+    int rc = validate_typed(meta_bf16 ? "matmul_affine_bf16" : "matmul_affine", p, 5);
+    if (rc != QMR_OK) return rc;
+    const Modes m = modes();
+    if (m.reference) return fail(QMR_EUNSUPPORTED, "Block matrix dispatch is unavailable in reference mode");
+    const char *sel = specialized_matmul(meta_bf16 ? "matmul_affine_bf16" : "matmul_affine", p,
+                                         m.gemv == QMR_GEMV_ALIGNED, m.block);
+    const bool r2 = sel != nullptr && strcmp(sel, "matmul_q4_g64_b3_mlp_r2_aligned_bf16") == 0;
+    return matmul_static(w, scales, biases, x, y, rows, cols, bits, group, batch, meta_bf16 != 0, r2, m.stream_path,
+                         static_cast<cudaStream_t>(stream));
+}
+
 int qmr_embed_affine(const void *w, const void *scales, const void *biases, uint32_t row, float *y, uint32_t cols,
                      uint32_t bits, uint32_t group, int meta_bf16, void *stream) {
     const uint32_t p[4] = {row, cols, bits, group};

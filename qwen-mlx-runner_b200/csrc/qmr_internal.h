@@ -52,5 +52,9 @@ int run_generic(const void *w, const void *s, const void *b, const float *x, flo
 int run_embed(const void *w, const void *s, const void *b, uint32_t row, float *y, uint32_t cols, uint32_t bits,
               uint32_t group, bool bf16, cudaStream_t stream);
 int device_error(int *code, bool clear);
+// qmr_matmul_affine on the fixed per-device static scratch (static_scratch.cu).
+int matmul_static(const void *w, const void *s, const void *b, const float *x, float *y, uint32_t rows,
+                  uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch, bool bf16, bool r2, int path,
+                  cudaStream_t stream);
 
 }  // namespace qmr

@@ -73,6 +73,7 @@ SIGNATURES = {
                           ctypes.POINTER(_u32), _sz, _u64, _u64, _vp]),
     "qmr_matvec_affine": (_int, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _int, _vp]),
     "qmr_matmul_affine": (_int, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _int, _vp]),
+    "qmr_matmul_affine_static": (_int, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _int, _vp]),
     "qmr_embed_affine": (_int, [_vp, _vp, _vp, _u32, _vp, _u32, _u32, _u32, _int, _vp]),
     "qmr_gateup_swiglu": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32,
                                  _u32, _int, _vp]),

@@ -26,9 +26,10 @@ UNITS = [
     ("kernels_tile.cu", [], "kernels_tile.o"),
     ("kernels_mma.cu", ["-DQMR_MMA_BITS=4"], "kernels_mma4.o"),
     ("kernels_mma.cu", ["-DQMR_MMA_BITS=8"], "kernels_mma8.o"),
+    ("static_scratch.cu", [], "static_scratch.o"),
 ]
 SOURCES = sorted({u[0] for u in UNITS})
-HEADERS = ["matrix_kernels.cuh", "qmr_internal.h", "tile.cuh", "mma_stream.cuh", "launch.h"]
+HEADERS = ["matrix_kernels.cuh", "qmr_internal.h", "tile.cuh", "mma_stream.cuh", "launch.h", "pipe.cuh"]
 OBJ_DIR = PKG_ROOT / "_build"
 
 NVCC_FLAGS = [

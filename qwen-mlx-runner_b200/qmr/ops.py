@@ -84,6 +84,15 @@ def matmul_affine(m: PackedMatrix, x, y, batch: int, stream=None) -> None:
                                        int(m.meta_bf16), _stream(stream)))
 
 
+def matmul_affine_static(m: PackedMatrix, x, y, batch: int, stream=None) -> None:
+    """matmul_affine on the library's fixed per-device scratch: allocates no
+    device memory (cols <= 32768); calls must not overlap in time."""
+    w, sc, bi = _mat(m)
+    check(_lib.lib().qmr_matmul_affine_static(w, sc, bi, _ptr(x, 4 * batch * m.cols, "x"),
+                                              _ptr(y, 4 * batch * m.rows, "y"), m.rows, m.cols, m.bits, m.group,
+                                              batch, int(m.meta_bf16), _stream(stream)))
+
+
 def embed_affine(m: PackedMatrix, row: int, y, stream=None) -> None:
     w, sc, bi = _mat(m)
     if not 0 <= row < m.rows:
