@@ -130,7 +130,7 @@ int launch_e(const CUtensorMap &m1, const CUtensorMap &m2, const MmaArgs &a, con
 #define QMR_MMA_PREP launch_mma_prep8
 #endif
 
-int QMR_MMA_LAUNCH(const FastCall &c, const MmaPlan &p, const ScratchView &sv, const MmaImageView &v,
+int QMR_MMA_LAUNCH(const FastCall &c, const MmaPlan &p, const ScratchView &sv, const MmaImageView &v, bool fuse,
                    cudaStream_t stream) {
     const uint64_t row_words = (uint64_t)c.cols * kBits / 32;
     CUtensorMap m1, m2;
@@ -148,7 +148,6 @@ int QMR_MMA_LAUNCH(const FastCall &c, const MmaPlan &p, const ScratchView &sv, c
     a.b2 = static_cast<const unsigned char *>(c.epilogue == 1 ? c.b2 : c.b);
     a.image = v.image;
     a.table = v.table;
-    a.cf = v.cf;
     a.y = c.y;
     a.keys = sv.keys;
     a.done = sv.done;
@@ -173,6 +172,9 @@ int QMR_MMA_LAUNCH(const FastCall &c, const MmaPlan &p, const ScratchView &sv, c
     a.off_part = p.off_part;
     a.off_bars = p.off_bars;
     a.zero = 0u;
+    a.x = c.x;
+    a.cols = (int)c.cols;
+    a.fuse = fuse ? 1 : 0;
     switch (c.epilogue) {
         case 0: return launch_e<0>(m1, m2, a, p, c.bf16, c.group, c.batch, c.overlap, stream);
         case 1: return launch_e<1>(m1, m2, a, p, c.bf16, c.group, c.batch, c.overlap, stream);

@@ -50,9 +50,10 @@ bool mma_plan(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint3
 // kernels_mma.cu (one translation unit per bit width)
 int launch_mma_prep_bits(int bits, const float *x, uint32_t cols, uint32_t group, uint32_t batch, int ngroups_pad,
                          const MmaImageView &v, cudaStream_t stream);
-int launch_mma4(const FastCall &c, const MmaPlan &p, const ScratchView &sv, const MmaImageView &v,
+// fuse: the kernel builds its activation image from c.x itself (no prep).
+int launch_mma4(const FastCall &c, const MmaPlan &p, const ScratchView &sv, const MmaImageView &v, bool fuse,
                 cudaStream_t stream);
-int launch_mma8(const FastCall &c, const MmaPlan &p, const ScratchView &sv, const MmaImageView &v,
+int launch_mma8(const FastCall &c, const MmaPlan &p, const ScratchView &sv, const MmaImageView &v, bool fuse,
                 cudaStream_t stream);
 int launch_mma_prep4(const float *x, uint32_t cols, uint32_t group, uint32_t batch, int ngroups_pad,
                      const MmaImageView &v, cudaStream_t stream);

@@ -40,11 +40,12 @@ size_t prepared_floats(int bits, uint32_t cols, uint32_t batch) {
     return batch * nblocks * bf;
 }
 
-// Bytes of the tensor-core activation image and its group-sum table, sized
-// for the widest window (1024 columns) and the smallest group (32).
+// Bytes of the tensor-core activation image and its table (two floats per
+// group and RHS), sized for the widest window (1024 columns) and the
+// smallest group (32).
 size_t mma_prepared_bytes(uint32_t cols, uint32_t batch) {
     const size_t padded = ((size_t)cols + 1023) / 1024 * 1024;
-    return align_up(padded * 4 * batch) + align_up(padded / 2);
+    return align_up(padded * 4 * batch) + align_up(padded);
 }
 
 // The activation region holds either path's layout.
@@ -54,17 +55,19 @@ size_t prepared_region(int bits, uint32_t cols, uint32_t batch) {
     return a > b ? a : b;
 }
 
+// Fixed part of every scratch buffer, at the same offsets whatever the shape
+// of the call: the output factors, the argmax keys and CTA counter (which
+// must read zero between calls), the split-tile counters and partial sums.
+// The shape-dependent prepared activations follow it.
+size_t fixed_region() {
+    return align_up(8 * sizeof(float)) + align_up(4 * sizeof(unsigned long long) + sizeof(unsigned int)) +
+           align_up(kCounterCount * sizeof(unsigned int)) + align_up(kPartialFloats * sizeof(float));
+}
+
 void scratch_layout(void *base, int bits, uint32_t cols, uint32_t batch, ScratchView *v, MmaImageView *mv = nullptr) {
+    (void)bits;
     char *p = static_cast<char *>(base);
-    v->xp = reinterpret_cast<float *>(p);
-    if (mv != nullptr) {
-        const size_t padded = ((size_t)cols + 1023) / 1024 * 1024;
-        mv->image = reinterpret_cast<__half *>(p);
-        mv->table = reinterpret_cast<float *>(p + align_up(padded * 4 * batch));
-    }
-    p += prepared_region(bits, cols, batch);
     v->cf = reinterpret_cast<float *>(p);
-    if (mv != nullptr) mv->cf = v->cf;
     p += align_up(8 * sizeof(float));
     v->keys = reinterpret_cast<unsigned long long *>(p);
     v->done = reinterpret_cast<unsigned int *>(p + 4 * sizeof(unsigned long long));
@@ -72,7 +75,12 @@ void scratch_layout(void *base, int bits, uint32_t cols, uint32_t batch, Scratch
     v->counters = reinterpret_cast<unsigned int *>(p);
     p += align_up(kCounterCount * sizeof(unsigned int));
     v->partial = reinterpret_cast<float *>(p);
+    p += align_up(kPartialFloats * sizeof(float));
+    v->xp = reinterpret_cast<float *>(p);
     if (mv != nullptr) {
+        const size_t padded = ((size_t)cols + 1023) / 1024 * 1024;
+        mv->image = reinterpret_cast<__half *>(p);
+        mv->table = reinterpret_cast<float *>(p + align_up(padded * 4 * batch));
         mv->keys = v->keys;
         mv->done = v->done;
     }
@@ -96,9 +104,7 @@ bool aligned16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0;
 }  // namespace
 
 size_t scratch_bytes(int bits, uint32_t cols, uint32_t batch) {
-    return prepared_region(bits, cols, batch) + align_up(8 * sizeof(float)) +
-           align_up(4 * sizeof(unsigned long long) + sizeof(unsigned int)) +
-           align_up(kCounterCount * sizeof(unsigned int)) + align_up(kPartialFloats * sizeof(float));
+    return fixed_region() + prepared_region(bits, cols, batch);
 }
 
 // Per (device, stream) scratch.  The first call on a stream reserves enough
@@ -213,11 +219,11 @@ bool mma_plan_b(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uin
                                      mma_slot_meta_bytes((int)group, nm, bf16 ? 2 : 4));
     const uint32_t image = (uint32_t)nh_max * win_cols * 4 * batch;
     const uint32_t ngroups_pad = (uint32_t)nwin * wg;
-    const uint32_t table = 16 * ngroups_pad;
+    const uint32_t table = 32 * ngroups_pad;
     const uint32_t pieces_bytes = (uint32_t)warps * pieces * piece_bytes;
     const uint32_t part_bytes = kc > 1 ? (uint32_t)((tmax + kc - 1) / kc * kc) * piece_bytes : 0u;
     if (nh_max > 32) return false;  // image-window barriers and the per-warp ready mask
-    const int limit = smem_optin() - 128;  // room for the kernel's static shared variables (16 bytes)
+    const int limit = smem_optin() - 512;  // room for the kernel's static shared variables (under 300 bytes)
     for (int st = kMmaMaxStages; st >= 2; --st) {
         const uint32_t off_image = (uint32_t)warps * st * slot;
         const uint32_t off_table = off_image + (image + 127) / 128 * 128;
@@ -323,7 +329,7 @@ int run_stream(const FastCall &c, void *base, cudaStream_t stream) {
             return fail(QMR_EUNSUPPORTED,
                         "activations prepared for the tensor-core kernel, which does not take this matrix "
                         "(unaligned weights or metadata, or no launch plan)");
-        return c.bits == 4 ? launch_mma4(c, p, sv, mv, stream) : launch_mma8(c, p, sv, mv, stream);
+        return c.bits == 4 ? launch_mma4(c, p, sv, mv, false, stream) : launch_mma8(c, p, sv, mv, false, stream);
     }
     if (c.path != kPathRegisters && tile_eligible(c)) return launch_tile_call(c, sv, stream);
     StreamArgs a = {};
@@ -360,6 +366,17 @@ int run_fast(const FastCall &c, cudaStream_t stream) {
     FastCall call = c;
     MmaPlan plan;
     if (call.path == kPathMma && !mma_takes(call, &plan)) call.path = kPathTile;  // FP32 kernels take the rest
+    if (call.path == kPathMma) {
+        // One launch: the streaming kernel prepares its own activation image.
+        // Programmatic dependent launch lets it start loading weights while
+        // the previous kernel finishes; it waits for that kernel before x.
+        ScratchView sv;
+        MmaImageView mv;
+        scratch_layout(base, (int)call.bits, call.cols, call.batch, &sv, &mv);
+        call.overlap = true;
+        return call.bits == 4 ? launch_mma4(call, plan, sv, mv, true, stream)
+                              : launch_mma8(call, plan, sv, mv, true, stream);
+    }
     const int rc = run_prepare(call.x, call.cols, call.bits, call.group, call.batch, base, call.path, stream);
     if (rc != QMR_OK) return rc;
     call.overlap = true;  // the preceding kernel is our prep, which writes no weights

@@ -16,15 +16,15 @@
 //    bits 8..15 come from `w >> 8` the same way.  The k order inside an MMA
 //    is a fixed permutation of the group's columns (block_perm); the
 //    activation image is stored in that order.
-//  * B (activations): x[b] * 2^E_b (E_b puts max|x[b]| just below the fp16
-//    maximum) split into an fp16 high part and an fp16 low part; the MMA
-//    columns are n = 2b + part, so each thread's accumulator pair holds both
-//    parts of one RHS for two rows.
+//  * B (activations): x * 2^E_g, with one exponent per group and RHS that
+//    puts the group's largest |x| just below the fp16 maximum, split into an
+//    fp16 high part and an fp16 low part; the MMA columns are n = 2b + part,
+//    so each thread's accumulator pair holds both parts of one RHS for two
+//    rows.
 //  * Per quantisation group the group's MMAs start from zero; the f32 result
-//    P = (q*x summed over the group) * 2^(E_b-24) is folded as
-//    acc += s*P (both parts, FFMA2) and acc.hi += bias*xsum' with
-//    xsum' = (sum of x over the group) * 2^(E_b-24); the output is
-//    (acc.hi + acc.lo) * 2^(24-E_b) (two exact power-of-two factors).
+//    P = (q*x summed over the group) * 2^(E_g-24) is folded as
+//    acc += (s * 2^(24-E_g)) * P (both parts) and acc.hi += bias * sum(x);
+//    the output is acc.hi + acc.lo.
 //
 // Work split: the CTAs form clusters of kc CTAs (kc = 1, 2 or 4 column
 // slices).  Cluster i owns the 16-row tiles [i*T/C, (i+1)*T/C) of the matrix
@@ -114,18 +114,153 @@ __host__ __device__ constexpr int block_perm(int reg, int h) {
 // The prepared activation image, shared by the prep kernel (writer) and the
 // streaming kernel (reader, copied into shared memory verbatim):
 //   image [ngroups_pad][NCH][NB = 2B][4 lanes][8 halves]  (block_perm order;
-//          Q4 odd registers pre-scaled by 2^-4; padding groups are zero)
-//   table [4][ngroups_pad] f32   (sum of x over the group) * 2^(E_b - 24)
-//   cf    [B][2] f32             2^a, 2^(24 - E_b - a)
+//          x * 2^E_g with the group's own exponent; Q4 odd registers scaled
+//          by a further 2^-4; padding groups are zero)
+//   table [4][ngroups_pad][2] f32  2^(24 - E_g), sum of x over the group
 struct MmaImageView {
     __half *image;
     float *table;
-    float *cf;
     unsigned long long *keys;  // argmax keys, cleared by the prep
     unsigned int *done;        // CTA counter, cleared by the prep
 };
 
-// One CTA per RHS: E_b from max|x|, then the group sums and the split halves.
+// ---- activation image arithmetic (shared by the prep kernel and the
+// streaming kernel's own prep, so both produce the same bits) ----
+
+// E from the largest |x| bit pattern of a group (>= 0x7f800000: not
+// finite): max|x| * 2^E < 2^15, just below the fp16 maximum.
+__device__ __forceinline__ int act_exponent(uint32_t max_abs_bits) {
+    int e = max_abs_bits >= 0x7f800000u ? 128 : (int)(max_abs_bits >> 23) - 127;
+    if (e < -127) e = -127;
+    return 14 - e;
+}
+
+// v * 2^n with one rounding (a power-of-two product while 2^n is a normal
+// float, ldexpf beyond).
+__device__ __forceinline__ float pow2_scale(float v, int n) {
+    if (n >= -126 && n <= 127) return __fmul_rn(v, __int_as_float((n + 127) << 23));
+    return ldexpf(v, n);
+}
+
+// High and low fp16 parts of (x0, x1) * 2^n as two half2 words.
+__device__ __forceinline__ void act_split2(float x0, float x1, int n, uint32_t *hi2, uint32_t *lo2) {
+    const float v0 = pow2_scale(x0, n), v1 = pow2_scale(x1, n);
+    const __half2 h = __floats2half2_rn(v0, v1);
+    const float2 back = __half22float2(h);
+    const __half2 l = __floats2half2_rn(__fsub_rn(v0, back.x), __fsub_rn(v1, back.y));
+    *hi2 = *reinterpret_cast<const uint32_t *>(&h);
+    *lo2 = *reinterpret_cast<const uint32_t *>(&l);
+}
+
+// Largest |x| bit pattern over n floats at x (all of them read by the calling
+// threads together: thread `tid` of `nthreads`), float4 loads when aligned.
+__device__ __forceinline__ uint32_t max_abs_bits(const float *x, int n, int tid, int nthreads) {
+    uint32_t m = 0;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (n & 3) == 0) {
+        const float4 *x4 = reinterpret_cast<const float4 *>(x);
+#pragma unroll 8
+        for (int i = tid; i < n / 4; i += nthreads) {
+            const float4 v = __ldcg(x4 + i);
+            m = max(m, max(max(__float_as_uint(v.x) & 0x7fffffffu, __float_as_uint(v.y) & 0x7fffffffu),
+                           max(__float_as_uint(v.z) & 0x7fffffffu, __float_as_uint(v.w) & 0x7fffffffu)));
+        }
+    } else {
+#pragma unroll 8
+        for (int i = tid; i < n; i += nthreads) m = max(m, __float_as_uint(__ldcg(x + i)) & 0x7fffffffu);
+    }
+    return m;
+}
+
+// One group of one RHS into the activation image: xg points at the group's
+// G activations (the first `valid` of them inside the matrix, the rest read
+// as zero); dst points at the group's image block [NCH][NB][4 lanes][8
+// halves] and n0 is the RHS's high-part column (2b).  The group's exponent E
+// puts its largest |x| just below the fp16 maximum.  Returns the group's
+// table entry (2^(24 - E), sum of the G values left to right).  Used by the
+// prep kernel and by the streaming kernel's own prep alike.
+template <int BITS, int G>
+__device__ __forceinline__ float2 act_group(const float *xg, int valid, uint32_t *dst, int NB, int n0) {
+    using S = MmaShape<BITS, G>;
+    constexpr int CPL = S::CPL;
+    const bool vec = (reinterpret_cast<uintptr_t>(xg) & 15) == 0 && valid >= G;
+    auto load = [&](int t, float (&v)[CPL]) {
+        if (vec) {
+            const float4 *x4 = reinterpret_cast<const float4 *>(xg + t * CPL);
+#pragma unroll
+            for (int k = 0; k < CPL / 4; ++k) {
+                const float4 q = __ldcg(x4 + k);
+                v[4 * k] = q.x;
+                v[4 * k + 1] = q.y;
+                v[4 * k + 2] = q.z;
+                v[4 * k + 3] = q.w;
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < CPL; ++k) v[k] = t * CPL + k < valid ? __ldcg(xg + t * CPL + k) : 0.0f;
+        }
+    };
+    // Pass 1: largest |x| and the sum in column order (values kept for
+    // groups of up to 64 columns).
+    constexpr bool KEEP = G <= 64;
+    float keep[KEEP ? 4 : 1][CPL];
+    float sum = 0.0f;
+    uint32_t m = 0;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        float v[CPL];
+        load(t, v);
+#pragma unroll
+        for (int k = 0; k < CPL; ++k) {
+            sum = __fadd_rn(sum, v[k]);
+            m = max(m, __float_as_uint(v[k]) & 0x7fffffffu);
+            if constexpr (KEEP) keep[t][k] = v[k];
+        }
+    }
+    const int E = act_exponent(m);
+    // Pass 2: the split halves.  Registers of lane t: pair (reg, h = 0/1)
+    // holds columns block_perm(reg, 0/1); 4 registers (8 halves) per 16-byte
+    // chunk jj.
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        float v[CPL];
+        if constexpr (KEEP) {
+#pragma unroll
+            for (int k = 0; k < CPL; ++k) v[k] = keep[t][k];
+        } else {
+            load(t, v);
+        }
+#pragma unroll
+        for (int jj = 0; jj < S::NCH; ++jj) {
+            uint32_t hi[4], lo[4];
+#pragma unroll
+            for (int r4 = 0; r4 < 4; ++r4) {
+                const int reg = jj * 4 + r4;
+                const int shift = (BITS == 4 && (reg & 1)) ? 4 : 0;
+                act_split2(v[block_perm<BITS>(reg, 0)], v[block_perm<BITS>(reg, 1)], E - shift, &hi[r4], &lo[r4]);
+            }
+            uint4 *blk = reinterpret_cast<uint4 *>(dst + ((jj * NB + n0) * 4 + t) * 4);
+            blk[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            blk[4] = make_uint4(lo[0], lo[1], lo[2], lo[3]);  // column n0 + 1: 4 lanes x 16 bytes on
+        }
+    }
+    return make_float2(ldexpf(1.0f, 24 - E), sum);
+}
+
+// Zero image block and table entry of a padding group past the matrix (its
+// weights are zero-filled; zero times uninitialised data could be NaN).
+template <int BITS, int G>
+__device__ __forceinline__ void act_group_zero(uint32_t *dst, int NB, int n0) {
+    using S = MmaShape<BITS, G>;
+    for (int jj = 0; jj < S::NCH; ++jj)
+        for (int t = 0; t < 4; ++t) {
+            uint4 *blk = reinterpret_cast<uint4 *>(dst + ((jj * NB + n0) * 4 + t) * 4);
+            blk[0] = make_uint4(0u, 0u, 0u, 0u);
+            blk[4] = make_uint4(0u, 0u, 0u, 0u);
+        }
+}
+
+// Prep kernel of the prepared-activation API: one CTA per RHS writes the
+// global image and table that the streaming kernel then copies.
 template <int BITS, int G>
 __global__ void __launch_bounds__(512) mma_prep_kernel(const float *__restrict__ x, int cols, int batch,
                                                       int ngroups_pad, MmaImageView v) {
@@ -137,7 +272,7 @@ __global__ void __launch_bounds__(512) mma_prep_kernel(const float *__restrict__
     using S = MmaShape<BITS, G>;
     const int b = blockIdx.x;
     const float *xb = x + (size_t)b * cols;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const int tid = threadIdx.x;
     const int ngroups = cols / G;
     const int NB = 2 * batch;
     if (b == 0) {
@@ -146,58 +281,16 @@ __global__ void __launch_bounds__(512) mma_prep_kernel(const float *__restrict__
         if (tid < 4) v.keys[tid] = 0ull;
         if (tid == 0) *v.done = 0u;
     }
-    __shared__ float wmax[32];
-    __shared__ int s_e;
-    float mx = 0.0f;
-    bool nonfinite = false;
-    for (int i = tid; i < cols; i += blockDim.x) {
-        const float a = fabsf(xb[i]);
-        nonfinite |= !(a <= 3.402823466e38f);
-        mx = fmaxf(mx, a);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    nonfinite = __any_sync(0xffffffffu, nonfinite);
-    if (lane == 0) wmax[warp] = nonfinite ? __int_as_float(0x7f800000) : mx;
-    __syncthreads();
-    if (tid == 0) {
-        float m = 0.0f;
-        for (int w = 0; w < nw; ++w) m = fmaxf(m, wmax[w]);
-        int e = (int)((__float_as_uint(m) >> 23) & 0xff) - 127;  // max|x| < 2^(e+1); inf -> 128
-        if (e < -127) e = -127;
-        s_e = e;
-    }
-    __syncthreads();
-    const int E = 14 - s_e;  // max|x| * 2^E < 2^15 (fp16 max 65504)
-    if (tid == 0) {
-        const int t = 24 - E;
-        const int a = t > 120 ? 120 : (t < -120 ? -120 : t);
-        v.cf[2 * b] = ldexpf(1.0f, a);
-        v.cf[2 * b + 1] = ldexpf(1.0f, t - a);
-    }
-    // Group sums: one warp per group, fixed order (strided lane sums, butterfly).
-    for (int g = warp; g < ngroups_pad; g += nw) {
-        float s = 0.0f;
-        if (g < ngroups) {
-            for (int c = lane; c < G; c += 32) s = __fadd_rn(s, xb[(size_t)g * G + c]);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
-        }
-        if (lane == 0) v.table[(size_t)b * ngroups_pad + g] = g < ngroups ? ldexpf(s, E - 24) : 0.0f;
-    }
-    // Split halves: element (group g, chunk jj, lane slot t, half index k).
-    for (int i = tid; i < ngroups_pad * G; i += blockDim.x) {
-        const int g = i / G, rem = i % G;
-        const int jj = rem >> 5, t = (rem >> 3) & 3, k = rem & 7;
-        const int reg = jj * 4 + (k >> 1), h = k & 1;
-        const int col = g * G + t * S::CPL + block_perm<BITS>(reg, h);
-        const int shift = (BITS == 4 && (reg & 1)) ? 4 : 0;
-        const float xv = col < cols ? ldexpf(xb[col], E - shift) : 0.0f;
-        const __half hi = __float2half_rn(xv);
-        const __half lo = __float2half_rn(xv - __half2float(hi));
-        __half *dst = v.image + ((((size_t)g * S::NCH + jj) * NB + 2 * b) * 4 + t) * 8 + k;
-        dst[0] = hi;
-        dst[32] = lo;  // column n + 1
+    uint32_t *img = reinterpret_cast<uint32_t *>(v.image);
+    float2 *tab = reinterpret_cast<float2 *>(v.table);
+    for (int g = tid; g < ngroups_pad; g += blockDim.x) {
+        uint32_t *dst = img + (size_t)g * S::NCH * NB * 16;
+        float2 e = make_float2(0.0f, 0.0f);
+        if (g < ngroups)
+            e = act_group<BITS, G>(xb + (size_t)g * G, cols - g * G, dst, NB, 2 * b);
+        else
+            act_group_zero<BITS, G>(dst, NB, 2 * b);
+        tab[(size_t)b * ngroups_pad + g] = e;
     }
 }
 
@@ -300,8 +393,7 @@ __device__ __forceinline__ void cluster_sync() {
 struct MmaArgs {
     const unsigned char *s, *b, *s2, *b2;  // metadata [rows][ngroups] (f32 or bf16 bits)
     const __half *image;                   // prepared activation image
-    const float *table;                    // group sums [4][ngroups_pad]
-    const float *cf;                       // output factors [B][2]
+    const float *table;                    // [4][ngroups_pad] x (2^(24 - E_g), group sum)
     float *y;
     unsigned long long *keys;              // [B] packed argmax (EPI 2)
     unsigned int *done;                    // CTAs finished (EPI 2)
@@ -311,6 +403,8 @@ struct MmaArgs {
     int rows, ngroups, ngroups_pad, ystride, row_base;
     int tiles, nwin, kc, clusters, pieces, stages;
     uint32_t zero;                         // always 0 (an opaque operand, see the slot refill)
+    const float *x;                        // activations [B][cols] when fuse != 0
+    int cols, fuse;                        // fuse: build the activation image here from x
     uint32_t off_image, off_table, off_pieces, off_part, off_bars;  // offsets into the 1024-aligned dynamic smem
 };
 
@@ -438,9 +532,31 @@ __global__ void __launch_bounds__(32 * NW, 1)
     // The activation image arrives window by window (the group-sum table with
     // the first), so each warp starts as soon as its first window is in.
     bool ok = true;
-    if (U > 0 && threadIdx.x == 0) {
+    if (a.fuse && U > 0) {
+        // Own activation prep (the same arithmetic as mma_prep_kernel): E_b
+        // from all of x, then this slice's group sums and split halves,
+        // written straight into shared memory while the first weight units
+        // are in flight.
+        const int cols = a.cols;
+        // One thread per (group of the slice, RHS): the group's activations in
+        // registers, its image block and table entry out.
+        const int g0 = win0 * S::WG, ng = nh * S::WG;
+        float2 *tab = reinterpret_cast<float2 *>(smem + a.off_table);
+        uint32_t *img = reinterpret_cast<uint32_t *>(smem + a.off_image);
+        for (int i = threadIdx.x; i < B * ng; i += 32 * NW) {
+            const int b = i / ng, gl = i % ng, g = g0 + gl;
+            uint32_t *dst = img + (size_t)gl * S::NCH * NB * 16;
+            float2 e = make_float2(0.0f, 0.0f);
+            if (g < a.ngroups)
+                e = act_group<BITS, G>(a.x + (size_t)b * cols + (size_t)g * G, cols - g * G, dst, NB, 2 * b);
+            else
+                act_group_zero<BITS, G>(dst, NB, 2 * b);
+            tab[b * a.ngroups_pad + g] = e;
+        }
+        __syncthreads();
+    } else if (U > 0 && threadIdx.x == 0) {
         const uint32_t chunk = (uint32_t)S::WG * XG;
-        const uint32_t tab_bytes = 4u * (uint32_t)a.ngroups_pad * 4u;
+        const uint32_t tab_bytes = 4u * (uint32_t)a.ngroups_pad * 8u;  // [4][ngroups_pad] float2
         const unsigned char *src = reinterpret_cast<const unsigned char *>(a.image) + (size_t)win0 * chunk;
         for (int i = 0; i < nh; ++i) {
             mbar_arrive_expect_tx(&ibar[i], chunk + (i == 0 ? tab_bytes : 0u));
@@ -448,7 +564,9 @@ __global__ void __launch_bounds__(32 * NW, 1)
             bulk_g2s(smem + a.off_image + (size_t)i * chunk, src + (size_t)i * chunk, chunk, &ibar[i], pol_keep);
         }
     }
-    uint32_t img_ready = 0;  // windows of the image this warp has waited for (bit 0 also covers the table)
+    // Windows of the image this warp has waited for (bit 0 also covers the
+    // table); with the kernel's own prep everything is already in place.
+    uint32_t img_ready = a.fuse ? 0xffffffffu : 0u;
 
     // Per-lane byte offsets: A words of row gq for the GPB groups of a box
     // line (128-byte swizzle: 16-byte unit u of row r at u ^ (r & 7)), the
@@ -462,7 +580,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
     }
     const int n = gq < NB ? gq : NB - 1;
     const uint32_t x_lane = sbase + a.off_image + (uint32_t)((n * 4 + t) * 16);
-    const uint32_t t_lane = sbase + a.off_table + (uint32_t)(t * a.ngroups_pad * 4);
+    const uint32_t t_lane = sbase + a.off_table + (uint32_t)(t * a.ngroups_pad * 8);
     const uint32_t m_lane = (uint32_t)(2 * gq * META_LANE);
     const uint32_t piece_base = sbase + a.off_pieces + (uint32_t)(warp * a.pieces * PIECE);
 
@@ -470,14 +588,12 @@ __global__ void __launch_bounds__(32 * NW, 1)
     // The epilogue of one finished tile: scale, activation, store, argmax key.
     auto finish_tile = [&](int T, const float (&v)[NM][2]) {
         if (t < B) {
-            const float c1 = __ldcg(a.cf + 2 * t), c2 = __ldcg(a.cf + 2 * t + 1);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const int row = T * kTileRows + gq + 8 * h;
                 if (row < a.rows) {
-                    float val = __fmul_rn(__fmul_rn(v[0][h], c1), c2);
-                    if constexpr (EPI == 1)
-                        val = __fmul_rn(silu_f32(val), __fmul_rn(__fmul_rn(v[NM - 1][h], c1), c2));
+                    float val = v[0][h];
+                    if constexpr (EPI == 1) val = __fmul_rn(silu_f32(val), v[NM - 1][h]);
                     a.y[(size_t)t * a.ystride + row] = val;
                     if constexpr (EPI == 2) {
                         const unsigned long long key = ((unsigned long long)total_order_key(val) << 32) |
@@ -574,7 +690,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
             img_ready |= 1u | (1u << wi);
         }
         const uint32_t xw = x_lane + (uint32_t)(wi * S::WG * XG);
-        const uint32_t tw = t_lane + (uint32_t)((win0 + wi) * S::WG * 4);
+        const uint32_t tw = t_lane + (uint32_t)((win0 + wi) * S::WG * 8);
 #pragma unroll
         for (int gl = 0; gl < S::WG; gl += 2) {
             uint32_t xb[2][S::NREG];
@@ -588,8 +704,11 @@ __global__ void __launch_bounds__(32 * NW, 1)
                     xb[e][4 * jj + 2] = v.z;
                     xb[e][4 * jj + 3] = v.w;
                 }
-            const uint2 xsv = lds64(tw + (uint32_t)(gl * 4));
-            const float xs[2] = {__uint_as_float(xsv.x), __uint_as_float(xsv.y)};
+            // Table entries of groups gl, gl+1 for this lane's RHS: 2^(24 - E_g)
+            // and the group sum.
+            const uint4 tv = lds128(tw + (uint32_t)(gl * 8));
+            const float fg[2] = {__uint_as_float(tv.x), __uint_as_float(tv.z)};
+            const float xs[2] = {__uint_as_float(tv.y), __uint_as_float(tv.w)};
 #pragma unroll
             for (int q = 0; q < NM; ++q) {
                 float d[2][4];
@@ -616,11 +735,12 @@ __global__ void __launch_bounds__(32 * NW, 1)
                             m4[k] = __uint_as_float(mr[q][gl / 2][k][e]);
                         }
                     }
-                    acc[q][0][0] = __fmaf_rn(m4[0], d[e][0], acc[q][0][0]);
-                    acc[q][0][1] = __fmaf_rn(m4[0], d[e][1], acc[q][0][1]);
+                    const float sa = __fmul_rn(m4[0], fg[e]), sb = __fmul_rn(m4[2], fg[e]);
+                    acc[q][0][0] = __fmaf_rn(sa, d[e][0], acc[q][0][0]);
+                    acc[q][0][1] = __fmaf_rn(sa, d[e][1], acc[q][0][1]);
                     acc[q][0][0] = __fmaf_rn(m4[1], xs[e], acc[q][0][0]);
-                    acc[q][1][0] = __fmaf_rn(m4[2], d[e][2], acc[q][1][0]);
-                    acc[q][1][1] = __fmaf_rn(m4[2], d[e][3], acc[q][1][1]);
+                    acc[q][1][0] = __fmaf_rn(sb, d[e][2], acc[q][1][0]);
+                    acc[q][1][1] = __fmaf_rn(sb, d[e][3], acc[q][1][1]);
                     acc[q][1][0] = __fmaf_rn(m4[3], xs[e], acc[q][1][0]);
                 }
             }
@@ -663,7 +783,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
 
     // Every image copy has landed before the CTA can exit (normally already
     // waited for by the warps that read the window).
-    if (U > 0 && threadIdx.x == 0)
+    if (!a.fuse && U > 0 && threadIdx.x == 0)
         for (int i = 0; i < nh; ++i)
             if (!mbar_wait(&ibar[i], 0)) {
                 atomicCAS(a.err, 0u, kErrTimeoutDrain);
