@@ -214,8 +214,15 @@ def run_reference(args):
 # GPU arm
 # ---------------------------------------------------------------------------
 
+def sharded(name, world):
+    """The MLP and the head run row-sharded across the ranks (one model split
+    over N GPUs, strong scaling); the single matrices run one replica per
+    rank (weak scaling)."""
+    return world > 1 and name in ("mlp", "head")
+
+
 class Workload:
-    def __init__(self, name, spec, device, seed):
+    def __init__(self, name, spec, device, seed, world=1, rank=0):
         import torch
 
         from qmr import synth
@@ -223,6 +230,10 @@ class Workload:
         self.torch = torch
         bits, b = spec["bits"], spec["batch"]
         self.batch = b
+        self.sharded = sharded(name, world)
+        if self.sharded:
+            self._init_sharded(world, rank, seed)
+            return
         per_copy = (matrix_bytes(ROWS, COLS, 4, GROUP) * 3) if name == "mlp" else \
             matrix_bytes(spec["rows"], spec["cols"], bits, GROUP)
         l2 = torch.cuda.get_device_properties(device).L2_cache_size
@@ -251,10 +262,61 @@ class Workload:
             self.mats = [clone(m0) for _ in range(self.copies)]
             self.y = torch.empty(b * spec["rows"], dtype=torch.float32, device=device)
             self.idx = torch.empty(b, dtype=torch.int32, device=device)
-        self.launches_per_step = 4 if name == "mlp" else 2
+        self.launches_per_step = 2 if name == "mlp" else 1
+
+    def _init_sharded(self, world, rank, seed):
+        """This rank's row shards (random init of this rank's rows only)."""
+        import math
+
+        import torch
+
+        import qmr
+        from qmr import parallel, synth
+        from qmr.ops import PackedMatrix
+        b, dev = self.batch, self.device
+        l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+        self.l2 = l2
+
+        def dev_matrix(rows, cols, s):
+            m = synth.affine_matrix(rows, cols, 4, GROUP, seed=s)
+            return synth.to_device(m, rows, cols, 4, GROUP, dev)
+
+        def clone(m):
+            return PackedMatrix(m.weight.clone(), m.scales.clone(), m.biases.clone(), m.rows, m.cols, m.bits,
+                                m.group)
+
+        self.x = torch.from_numpy(synth.activations(b, COLS, seed=seed + 1).ravel()).to(dev)
+        s = seed + 100 * rank
+        if self.name == "mlp":
+            f0, f1 = parallel.shard_range(ROWS, world, rank)
+            h0, h1 = parallel.shard_range(COLS, world, rank)
+            g0, u0 = dev_matrix(f1 - f0, COLS, s + 10), dev_matrix(f1 - f0, COLS, s + 11)
+            d0 = dev_matrix(h1 - h0, ROWS, s + 12)
+            per_copy = g0.nbytes + u0.nbytes + d0.nbytes
+            self.copies = max(2, math.ceil(4 * l2 / per_copy) + 1)
+            self.mods = [parallel.ShardedMLP(clone(g0), clone(u0), clone(d0), COLS, ROWS, qmr.ops)
+                         for _ in range(self.copies)]
+            self.y = torch.empty(b * COLS, dtype=torch.float32, device=dev)
+            self.launches_per_step = 2
+        else:
+            v0, v1 = parallel.shard_range(VOCAB, world, rank)
+            h = dev_matrix(v1 - v0, COLS, s + 10)
+            self.copies = max(2, math.ceil(4 * l2 / h.nbytes) + 1)
+            self.mods = [parallel.ShardedHead(clone(h), VOCAB, v0, qmr.ops) for _ in range(self.copies)]
+            self.y = torch.empty(b * (v1 - v0), dtype=torch.float32, device=dev)
+            self.idx = torch.empty(b, dtype=torch.int32, device=dev)
+            self.launches_per_step = 1
 
     def step(self, i, stream=None):
         import qmr
+        if self.sharded:
+            mod = self.mods[i % self.copies]
+            if self.name == "mlp":
+                mod(self.x, self.batch, out=self.y)
+            else:
+                idx, _ = mod(self.x, self.batch, logits=self.y)
+                self.idx.copy_(idx)
+            return
         m = self.mats[i % self.copies]
         if self.name == "mlp":
             g, u, d = m
@@ -310,8 +372,11 @@ def run_gpu(args):
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
     qmr.ops.init(local)
     spec = workload_spec(args.workload)
-    wl = Workload(args.workload, spec, device, seed=1000 + 17 * rank)
+    wl = Workload(args.workload, spec, device, seed=1000 + 17 * rank, world=world, rank=rank)
     nbytes = algorithmic_bytes(args.workload, spec)
+    # Replicas: every rank processes nbytes per step.  Shards: the ranks
+    # together process one model's nbytes per step.
+    job_factor = 1 if wl.sharded else world
 
     stream = torch.cuda.Stream(device)
     torch.cuda.synchronize()
@@ -371,7 +436,7 @@ def run_gpu(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
     ms_per_step = ms_max / args.steps
-    value = world * nbytes * args.steps / (ms_max * 1e-3) / 1e9
+    value = job_factor * nbytes * args.steps / (ms_max * 1e-3) / 1e9
 
     # End to end through the public API: pinned host x in, result out, every step.
     e2e_steps = min(args.steps, 200 if args.quick else 2000)
@@ -402,7 +467,7 @@ def run_gpu(args):
     te = torch.tensor([e0.elapsed_time(e1)], device=device)
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = world * nbytes * e2e_steps / (float(te.item()) * 1e-3) / 1e9
+    e2e_value = job_factor * nbytes * e2e_steps / (float(te.item()) * 1e-3) / 1e9
 
     peak, peak_kind = load_peaks()
     if kernel_ms is not None:
@@ -410,17 +475,21 @@ def run_gpu(args):
         achieved = kernel_nbytes / (kernel_ms * 1e-3) / 1e9
         timing_note = "streaming kernel alone: activations prepared once, K launches in one graph"
     else:
-        achieved = nbytes / (ms_per_step * 1e-3) / 1e9
-        timing_note = "whole call (prep + streaming kernels)"
+        # per GPU: its share of the job's bytes over the step time
+        achieved = job_factor * nbytes / world / (ms_per_step * 1e-3) / 1e9
+        timing_note = "whole call" + (", sharded step incl. NCCL all-gathers" if wl.sharded else "")
     traffic = profile_traffic(args.workload)
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6), "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6), "higher_is_better": True,
+        "scaling": "strong" if wl.sharded else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; benchmark distributions)",
         "config": {"workload": spec["desc"], "batch": spec["batch"], "rows": spec["rows"], "cols": spec["cols"],
                    "bits": spec["bits"], "group": GROUP, "metadata": "bf16", "weight_copies": wl.copies,
                    "l2_bytes": wl.l2, "l2_policy": f"{wl.copies} distinct weight copies rotated (> 4x L2)",
-                   "bytes_per_step": nbytes, "parallelism": f"replicas{world}" if world > 1 else "single"},
+                   "bytes_per_step": nbytes,
+                   "parallelism": (f"rowshard{world} (NCCL all-gather)" if wl.sharded else
+                                   f"replicas{world}" if world > 1 else "single")},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "steps": e2e_steps},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
@@ -444,7 +513,14 @@ def run_gpu(args):
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
-        del graphs
+        # Every graph that holds NCCL calls must be gone before the process
+        # group is destroyed (the loop variable above holds one too).
+        g = None
+        graphs.clear()
+        del graphs, g
+        import gc
+        gc.collect()
+        torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
     return 0

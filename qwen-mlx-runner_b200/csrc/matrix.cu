@@ -161,7 +161,7 @@ constexpr size_t kMmaImageBudget = 96 * 1024;
 namespace {
 
 bool mma_plan_b(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint32_t batch, int epi, bool bf16,
-                MmaPlan *p);
+                int only_kc, MmaPlan *p);
 
 }  // namespace
 
@@ -171,14 +171,15 @@ bool mma_plan_b(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uin
 bool mma_plan(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint32_t batch, int epi, bool bf16,
               MmaPlan *p) {
     MmaPlan widest;
-    if (!mma_plan_b(bits, group, rows, cols, 4, epi, bf16, &widest)) return false;
-    return mma_plan_b(bits, group, rows, cols, batch, epi, bf16, p);
+    if (!mma_plan_b(bits, group, rows, cols, 4, epi, bf16, 0, &widest)) return false;
+    return mma_plan_b(bits, group, rows, cols, batch, epi, bf16, widest.kc, p);
 }
 
 namespace {
 
+// only_kc: 0 searches the slice count, otherwise the plan must use that one.
 bool mma_plan_b(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint32_t batch, int epi, bool bf16,
-                MmaPlan *p) {
+                int only_kc, MmaPlan *p) {
     if (bits != 4 && bits != 8) return false;
     if (group != 32 && group != 64 && group != 128) return false;
     if (bits == 8 && group == 128) return false;
@@ -193,61 +194,59 @@ bool mma_plan_b(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uin
     const int warps = kMmaWarps;
     const int sms = sm_count();
     // Column slices (= cluster size): the smallest kc whose activation slice
-    // fits the budget.
-    int kc = 0;
-    for (int c : {1, 2, 4}) {
-        const size_t nh_max = ((size_t)nwin + c - 1) / c;
-        if (nwin >= c && sms >= c && nh_max * win_cols * 16 <= kMmaImageBudget) {
-            kc = c;
-            break;
-        }
-    }
-    if (kc == 0) return false;
-    const int clusters = sms / kc;
-    const int ctas = clusters * kc;
-    const int nh_min = nwin / kc, nh_max = (nwin + kc - 1) / kc;
-    const int tmax = (tiles + clusters - 1) / clusters;
-    if ((long long)tmax * nh_max * warps >= (1ll << 31)) return false;  // 32-bit unit arithmetic
-    int pieces = 2;
-    if (kc > 1) {
-        const int lmax = (tmax * nh_max + warps - 1) / warps;
-        pieces = (lmax + nh_min - 1) / nh_min + 1;
-        if (pieces > kMaxPieces) return false;
-    }
+    // fits the image budget and whose whole plan (rings of at least two
+    // stages, image, table, pieces) fits the shared memory of one SM.  Two
+    // matrices per unit (the gate/up epilogue) double the ring slots, which
+    // can push a wide matrix from one slice to two.
     const uint32_t piece_bytes = (uint32_t)nm * 64 * 4;
     const uint32_t slot = (uint32_t)(mma_slot_weight_bytes((int)bits, (int)group, nm) +
                                      mma_slot_meta_bytes((int)group, nm, bf16 ? 2 : 4));
-    const uint32_t image = (uint32_t)nh_max * win_cols * 4 * batch;
     const uint32_t ngroups_pad = (uint32_t)nwin * wg;
     const uint32_t table = 32 * ngroups_pad;
-    const uint32_t pieces_bytes = (uint32_t)warps * pieces * piece_bytes;
-    const uint32_t part_bytes = kc > 1 ? (uint32_t)((tmax + kc - 1) / kc * kc) * piece_bytes : 0u;
-    if (nh_max > 32) return false;  // image-window barriers and the per-warp ready mask
     const int limit = smem_optin() - 512;  // room for the kernel's static shared variables (under 300 bytes)
-    for (int st = kMmaMaxStages; st >= 2; --st) {
-        const uint32_t off_image = (uint32_t)warps * st * slot;
-        const uint32_t off_table = off_image + (image + 127) / 128 * 128;
-        const uint32_t off_pieces = off_table + (table + 127) / 128 * 128;
-        const uint32_t off_part = off_pieces + pieces_bytes;
-        const uint32_t off_bars = off_part + part_bytes;
-        const uint32_t total = 1024 + off_bars + (uint32_t)(warps * st + nh_max) * 8;
-        if ((int)total <= limit) {
-            p->kc = kc;
-            p->clusters = clusters;
-            p->ctas = ctas;
-            p->stages = st;
-            p->pieces = pieces;
-            p->nwin = nwin;
-            p->ngroups_pad = (int)ngroups_pad;
-            p->tiles = tiles;
-            p->warps = warps;
-            p->smem = total;
-            p->off_image = off_image;
-            p->off_table = off_table;
-            p->off_pieces = off_pieces;
-            p->off_part = off_part;
-            p->off_bars = off_bars;
-            return true;
+    for (int kc : {1, 2, 4}) {
+        if (only_kc != 0 && kc != only_kc) continue;
+        const int nh_min = nwin / kc, nh_max = (nwin + kc - 1) / kc;
+        if (nwin < kc || sms < kc || (size_t)nh_max * win_cols * 16 > kMmaImageBudget) continue;
+        if (nh_max > 32) continue;  // image-window barriers and the per-warp ready mask
+        const int clusters = sms / kc;
+        const int ctas = clusters * kc;
+        const int tmax = (tiles + clusters - 1) / clusters;
+        if ((long long)tmax * nh_max * warps >= (1ll << 31)) continue;  // 32-bit unit arithmetic
+        int pieces = 2;
+        if (kc > 1) {
+            const int lmax = (tmax * nh_max + warps - 1) / warps;
+            pieces = (lmax + nh_min - 1) / nh_min + 1;
+            if (pieces > kMaxPieces) continue;
+        }
+        const uint32_t image = (uint32_t)nh_max * win_cols * 4 * batch;
+        const uint32_t pieces_bytes = (uint32_t)warps * pieces * piece_bytes;
+        const uint32_t part_bytes = kc > 1 ? (uint32_t)((tmax + kc - 1) / kc * kc) * piece_bytes : 0u;
+        for (int st = kMmaMaxStages; st >= 2; --st) {
+            const uint32_t off_image = (uint32_t)warps * st * slot;
+            const uint32_t off_table = off_image + (image + 127) / 128 * 128;
+            const uint32_t off_pieces = off_table + (table + 127) / 128 * 128;
+            const uint32_t off_part = off_pieces + pieces_bytes;
+            const uint32_t off_bars = off_part + part_bytes;
+            const uint32_t total = 1024 + off_bars + (uint32_t)(warps * st + nh_max) * 8;
+            if ((int)total <= limit) {
+                p->kc = kc;
+                p->clusters = clusters;
+                p->ctas = ctas;
+                p->stages = st;
+                p->pieces = pieces;
+                p->nwin = nwin;
+                p->ngroups_pad = (int)ngroups_pad;
+                p->tiles = tiles;
+                p->warps = warps;
+                p->smem = total;
+                p->off_image = off_image;
+                p->off_table = off_table;
+                p->off_pieces = off_pieces;
+                p->off_part = off_part;
+                p->off_bars = off_bars;
+                return true;
+            }
         }
     }
     return false;

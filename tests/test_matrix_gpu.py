@@ -344,6 +344,12 @@ def test_gateup_swiglu_matches_oracle_and_separate_projections(cuda):
         # The fused pair against the two plain projections (whose split of the columns may differ):
         # both sides carry the bound once.
         assert_ns_bound(a, ref, 2 * mag + np.abs(ref) * 0.1, f"swiglu vs separate B{batch}")
+        if batch == 3:
+            # The fused pair is B-independent too: RHS 1 of the block equals a single-RHS call.
+            a1 = torch.empty(rows, dtype=torch.float32, device="cuda")
+            qmr.gateup_swiglu(gm, um, xd.reshape(-1)[cols:2 * cols], a1, 1)
+            torch.cuda.synchronize()
+            assert np.array_equal(a[1].view(np.uint32), a1.cpu().numpy().view(np.uint32))
 
 
 def test_head_argmax_matches_logits_and_oracle(cuda):
