@@ -21,8 +21,8 @@ template <int G>
 int launch_prep_g(const float *x, uint32_t cols, uint32_t batch, int ngroups_pad, const MmaImageView &v,
                   cudaStream_t stream) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(batch, 1, 1);
-    cfg.blockDim = dim3(512, 1, 1);
+    cfg.gridDim = dim3((unsigned)((ngroups_pad + kPrepGroupsPerCta - 1) / kPrepGroupsPerCta), batch, 1);
+    cfg.blockDim = dim3(4 * kPrepGroupsPerCta, 1, 1);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1] = {pdl_attr()};
     cfg.attrs = attr;
@@ -130,7 +130,7 @@ int launch_e(const CUtensorMap &m1, const CUtensorMap &m2, const MmaArgs &a, con
 #define QMR_MMA_PREP launch_mma_prep8
 #endif
 
-int QMR_MMA_LAUNCH(const FastCall &c, const MmaPlan &p, const ScratchView &sv, const MmaImageView &v, bool fuse,
+int QMR_MMA_LAUNCH(const FastCall &c, const MmaPlan &p, const ScratchView &sv, const MmaImageView &v,
                    cudaStream_t stream) {
     const uint64_t row_words = (uint64_t)c.cols * kBits / 32;
     CUtensorMap m1, m2;
@@ -172,15 +172,52 @@ int QMR_MMA_LAUNCH(const FastCall &c, const MmaPlan &p, const ScratchView &sv, c
     a.off_part = p.off_part;
     a.off_bars = p.off_bars;
     a.zero = 0u;
-    a.x = c.x;
-    a.cols = (int)c.cols;
-    a.fuse = fuse ? 1 : 0;
     switch (c.epilogue) {
         case 0: return launch_e<0>(m1, m2, a, p, c.bf16, c.group, c.batch, c.overlap, stream);
         case 1: return launch_e<1>(m1, m2, a, p, c.bf16, c.group, c.batch, c.overlap, stream);
         default: return launch_e<2>(m1, m2, a, p, c.bf16, c.group, c.batch, c.overlap, stream);
     }
 }
+
+#if QMR_MMA_BITS == 4
+// How many clusters of kc CTAs can be resident at once.  Every plan holds
+// more than half of an SM's shared memory (one CTA per SM), so the answer
+// depends only on kc and on how the SMs group into GPCs: 148 SMs do not
+// split into 37 co-resident clusters of 4.  Cached per (device, kc).
+int mma_cluster_capacity(int kc) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || kc < 1 || kc > 8) return 0;
+    static std::atomic<int> cache[64][9] = {};
+    const int have = cache[dev][kc].load(std::memory_order_acquire);
+    if (have != 0) return have;
+    auto kern = mma_kernel<4, 64, 4, true, 0, kMmaWarps>;
+    static std::atomic<uint64_t> opted{0};
+    if (opt_in_smem(kern, opted) != QMR_OK) return 0;
+    int max_optin = 0;
+    cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return 0;
+    const int sms = sm_count();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(sms / kc * kc), 1, 1);
+    cfg.blockDim = dim3(32 * kMmaWarps, 1, 1);
+    cfg.dynamicSmemBytes = (size_t)(max_optin - (int)fa.sharedSizeBytes);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)kc;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+        (void)cudaGetLastError();
+        return 0;
+    }
+    cache[dev][kc].store(n, std::memory_order_release);
+    return n;
+}
+#endif
 
 int QMR_MMA_PREP(const float *x, uint32_t cols, uint32_t group, uint32_t batch, int ngroups_pad,
                  const MmaImageView &v, cudaStream_t stream) {

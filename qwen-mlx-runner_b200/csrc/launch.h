@@ -17,6 +17,9 @@ namespace qmr {
 
 cudaLaunchAttribute pdl_attr();
 int sm_count();
+// Clusters of kc CTAs (one CTA per SM) that fit on the device at once; 0 if
+// the occupancy query failed.
+int mma_cluster_capacity(int kc);
 int log2i(uint32_t v);
 
 // kernels_reg.cu
@@ -50,10 +53,9 @@ bool mma_plan(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint3
 // kernels_mma.cu (one translation unit per bit width)
 int launch_mma_prep_bits(int bits, const float *x, uint32_t cols, uint32_t group, uint32_t batch, int ngroups_pad,
                          const MmaImageView &v, cudaStream_t stream);
-// fuse: the kernel builds its activation image from c.x itself (no prep).
-int launch_mma4(const FastCall &c, const MmaPlan &p, const ScratchView &sv, const MmaImageView &v, bool fuse,
+int launch_mma4(const FastCall &c, const MmaPlan &p, const ScratchView &sv, const MmaImageView &v,
                 cudaStream_t stream);
-int launch_mma8(const FastCall &c, const MmaPlan &p, const ScratchView &sv, const MmaImageView &v, bool fuse,
+int launch_mma8(const FastCall &c, const MmaPlan &p, const ScratchView &sv, const MmaImageView &v,
                 cudaStream_t stream);
 int launch_mma_prep4(const float *x, uint32_t cols, uint32_t group, uint32_t batch, int ngroups_pad,
                      const MmaImageView &v, cudaStream_t stream);

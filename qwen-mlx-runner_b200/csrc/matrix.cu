@@ -209,7 +209,12 @@ bool mma_plan_b(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uin
         const int nh_min = nwin / kc, nh_max = (nwin + kc - 1) / kc;
         if (nwin < kc || sms < kc || (size_t)nh_max * win_cols * 16 > kMmaImageBudget) continue;
         if (nh_max > 32) continue;  // image-window barriers and the per-warp ready mask
-        const int clusters = sms / kc;
+        // One wave: no more clusters than can be resident together.
+        int clusters = sms / kc;
+        if (kc > 1) {
+            const int cap = mma_cluster_capacity(kc);
+            if (cap > 0 && cap < clusters) clusters = cap;
+        }
         const int ctas = clusters * kc;
         const int tmax = (tiles + clusters - 1) / clusters;
         if ((long long)tmax * nh_max * warps >= (1ll << 31)) continue;  // 32-bit unit arithmetic
@@ -328,7 +333,7 @@ int run_stream(const FastCall &c, void *base, cudaStream_t stream) {
             return fail(QMR_EUNSUPPORTED,
                         "activations prepared for the tensor-core kernel, which does not take this matrix "
                         "(unaligned weights or metadata, or no launch plan)");
-        return c.bits == 4 ? launch_mma4(c, p, sv, mv, false, stream) : launch_mma8(c, p, sv, mv, false, stream);
+        return c.bits == 4 ? launch_mma4(c, p, sv, mv, stream) : launch_mma8(c, p, sv, mv, stream);
     }
     if (c.path != kPathRegisters && tile_eligible(c)) return launch_tile_call(c, sv, stream);
     StreamArgs a = {};
@@ -365,17 +370,6 @@ int run_fast(const FastCall &c, cudaStream_t stream) {
     FastCall call = c;
     MmaPlan plan;
     if (call.path == kPathMma && !mma_takes(call, &plan)) call.path = kPathTile;  // FP32 kernels take the rest
-    if (call.path == kPathMma) {
-        // One launch: the streaming kernel prepares its own activation image.
-        // Programmatic dependent launch lets it start loading weights while
-        // the previous kernel finishes; it waits for that kernel before x.
-        ScratchView sv;
-        MmaImageView mv;
-        scratch_layout(base, (int)call.bits, call.cols, call.batch, &sv, &mv);
-        call.overlap = true;
-        return call.bits == 4 ? launch_mma4(call, plan, sv, mv, true, stream)
-                              : launch_mma8(call, plan, sv, mv, true, stream);
-    }
     const int rc = run_prepare(call.x, call.cols, call.bits, call.group, call.batch, base, call.path, stream);
     if (rc != QMR_OK) return rc;
     call.overlap = true;  // the preceding kernel is our prep, which writes no weights

@@ -124,8 +124,7 @@ struct MmaImageView {
     unsigned int *done;        // CTA counter, cleared by the prep
 };
 
-// ---- activation image arithmetic (shared by the prep kernel and the
-// streaming kernel's own prep, so both produce the same bits) ----
+// ---- activation image arithmetic (the prep kernel's) ----
 
 // E from the largest |x| bit pattern of a group (>= 0x7f800000: not
 // finite): max|x| * 2^E < 2^15, just below the fp16 maximum.
@@ -135,11 +134,24 @@ __device__ __forceinline__ int act_exponent(uint32_t max_abs_bits) {
     return 14 - e;
 }
 
-// v * 2^n with one rounding (a power-of-two product while 2^n is a normal
-// float, ldexpf beyond).
+// 2^e as a float: exact for e in [-149, 127], 0 below, +inf above (the
+// values ldexpf(1, e) gives).
+__device__ __forceinline__ float pow2f(int e) {
+    if (e > 127) return __int_as_float(0x7f800000);
+    if (e >= -126) return __int_as_float((e + 127) << 23);
+    if (e >= -149) return __int_as_float(1 << (e + 149));
+    return 0.0f;
+}
+
+// v * 2^n: one rounding while 2^n is a normal float; beyond that (groups
+// whose largest |x| is below 2^-112 or above 2^126) two power-of-two
+// products, 2^(n/2) and the rest, both normal for the exponents act_exponent
+// produces.  Short and branch-light: this runs once per activation in every
+// CTA's prologue.
 __device__ __forceinline__ float pow2_scale(float v, int n) {
     if (n >= -126 && n <= 127) return __fmul_rn(v, __int_as_float((n + 127) << 23));
-    return ldexpf(v, n);
+    const int h = n / 2;
+    return __fmul_rn(__fmul_rn(v, __int_as_float((h + 127) << 23)), __int_as_float((n - h + 127) << 23));
 }
 
 // High and low fp16 parts of (x0, x1) * 2^n as two half2 words.
@@ -152,130 +164,85 @@ __device__ __forceinline__ void act_split2(float x0, float x1, int n, uint32_t *
     *lo2 = *reinterpret_cast<const uint32_t *>(&l);
 }
 
-// Largest |x| bit pattern over n floats at x (all of them read by the calling
-// threads together: thread `tid` of `nthreads`), float4 loads when aligned.
-__device__ __forceinline__ uint32_t max_abs_bits(const float *x, int n, int tid, int nthreads) {
+// One quarter of one group of one RHS into the activation image.  The four
+// threads of an aligned quad (lanes 4k..4k+3 of one warp, t = lane & 3) take
+// one (group, RHS) together: thread t holds the group's columns t*CPL ..
+// t*CPL+CPL-1 (exactly the columns MMA lane t reads) in v; the quad shares
+// its largest |x| and adds its four partial sums as (s0 + s1) + (s2 + s3).
+// Every lane of the warp must call act_quad_stats (it shuffles with the full
+// mask); quads with nothing to do pass zeros.  The group's exponent E puts
+// its largest |x| just below the fp16 maximum.
+template <int CPL>
+__device__ __forceinline__ void act_quad_stats(const float (&v)[CPL], int *E, float *sum) {
+    float s = 0.0f;
     uint32_t m = 0;
-    if ((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (n & 3) == 0) {
-        const float4 *x4 = reinterpret_cast<const float4 *>(x);
-#pragma unroll 8
-        for (int i = tid; i < n / 4; i += nthreads) {
-            const float4 v = __ldcg(x4 + i);
-            m = max(m, max(max(__float_as_uint(v.x) & 0x7fffffffu, __float_as_uint(v.y) & 0x7fffffffu),
-                           max(__float_as_uint(v.z) & 0x7fffffffu, __float_as_uint(v.w) & 0x7fffffffu)));
-        }
-    } else {
-#pragma unroll 8
-        for (int i = tid; i < n; i += nthreads) m = max(m, __float_as_uint(__ldcg(x + i)) & 0x7fffffffu);
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) {
+        s = __fadd_rn(s, v[k]);
+        m = max(m, __float_as_uint(v[k]) & 0x7fffffffu);
     }
-    return m;
+    m = max(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = max(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 1));  // s0 + s1 | s2 + s3 (addition commutes)
+    s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 2));
+    *E = act_exponent(m);
+    *sum = s;
 }
 
-// One group of one RHS into the activation image: xg points at the group's
-// G activations (the first `valid` of them inside the matrix, the rest read
-// as zero); dst points at the group's image block [NCH][NB][4 lanes][8
-// halves] and n0 is the RHS's high-part column (2b).  The group's exponent E
-// puts its largest |x| just below the fp16 maximum.  Returns the group's
-// table entry (2^(24 - E), sum of the G values left to right).  Used by the
-// prep kernel and by the streaming kernel's own prep alike.
+// Thread t's part of the group's image block: dst points at the block
+// [NCH][NB][4 lanes][8 halves], n0 is the RHS's high-part column (2b).
+// Registers of lane t: pair (reg, h = 0/1) holds columns block_perm(reg,
+// 0/1); 4 registers (8 halves) per 16-byte chunk jj, high parts at column n0
+// and low parts at n0 + 1 (the next 64 bytes).  zero: a padding group past
+// the matrix (zeros).
 template <int BITS, int G>
-__device__ __forceinline__ float2 act_group(const float *xg, int valid, uint32_t *dst, int NB, int n0) {
+__device__ __forceinline__ void act_quad_store(const float (&v)[G / 4], int E, bool zero, uint32_t *dst, int NB, int n0,
+                                               int t) {
     using S = MmaShape<BITS, G>;
-    constexpr int CPL = S::CPL;
-    const bool vec = (reinterpret_cast<uintptr_t>(xg) & 15) == 0 && valid >= G;
-    auto load = [&](int t, float (&v)[CPL]) {
-        if (vec) {
-            const float4 *x4 = reinterpret_cast<const float4 *>(xg + t * CPL);
 #pragma unroll
-            for (int k = 0; k < CPL / 4; ++k) {
-                const float4 q = __ldcg(x4 + k);
-                v[4 * k] = q.x;
-                v[4 * k + 1] = q.y;
-                v[4 * k + 2] = q.z;
-                v[4 * k + 3] = q.w;
-            }
-        } else {
-#pragma unroll
-            for (int k = 0; k < CPL; ++k) v[k] = t * CPL + k < valid ? __ldcg(xg + t * CPL + k) : 0.0f;
-        }
-    };
-    // Pass 1: largest |x| and the sum in column order (values kept for
-    // groups of up to 64 columns).
-    constexpr bool KEEP = G <= 64;
-    float keep[KEEP ? 4 : 1][CPL];
-    float sum = 0.0f;
-    uint32_t m = 0;
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-        float v[CPL];
-        load(t, v);
-#pragma unroll
-        for (int k = 0; k < CPL; ++k) {
-            sum = __fadd_rn(sum, v[k]);
-            m = max(m, __float_as_uint(v[k]) & 0x7fffffffu);
-            if constexpr (KEEP) keep[t][k] = v[k];
-        }
-    }
-    const int E = act_exponent(m);
-    // Pass 2: the split halves.  Registers of lane t: pair (reg, h = 0/1)
-    // holds columns block_perm(reg, 0/1); 4 registers (8 halves) per 16-byte
-    // chunk jj.
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-        float v[CPL];
-        if constexpr (KEEP) {
-#pragma unroll
-            for (int k = 0; k < CPL; ++k) v[k] = keep[t][k];
-        } else {
-            load(t, v);
-        }
-#pragma unroll
-        for (int jj = 0; jj < S::NCH; ++jj) {
-            uint32_t hi[4], lo[4];
+    for (int jj = 0; jj < S::NCH; ++jj) {
+        uint32_t hi[4] = {0u, 0u, 0u, 0u}, lo[4] = {0u, 0u, 0u, 0u};
+        if (!zero) {
 #pragma unroll
             for (int r4 = 0; r4 < 4; ++r4) {
                 const int reg = jj * 4 + r4;
                 const int shift = (BITS == 4 && (reg & 1)) ? 4 : 0;
                 act_split2(v[block_perm<BITS>(reg, 0)], v[block_perm<BITS>(reg, 1)], E - shift, &hi[r4], &lo[r4]);
             }
-            uint4 *blk = reinterpret_cast<uint4 *>(dst + ((jj * NB + n0) * 4 + t) * 4);
-            blk[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-            blk[4] = make_uint4(lo[0], lo[1], lo[2], lo[3]);  // column n0 + 1: 4 lanes x 16 bytes on
         }
+        uint4 *blk = reinterpret_cast<uint4 *>(dst + ((jj * NB + n0) * 4 + t) * 4);
+        blk[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        blk[4] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     }
-    return make_float2(ldexpf(1.0f, 24 - E), sum);
 }
 
-// Zero image block and table entry of a padding group past the matrix (its
-// weights are zero-filled; zero times uninitialised data could be NaN).
-template <int BITS, int G>
-__device__ __forceinline__ void act_group_zero(uint32_t *dst, int NB, int n0) {
-    using S = MmaShape<BITS, G>;
-    for (int jj = 0; jj < S::NCH; ++jj)
-        for (int t = 0; t < 4; ++t) {
-            uint4 *blk = reinterpret_cast<uint4 *>(dst + ((jj * NB + n0) * 4 + t) * 4);
-            blk[0] = make_uint4(0u, 0u, 0u, 0u);
-            blk[4] = make_uint4(0u, 0u, 0u, 0u);
-        }
+// Table entry of a group: (2^(24 - E), group sum); zero for padding groups.
+__device__ __forceinline__ float2 act_table_entry(int E, float sum, bool zero) {
+    return zero ? make_float2(0.0f, 0.0f) : make_float2(pow2f(24 - E), sum);
 }
 
-// Prep kernel of the prepared-activation API: one CTA per RHS writes the
-// global image and table that the streaming kernel then copies.
+// Prep kernel of the prepared-activation API: CTA (c, b) writes groups
+// [128 c, 128 c + 128) of RHS b into the global image and table that the
+// streaming kernel then copies, four threads per group (one round: every
+// load of the CTA is in flight at once).
+constexpr int kPrepGroupsPerCta = 128;
+
 template <int BITS, int G>
-__global__ void __launch_bounds__(512) mma_prep_kernel(const float *__restrict__ x, int cols, int batch,
-                                                      int ngroups_pad, MmaImageView v) {
+__global__ void __launch_bounds__(4 * kPrepGroupsPerCta) mma_prep_kernel(const float *__restrict__ x, int cols,
+                                                                         int batch, int ngroups_pad, MmaImageView v) {
     // Launched behind the previous kernel (programmatic dependent launch): let
     // the streaming kernel launch now, then wait for x and for the previous
     // user of this scratch before touching either.
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
     using S = MmaShape<BITS, G>;
-    const int b = blockIdx.x;
+    constexpr int CPL = S::CPL;
+    const int b = blockIdx.y;
     const float *xb = x + (size_t)b * cols;
     const int tid = threadIdx.x;
     const int ngroups = cols / G;
     const int NB = 2 * batch;
-    if (b == 0) {
+    if (blockIdx.x == 0 && b == 0) {
         // Every call starts with clear argmax state, even after a launch that
         // stopped early on a device error.
         if (tid < 4) v.keys[tid] = 0ull;
@@ -283,14 +250,34 @@ __global__ void __launch_bounds__(512) mma_prep_kernel(const float *__restrict__
     }
     uint32_t *img = reinterpret_cast<uint32_t *>(v.image);
     float2 *tab = reinterpret_cast<float2 *>(v.table);
-    for (int g = tid; g < ngroups_pad; g += blockDim.x) {
-        uint32_t *dst = img + (size_t)g * S::NCH * NB * 16;
-        float2 e = make_float2(0.0f, 0.0f);
-        if (g < ngroups)
-            e = act_group<BITS, G>(xb + (size_t)g * G, cols - g * G, dst, NB, 2 * b);
-        else
-            act_group_zero<BITS, G>(dst, NB, 2 * b);
-        tab[(size_t)b * ngroups_pad + g] = e;
+    // Every lane takes part in the quad shuffles of act_quad_stats.
+    const int g = blockIdx.x * kPrepGroupsPerCta + (tid >> 2), t = tid & 3;
+    const bool here = g < ngroups_pad, real = g < ngroups;
+    float v_[CPL];
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) v_[k] = 0.0f;
+    if (real) {
+        const float *xl = xb + (size_t)g * G + t * CPL;
+        if ((reinterpret_cast<uintptr_t>(xl) & 15) == 0) {
+#pragma unroll
+            for (int k = 0; k < CPL / 4; ++k) {
+                const float4 q = __ldcg(reinterpret_cast<const float4 *>(xl) + k);
+                v_[4 * k] = q.x;
+                v_[4 * k + 1] = q.y;
+                v_[4 * k + 2] = q.z;
+                v_[4 * k + 3] = q.w;
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < CPL; ++k) v_[k] = __ldcg(xl + k);
+        }
+    }
+    int E;
+    float sum;
+    act_quad_stats<CPL>(v_, &E, &sum);
+    if (here) {
+        act_quad_store<BITS, G>(v_, E, !real, img + (size_t)g * S::NCH * NB * 16, NB, 2 * b, t);
+        if (t == 0) tab[(size_t)b * ngroups_pad + g] = act_table_entry(E, sum, !real);
     }
 }
 
@@ -403,8 +390,6 @@ struct MmaArgs {
     int rows, ngroups, ngroups_pad, ystride, row_base;
     int tiles, nwin, kc, clusters, pieces, stages;
     uint32_t zero;                         // always 0 (an opaque operand, see the slot refill)
-    const float *x;                        // activations [B][cols] when fuse != 0
-    int cols, fuse;                        // fuse: build the activation image here from x
     uint32_t off_image, off_table, off_pieces, off_part, off_bars;  // offsets into the 1024-aligned dynamic smem
 };
 
@@ -532,29 +517,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
     // The activation image arrives window by window (the group-sum table with
     // the first), so each warp starts as soon as its first window is in.
     bool ok = true;
-    if (a.fuse && U > 0) {
-        // Own activation prep (the same arithmetic as mma_prep_kernel): E_b
-        // from all of x, then this slice's group sums and split halves,
-        // written straight into shared memory while the first weight units
-        // are in flight.
-        const int cols = a.cols;
-        // One thread per (group of the slice, RHS): the group's activations in
-        // registers, its image block and table entry out.
-        const int g0 = win0 * S::WG, ng = nh * S::WG;
-        float2 *tab = reinterpret_cast<float2 *>(smem + a.off_table);
-        uint32_t *img = reinterpret_cast<uint32_t *>(smem + a.off_image);
-        for (int i = threadIdx.x; i < B * ng; i += 32 * NW) {
-            const int b = i / ng, gl = i % ng, g = g0 + gl;
-            uint32_t *dst = img + (size_t)gl * S::NCH * NB * 16;
-            float2 e = make_float2(0.0f, 0.0f);
-            if (g < a.ngroups)
-                e = act_group<BITS, G>(a.x + (size_t)b * cols + (size_t)g * G, cols - g * G, dst, NB, 2 * b);
-            else
-                act_group_zero<BITS, G>(dst, NB, 2 * b);
-            tab[b * a.ngroups_pad + g] = e;
-        }
-        __syncthreads();
-    } else if (U > 0 && threadIdx.x == 0) {
+    if (U > 0 && threadIdx.x == 0) {
         const uint32_t chunk = (uint32_t)S::WG * XG;
         const uint32_t tab_bytes = 4u * (uint32_t)a.ngroups_pad * 8u;  // [4][ngroups_pad] float2
         const unsigned char *src = reinterpret_cast<const unsigned char *>(a.image) + (size_t)win0 * chunk;
@@ -565,8 +528,8 @@ __global__ void __launch_bounds__(32 * NW, 1)
         }
     }
     // Windows of the image this warp has waited for (bit 0 also covers the
-    // table); with the kernel's own prep everything is already in place.
-    uint32_t img_ready = a.fuse ? 0xffffffffu : 0u;
+    // table).
+    uint32_t img_ready = 0u;
 
     // Per-lane byte offsets: A words of row gq for the GPB groups of a box
     // line (128-byte swizzle: 16-byte unit u of row r at u ^ (r & 7)), the
@@ -783,7 +746,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
 
     // Every image copy has landed before the CTA can exit (normally already
     // waited for by the warps that read the window).
-    if (!a.fuse && U > 0 && threadIdx.x == 0)
+    if (U > 0 && threadIdx.x == 0)
         for (int i = 0; i < nh; ++i)
             if (!mbar_wait(&ibar[i], 0)) {
                 atomicCAS(a.err, 0u, kErrTimeoutDrain);

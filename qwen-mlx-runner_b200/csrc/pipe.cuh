@@ -129,6 +129,12 @@ __device__ __forceinline__ void tma_load_2d_s(uint32_t dst, const CUtensorMap *m
         : "memory");
 }
 
+// 4-byte cp.async (through L1) to a 32-bit shared address; src_bytes 0
+// writes zeros.
+__device__ __forceinline__ void cp_async4_s(uint32_t dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+
 // 16-byte cp.async to a 32-bit shared address (see cp_async16).
 __device__ __forceinline__ void cp_async16_s(uint32_t dst, const void *src, uint32_t src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
