@@ -52,8 +52,7 @@ int opt_in_smem(Kern kern, std::atomic<uint64_t> &done) {
 }
 
 template <int G, int B, bool BF16, int EPI, int NW>
-int launch_w(const CUtensorMap &m1, const CUtensorMap &m2, const MmaArgs &a, const MmaPlan &p, bool overlap,
-             cudaStream_t stream) {
+int launch_w(const MmaMaps &maps, const MmaArgs &a, const MmaPlan &p, bool overlap, cudaStream_t stream) {
     auto kern = mma_kernel<kBits, G, B, BF16, EPI, NW>;
     static std::atomic<uint64_t> opted{0};
     const int rc = opt_in_smem(kern, opted);
@@ -75,49 +74,50 @@ int launch_w(const CUtensorMap &m1, const CUtensorMap &m2, const MmaArgs &a, con
     if (overlap) attr[na++] = pdl_attr();
     cfg.attrs = attr;
     cfg.numAttrs = na;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, m1, m2, a);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps, a);
     if (e != cudaSuccess) return fail(QMR_ECUDA, "tensor-core kernel launch failed: %s", cudaGetErrorString(e));
     return QMR_OK;
 }
 
 template <int G, int B, bool BF16, int EPI>
-int launch_t(const CUtensorMap &m1, const CUtensorMap &m2, const MmaArgs &a, const MmaPlan &p, bool overlap,
-             cudaStream_t stream) {
-    constexpr int NW = kMmaWarps;
-    if (p.warps != NW) return fail(QMR_EUNSUPPORTED, "no tensor-core kernel with %d warps", p.warps);
-    return launch_w<G, B, BF16, EPI, NW>(m1, m2, a, p, overlap, stream);
+int launch_t(const MmaMaps &m, const MmaArgs &a, const MmaPlan &p, bool overlap, cudaStream_t stream) {
+    if (p.warps == kMmaWarps) return launch_w<G, B, BF16, EPI, kMmaWarps>(m, a, p, overlap, stream);
+    // Two matrices per unit (gate/up), Q8 words and 128-column groups need
+    // more registers than 12 warps leave; those never take the long plan.
+    if constexpr (EPI != 1 && kBits == 4 && G <= 64)
+        if (p.warps == kMmaWarpsLong) return launch_w<G, B, BF16, EPI, kMmaWarpsLong>(m, a, p, overlap, stream);
+    return fail(QMR_EUNSUPPORTED, "no tensor-core kernel with %d warps", p.warps);
 }
 
 template <int G, bool BF16, int EPI>
-int launch_b(const CUtensorMap &m1, const CUtensorMap &m2, const MmaArgs &a, const MmaPlan &p, uint32_t batch,
-             bool ov, cudaStream_t stream) {
+int launch_b(const MmaMaps &m, const MmaArgs &a, const MmaPlan &p, uint32_t batch, bool ov, cudaStream_t stream) {
     switch (batch) {
-        case 1: return launch_t<G, 1, BF16, EPI>(m1, m2, a, p, ov, stream);
-        case 2: return launch_t<G, 2, BF16, EPI>(m1, m2, a, p, ov, stream);
-        case 3: return launch_t<G, 3, BF16, EPI>(m1, m2, a, p, ov, stream);
-        default: return launch_t<G, 4, BF16, EPI>(m1, m2, a, p, ov, stream);
+        case 1: return launch_t<G, 1, BF16, EPI>(m, a, p, ov, stream);
+        case 2: return launch_t<G, 2, BF16, EPI>(m, a, p, ov, stream);
+        case 3: return launch_t<G, 3, BF16, EPI>(m, a, p, ov, stream);
+        default: return launch_t<G, 4, BF16, EPI>(m, a, p, ov, stream);
     }
 }
 
 template <bool BF16, int EPI>
-int launch_g(const CUtensorMap &m1, const CUtensorMap &m2, const MmaArgs &a, const MmaPlan &p, uint32_t group,
-             uint32_t batch, bool ov, cudaStream_t stream) {
+int launch_g(const MmaMaps &m, const MmaArgs &a, const MmaPlan &p, uint32_t group, uint32_t batch, bool ov,
+             cudaStream_t stream) {
     switch (group) {
-        case 32: return launch_b<32, BF16, EPI>(m1, m2, a, p, batch, ov, stream);
-        case 64: return launch_b<64, BF16, EPI>(m1, m2, a, p, batch, ov, stream);
+        case 32: return launch_b<32, BF16, EPI>(m, a, p, batch, ov, stream);
+        case 64: return launch_b<64, BF16, EPI>(m, a, p, batch, ov, stream);
         default:
             // A Q8 window of 1024 columns needs 16 KiB slots, which the plan
             // never accepts; only Q4 instantiates group 128.
-            if constexpr (kBits == 4) return launch_b<128, BF16, EPI>(m1, m2, a, p, batch, ov, stream);
+            if constexpr (kBits == 4) return launch_b<128, BF16, EPI>(m, a, p, batch, ov, stream);
             return fail(QMR_EUNSUPPORTED, "the tensor-core kernel does not take Q8 group 128");
     }
 }
 
 template <int EPI>
-int launch_e(const CUtensorMap &m1, const CUtensorMap &m2, const MmaArgs &a, const MmaPlan &p, bool bf16,
-             uint32_t group, uint32_t batch, bool ov, cudaStream_t stream) {
-    return bf16 ? launch_g<true, EPI>(m1, m2, a, p, group, batch, ov, stream)
-                : launch_g<false, EPI>(m1, m2, a, p, group, batch, ov, stream);
+int launch_e(const MmaMaps &m, const MmaArgs &a, const MmaPlan &p, bool bf16, uint32_t group, uint32_t batch, bool ov,
+             cudaStream_t stream) {
+    return bf16 ? launch_g<true, EPI>(m, a, p, group, batch, ov, stream)
+                : launch_g<false, EPI>(m, a, p, group, batch, ov, stream);
 }
 
 }  // namespace
@@ -133,12 +133,17 @@ int launch_e(const CUtensorMap &m1, const CUtensorMap &m2, const MmaArgs &a, con
 int QMR_MMA_LAUNCH(const FastCall &c, const MmaPlan &p, const ScratchView &sv, const MmaImageView &v,
                    cudaStream_t stream) {
     const uint64_t row_words = (uint64_t)c.cols * kBits / 32;
-    CUtensorMap m1, m2;
-    int rc = tensor_map_2d(&m1, c.w, 4, row_words, c.rows, 32, kTileRows, true);
-    if (rc != QMR_OK) return rc;
-    m2 = m1;
-    if (c.epilogue == 1) {
-        rc = tensor_map_2d(&m2, c.w2, 4, row_words, c.rows, 32, kTileRows, true);
+    const uint64_t ngroups = c.cols / c.group;
+    const uint32_t wg = (8 * c.group > 512 ? 8 * c.group : 512) / c.group;  // groups of one window
+    const int msz = c.bf16 ? 2 : 4;
+    MmaMaps maps;
+    const int nm = c.epilogue == 1 ? 2 : 1;
+    for (int q = 0; q < 2; ++q) {
+        const bool second = q == 1 && nm == 2;
+        const void *w = second ? c.w2 : c.w, *s = second ? c.s2 : c.s, *b = second ? c.b2 : c.b;
+        int rc = tensor_map_2d(&maps.w[q], w, 4, row_words, c.rows, 32, kTileRows, true);
+        if (rc == QMR_OK) rc = tensor_map_2d(&maps.s[q], s, msz, ngroups, c.rows, wg, kTileRows, false);
+        if (rc == QMR_OK) rc = tensor_map_2d(&maps.b[q], b, msz, ngroups, c.rows, wg, kTileRows, false);
         if (rc != QMR_OK) return rc;
     }
     MmaArgs a = {};
@@ -173,9 +178,9 @@ int QMR_MMA_LAUNCH(const FastCall &c, const MmaPlan &p, const ScratchView &sv, c
     a.off_bars = p.off_bars;
     a.zero = 0u;
     switch (c.epilogue) {
-        case 0: return launch_e<0>(m1, m2, a, p, c.bf16, c.group, c.batch, c.overlap, stream);
-        case 1: return launch_e<1>(m1, m2, a, p, c.bf16, c.group, c.batch, c.overlap, stream);
-        default: return launch_e<2>(m1, m2, a, p, c.bf16, c.group, c.batch, c.overlap, stream);
+        case 0: return launch_e<0>(maps, a, p, c.bf16, c.group, c.batch, c.overlap, stream);
+        case 1: return launch_e<1>(maps, a, p, c.bf16, c.group, c.batch, c.overlap, stream);
+        default: return launch_e<2>(maps, a, p, c.bf16, c.group, c.batch, c.overlap, stream);
     }
 }
 

@@ -161,7 +161,7 @@ constexpr size_t kMmaImageBudget = 96 * 1024;
 namespace {
 
 bool mma_plan_b(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint32_t batch, int epi, bool bf16,
-                int only_kc, MmaPlan *p);
+                int only_kc, int only_warps, MmaPlan *p);
 
 }  // namespace
 
@@ -171,15 +171,16 @@ bool mma_plan_b(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uin
 bool mma_plan(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint32_t batch, int epi, bool bf16,
               MmaPlan *p) {
     MmaPlan widest;
-    if (!mma_plan_b(bits, group, rows, cols, 4, epi, bf16, 0, &widest)) return false;
-    return mma_plan_b(bits, group, rows, cols, batch, epi, bf16, widest.kc, p);
+    if (!mma_plan_b(bits, group, rows, cols, 4, epi, bf16, 0, 0, &widest)) return false;
+    return mma_plan_b(bits, group, rows, cols, batch, epi, bf16, widest.kc, widest.warps, p);
 }
 
 namespace {
 
-// only_kc: 0 searches the slice count, otherwise the plan must use that one.
+// only_kc / only_warps: 0 searches the slice count / warps per CTA,
+// otherwise the plan must use that one.
 bool mma_plan_b(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint32_t batch, int epi, bool bf16,
-                int only_kc, MmaPlan *p) {
+                int only_kc, int only_warps, MmaPlan *p) {
     if (bits != 4 && bits != 8) return false;
     if (group != 32 && group != 64 && group != 128) return false;
     if (bits == 8 && group == 128) return false;
@@ -191,66 +192,75 @@ bool mma_plan_b(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uin
     const int nwin = (int)((cols + win_cols - 1) / win_cols);
     const int tiles = (int)((rows + kTileRows - 1) / kTileRows);
     const int nm = epi == 1 ? 2 : 1;
-    const int warps = kMmaWarps;
     const int sms = sm_count();
-    // Column slices (= cluster size): the smallest kc whose activation slice
-    // fits the image budget and whose whole plan (rings of at least two
-    // stages, image, table, pieces) fits the shared memory of one SM.  Two
-    // matrices per unit (the gate/up epilogue) double the ring slots, which
-    // can push a wide matrix from one slice to two.
-    const uint32_t piece_bytes = (uint32_t)nm * 64 * 4;
-    const uint32_t slot = (uint32_t)(mma_slot_weight_bytes((int)bits, (int)group, nm) +
-                                     mma_slot_meta_bytes((int)group, nm, bf16 ? 2 : 4));
-    const uint32_t ngroups_pad = (uint32_t)nwin * wg;
-    const uint32_t table = 32 * ngroups_pad;
-    const int limit = smem_optin() - 512;  // room for the kernel's static shared variables (under 300 bytes)
-    for (int kc : {1, 2, 4}) {
-        if (only_kc != 0 && kc != only_kc) continue;
-        const int nh_min = nwin / kc, nh_max = (nwin + kc - 1) / kc;
-        if (nwin < kc || sms < kc || (size_t)nh_max * win_cols * 16 > kMmaImageBudget) continue;
-        if (nh_max > 32) continue;  // image-window barriers and the per-warp ready mask
-        // One wave: no more clusters than can be resident together.
-        int clusters = sms / kc;
-        if (kc > 1) {
-            const int cap = mma_cluster_capacity(kc);
-            if (cap > 0 && cap < clusters) clusters = cap;
-        }
-        const int ctas = clusters * kc;
-        const int tmax = (tiles + clusters - 1) / clusters;
-        if ((long long)tmax * nh_max * warps >= (1ll << 31)) continue;  // 32-bit unit arithmetic
-        int pieces = 2;
-        if (kc > 1) {
-            const int lmax = (tmax * nh_max + warps - 1) / warps;
-            pieces = (lmax + nh_min - 1) / nh_min + 1;
-            if (pieces > kMaxPieces) continue;
-        }
-        const uint32_t image = (uint32_t)nh_max * win_cols * 4 * batch;
-        const uint32_t pieces_bytes = (uint32_t)warps * pieces * piece_bytes;
-        const uint32_t part_bytes = kc > 1 ? (uint32_t)((tmax + kc - 1) / kc * kc) * piece_bytes : 0u;
-        for (int st = kMmaMaxStages; st >= 2; --st) {
-            const uint32_t off_image = (uint32_t)warps * st * slot;
-            const uint32_t off_table = off_image + (image + 127) / 128 * 128;
-            const uint32_t off_pieces = off_table + (table + 127) / 128 * 128;
-            const uint32_t off_part = off_pieces + pieces_bytes;
-            const uint32_t off_bars = off_part + part_bytes;
-            const uint32_t total = 1024 + off_bars + (uint32_t)(warps * st + nh_max) * 8;
-            if ((int)total <= limit) {
-                p->kc = kc;
-                p->clusters = clusters;
-                p->ctas = ctas;
-                p->stages = st;
-                p->pieces = pieces;
-                p->nwin = nwin;
-                p->ngroups_pad = (int)ngroups_pad;
-                p->tiles = tiles;
-                p->warps = warps;
-                p->smem = total;
-                p->off_image = off_image;
-                p->off_table = off_table;
-                p->off_pieces = off_pieces;
-                p->off_part = off_part;
-                p->off_bars = off_bars;
-                return true;
+    // Warps per CTA: 12 for long Q4 streams (groups of 32 or 64), where the per-unit instruction
+    // latency of 8 warps (2 per scheduler) limits the rate; 8 otherwise, where
+    // the deeper rings that 8 warps leave room for matter more (they fill
+    // while the call waits for its activations).  Chosen from the shape only.
+    for (int warps : {kMmaWarpsLong, kMmaWarps}) {
+        if (only_warps != 0 && warps != only_warps) continue;
+        if (only_warps == 0 && warps == kMmaWarpsLong &&
+            (epi == 1 || bits != 4 || group > 64 || (long long)tiles * nwin < (long long)kLongUnitsPerCta * sms))
+            continue;
+        // Column slices (= cluster size): the smallest kc whose activation slice
+        // fits the image budget and whose whole plan (rings of at least two
+        // stages, image, table, pieces) fits the shared memory of one SM.  Two
+        // matrices per unit (the gate/up epilogue) double the ring slots, which
+        // can push a wide matrix from one slice to two.
+        const uint32_t piece_bytes = (uint32_t)nm * 64 * 4;
+        const uint32_t slot = (uint32_t)(mma_slot_weight_bytes((int)bits, (int)group, nm) +
+                                         mma_slot_meta_bytes((int)group, nm, bf16 ? 2 : 4));
+        const uint32_t ngroups_pad = (uint32_t)nwin * wg;
+        const uint32_t table = 32 * ngroups_pad;
+        const int limit = smem_optin() - 512;  // room for the kernel's static shared variables (under 300 bytes)
+        for (int kc : {1, 2, 4}) {
+            if (only_kc != 0 && kc != only_kc) continue;
+            const int nh_min = nwin / kc, nh_max = (nwin + kc - 1) / kc;
+            if (nwin < kc || sms < kc || (size_t)nh_max * win_cols * 16 > kMmaImageBudget) continue;
+            if (nh_max > 32) continue;  // image-window barriers and the per-warp ready mask
+            // One wave: no more clusters than can be resident together.
+            int clusters = sms / kc;
+            if (kc > 1) {
+                const int cap = mma_cluster_capacity(kc);
+                if (cap > 0 && cap < clusters) clusters = cap;
+            }
+            const int ctas = clusters * kc;
+            const int tmax = (tiles + clusters - 1) / clusters;
+            if ((long long)tmax * nh_max * warps >= (1ll << 31)) continue;  // 32-bit unit arithmetic
+            int pieces = 2;
+            if (kc > 1) {
+                const int lmax = (tmax * nh_max + warps - 1) / warps;
+                pieces = (lmax + nh_min - 1) / nh_min + 1;
+                if (pieces > kMaxPieces) continue;
+            }
+            const uint32_t image = (uint32_t)nh_max * win_cols * 4 * batch;
+            const uint32_t pieces_bytes = (uint32_t)warps * pieces * piece_bytes;
+            const uint32_t part_bytes = kc > 1 ? (uint32_t)((tmax + kc - 1) / kc * kc) * piece_bytes : 0u;
+            for (int st = kMmaMaxStages; st >= 2; --st) {
+                const uint32_t off_image = (uint32_t)warps * st * slot;
+                const uint32_t off_table = off_image + (image + 127) / 128 * 128;
+                const uint32_t off_pieces = off_table + (table + 127) / 128 * 128;
+                const uint32_t off_part = off_pieces + pieces_bytes;
+                const uint32_t off_bars = off_part + part_bytes;
+                const uint32_t total = 1024 + off_bars + (uint32_t)(warps * st + nh_max) * 8;
+                if ((int)total <= limit) {
+                    p->kc = kc;
+                    p->clusters = clusters;
+                    p->ctas = ctas;
+                    p->stages = st;
+                    p->pieces = pieces;
+                    p->nwin = nwin;
+                    p->ngroups_pad = (int)ngroups_pad;
+                    p->tiles = tiles;
+                    p->warps = warps;
+                    p->smem = total;
+                    p->off_image = off_image;
+                    p->off_table = off_table;
+                    p->off_pieces = off_pieces;
+                    p->off_part = off_part;
+                    p->off_bars = off_bars;
+                    return true;
+                }
             }
         }
     }

@@ -64,6 +64,8 @@
 namespace qmr {
 
 constexpr int kMmaWarps = 8;     // warps per CTA, each with its own copy ring
+constexpr int kMmaWarpsLong = 12;  // warps per CTA for long streams (shallower rings, more issue slots)
+constexpr int kLongUnitsPerCta = 128;  // (tile, window) units per CTA from which the long plan is tried
 constexpr int kTileRows = 16;    // rows of one MMA tile
 constexpr int kMaxPieces = 4;    // tile pieces one warp may leave in shared memory
 constexpr int kMmaMaxStages = 6;
@@ -86,8 +88,8 @@ struct MmaShape {
 
 // Bytes of one ring slot: the weights of NM matrices (a multiple of 2 KiB, so
 // every slot stays 1024-byte aligned for the swizzle) and, in a separate
-// region, their metadata (32 lanes x the window's groups of one
-// (row, scale|bias) each).
+// region, their metadata: per matrix a scale box then a bias box, each
+// [16 rows][the window's groups].
 __host__ __device__ constexpr int mma_slot_weight_bytes(int bits, int group, int nm) {
     return nm * kTileRows * (8 * group > 512 ? 8 * group : 512) * bits / 8;
 }
@@ -393,15 +395,22 @@ struct MmaArgs {
     uint32_t off_image, off_table, off_pieces, off_part, off_bars;  // offsets into the 1024-aligned dynamic smem
 };
 
+// Tensor maps of the (up to two) matrices of a call: packed weights (boxes
+// of 32 words x 16 rows, 128-byte swizzle), scales and biases (boxes of one
+// window's groups x 16 rows).
+struct MmaMaps {
+    CUtensorMap w[2], s[2], b[2];
+};
+
 template <int BITS, int G, int B, bool BF16, int EPI, int NW>
 __global__ void __launch_bounds__(32 * NW, 1)
-    mma_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap wmap2, const MmaArgs a) {
+    mma_kernel(const __grid_constant__ MmaMaps maps, const MmaArgs a) {
     using S = MmaShape<BITS, G>;
     constexpr int NM = (EPI == 1) ? 2 : 1;
     constexpr int NB = 2 * B;
     constexpr int MSZ = BF16 ? 2 : 4;
-    constexpr int META_LANE = S::WG * MSZ;
-    constexpr int META_BYTES = 32 * META_LANE;
+    constexpr int META_ROW = S::WG * MSZ;  // bytes of one row of a scale or bias box
+    constexpr int META_BYTES = 32 * META_ROW;
     constexpr int SLOT_W = mma_slot_weight_bytes(BITS, G, NM);
     constexpr int SLOT_M = mma_slot_meta_bytes(G, NM, MSZ);
     constexpr int GPB = 128 / S::GROUP_BYTES;  // groups per 128-byte line of a box
@@ -418,8 +427,12 @@ __global__ void __launch_bounds__(32 * NW, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gq = lane >> 2, t = lane & 3;
     if (threadIdx.x == 0) {
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap)) : "memory");
-        if (NM == 2) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&wmap2)) : "memory");
+#pragma unroll
+        for (int q = 0; q < NM; ++q) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.w[q])) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.s[q])) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.b[q])) : "memory");
+        }
     }
     const int nst = a.stages;
     const uint32_t ring_w = sbase + (uint32_t)(warp * nst * SLOT_W);
@@ -449,55 +462,30 @@ __global__ void __launch_bounds__(32 * NW, 1)
     const uint64_t pol_stream = evict_first_policy();
     const uint64_t pol_keep = evict_normal_policy();
 
-    // Metadata source of this lane (row 2r + kind of a unit's 16 rows) for the
-    // CTA's first tile and the slice's first window.
-    const int mrow = lane >> 1, mkind = lane & 1;
-    const unsigned char *msrc[NM];
-#pragma unroll
-    for (int q = 0; q < NM; ++q) {
-        const unsigned char *base = mkind ? (q ? a.b2 : a.b) : (q ? a.s2 : a.s);
-        msrc[q] = base + ((size_t)(t0 * kTileRows + mrow) * a.ngroups + (size_t)win0 * S::WG) * MSZ;
-    }
-
-    // Issue unit (local tile tl, window wi of the slice) into ring slot sl.
+    // Issue unit (local tile tl, window wi of the slice) into ring slot sl:
+    // one elected lane copies the weight boxes and the scale and bias boxes
+    // [16 rows][window groups] of every matrix, all completing on the slot's
+    // barrier.  Rows past the matrix and groups past the row arrive as zeros.
     auto issue = [&](int tl, int wi, int sl) {
-        const int T = t0 + tl;
-        const uint32_t slot = ring_w + (uint32_t)(sl * SLOT_W);
-        const uint32_t mslot = ring_m + (uint32_t)(sl * SLOT_M);
-        uint64_t *bar = &full[sl];
         if (lane == 0) {
-            mbar_arrive_expect_tx(bar, SLOT_W);
+            const int T = t0 + tl;
+            const uint32_t slot = ring_w + (uint32_t)(sl * SLOT_W);
+            const uint32_t mslot = ring_m + (uint32_t)(sl * SLOT_M);
+            uint64_t *bar = &full[sl];
+            mbar_arrive_expect_tx(bar, SLOT_W + SLOT_M);
 #pragma unroll
-            for (int q = 0; q < NM; ++q)
+            for (int q = 0; q < NM; ++q) {
 #pragma unroll
                 for (int c = 0; c < S::NBOX; ++c)
-                    tma_load_2d_s(slot + q * S::W_BYTES + c * 2048, q ? &wmap2 : &wmap,
-                                  (win0 + wi) * S::ROW_WORDS + c * 32, T * kTileRows, bar, pol_stream);
-        }
-        __syncwarp();
-        const int row = T * kTileRows + mrow;
-        const int gbeg = (win0 + wi) * S::WG;
-        const size_t moff = ((size_t)tl * kTileRows * a.ngroups + (size_t)wi * S::WG) * MSZ;
-        const bool inside = row < a.rows && gbeg + S::WG <= a.ngroups;
-#pragma unroll
-        for (int q = 0; q < NM; ++q) {
-            const uint32_t dst = mslot + (uint32_t)(q * META_BYTES + lane * META_LANE);
-            if (inside) {
-#pragma unroll
-                for (int p = 0; p < META_LANE / 16; ++p) cp_async16_s(dst + 16 * p, msrc[q] + moff + 16 * p, 16u);
-            } else {
-                // Rows past the matrix and groups past the row read nothing.
-                int valid = row < a.rows ? (a.ngroups - gbeg) * MSZ : 0;
-                valid = valid < 0 ? 0 : (valid > META_LANE ? META_LANE : valid);
-#pragma unroll
-                for (int p = 0; p < META_LANE / 16; ++p) {
-                    const int n = valid - 16 * p;
-                    const unsigned char *src = n > 0 ? msrc[q] + moff + 16 * p : (q ? a.s2 : a.s);
-                    cp_async16_s(dst + 16 * p, src, n <= 0 ? 0u : (n > 16 ? 16u : (uint32_t)n));
-                }
+                    tma_load_2d_s(slot + q * S::W_BYTES + c * 2048, &maps.w[q], (win0 + wi) * S::ROW_WORDS + c * 32,
+                                  T * kTileRows, bar, pol_stream);
+                tma_load_2d_s(mslot + q * META_BYTES, &maps.s[q], (win0 + wi) * S::WG, T * kTileRows, bar,
+                              pol_stream);
+                tma_load_2d_s(mslot + q * META_BYTES + 16 * META_ROW, &maps.b[q], (win0 + wi) * S::WG,
+                              T * kTileRows, bar, pol_stream);
             }
         }
-        cp_async_commit();  // one cp.async group per unit
+        __syncwarp();
     };
 
     // Issue cursor: unit `issued` = (local tile it, window iw), ring slot is_.
@@ -544,7 +532,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
     const int n = gq < NB ? gq : NB - 1;
     const uint32_t x_lane = sbase + a.off_image + (uint32_t)((n * 4 + t) * 16);
     const uint32_t t_lane = sbase + a.off_table + (uint32_t)(t * a.ngroups_pad * 8);
-    const uint32_t m_lane = (uint32_t)(2 * gq * META_LANE);
+    const uint32_t m_lane = (uint32_t)(gq * META_ROW);  // row gq of the scale box
     const uint32_t piece_base = sbase + a.off_pieces + (uint32_t)(warp * a.pieces * PIECE);
 
     unsigned long long best = 0ull;
@@ -590,11 +578,6 @@ __global__ void __launch_bounds__(32 * NW, 1)
             if (lane == 0) atomicCAS(a.err, 0u, kErrTimeoutFull);
             break;
         }
-        // This unit's metadata group is complete once at most the groups of
-        // the units issued after it are pending; the warp barrier makes every
-        // lane's copies visible to the warp.
-        cp_async_wait_pending(issued - u - 1u);
-        __syncwarp();
         const uint32_t wslot = ring_w + (uint32_t)(cur * SLOT_W);
         const uint32_t mw = ring_m + (uint32_t)(cur * SLOT_M) + m_lane;
         // Stage the unit's weight words and metadata in registers, then hand
@@ -613,7 +596,9 @@ __global__ void __launch_bounds__(32 * NW, 1)
 #pragma unroll
             for (int pr = 0; pr < S::WG / 2; ++pr) {
                 const uint32_t mq = mw + (uint32_t)(q * META_BYTES + 2 * pr * MSZ);
-                const uint32_t offs[4] = {0u, (uint32_t)META_LANE, (uint32_t)(16 * META_LANE), (uint32_t)(17 * META_LANE)};
+                // scale and bias of row gq, scale and bias of row gq + 8
+                const uint32_t offs[4] = {0u, (uint32_t)(16 * META_ROW), (uint32_t)(8 * META_ROW),
+                                          (uint32_t)(24 * META_ROW)};
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                     if constexpr (BF16) {
@@ -734,7 +719,6 @@ __global__ void __launch_bounds__(32 * NW, 1)
         ++u;
         if (++wi == nh) wi = 0, ++tl;
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");  // no metadata copy outlives the CTA
     // Drain copies issued but not consumed (only after a failed wait).
     for (uint32_t d = u; d < issued; ++d) {
         const uint32_t j = d - ua;

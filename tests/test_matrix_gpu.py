@@ -515,7 +515,8 @@ def test_all_streaming_paths_meet_the_bound(cuda, bits, meta):
     oracle bound on every shape, and
     within each path a B-wide block equals B single-RHS calls bit for bit.
     Also checks that no bounded device wait ran out."""
-    shapes = [(17408, 5120), (5120, 17408), (4, 512), (37, 2176), (1000, 3072), (300, 1024)]
+    # 40008 x 5120 has enough (tile, window) units for the 12-warp plan (Q4).
+    shapes = [(17408, 5120), (5120, 17408), (4, 512), (37, 2176), (1000, 3072), (300, 1024), (40008, 5120)]
     try:
         for rows, cols in shapes:
             mat = synth.affine_matrix(rows, cols, bits, 64, seed=rows + cols, meta=meta)
