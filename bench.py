@@ -81,14 +81,17 @@ def load_peaks():
     return 6650.0, "fallback"
 
 
-def profile_traffic(kernel_tag):
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
-    p = ROOT / "profiles" / "traffic.json"
+def profile_traffic(workload):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu
+    summaries (profiles/traffic.txt: `workload bytes` lines), or None."""
+    p = ROOT / "profiles" / "traffic.txt"
     if not p.exists():
         return None
-    d = json.loads(p.read_text())
-    v = d.get(kernel_tag)
-    return None if v is None else float(v)
+    for line in p.read_text().splitlines():
+        parts = line.split()
+        if len(parts) == 2 and not line.startswith("#") and parts[0] == workload:
+            return float(parts[1])
+    return None
 
 
 class Clocks:
