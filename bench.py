@@ -225,7 +225,7 @@ def sharded(name, world):
 
 
 class Workload:
-    def __init__(self, name, spec, device, seed, world=1, rank=0):
+    def __init__(self, name, spec, device, seed, world=1, rank=0, exchange="p2p"):
         import torch
 
         from qmr import synth
@@ -234,6 +234,7 @@ class Workload:
         bits, b = spec["bits"], spec["batch"]
         self.batch = b
         self.sharded = sharded(name, world)
+        self.exchange = exchange
         if self.sharded:
             self._init_sharded(world, rank, seed)
             return
@@ -297,15 +298,16 @@ class Workload:
             d0 = dev_matrix(h1 - h0, ROWS, s + 12)
             per_copy = g0.nbytes + u0.nbytes + d0.nbytes
             self.copies = max(2, math.ceil(4 * l2 / per_copy) + 1)
-            self.mods = [parallel.ShardedMLP(clone(g0), clone(u0), clone(d0), COLS, ROWS, qmr.ops)
-                         for _ in range(self.copies)]
+            self.mods = [parallel.ShardedMLP(clone(g0), clone(u0), clone(d0), COLS, ROWS, qmr.ops,
+                                             exchange=self.exchange) for _ in range(self.copies)]
             self.y = torch.empty(b * COLS, dtype=torch.float32, device=dev)
             self.launches_per_step = 2
         else:
             v0, v1 = parallel.shard_range(VOCAB, world, rank)
             h = dev_matrix(v1 - v0, COLS, s + 10)
             self.copies = max(2, math.ceil(4 * l2 / h.nbytes) + 1)
-            self.mods = [parallel.ShardedHead(clone(h), VOCAB, v0, qmr.ops) for _ in range(self.copies)]
+            self.mods = [parallel.ShardedHead(clone(h), VOCAB, v0, qmr.ops, exchange=self.exchange)
+                         for _ in range(self.copies)]
             self.y = torch.empty(b * (v1 - v0), dtype=torch.float32, device=dev)
             self.idx = torch.empty(b, dtype=torch.int32, device=dev)
             self.launches_per_step = 1
@@ -375,7 +377,7 @@ def run_gpu(args):
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
     qmr.ops.init(local)
     spec = workload_spec(args.workload)
-    wl = Workload(args.workload, spec, device, seed=1000 + 17 * rank, world=world, rank=rank)
+    wl = Workload(args.workload, spec, device, seed=1000 + 17 * rank, world=world, rank=rank, exchange=args.exchange)
     nbytes = algorithmic_bytes(args.workload, spec)
     # Replicas: every rank processes nbytes per step.  Shards: the ranks
     # together process one model's nbytes per step.
@@ -480,7 +482,7 @@ def run_gpu(args):
     else:
         # per GPU: its share of the job's bytes over the step time
         achieved = job_factor * nbytes / world / (ms_per_step * 1e-3) / 1e9
-        timing_note = "whole call" + (", sharded step incl. NCCL all-gathers" if wl.sharded else "")
+        timing_note = "whole call" + (f", sharded step incl. the {wl.exchange} exchange" if wl.sharded else "")
     traffic = profile_traffic(args.workload)
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -491,7 +493,8 @@ def run_gpu(args):
                    "bits": spec["bits"], "group": GROUP, "metadata": "bf16", "weight_copies": wl.copies,
                    "l2_bytes": wl.l2, "l2_policy": f"{wl.copies} distinct weight copies rotated (> 4x L2)",
                    "bytes_per_step": nbytes,
-                   "parallelism": (f"rowshard{world} (NCCL all-gather)" if wl.sharded else
+                   "parallelism": (f"rowshard{world} ({'peer-memory exchange in the kernels' if wl.exchange == 'p2p' else 'NCCL all-gather'})"
+                                   if wl.sharded else
                                    f"replicas{world}" if world > 1 else "single")},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "steps": e2e_steps},
@@ -524,6 +527,9 @@ def run_gpu(args):
         import gc
         gc.collect()
         torch.cuda.synchronize()
+        if wl.sharded:
+            for m in wl.mods:
+                m.close()
         dist.barrier()
         dist.destroy_process_group()
     return 0
@@ -537,6 +543,8 @@ def main():
     ap.add_argument("--impl", default="qmr", choices=["qmr", "reference"])
     ap.add_argument("--workload", default="b3", choices=["b3", "b1", "q8b3", "mlp", "head"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="sharded workloads: output exchange over peer memory in the kernels, or NCCL all-gathers")
     ap.add_argument("--quick", action="store_true",
                     help="profiling runs: no clock-sampling loop, short e2e, no CPU baseline")
     args = ap.parse_args()

@@ -246,6 +246,67 @@ int qmr_device_error(int *code, int clear);
  * report a device error as QMR_ECUDA (Gpu::finish, src/gpu.rs:849-876). */
 int qmr_stream_sync(void *stream);
 
+/* ---- sharded calls with the output exchange over peer memory -------------
+ * No single reference counterpart: the reference runs on one GPU.  These
+ * carry the row-sharded MLP (gate/up and down split by output rows,
+ * src/engine.rs:755-763 on n GPUs) and the vocabulary-sharded head
+ * (src/engine.rs:777-780 + src/chat.rs:383-390) of the multi-GPU plan: one
+ * process per GPU, each rank computing a contiguous block of output rows.
+ * The streaming kernel itself stores every finished output row into every
+ * rank's full output buffer (peer stores over NVLink through CUDA IPC
+ * mappings; no multicast), and its last CTA publishes an epoch to every
+ * rank's flag array.  qmr_exchange_wait, enqueued before the consumer,
+ * waits (bounded, 2 s; QMR device error 4 on timeout) until every rank has
+ * published the same epoch.  The head exchanges only its per-RHS argmax keys
+ * and qmr_exchange_wait merges them (highest logit under f32 total order,
+ * ties to the lowest vocabulary index), the single-GPU rule.
+ *
+ * Buffers come from qmr_exchange_alloc (zeroed device memory whose base is
+ * an IPC allocation); every rank shares qmr_ipc_handle of each and maps the
+ * peers' with qmr_ipc_open.  Exchanges on one QmrExchange must be issued by
+ * every rank in the same order; a rank may reuse an output buffer only after
+ * its own qmr_exchange_wait of the exchange after next (double-buffer the
+ * outputs to overlap steps). */
+#define QMR_MAX_RANKS 8
+#define QMR_IPC_HANDLE_BYTES 64
+
+typedef struct QmrExchange {
+    uint32_t world;                      /* ranks, 2..QMR_MAX_RANKS */
+    uint32_t rank;                       /* this rank */
+    uint32_t total_rows;                 /* rows of the full output (the row stride per RHS) */
+    uint32_t row_base;                   /* first output row of this rank's shard */
+    float *out[QMR_MAX_RANKS];           /* every rank's full output [batch][total_rows]; NULL for the head */
+    uint32_t *flags[QMR_MAX_RANKS];      /* every rank's flag array [world] (epoch per source rank) */
+    uint64_t *keys[QMR_MAX_RANKS];       /* head: every rank's key array [world][4]; else NULL */
+    uint32_t *epoch;                     /* this rank's exchange counter (zeroed device word) */
+} QmrExchange;
+
+int qmr_exchange_alloc(size_t bytes, void **dev_ptr);
+int qmr_exchange_free(void *dev_ptr);
+int qmr_ipc_handle(const void *dev_ptr, void *handle /* QMR_IPC_HANDLE_BYTES */);
+int qmr_ipc_open(const void *handle, void **dev_ptr);
+int qmr_ipc_close(void *dev_ptr);
+
+/* qmr_matmul_affine / qmr_gateup_swiglu on this rank's rows (the matrices
+ * are the shards: `rows` rows starting at ex->row_base of the full output),
+ * writing the full outputs of all ranks.  Tensor-core path only
+ * (QMR_EUNSUPPORTED for shapes it does not take). */
+int qmr_matmul_affine_exchange(const void *w, const void *scales, const void *biases, const float *x,
+                               uint32_t rows, uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch,
+                               int meta_bf16, const QmrExchange *ex, void *stream);
+int qmr_gateup_swiglu_exchange(const void *w_gate, const void *s_gate, const void *b_gate,
+                               const void *w_up, const void *s_up, const void *b_up, const float *x,
+                               uint32_t rows, uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch,
+                               int meta_bf16, const QmrExchange *ex, void *stream);
+/* The vocabulary shard's logits stay local (logits [batch][rows]); the
+ * shard's best key per RHS goes to every rank. */
+int qmr_head_argmax_exchange(const void *w, const void *scales, const void *biases, const float *x,
+                             float *logits, uint32_t rows, uint32_t cols, uint32_t bits, uint32_t group,
+                             uint32_t batch, int meta_bf16, const QmrExchange *ex, void *stream);
+/* Wait for every rank's current exchange; for the head also write the
+ * merged argmax (token ids, may be NULL) and keys (may be NULL) per RHS. */
+int qmr_exchange_wait(const QmrExchange *ex, uint32_t batch, int32_t *argmax, uint64_t *best_key, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

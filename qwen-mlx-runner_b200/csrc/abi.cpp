@@ -927,4 +927,148 @@ int qmr_stream_sync(void *stream) {
     return check_cuda(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "stream synchronize");
 }
 
+// ---- sharded calls with the output exchange over peer memory -------------
+
+int qmr_exchange_alloc(size_t bytes, void **dev_ptr) {
+    if (dev_ptr == nullptr || bytes == 0) return fail(QMR_EINVAL, "qmr_exchange_alloc needs a size and an out pointer");
+    *dev_ptr = nullptr;
+    void *p = nullptr;
+    int rc = check_cuda(cudaMalloc(&p, bytes), "exchange buffer allocation");
+    if (rc != QMR_OK) return rc;
+    rc = check_cuda(cudaMemset(p, 0, bytes), "exchange buffer clear");
+    if (rc != QMR_OK) {
+        cudaFree(p);
+        return rc;
+    }
+    *dev_ptr = p;
+    return QMR_OK;
+}
+
+int qmr_exchange_free(void *dev_ptr) { return check_cuda(cudaFree(dev_ptr), "exchange buffer free"); }
+
+int qmr_ipc_handle(const void *dev_ptr, void *handle) {
+    static_assert(sizeof(cudaIpcMemHandle_t) == QMR_IPC_HANDLE_BYTES, "IPC handle size");
+    if (dev_ptr == nullptr || handle == nullptr) return fail(QMR_EINVAL, "qmr_ipc_handle: null pointer");
+    cudaIpcMemHandle_t h;
+    const int rc = check_cuda(cudaIpcGetMemHandle(&h, const_cast<void *>(dev_ptr)), "cudaIpcGetMemHandle");
+    if (rc != QMR_OK) return rc;
+    memcpy(handle, &h, sizeof(h));
+    return QMR_OK;
+}
+
+int qmr_ipc_open(const void *handle, void **dev_ptr) {
+    if (dev_ptr == nullptr || handle == nullptr) return fail(QMR_EINVAL, "qmr_ipc_open: null pointer");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    return check_cuda(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+}
+
+int qmr_ipc_close(void *dev_ptr) { return check_cuda(cudaIpcCloseMemHandle(dev_ptr), "cudaIpcCloseMemHandle"); }
+
+static int check_exchange(const QmrExchange *ex, bool head) {
+    if (ex == nullptr) return fail(QMR_EINVAL, "null exchange");
+    if (ex->world < 2 || ex->world > QMR_MAX_RANKS || ex->rank >= ex->world)
+        return fail(QMR_EINVAL, "exchange needs 2..%d ranks and rank < world", QMR_MAX_RANKS);
+    if (ex->epoch == nullptr) return fail(QMR_EINVAL, "exchange epoch word is null");
+    for (uint32_t p = 0; p < ex->world; ++p) {
+        if (ex->flags[p] == nullptr) return fail(QMR_EINVAL, "exchange flags of rank %u are null", p);
+        if (head ? ex->keys[p] == nullptr : ex->out[p] == nullptr)
+            return fail(QMR_EINVAL, "exchange %s of rank %u are null", head ? "keys" : "outputs", p);
+    }
+    return QMR_OK;
+}
+
+int qmr_matmul_affine_exchange(const void *w, const void *scales, const void *biases, const float *x, uint32_t rows,
+                               uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch, int meta_bf16,
+                               const QmrExchange *ex, void *stream) {
+    int rc = typed_fast_check(w, rows, cols, bits, group, batch, meta_bf16, "qmr_matmul_affine_exchange");
+    if (rc == QMR_OK) rc = check_exchange(ex, false);
+    if (rc != QMR_OK) return rc;
+    if ((uint64_t)ex->row_base + rows > ex->total_rows) return fail(QMR_ERANGE, "shard rows exceed the full output");
+    FastCall c = {};
+    c.w = w;
+    c.s = scales;
+    c.b = biases;
+    c.x = x;
+    c.y = ex->out[ex->rank] + ex->row_base;
+    c.ystride = ex->total_rows;
+    c.rows = rows;
+    c.cols = cols;
+    c.bits = bits;
+    c.group = group;
+    c.batch = batch;
+    c.bf16 = meta_bf16 != 0;
+    c.epilogue = 0;
+    c.path = kPathMma;
+    c.ex = ex;
+    return run_fast(c, static_cast<cudaStream_t>(stream));
+}
+
+int qmr_gateup_swiglu_exchange(const void *w_gate, const void *s_gate, const void *b_gate, const void *w_up,
+                               const void *s_up, const void *b_up, const float *x, uint32_t rows, uint32_t cols,
+                               uint32_t bits, uint32_t group, uint32_t batch, int meta_bf16, const QmrExchange *ex,
+                               void *stream) {
+    int rc = typed_fast_check(w_gate, rows, cols, bits, group, batch, meta_bf16, "qmr_gateup_swiglu_exchange");
+    if (rc == QMR_OK && !fast_eligible(w_up, cols, bits, group))
+        rc = fail(QMR_EALIGN, "qmr_gateup_swiglu_exchange needs 16-byte aligned up weights");
+    if (rc == QMR_OK) rc = check_exchange(ex, false);
+    if (rc != QMR_OK) return rc;
+    if ((uint64_t)ex->row_base + rows > ex->total_rows) return fail(QMR_ERANGE, "shard rows exceed the full output");
+    FastCall c = {};
+    c.w = w_gate;
+    c.s = s_gate;
+    c.b = b_gate;
+    c.w2 = w_up;
+    c.s2 = s_up;
+    c.b2 = b_up;
+    c.x = x;
+    c.y = ex->out[ex->rank] + ex->row_base;
+    c.ystride = ex->total_rows;
+    c.rows = rows;
+    c.cols = cols;
+    c.bits = bits;
+    c.group = group;
+    c.batch = batch;
+    c.bf16 = meta_bf16 != 0;
+    c.epilogue = 1;
+    c.path = kPathMma;
+    c.ex = ex;
+    return run_fast(c, static_cast<cudaStream_t>(stream));
+}
+
+int qmr_head_argmax_exchange(const void *w, const void *scales, const void *biases, const float *x, float *logits,
+                             uint32_t rows, uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch,
+                             int meta_bf16, const QmrExchange *ex, void *stream) {
+    int rc = typed_fast_check(w, rows, cols, bits, group, batch, meta_bf16, "qmr_head_argmax_exchange");
+    if (rc == QMR_OK) rc = check_exchange(ex, true);
+    if (rc != QMR_OK) return rc;
+    if ((uint64_t)ex->row_base + rows > 0xffffffffull) return fail(QMR_ERANGE, "row_base + rows exceeds u32 token ids");
+    FastCall c = {};
+    c.w = w;
+    c.s = scales;
+    c.b = biases;
+    c.x = x;
+    c.y = logits;
+    c.rows = rows;
+    c.cols = cols;
+    c.bits = bits;
+    c.group = group;
+    c.batch = batch;
+    c.row_base = ex->row_base;
+    c.bf16 = meta_bf16 != 0;
+    c.epilogue = 2;
+    c.path = kPathMma;
+    c.ex = ex;
+    return run_fast(c, static_cast<cudaStream_t>(stream));
+}
+
+int qmr_exchange_wait(const QmrExchange *ex, uint32_t batch, int32_t *argmax, uint64_t *best_key, void *stream) {
+    const bool head = ex != nullptr && ex->keys[0] != nullptr;
+    int rc = check_exchange(ex, head);
+    if (rc != QMR_OK) return rc;
+    if (batch < 1 || batch > 4) return fail(QMR_EINVAL, "Matrix blocks support one through four RHS");
+    return launch_exchange_wait(*ex, batch, head ? argmax : nullptr, head ? best_key : nullptr,
+                                static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -163,8 +163,19 @@ int QMR_MMA_LAUNCH(const FastCall &c, const MmaPlan &p, const ScratchView &sv, c
     a.rows = (int)c.rows;
     a.ngroups = (int)(c.cols / c.group);
     a.ngroups_pad = p.ngroups_pad;
-    a.ystride = (int)c.rows;
+    a.ystride = (int)(c.ystride != 0 ? c.ystride : c.rows);
     a.row_base = (int)c.row_base;
+    if (c.ex != nullptr) {
+        const QmrExchange &ex = *c.ex;
+        a.xworld = (int)ex.world;
+        a.xrank = (int)ex.rank;
+        a.xepoch = ex.epoch;
+        for (uint32_t p = 0; p < ex.world; ++p) {
+            a.xflags[p] = ex.flags[p];
+            a.xkeys[p] = reinterpret_cast<unsigned long long *>(ex.keys[p]);
+            a.peer_y[p] = c.epilogue == 2 ? nullptr : ex.out[p] + ex.row_base;
+        }
+    }
     a.tiles = p.tiles;
     a.nwin = p.nwin;
     a.kc = p.kc;
@@ -185,6 +196,56 @@ int QMR_MMA_LAUNCH(const FastCall &c, const MmaPlan &p, const ScratchView &sv, c
 }
 
 #if QMR_MMA_BITS == 4
+// Waits (one warp) until every rank has published this rank's current
+// exchange epoch, then, for the head, merges the ranks' keys per RHS: the
+// unsigned maximum is the highest logit under f32 total order with ties to
+// the lowest index.  Bounded: after kWaitLimitNs it records kErrTimeoutPeer
+// and returns.
+__global__ void __launch_bounds__(32) exchange_wait_kernel(const unsigned int *flags, const unsigned int *epoch,
+                                                           int world, const unsigned long long *keys, int batch,
+                                                           int *argmax, unsigned long long *best_key,
+                                                           unsigned int *err) {
+    const int lane = threadIdx.x;
+    const unsigned int e = *epoch;
+    bool ok = true;
+    if (lane < world) {
+        const unsigned long long start = global_ns();
+        for (;;) {
+            unsigned int f;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(flags + lane) : "memory");
+            if ((int)(f - e) >= 0) break;
+            if (global_ns() - start > kWaitLimitNs) {
+                ok = false;
+                atomicCAS(err, 0u, kErrTimeoutPeer);
+                break;
+            }
+            __nanosleep(200);
+        }
+    }
+    if (!__all_sync(0xffffffffu, ok) || keys == nullptr || lane >= batch) return;
+    unsigned long long k = 0ull;
+    for (int r = 0; r < world; ++r) {
+        unsigned long long v;
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(keys + r * 4 + lane) : "memory");
+        k = v > k ? v : k;
+    }
+    if (argmax) argmax[lane] = (int)(0xffffffffu - (uint32_t)(k & 0xffffffffu));
+    if (best_key) best_key[lane] = k;
+}
+
+int launch_exchange_wait(const QmrExchange &ex, uint32_t batch, int32_t *argmax, uint64_t *best_key,
+                         cudaStream_t stream) {
+    unsigned int *err = device_error_word();
+    if (err == nullptr) return fail(QMR_ECUDA, "device error word is unavailable");
+    exchange_wait_kernel<<<1, 32, 0, stream>>>(ex.flags[ex.rank], ex.epoch, (int)ex.world,
+                                               reinterpret_cast<const unsigned long long *>(ex.keys[ex.rank]),
+                                               (int)batch, argmax, reinterpret_cast<unsigned long long *>(best_key),
+                                               err);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(QMR_ECUDA, "exchange wait launch failed: %s", cudaGetErrorString(e));
+    return QMR_OK;
+}
+
 // How many clusters of kc CTAs can be resident at once.  Every plan holds
 // more than half of an SM's shared memory (one CTA per SM), so the answer
 // depends only on kc and on how the SMs group into GPCs: 148 SMs do not

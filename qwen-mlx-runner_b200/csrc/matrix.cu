@@ -6,6 +6,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -276,9 +277,13 @@ int log2i(uint32_t v) {
 }
 
 int sm_count() {
+    static std::atomic<int> cached[64] = {};
     int dev = 0, n = 0;
-    cudaGetDevice(&dev);
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    n = cached[dev].load(std::memory_order_relaxed);
+    if (n > 0) return n;
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cached[dev].store(n, std::memory_order_relaxed);
     return n;
 }
 
@@ -379,7 +384,25 @@ int run_fast(const FastCall &c, cudaStream_t stream) {
     }
     FastCall call = c;
     MmaPlan plan;
+    if (call.ex != nullptr) {
+        // The output exchange lives in the tensor-core kernel's epilogue.
+        call.path = kPathMma;
+        if (!mma_takes(call, &plan))
+            return fail(QMR_EUNSUPPORTED, "the exchange calls need a shape the tensor-core kernel takes");
+    }
     if (call.path == kPathMma && !mma_takes(call, &plan)) call.path = kPathTile;  // FP32 kernels take the rest
+    if (call.path == kPathMma) {
+        // Prep kernel, then the streaming kernel behind it (programmatic
+        // dependent launch: the prep writes no weights), one plan for both.
+        ScratchView sv;
+        MmaImageView mv;
+        scratch_layout(base, (int)call.bits, call.cols, call.batch, &sv, &mv);
+        const int rc = launch_mma_prep_bits((int)call.bits, call.x, call.cols, call.group, call.batch,
+                                            plan.ngroups_pad, mv, stream);
+        if (rc != QMR_OK) return rc;
+        call.overlap = true;
+        return call.bits == 4 ? launch_mma4(call, plan, sv, mv, stream) : launch_mma8(call, plan, sv, mv, stream);
+    }
     const int rc = run_prepare(call.x, call.cols, call.bits, call.group, call.batch, base, call.path, stream);
     if (rc != QMR_OK) return rc;
     call.overlap = true;  // the preceding kernel is our prep, which writes no weights

@@ -69,6 +69,7 @@ constexpr int kLongUnitsPerCta = 128;  // (tile, window) units per CTA from whic
 constexpr int kTileRows = 16;    // rows of one MMA tile
 constexpr int kMaxPieces = 4;    // tile pieces one warp may leave in shared memory
 constexpr int kMmaMaxStages = 6;
+constexpr int kMaxRanks = 8;     // ranks of an output exchange over peer memory
 
 template <int BITS, int G>
 struct MmaShape {
@@ -393,6 +394,15 @@ struct MmaArgs {
     int tiles, nwin, kc, clusters, pieces, stages;
     uint32_t zero;                         // always 0 (an opaque operand, see the slot refill)
     uint32_t off_image, off_table, off_pieces, off_part, off_bars;  // offsets into the 1024-aligned dynamic smem
+    // Output exchange over peer memory (xworld > 1): rows also go to every
+    // rank's output (peer_y, same index as y; not for EPI 2, whose keys go to
+    // xkeys instead), then the last CTA publishes ++*xepoch to every rank's
+    // flag array at index xrank.
+    float *peer_y[kMaxRanks];
+    unsigned int *xflags[kMaxRanks];
+    unsigned long long *xkeys[kMaxRanks];  // [world][4] per rank
+    unsigned int *xepoch;
+    int xworld, xrank;
 };
 
 // Tensor maps of the (up to two) matrices of a call: packed weights (boxes
@@ -545,7 +555,12 @@ __global__ void __launch_bounds__(32 * NW, 1)
                 if (row < a.rows) {
                     float val = v[0][h];
                     if constexpr (EPI == 1) val = __fmul_rn(silu_f32(val), v[NM - 1][h]);
-                    a.y[(size_t)t * a.ystride + row] = val;
+                    const size_t yi = (size_t)t * a.ystride + row;
+                    a.y[yi] = val;
+                    if constexpr (EPI != 2) {
+                        for (int p = 0; p < a.xworld; ++p)  // xworld is 0 without an exchange
+                            if (p != a.xrank) a.peer_y[p][yi] = val;
+                    }
                     if constexpr (EPI == 2) {
                         const unsigned long long key = ((unsigned long long)total_order_key(val) << 32) |
                                                        (unsigned long long)(0xffffffffu - (uint32_t)(a.row_base + row));
@@ -795,24 +810,47 @@ __global__ void __launch_bounds__(32 * NW, 1)
 
     if constexpr (EPI == 2) {
         // Maximum per RHS over the lanes that share it, one atomic per RHS and
-        // warp, then the last CTA publishes the winners and clears the keys.
+        // warp; the last CTA publishes the winners and clears the keys.
 #pragma unroll
         for (int o = 4; o < 32; o <<= 1) {
             const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
             best = other > best ? other : best;
         }
         if (lane < B && best != 0ull) atomicMax(a.keys + lane, best);
-        __threadfence();
+    }
+    const bool xchg = a.xworld > 1;
+    if (EPI == 2 || xchg) {
+        // Last CTA: this CTA's stores (peer stores included) are ordered
+        // before its count, the last CTA's epilogue after all counts.
+        if (xchg)
+            __threadfence_system();
+        else
+            __threadfence();
         __syncthreads();
         if (threadIdx.x == 0) flag = (atomicAdd(a.done, 1u) == gridDim.x - 1) ? 1u : 0u;
         __syncthreads();
-        if (flag && threadIdx.x < B) {
+        if (flag) {
             __threadfence();
-            const unsigned long long k = atomicExch(a.keys + threadIdx.x, 0ull);
-            if (a.argmax) a.argmax[threadIdx.x] = (int)(0xffffffffu - (uint32_t)(k & 0xffffffffu));
-            if (a.best_key_out) a.best_key_out[threadIdx.x] = k;
+            if (EPI == 2 && threadIdx.x < B) {
+                const unsigned long long k = atomicExch(a.keys + threadIdx.x, 0ull);
+                if (a.argmax) a.argmax[threadIdx.x] = (int)(0xffffffffu - (uint32_t)(k & 0xffffffffu));
+                if (a.best_key_out) a.best_key_out[threadIdx.x] = k;
+                if (xchg)
+                    for (int p = 0; p < a.xworld; ++p) a.xkeys[p][a.xrank * 4 + threadIdx.x] = k;
+            }
+            if (xchg) {
+                __threadfence_system();
+                __syncthreads();  // flag is the same for the whole CTA
+                if (threadIdx.x == 0) {
+                    const unsigned int e = *a.xepoch + 1u;
+                    *a.xepoch = e;
+                    for (int p = 0; p < a.xworld; ++p)
+                        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.xflags[p] + a.xrank), "r"(e)
+                                     : "memory");
+                }
+            }
+            if (threadIdx.x == 0) *a.done = 0u;
         }
-        if (flag && threadIdx.x == 0) *a.done = 0u;
     }
     (void)best;
 }

@@ -12,6 +12,7 @@ namespace qmr {
 constexpr unsigned int kErrTimeoutFull = 1u;
 constexpr unsigned int kErrTimeoutEmpty = 2u;
 constexpr unsigned int kErrTimeoutDrain = 3u;
+constexpr unsigned int kErrTimeoutPeer = 4u;  // a rank's exchange epoch did not arrive
 // A wait gives up after this many nanoseconds of the global timer: far beyond
 // any legitimate wait of these kernels (microseconds), far below a hang.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;

@@ -29,6 +29,8 @@ struct FastCall {
     bool overlap;              // programmatic dependent launch behind the previous kernel
     void *scratch;             // caller scratch or nullptr for the per-stream pool
     size_t scratch_bytes;
+    uint32_t ystride;          // output row stride per RHS (0: rows)
+    const QmrExchange *ex;     // output exchange over peer memory, or nullptr
 };
 
 // Streaming kernels of the fast path.
@@ -52,6 +54,9 @@ int run_generic(const void *w, const void *s, const void *b, const float *x, flo
 int run_embed(const void *w, const void *s, const void *b, uint32_t row, float *y, uint32_t cols, uint32_t bits,
               uint32_t group, bool bf16, cudaStream_t stream);
 int device_error(int *code, bool clear);
+// The bounded wait for every rank's current exchange epoch (+ key merge).
+int launch_exchange_wait(const QmrExchange &ex, uint32_t batch, int32_t *argmax, uint64_t *best_key,
+                         cudaStream_t stream);
 // qmr_matmul_affine on the fixed per-device static scratch (static_scratch.cu).
 int matmul_static(const void *w, const void *s, const void *b, const float *x, float *y, uint32_t rows,
                   uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch, bool bf16, bool r2, int path,

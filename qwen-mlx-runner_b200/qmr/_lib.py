@@ -50,6 +50,18 @@ _lib = None
 _lock = threading.Lock()
 
 _vp = ctypes.c_void_p
+
+QMR_MAX_RANKS = 8
+QMR_IPC_HANDLE_BYTES = 64
+
+
+class QmrExchange(ctypes.Structure):
+    """struct QmrExchange (include/qmr.h): the peer buffers of one output
+    exchange."""
+    _fields_ = [("world", ctypes.c_uint32), ("rank", ctypes.c_uint32), ("total_rows", ctypes.c_uint32),
+                ("row_base", ctypes.c_uint32), ("out", ctypes.c_void_p * QMR_MAX_RANKS),
+                ("flags", ctypes.c_void_p * QMR_MAX_RANKS), ("keys", ctypes.c_void_p * QMR_MAX_RANKS),
+                ("epoch", ctypes.c_void_p)]
 _u32 = ctypes.c_uint32
 _u64 = ctypes.c_uint64
 _int = ctypes.c_int
@@ -86,6 +98,18 @@ SIGNATURES = {
     "qmr_stream_sync": (_int, [_vp]),
     "qmr_set_stream_path": (_int, [_cstr]),
     "qmr_device_error": (_int, [ctypes.POINTER(_int), _int]),
+    "qmr_exchange_alloc": (_int, [_sz, ctypes.POINTER(_vp)]),
+    "qmr_exchange_free": (_int, [_vp]),
+    "qmr_ipc_handle": (_int, [_vp, ctypes.c_char_p]),
+    "qmr_ipc_open": (_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    "qmr_ipc_close": (_int, [_vp]),
+    "qmr_matmul_affine_exchange": (_int, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _int,
+                                          ctypes.POINTER(QmrExchange), _vp]),
+    "qmr_gateup_swiglu_exchange": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _int,
+                                          ctypes.POINTER(QmrExchange), _vp]),
+    "qmr_head_argmax_exchange": (_int, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _int,
+                                        ctypes.POINTER(QmrExchange), _vp]),
+    "qmr_exchange_wait": (_int, [ctypes.POINTER(QmrExchange), _u32, _vp, _vp, _vp]),
 }
 
 

@@ -25,19 +25,26 @@ def _ptr(t, min_bytes: int = 0, what: str = "tensor"):
         raise QmrError(_lib.QMR_EINVAL, f"{what} must live on a CUDA device")
     if not t.is_contiguous():
         raise QmrError(_lib.QMR_EINVAL, f"{what} must be contiguous")
-    nbytes = t.numel() * t.element_size()
+    nbytes = t.nbytes
     if nbytes < min_bytes:
         raise QmrError(_lib.QMR_ERANGE, f"{what} holds {nbytes} bytes, the call needs {min_bytes}")
     return t.data_ptr()
 
 
 def _mat(m: "PackedMatrix"):
-    """Pointers of a packed matrix after checking its buffers cover the shape."""
+    """Pointers of a packed matrix after checking its buffers cover the shape
+    (checked once per set of buffer objects, then reused)."""
+    key = (id(m.weight), id(m.scales), id(m.biases), m.rows, m.cols, m.bits, m.group)
+    cached = m.__dict__.get("_ptrs")
+    if cached is not None and cached[0] == key:
+        return cached[1]
     elems = m.rows * m.cols
     wbytes = elems * m.bits // 8
     mbytes = (elems // m.group) * (2 if m.meta_bf16 else 4) if m.group else 0
-    return (_ptr(m.weight, wbytes, "weights"), _ptr(m.scales, mbytes, "scales"),
+    ptrs = (_ptr(m.weight, wbytes, "weights"), _ptr(m.scales, mbytes, "scales"),
             _ptr(m.biases, mbytes, "biases"))
+    m.__dict__["_ptrs"] = (key, ptrs)
+    return ptrs
 
 
 def _stream(stream):
@@ -145,6 +152,39 @@ def matmul_prepared(m: PackedMatrix, prepared, y, batch: int, overlap: bool = Fa
                                                          "prepared"),
                                          _ptr(y, 4 * batch * m.rows, "y"), m.rows, m.cols, m.bits, m.group, batch,
                                          int(m.meta_bf16), 1 if overlap else 0, _stream(stream)))
+
+
+def gateup_swiglu_exchange(gate: PackedMatrix, up: PackedMatrix, x, batch: int, exchange, stream=None) -> None:
+    """This rank's rows of silu(gate x) * (up x) into every rank's full
+    activation buffer (`exchange`: a _lib.QmrExchange; see qmr.parallel)."""
+    wg, sg, bg = _mat(gate)
+    wu, su, bu = _mat(up)
+    check(_lib.lib().qmr_gateup_swiglu_exchange(wg, sg, bg, wu, su, bu, _ptr(x, 4 * batch * gate.cols, "x"),
+                                                gate.rows, gate.cols, gate.bits, gate.group, batch,
+                                                int(gate.meta_bf16), exchange, _stream(stream)))
+
+
+def matmul_affine_exchange(m: PackedMatrix, x, batch: int, exchange, stream=None) -> None:
+    """This rank's rows of m x into every rank's full output buffer."""
+    w, sc, bi = _mat(m)
+    check(_lib.lib().qmr_matmul_affine_exchange(w, sc, bi, _ptr(x, 4 * batch * m.cols, "x"), m.rows, m.cols, m.bits,
+                                                m.group, batch, int(m.meta_bf16), exchange, _stream(stream)))
+
+
+def head_argmax_exchange(m: PackedMatrix, x, logits, batch: int, exchange, stream=None) -> None:
+    """This rank's vocabulary shard: local logits, its best key per RHS to
+    every rank."""
+    w, sc, bi = _mat(m)
+    check(_lib.lib().qmr_head_argmax_exchange(w, sc, bi, _ptr(x, 4 * batch * m.cols, "x"),
+                                              _ptr(logits, 4 * batch * m.rows, "logits"), m.rows, m.cols, m.bits,
+                                              m.group, batch, int(m.meta_bf16), exchange, _stream(stream)))
+
+
+def exchange_wait(exchange, batch: int, argmax=None, best_key=None, stream=None) -> None:
+    """Wait for every rank's current exchange; for a head exchange also write
+    the merged token ids (int32 [batch]) and keys (int64 [batch])."""
+    check(_lib.lib().qmr_exchange_wait(exchange, batch, _ptr(argmax, 4 * batch, "argmax"),
+                                       _ptr(best_key, 8 * batch, "best_key"), _stream(stream)))
 
 
 def copy_f32(x, y, n: int, stream=None) -> None:
