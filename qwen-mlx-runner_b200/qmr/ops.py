@@ -31,6 +31,19 @@ def _ptr(t, min_bytes: int = 0, what: str = "tensor"):
     return t.data_ptr()
 
 
+def _act(t, min_bytes: int, what: str = "x"):
+    """Address of an activation input: a contiguous CUDA tensor, or a pinned
+    (page-locked) host tensor, which the kernels read directly over the host
+    link (unified addressing) instead of a separate copy."""
+    if t is not None and not t.is_cuda and t.is_pinned():
+        if not t.is_contiguous():
+            raise QmrError(_lib.QMR_EINVAL, f"{what} must be contiguous")
+        if t.nbytes < min_bytes:
+            raise QmrError(_lib.QMR_ERANGE, f"{what} holds {t.nbytes} bytes, the call needs {min_bytes}")
+        return t.data_ptr()
+    return _ptr(t, min_bytes, what)
+
+
 def _mat(m: "PackedMatrix"):
     """Pointers of a packed matrix after checking its buffers cover the shape
     (checked once per set of buffer objects, then reused)."""
@@ -80,13 +93,13 @@ class PackedMatrix:
 
 def matvec_affine(m: PackedMatrix, x, y, stream=None) -> None:
     w, sc, bi = _mat(m)
-    check(_lib.lib().qmr_matvec_affine(w, sc, bi, _ptr(x, 4 * m.cols, "x"), _ptr(y, 4 * m.rows, "y"),
+    check(_lib.lib().qmr_matvec_affine(w, sc, bi, _act(x, 4 * m.cols), _ptr(y, 4 * m.rows, "y"),
                                        m.rows, m.cols, m.bits, m.group, int(m.meta_bf16), _stream(stream)))
 
 
 def matmul_affine(m: PackedMatrix, x, y, batch: int, stream=None) -> None:
     w, sc, bi = _mat(m)
-    check(_lib.lib().qmr_matmul_affine(w, sc, bi, _ptr(x, 4 * batch * m.cols, "x"),
+    check(_lib.lib().qmr_matmul_affine(w, sc, bi, _act(x, 4 * batch * m.cols),
                                        _ptr(y, 4 * batch * m.rows, "y"), m.rows, m.cols, m.bits, m.group, batch,
                                        int(m.meta_bf16), _stream(stream)))
 
@@ -95,7 +108,7 @@ def matmul_affine_static(m: PackedMatrix, x, y, batch: int, stream=None) -> None
     """matmul_affine on the library's fixed per-device scratch: allocates no
     device memory (cols <= 32768); calls must not overlap in time."""
     w, sc, bi = _mat(m)
-    check(_lib.lib().qmr_matmul_affine_static(w, sc, bi, _ptr(x, 4 * batch * m.cols, "x"),
+    check(_lib.lib().qmr_matmul_affine_static(w, sc, bi, _act(x, 4 * batch * m.cols),
                                               _ptr(y, 4 * batch * m.rows, "y"), m.rows, m.cols, m.bits, m.group,
                                               batch, int(m.meta_bf16), _stream(stream)))
 
@@ -114,7 +127,7 @@ def gateup_swiglu(gate: PackedMatrix, up: PackedMatrix, x, act, batch: int, stre
         raise QmrError(_lib.QMR_EINVAL, "gate and up matrices must share shape and format")
     gw, gs, gb = _mat(gate)
     uw, us, ub = _mat(up)
-    check(_lib.lib().qmr_gateup_swiglu(gw, gs, gb, uw, us, ub, _ptr(x, 4 * batch * gate.cols, "x"),
+    check(_lib.lib().qmr_gateup_swiglu(gw, gs, gb, uw, us, ub, _act(x, 4 * batch * gate.cols),
                                        _ptr(act, 4 * batch * gate.rows, "act"), gate.rows, gate.cols, gate.bits,
                                        gate.group, batch, int(gate.meta_bf16), _stream(stream)))
 
@@ -122,7 +135,7 @@ def gateup_swiglu(gate: PackedMatrix, up: PackedMatrix, x, act, batch: int, stre
 def head_argmax(m: PackedMatrix, x, logits, argmax, batch: int, best_key=None, row_base: int = 0,
                 stream=None) -> None:
     w, sc, bi = _mat(m)
-    check(_lib.lib().qmr_head_argmax(w, sc, bi, _ptr(x, 4 * batch * m.cols, "x"),
+    check(_lib.lib().qmr_head_argmax(w, sc, bi, _act(x, 4 * batch * m.cols),
                                      _ptr(logits, 4 * batch * m.rows, "logits"), _ptr(argmax, 4 * batch, "argmax"),
                                      _ptr(best_key, 8 * batch, "best_key"), m.rows, m.cols, m.bits, m.group,
                                      batch, int(m.meta_bf16), row_base, _stream(stream)))
@@ -139,7 +152,7 @@ def alloc_prepared(bits: int, cols: int, batch: int, device="cuda"):
 
 
 def prepare_activations(x, cols: int, bits: int, batch: int, prepared, group: int = 64, stream=None) -> None:
-    check(_lib.lib().qmr_prepare_activations(_ptr(x, 4 * batch * cols, "x"), cols, bits, group, batch,
+    check(_lib.lib().qmr_prepare_activations(_act(x, 4 * batch * cols), cols, bits, group, batch,
                                              _ptr(prepared, prepared_bytes(bits, cols, batch), "prepared"),
                                              prepared.numel() * prepared.element_size(), _stream(stream)))
 
@@ -159,7 +172,7 @@ def gateup_swiglu_exchange(gate: PackedMatrix, up: PackedMatrix, x, batch: int, 
     activation buffer (`exchange`: a _lib.QmrExchange; see qmr.parallel)."""
     wg, sg, bg = _mat(gate)
     wu, su, bu = _mat(up)
-    check(_lib.lib().qmr_gateup_swiglu_exchange(wg, sg, bg, wu, su, bu, _ptr(x, 4 * batch * gate.cols, "x"),
+    check(_lib.lib().qmr_gateup_swiglu_exchange(wg, sg, bg, wu, su, bu, _act(x, 4 * batch * gate.cols),
                                                 gate.rows, gate.cols, gate.bits, gate.group, batch,
                                                 int(gate.meta_bf16), exchange, _stream(stream)))
 
@@ -167,7 +180,7 @@ def gateup_swiglu_exchange(gate: PackedMatrix, up: PackedMatrix, x, batch: int, 
 def matmul_affine_exchange(m: PackedMatrix, x, batch: int, exchange, stream=None) -> None:
     """This rank's rows of m x into every rank's full output buffer."""
     w, sc, bi = _mat(m)
-    check(_lib.lib().qmr_matmul_affine_exchange(w, sc, bi, _ptr(x, 4 * batch * m.cols, "x"), m.rows, m.cols, m.bits,
+    check(_lib.lib().qmr_matmul_affine_exchange(w, sc, bi, _act(x, 4 * batch * m.cols), m.rows, m.cols, m.bits,
                                                 m.group, batch, int(m.meta_bf16), exchange, _stream(stream)))
 
 
@@ -175,7 +188,7 @@ def head_argmax_exchange(m: PackedMatrix, x, logits, batch: int, exchange, strea
     """This rank's vocabulary shard: local logits, its best key per RHS to
     every rank."""
     w, sc, bi = _mat(m)
-    check(_lib.lib().qmr_head_argmax_exchange(w, sc, bi, _ptr(x, 4 * batch * m.cols, "x"),
+    check(_lib.lib().qmr_head_argmax_exchange(w, sc, bi, _act(x, 4 * batch * m.cols),
                                               _ptr(logits, 4 * batch * m.rows, "logits"), m.rows, m.cols, m.bits,
                                               m.group, batch, int(m.meta_bf16), exchange, _stream(stream)))
 

@@ -561,3 +561,33 @@ def test_all_streaming_paths_meet_the_bound(cuda, bits, meta):
         assert qmr.ops.device_error() == 0
     finally:
         qmr.ops.set_stream_path("mma")
+
+
+def test_pinned_host_activations_give_the_same_bits(cuda):
+    """x may be a pinned host tensor (read by the kernels over the host link):
+    the same bits as the device copy for the block, the GEMV, the fused
+    gate/up pair and the head."""
+    rows, cols = 4096, 5120
+    mat = synth.affine_matrix(rows, cols, 4, 64, seed=61)
+    m = synth.to_device(mat, rows, cols, 4, 64)
+    x_np = synth.activations(3, cols, seed=62)
+    xd = f32_tensor(x_np.ravel())
+    xh = torch.from_numpy(np.ascontiguousarray(x_np.ravel(), np.float32)).pin_memory()
+    outs = {}
+    for name, x in (("dev", xd), ("host", xh)):
+        y3 = torch.empty(3 * rows, dtype=torch.float32, device="cuda")
+        qmr.matmul_affine(m, x, y3, 3)
+        y1 = torch.empty(rows, dtype=torch.float32, device="cuda")
+        qmr.matvec_affine(m, x[:cols], y1)
+        act = torch.empty(3 * rows, dtype=torch.float32, device="cuda")
+        qmr.gateup_swiglu(m, m, x, act, 3)
+        lg = torch.empty(3 * rows, dtype=torch.float32, device="cuda")
+        idx = torch.empty(3, dtype=torch.int32, device="cuda")
+        qmr.head_argmax(m, x, lg, idx, 3)
+        torch.cuda.synchronize()
+        outs[name] = [t.cpu().numpy() for t in (y3, y1, act, lg, idx)]
+    for a, b in zip(outs["dev"], outs["host"]):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    pageable = torch.from_numpy(np.ascontiguousarray(x_np.ravel(), np.float32))
+    with pytest.raises(qmr.QmrError):
+        qmr.matmul_affine(m, pageable, torch.empty(3 * rows, dtype=torch.float32, device="cuda"), 3)
