@@ -6,19 +6,19 @@ rank and each shard is an ordinary matrix for the library's kernels:
 
 * MLP (src/engine.rs:755-763 run on n GPUs): rank r holds rows
   [r*F/n, (r+1)*F/n) of gate and up, computes silu(gate x) * (up x) for them
-  with the fused gate/up kernel, the ranks all-gather the activations, and
+  with the fused gate/up kernel, the ranks exchange the activations, and
   rank r computes rows [r*H/n, (r+1)*H/n) of down from the full activation
-  vector; a second all-gather assembles the output.  Both exchanges are the
+  vector; a second exchange assembles the output.  Both exchanges are the
   activation vectors only (F*B and H*B floats); no weight moves.
 * Head (src/engine.rs:777-780 + src/chat.rs:383-390): rank r holds vocabulary
   rows [r*V/n, (r+1)*V/n); each rank's fused logits+argmax kernel returns its
-  best (value, index) as one packed key per RHS, the ranks all-gather the
+  best (value, index) as one packed key per RHS, the ranks exchange the
   keys and take the largest: the highest logit under f32 total order, ties
   to the lowest vocabulary index, exactly the single-GPU rule.
 
 Two ways to exchange the shards:
 
-* `exchange="p2p"` (default with qmr.ops on GPUs): the streaming kernel
+* `exchange="p2p"` (what bench.py uses on GPUs): the streaming kernel
   itself stores each finished row into every rank's full output buffer over
   NVLink (CUDA IPC mappings of buffers the library allocated, PeerExchange)
   and its last CTA publishes an epoch; a one-warp kernel on each rank waits
@@ -208,7 +208,7 @@ class ShardedMLP:
             self.xy.close()
 
     def __call__(self, x: torch.Tensor, batch: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        dev = x.device
+        dev = self.gate.weight.device  # x may be a pinned host tensor
         if self.exchange == "p2p":
             ea, par = self.xa.next()
             self.ops.gateup_swiglu_exchange(self.gate, self.up, x, batch, ea)
@@ -256,7 +256,7 @@ class ShardedHead:
     def __call__(self, x: torch.Tensor, batch: int, logits: Optional[torch.Tensor] = None):
         """Returns (token index per RHS as int32 [batch], winning keys int64
         [batch]); `logits` receives this rank's [batch][V/n] logits if given."""
-        dev = x.device
+        dev = self.head.weight.device  # x may be a pinned host tensor
         lg = logits if logits is not None else torch.empty(batch * self.head.rows, dtype=torch.float32, device=dev)
         if self.exchange == "p2p":
             ek, _ = self.xk.next()
