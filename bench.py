@@ -427,22 +427,22 @@ def run_gpu(args):
         end.record(stream)
     stream.synchronize()
     ms = start.elapsed_time(end)
-    # Keep the GPU in the same loop until the clock sampler has seen >= 1.5 s
-    # of it (untimed; only the first pass above is reported).
-    extra = 0
-    with torch.cuda.stream(stream):
-        while not args.quick and extra * ms < 1500 and extra < 400:
-            for g in graphs:
-                g.replay()
-            extra += 1
-    stream.synchronize()
-    clk = clocks.stop()
-    torch.cuda.synchronize()
-    kernel_ms = kernel_only_ms(wl, stream, args.steps) if args.workload in ("b3", "b1", "q8b3") else None
     t = torch.tensor([ms], device=device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
+    # Keep the GPU in the same loop until the clock sampler has seen >= 1.5 s
+    # of it (untimed; only the first pass above is reported).  The count comes
+    # from the slowest rank's time, so every rank replays the same exchanges.
+    extra = 0 if args.quick else min(400, int(math.ceil(1500.0 / max(ms_max, 1e-3))))
+    with torch.cuda.stream(stream):
+        for _ in range(extra):
+            for g in graphs:
+                g.replay()
+    stream.synchronize()
+    clk = clocks.stop()
+    torch.cuda.synchronize()
+    kernel_ms = kernel_only_ms(wl, stream, args.steps) if args.workload in ("b3", "b1", "q8b3") else None
     ms_per_step = ms_max / args.steps
     value = job_factor * nbytes * args.steps / (ms_max * 1e-3) / 1e9
 

@@ -207,6 +207,9 @@ __global__ void __launch_bounds__(32) exchange_wait_kernel(const unsigned int *f
                                                            unsigned int *err) {
     const int lane = threadIdx.x;
     const unsigned int e = *epoch;
+    // After a wait has run out (a rank fell behind or stopped), later waits
+    // return at once instead of each spending the full limit again.
+    if (*(volatile unsigned int *)err != 0u) return;
     bool ok = true;
     if (lane < world) {
         const unsigned long long start = global_ns();
