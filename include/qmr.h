@@ -223,7 +223,11 @@ int qmr_matmul_prepared(const void *w, const void *scales, const void *biases, c
                         uint32_t rows, uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch,
                         int meta_bf16, uint32_t flags, void *stream);
 
-/* copy_f32 (kernels/matmul_block.metal:315-318): y[i] = x[i], i < n. */
+/* copy_f32 (kernels/matmul_block.metal:315-318): y[i] = x[i], i < n, as a
+ * kernel chained behind the previous one on the stream (programmatic
+ * dependent launch).  x and y may also be pinned host memory: copying a
+ * result into pinned host memory this way is a device-to-host transfer
+ * without a copy-engine round trip. */
 int qmr_copy_f32(const float *x, float *y, uint32_t n, void *stream);
 
 /* Select the streaming kernel of the fast path: "mma" (default; tensor-core

@@ -718,8 +718,8 @@ int qmr_encode(const char *cname, const qmr_buffer *buffers, const uint64_t *off
                          params[3], ends_with(name, "_bf16"), stream);
     if (name == "copy_f32") {
         if (buffers[0].ptr == buffers[1].ptr && off(0) == off(1)) return QMR_OK;
-        return check_cuda(cudaMemcpyAsync(at(1), at(0), (size_t)params[0] * 4, cudaMemcpyDeviceToDevice, stream),
-                          "copy_f32");
+        return run_copy_f32(reinterpret_cast<const float *>(at(0)), reinterpret_cast<float *>(at(1)), params[0],
+                            stream);
     }
     return fail(QMR_EUNSUPPORTED, "%s: validated, but this build implements only the packed-affine matrix kernels",
                 cname);
@@ -898,8 +898,7 @@ int qmr_matmul_prepared(const void *w, const void *scales, const void *biases, c
 int qmr_copy_f32(const float *x, float *y, uint32_t n, void *stream) {
     if (n == 0) return fail(QMR_EINVAL, "copy_f32: dimensions must be nonzero");
     if (x == y) return QMR_OK;
-    return check_cuda(cudaMemcpyAsync(y, x, (size_t)n * 4, cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream)),
-                      "copy_f32");
+    return run_copy_f32(x, y, n, static_cast<cudaStream_t>(stream));
 }
 
 int qmr_set_stream_path(const char *path) {

@@ -67,6 +67,48 @@ int launch_reg(const StreamArgs &a, int bits, bool bf16, uint32_t batch, int epi
     }
 }
 
+namespace {
+
+// copy_f32 (kernels/matmul_block.metal:315-318): y[i] = x[i], 16-byte vectors
+// when both ends are 16-byte aligned.  Launched behind the previous kernel
+// (programmatic dependent launch): it lets the next kernel launch at once and
+// waits for the previous one before reading x or writing y.  y may be pinned
+// host memory (unified addressing): then this is the device-to-host copy,
+// written straight over the host link.
+__global__ void __launch_bounds__(256) copy_f32_kernel(const float *__restrict__ x, float *__restrict__ y, uint32_t n) {
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x, nt = (size_t)gridDim.x * blockDim.x;
+    size_t done = 0;
+    if (((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0) {
+        const size_t n4 = n / 4;
+        for (size_t i = tid; i < n4; i += nt)
+            reinterpret_cast<float4 *>(y)[i] = __ldcg(reinterpret_cast<const float4 *>(x) + i);
+        done = n4 * 4;
+    }
+    for (size_t i = done + tid; i < n; i += nt) y[i] = __ldcg(x + i);
+}
+
+}  // namespace
+
+int run_copy_f32(const float *x, float *y, uint32_t n, cudaStream_t stream) {
+    const uint64_t vec = ((uint64_t)n + 3) / 4;
+    uint64_t blocks = (vec + 255) / 256;
+    const uint64_t cap = 4ull * (uint64_t)sm_count();
+    if (blocks > cap) blocks = cap;
+    if (blocks == 0) blocks = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)blocks, 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1] = {pdl_attr()};
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, copy_f32_kernel, x, y, n);
+    if (e != cudaSuccess) return fail(QMR_ECUDA, "copy_f32 launch failed: %s", cudaGetErrorString(e));
+    return QMR_OK;
+}
+
 int run_generic(const void *w, const void *s, const void *b, const float *x, float *y, uint32_t rows, uint32_t cols,
                 uint32_t bits, uint32_t group, uint32_t batch, bool bf16, cudaStream_t stream) {
     const uint64_t threads = (uint64_t)rows * 32;

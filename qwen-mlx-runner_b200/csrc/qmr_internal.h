@@ -49,6 +49,7 @@ int run_fast(const FastCall &c, cudaStream_t stream);
 int run_prepare(const float *x, uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch, void *base, int path,
                 cudaStream_t stream);
 int run_stream(const FastCall &c, void *base, cudaStream_t stream);
+int run_copy_f32(const float *x, float *y, uint32_t n, cudaStream_t stream);
 int run_generic(const void *w, const void *s, const void *b, const float *x, float *y, uint32_t rows,
                 uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch, bool bf16, cudaStream_t stream);
 int run_embed(const void *w, const void *s, const void *b, uint32_t row, float *y, uint32_t cols, uint32_t bits,

@@ -201,7 +201,7 @@ def exchange_wait(exchange, batch: int, argmax=None, best_key=None, stream=None)
 
 
 def copy_f32(x, y, n: int, stream=None) -> None:
-    check(_lib.lib().qmr_copy_f32(_ptr(x, 4 * n, "x"), _ptr(y, 4 * n, "y"), n, _stream(stream)))
+    check(_lib.lib().qmr_copy_f32(_act(x, 4 * n, "x"), _act(y, 4 * n, "y"), n, _stream(stream)))
 
 
 def init(device: int = 0, reference: bool = False) -> None:

@@ -588,6 +588,14 @@ def test_pinned_host_activations_give_the_same_bits(cuda):
         outs[name] = [t.cpu().numpy() for t in (y3, y1, act, lg, idx)]
     for a, b in zip(outs["dev"], outs["host"]):
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    # copy_f32 into pinned host memory (and device to device) moves the bits unchanged.
+    yh = torch.empty(3 * rows, dtype=torch.float32).pin_memory()
+    yd = torch.empty(3 * rows, dtype=torch.float32, device="cuda")
+    qmr.copy_f32(y3, yh, 3 * rows)
+    qmr.copy_f32(y3, yd, 3 * rows - 1)
+    torch.cuda.synchronize()
+    assert np.array_equal(yh.numpy().view(np.uint32), outs["host"][0].view(np.uint32))
+    assert np.array_equal(yd.cpu().numpy()[:-1].view(np.uint32), outs["host"][0][:-1].view(np.uint32))
     pageable = torch.from_numpy(np.ascontiguousarray(x_np.ravel(), np.float32))
     with pytest.raises(qmr.QmrError):
         qmr.matmul_affine(m, pageable, torch.empty(3 * rows, dtype=torch.float32, device="cuda"), 3)
