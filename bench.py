@@ -1,19 +1,28 @@
 #!/usr/bin/env python3
 """Benchmark of the packed-affine B3 block matmul (metric: Q4 GEMV/B3 HBM GB/s).
 
-Workload (default `b3`): one step = one block matmul of a Q4/group-64
+Headline workload (`b3`): one step = one block matmul of a Q4/group-64
 17408x5120 matrix with BF16 scale/bias against 3 FP32 activation rows (one
 target + two MTP proposals), the R2-eligible gate/up shape.  Inputs are
 seeded synthetic data with the benchmark distributions (no dataset exists for
 this path).  Steps rotate over enough distinct weight copies to exceed 4x the
 L2 size, so every step streams its weights from HBM.
 
-Other workloads (--workload): b1 (same matrix, one RHS), q8b3 (Q8 config),
-mlp (gate/up SwiGLU + down at B3), head (152064-row vocabulary head + argmax).
+The same JSON line also carries, measured in the same run:
+  * `workloads`: the B1 GEMV (config 0) and the Q8 B3 block (config 1), each
+    as whole-call GB/s and as the streaming kernel alone, over a fixed 200
+    calls;
+  * `sharded`: the SwiGLU MLP (config 2) and the vocabulary head + argmax
+    (config 3).  At N=1 the unsharded call; under torchrun (N>1) the rows are
+    split over the ranks (strong scaling, outputs exchanged over peer memory
+    inside the kernels), timed as the max over ranks, and checked against the
+    1-GPU call on rank 0;
+  * `reps200`: the headline call timed over a fixed 200 calls, comparable
+    between runs whatever --steps is.
 
-Multi-GPU: one process per GPU (torchrun); each rank runs the same workload
-on its own weights (independent matrices, no data-path collective), value =
-all ranks' bytes / max-over-ranks time ("scaling": "weak").
+Multi-GPU headline: one process per GPU (torchrun); each rank runs the b3
+call on its own weights (independent matrices, no data-path collective),
+value = all ranks' bytes / max-over-ranks time ("scaling": "weak").
 
 --impl reference times the reference's CPU path on the host cores instead:
 the FP64 oracle restatement (oracle/), a bounded sample of rows per step.
@@ -38,6 +47,10 @@ import numpy as np  # noqa: E402
 ROWS, COLS, GROUP = 17408, 5120, 64
 VOCAB = 152064
 METRIC = "Q4 GEMV/B3 HBM GB/s"
+ARITH = ("tensor cores (mma.sync m16n8k16): exact fp16-subnormal Q4/Q8 weights x activations split into "
+         "fp16 high + low parts with a per-group exponent (about 22 significant bits), f32 accumulation and "
+         "f32 scale/bias fold; FP32 activations in, FP32 outputs")
+FIXED_REPS = 200
 
 
 def matrix_bytes(rows, cols, bits, group):
@@ -45,7 +58,6 @@ def matrix_bytes(rows, cols, bits, group):
 
 
 def workload_spec(name):
-    """(description, per-step algorithmic bytes, bits, batch)."""
     if name == "b3":
         return dict(desc="Q4/g64 BF16-metadata B3 block matmul 17408x5120", bits=4, batch=3, rows=ROWS,
                     cols=COLS)
@@ -60,6 +72,12 @@ def workload_spec(name):
         return dict(desc="Q4/g64 vocabulary head 152064x5120 + argmax at B3", bits=4, batch=3, rows=VOCAB,
                     cols=COLS)
     raise SystemExit(f"unknown workload {name}")
+
+
+def config_of(spec):
+    """The `config` object both arms print for a workload."""
+    return {"workload": spec["desc"], "batch": spec["batch"], "rows": spec["rows"], "cols": spec["cols"],
+            "bits": spec["bits"], "group": GROUP, "metadata": "bf16"}
 
 
 def algorithmic_bytes(name, spec):
@@ -156,6 +174,15 @@ def dist_env():
 # CPU reference arm
 # ---------------------------------------------------------------------------
 
+def host_threads():
+    """Every host core this process may run on (torchrun sets OMP_NUM_THREADS=1
+    for its children; the CPU baseline is measured on all cores regardless)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_sample(name, spec, rows_sample, seed=1):
     """Time the FP64 oracle on rows_sample rows of the workload; returns (seconds, bytes)."""
     import oracle
@@ -184,6 +211,7 @@ def run_reference(args):
     if rank != 0:
         return 0
     import oracle
+    oracle.set_threads(host_threads())
     spec = workload_spec(args.workload)
     threads = oracle.threads()
     # Bound the whole run to about a minute: per-step sample sized from K+W.
@@ -198,15 +226,18 @@ def run_reference(args):
         secs += dt
         nbytes += nb
     value = nbytes / secs / 1e9
+    config = config_of(spec)
+    config["cpu_rows_per_step"] = rows
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
         "data": "synthetic (seeded; benchmark distributions)",
-        "config": {"workload": spec["desc"], "cpu_rows_per_step": rows},
+        "config": config,
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"{rows} of {spec['rows']} rows per step, FP64 oracle (tests/quantized.rs:39-51 "
-                                   "restated in oracle/oracle.c), OpenMP over rows"},
+                         "sample": f"{rows} of {spec['rows']} rows per step (the same workload, a bounded row "
+                                   "sample), FP64 oracle (tests/quantized.rs:39-51 restated in oracle/oracle.c), "
+                                   "OpenMP over rows on all host cores"},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -217,100 +248,89 @@ def run_reference(args):
 # GPU arm
 # ---------------------------------------------------------------------------
 
-def sharded(name, world):
-    """The MLP and the head run row-sharded across the ranks (one model split
-    over N GPUs, strong scaling); the single matrices run one replica per
-    rank (weak scaling)."""
-    return world > 1 and name in ("mlp", "head")
+def _synth_matrix(rows, cols, bits, seed, device):
+    from qmr import synth
+    m = synth.affine_matrix(rows, cols, bits, GROUP, seed=seed)
+    return synth.to_device(m, rows, cols, bits, GROUP, device)
+
+
+def _clone(m):
+    from qmr.ops import PackedMatrix
+    return PackedMatrix(m.weight.clone(), m.scales.clone(), m.biases.clone(), m.rows, m.cols, m.bits, m.group)
+
+
+def _copies(l2, per_copy):
+    return max(2, math.ceil(4 * l2 / per_copy) + 1)
 
 
 class Workload:
-    def __init__(self, name, spec, device, seed, world=1, rank=0, exchange="p2p"):
+    """One workload on this rank: its weight copies (> 4x L2 in total), its
+    input and outputs, and one call per step through the public API."""
+
+    def __init__(self, name, device, seed, world=1, rank=0, shard=False, exchange="p2p"):
         import torch
 
         from qmr import synth
+        spec = workload_spec(name)
         self.name, self.spec, self.device = name, spec, device
-        self.torch = torch
-        bits, b = spec["bits"], spec["batch"]
-        self.batch = b
-        self.sharded = sharded(name, world)
+        self.batch = b = spec["batch"]
+        self.sharded = shard and world > 1
         self.exchange = exchange
-        if self.sharded:
-            self._init_sharded(world, rank, seed)
-            return
-        per_copy = (matrix_bytes(ROWS, COLS, 4, GROUP) * 3) if name == "mlp" else \
-            matrix_bytes(spec["rows"], spec["cols"], bits, GROUP)
-        l2 = torch.cuda.get_device_properties(device).L2_cache_size
-        self.copies = max(2, math.ceil(4 * l2 / per_copy) + 1)
-        self.l2 = l2
+        self.world, self.rank, self.seed = world, rank, seed
+        self.l2 = torch.cuda.get_device_properties(device).L2_cache_size
         self.x = torch.from_numpy(synth.activations(b, COLS, seed=seed + 1).ravel()).to(device)
-
-        def dev_matrix(rows, cols, s):
-            m = synth.affine_matrix(rows, cols, bits, GROUP, seed=s)
-            return synth.to_device(m, rows, cols, bits, GROUP, device)
-
-        def clone(m):
-            from qmr.ops import PackedMatrix
-            return PackedMatrix(m.weight.clone(), m.scales.clone(), m.biases.clone(), m.rows, m.cols, m.bits,
-                                m.group)
-
+        if self.sharded:
+            self._init_sharded()
+            return
+        bits = spec["bits"]
         if name == "mlp":
-            g0 = dev_matrix(ROWS, COLS, seed + 10)
-            u0 = dev_matrix(ROWS, COLS, seed + 11)
-            d0 = dev_matrix(COLS, ROWS, seed + 12)
-            self.mats = [(clone(g0), clone(u0), clone(d0)) for _ in range(self.copies)]
+            g0 = _synth_matrix(ROWS, COLS, bits, seed + 10, device)
+            u0 = _synth_matrix(ROWS, COLS, bits, seed + 11, device)
+            d0 = _synth_matrix(COLS, ROWS, bits, seed + 12, device)
+            self.copies = _copies(self.l2, g0.nbytes + u0.nbytes + d0.nbytes)
+            self.mats = [(_clone(g0), _clone(u0), _clone(d0)) for _ in range(self.copies)]
             self.act = torch.empty(b * ROWS, dtype=torch.float32, device=device)
             self.y = torch.empty(b * COLS, dtype=torch.float32, device=device)
+            self.launches_per_step = 4  # prep + fused gate/up, prep + down
         else:
-            m0 = dev_matrix(spec["rows"], spec["cols"], seed + 10)
-            self.mats = [clone(m0) for _ in range(self.copies)]
+            m0 = _synth_matrix(spec["rows"], spec["cols"], bits, seed + 10, device)
+            self.copies = _copies(self.l2, m0.nbytes)
+            self.mats = [_clone(m0) for _ in range(self.copies)]
             self.y = torch.empty(b * spec["rows"], dtype=torch.float32, device=device)
             self.idx = torch.empty(b, dtype=torch.int32, device=device)
-        self.launches_per_step = 2 if name == "mlp" else 1
+            self.launches_per_step = 2  # activation prep + streaming kernel
 
-    def _init_sharded(self, world, rank, seed):
+    def shard_seed(self, r):
+        return self.seed + 100 * r
+
+    def _init_sharded(self):
         """This rank's row shards (random init of this rank's rows only)."""
-        import math
-
         import torch
 
         import qmr
-        from qmr import parallel, synth
-        from qmr.ops import PackedMatrix
-        b, dev = self.batch, self.device
-        l2 = torch.cuda.get_device_properties(dev).L2_cache_size
-        self.l2 = l2
-
-        def dev_matrix(rows, cols, s):
-            m = synth.affine_matrix(rows, cols, 4, GROUP, seed=s)
-            return synth.to_device(m, rows, cols, 4, GROUP, dev)
-
-        def clone(m):
-            return PackedMatrix(m.weight.clone(), m.scales.clone(), m.biases.clone(), m.rows, m.cols, m.bits,
-                                m.group)
-
-        self.x = torch.from_numpy(synth.activations(b, COLS, seed=seed + 1).ravel()).to(dev)
-        s = seed + 100 * rank
+        from qmr import parallel
+        b, dev, world, rank = self.batch, self.device, self.world, self.rank
+        s = self.shard_seed(rank)
         if self.name == "mlp":
             f0, f1 = parallel.shard_range(ROWS, world, rank)
             h0, h1 = parallel.shard_range(COLS, world, rank)
-            g0, u0 = dev_matrix(f1 - f0, COLS, s + 10), dev_matrix(f1 - f0, COLS, s + 11)
-            d0 = dev_matrix(h1 - h0, ROWS, s + 12)
-            per_copy = g0.nbytes + u0.nbytes + d0.nbytes
-            self.copies = max(2, math.ceil(4 * l2 / per_copy) + 1)
-            self.mods = [parallel.ShardedMLP(clone(g0), clone(u0), clone(d0), COLS, ROWS, qmr.ops,
+            g0, u0 = _synth_matrix(f1 - f0, COLS, 4, s + 10, dev), _synth_matrix(f1 - f0, COLS, 4, s + 11, dev)
+            d0 = _synth_matrix(h1 - h0, ROWS, 4, s + 12, dev)
+            self.copies = _copies(self.l2, g0.nbytes + u0.nbytes + d0.nbytes)
+            self.mods = [parallel.ShardedMLP(_clone(g0), _clone(u0), _clone(d0), COLS, ROWS, qmr.ops,
                                              exchange=self.exchange) for _ in range(self.copies)]
             self.y = torch.empty(b * COLS, dtype=torch.float32, device=dev)
-            self.launches_per_step = 2
+            # prep + gate/up + exchange wait, prep + down + exchange wait (p2p)
+            self.launches_per_step = 6 if self.exchange == "p2p" else 4
         else:
             v0, v1 = parallel.shard_range(VOCAB, world, rank)
-            h = dev_matrix(v1 - v0, COLS, s + 10)
-            self.copies = max(2, math.ceil(4 * l2 / h.nbytes) + 1)
-            self.mods = [parallel.ShardedHead(clone(h), VOCAB, v0, qmr.ops, exchange=self.exchange)
+            h = _synth_matrix(v1 - v0, COLS, 4, s + 10, dev)
+            self.copies = _copies(self.l2, h.nbytes)
+            self.mods = [parallel.ShardedHead(_clone(h), VOCAB, v0, qmr.ops, exchange=self.exchange)
                          for _ in range(self.copies)]
             self.y = torch.empty(b * (v1 - v0), dtype=torch.float32, device=dev)
             self.idx = torch.empty(b, dtype=torch.int32, device=dev)
-            self.launches_per_step = 1
+            self.launches_per_step = 3 if self.exchange == "p2p" else 2  # prep + head (+ wait)
 
     def step(self, i, stream=None, x=None):
         """One call of the workload; x (default: the device activations) may
@@ -337,6 +357,55 @@ class Workload:
         else:
             qmr.matmul_affine(m, x, self.y, self.batch, stream=stream)
 
+    def close(self):
+        if self.sharded:
+            for m in self.mods:
+                m.close()
+
+
+def capture(wl, stream, n, start=0):
+    """CUDA graphs (at most 1000 calls each) of n consecutive steps."""
+    import torch
+    graphs, done = [], 0
+    while done < n:
+        k = min(1000, n - done)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(k):
+                wl.step(start + done + i, stream)
+        graphs.append(g)
+        done += k
+    return graphs
+
+
+def replay_ms(graphs, stream):
+    """Device time of one replay of every graph, with events on the replay stream."""
+    import torch
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for g in graphs:
+            g.replay()
+        e1.record(stream)
+    stream.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def max_over_ranks(v, device, world):
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(v)], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
 
 def kernel_only_ms(wl, stream, steps):
     """Average duration of the streaming kernel alone: prepare the activations
@@ -356,15 +425,172 @@ def kernel_only_ms(wl, stream, steps):
     with torch.cuda.graph(g, stream=stream):
         for i in range(n):
             qmr.ops.matmul_prepared(wl.mats[i % wl.copies], prepared, wl.y, wl.batch, overlap=True, stream=stream)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
+    replay_ms([g], stream)
+    return replay_ms([g], stream) / n
+
+
+def warm(wl, stream, n=3):
+    import torch
     with torch.cuda.stream(stream):
-        g.replay()
-        e0.record(stream)
-        g.replay()
-        e1.record(stream)
+        for i in range(n):
+            wl.step(i, stream)
+    torch.cuda.synchronize()
+
+
+def fixed_call_ms(wl, stream, world, reps=FIXED_REPS):
+    """Whole-call device time per step over a fixed number of calls (one
+    graph, replayed once untimed), max over ranks."""
+    warm(wl, stream)
+    graphs = capture(wl, stream, reps)
+    replay_ms(graphs, stream)
+    barrier(world)
+    ms = replay_ms(graphs, stream) / reps
+    graphs.clear()
+    return max_over_ranks(ms, wl.device, world)
+
+
+def single_record(name, device, seed, stream, world, peak):
+    """Whole call and streaming kernel alone for one single-matrix workload
+    (one replica per rank)."""
+    wl = Workload(name, device, seed)
+    nbytes = algorithmic_bytes(name, wl.spec)
+    call_ms = fixed_call_ms(wl, stream, world)
+    kern_ms = max_over_ranks(kernel_only_ms(wl, stream, FIXED_REPS), device, world)
+    rec = {"workload": wl.spec["desc"], "bytes_per_call": nbytes, "calls": FIXED_REPS,
+           "us_per_call": round(call_ms * 1e3, 3), "gbs": round(world * nbytes / (call_ms * 1e-3) / 1e9, 2),
+           "call_frac": round(nbytes / (call_ms * 1e-3) / 1e9 / peak, 4),
+           "kernel_us": round(kern_ms * 1e3, 3), "kernel_frac": round(nbytes / (kern_ms * 1e-3) / 1e9 / peak, 4),
+           "weight_copies": wl.copies, "replicas": world}
+    del wl
+    return rec
+
+
+# ---- the sharded MLP / head record ---------------------------------------
+
+def _dequant_torch(m):
+    """fp32 [rows, cols] dequantisation of a device PackedMatrix with torch
+    (for the consistency bound of the sharded check; the kernels never use
+    it)."""
+    import torch
+    w = m.weight.view(torch.int32)
+    per = 32 // m.bits
+    shifts = torch.arange(per, device=w.device, dtype=torch.int32) * m.bits
+    q = ((w.unsqueeze(-1) >> shifts) & ((1 << m.bits) - 1)).reshape(m.rows, m.cols).float()
+    if m.meta_bf16:
+        s = (m.scales.view(torch.int16).to(torch.int32) << 16).view(torch.float32)
+        b = (m.biases.view(torch.int16).to(torch.int32) << 16).view(torch.float32)
+    else:
+        s, b = m.scales, m.biases
+    s = s.reshape(m.rows, m.cols // m.group).repeat_interleave(m.group, dim=1)
+    b = b.reshape(m.rows, m.cols // m.group).repeat_interleave(m.group, dim=1)
+    return q * s + b
+
+
+def _full_matrix(wl, rows_total, cols, seed_off):
+    """Rank 0: the full matrix assembled from every rank's shard (each
+    shard's seeded synthetic data regenerated here)."""
+    from qmr import parallel, synth
+    parts = []
+    for r in range(wl.world):
+        r0, r1 = parallel.shard_range(rows_total, wl.world, r)
+        parts.append(synth.affine_matrix(r1 - r0, cols, 4, GROUP, seed=wl.shard_seed(r) + seed_off))
+    cat = {k: np.concatenate([p[k] for p in parts], axis=0) for k in ("weight", "scales", "biases")}
+    return synth.to_device(cat, rows_total, cols, 4, GROUP, wl.device)
+
+
+def sharded_check(wl, stream):
+    """Rank 0 compares the sharded outputs with the 1-GPU call on the full
+    matrices: every output within twice the north-star bound (both sides
+    are within 2e-5 * sum|w x| of FP64), argmax identical unless the top two
+    logits are within that bound.  Returns a dict for the JSON line."""
+    import torch
+    import torch.distributed as dist
+
+    import qmr
+    b, dev = wl.batch, wl.device
+    with torch.cuda.stream(stream):
+        wl.step(0, stream)
     stream.synchronize()
-    return e0.elapsed_time(e1) / n
+    if wl.name == "head":
+        lg = torch.empty(wl.world * wl.y.numel(), dtype=torch.float32, device=dev)
+        dist.all_gather_into_tensor(lg, wl.y)
+        got_logits = lg.view(wl.world, b, -1).permute(1, 0, 2).reshape(b, VOCAB)
+        got_idx = wl.idx.clone()
+    torch.cuda.synchronize()
+    if wl.rank != 0:
+        return None
+    x = wl.x.view(b, COLS)
+    if wl.name == "mlp":
+        g = _full_matrix(wl, ROWS, COLS, 10)
+        u = _full_matrix(wl, ROWS, COLS, 11)
+        d = _full_matrix(wl, COLS, ROWS, 12)
+        act = torch.empty(b * ROWS, dtype=torch.float32, device=dev)
+        y = torch.empty(b * COLS, dtype=torch.float32, device=dev)
+        qmr.gateup_swiglu(g, u, wl.x, act, b)
+        qmr.matmul_affine(d, act, y, b)
+        mod = wl.mods[0]
+        act_s = mod.xa.output(mod.xa.parity ^ 1, dev)[:b * ROWS].view(b, ROWS)
+        y_s = wl.y.view(b, COLS)
+        torch.cuda.synchronize()
+        G, U, D = _dequant_torch(g), _dequant_torch(u), _dequant_torch(d)
+        ax = x.abs()
+        gv, uv = x @ G.T, x @ U.T
+        sg, su = ax @ G.abs().T, ax @ U.abs().T
+        a1 = act.view(b, ROWS)
+        mag_a = uv.abs() * 1.1 * sg + (gv * torch.sigmoid(gv)).abs() * su + 0.05 * a1.abs()
+        ra = ((act_s - a1).abs() / (2 * 2e-5 * mag_a)).max().item()
+        # y_s came from act_s: its distance to y allows the down bound twice plus |D| |act_s - act|.
+        mag_y = a1.abs() @ D.abs().T
+        slack = (act_s - a1).abs() @ D.abs().T
+        ry = ((y_s - y.view(b, COLS)).abs() / (2 * 2e-5 * mag_y + slack)).max().item()
+        worst = max(ra, ry)
+        return {"vs_1gpu": "ok" if worst <= 1.0 else "FAILED", "worst_ratio": round(worst, 4),
+                "bound": "2 x 2e-5 sum|w x| per output (act and y)"}
+    h = _full_matrix(wl, VOCAB, COLS, 10)
+    logits = torch.empty(b * VOCAB, dtype=torch.float32, device=dev)
+    idx = torch.empty(b, dtype=torch.int32, device=dev)
+    qmr.head_argmax(h, wl.x, logits, idx, b)
+    torch.cuda.synchronize()
+    H = _dequant_torch(h)
+    mag = x.abs() @ H.abs().T
+    L = logits.view(b, VOCAB)
+    worst = ((got_logits - L).abs() / (2 * 2e-5 * mag)).max().item()
+    ids_ok = True
+    for bi in range(b):
+        gi, wi = int(got_idx[bi]), int(idx[bi])
+        if gi != wi:
+            # acceptable only for a near tie within the bound
+            ids_ok &= bool(abs(float(L[bi, gi]) - float(L[bi, wi])) <= 4 * 2e-5 * float(mag[bi, wi]))
+    ok = worst <= 1.0 and ids_ok
+    return {"vs_1gpu": "ok" if ok else "FAILED", "worst_ratio": round(worst, 4),
+            "argmax": got_idx.tolist(), "argmax_1gpu": idx.tolist(), "argmax_identical": got_idx.tolist() == idx.tolist(),
+            "bound": "2 x 2e-5 sum|w x| per logit"}
+
+
+def sharded_record(name, device, seed, stream, world, rank, peak):
+    """The MLP or head: unsharded at N=1, row-sharded over the ranks with the
+    peer-memory exchange at N>1 (strong scaling: one model's bytes per step)."""
+    wl = Workload(name, device, seed, world=world, rank=rank, shard=True, exchange="p2p")
+    nbytes = algorithmic_bytes(name, wl.spec)
+    ms = fixed_call_ms(wl, stream, world)
+    rec = {"workload": wl.spec["desc"], "bytes_per_step": nbytes, "steps": FIXED_REPS,
+           "us_per_step": round(ms * 1e3, 3), "gbs": round(nbytes / (ms * 1e-3) / 1e9, 2),
+           "gbs_per_gpu": round(nbytes / world / (ms * 1e-3) / 1e9, 2),
+           "frac_per_gpu": round(nbytes / world / (ms * 1e-3) / 1e9 / peak, 4),
+           "exchange": "peer-memory stores in the streaming kernel + bounded wait kernel" if wl.sharded else None,
+           "split": ("gate/up and down by output rows, activations and outputs exchanged" if name == "mlp" else
+                     "vocabulary rows, per-shard argmax keys exchanged and merged") if wl.sharded else "unsharded",
+           "gpus_active": world, "launches_per_step": wl.launches_per_step, "weight_copies": wl.copies}
+    if wl.sharded:
+        chk = sharded_check(wl, stream)
+        if chk is not None:
+            rec["check"] = chk
+    barrier(world)
+    import torch
+    torch.cuda.synchronize()
+    wl.close()
+    del wl
+    return rec
 
 
 def run_gpu(args):
@@ -380,7 +606,10 @@ def run_gpu(args):
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
     qmr.ops.init(local)
     spec = workload_spec(args.workload)
-    wl = Workload(args.workload, spec, device, seed=1000 + 17 * rank, world=world, rank=rank, exchange=args.exchange)
+    peak, peak_kind = load_peaks()
+    shard = args.workload in ("mlp", "head")
+    wl = Workload(args.workload, device, seed=1000 + 17 * rank, world=world, rank=rank, shard=shard,
+                  exchange=args.exchange)
     nbytes = algorithmic_bytes(args.workload, spec)
     # Replicas: every rank processes nbytes per step.  Shards: the ranks
     # together process one model's nbytes per step.
@@ -388,49 +617,17 @@ def run_gpu(args):
 
     stream = torch.cuda.Stream(device)
     torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        for i in range(max(args.warmup, 3)):
-            wl.step(i, stream)
-    torch.cuda.synchronize()
-
-    # Capture the timed steps into CUDA graphs of at most CHUNK steps each.
-    CHUNK = 1000
-    graphs = []
-    done = 0
-    while done < args.steps:
-        n = min(CHUNK, args.steps - done)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            for i in range(n):
-                wl.step(done + i, stream)
-        graphs.append(g)
-        done += n
-    # Warm the graphs (untimed).
-    for g in graphs[:1]:
-        g.replay()
+    warm(wl, stream, max(args.warmup, 3))
+    graphs = capture(wl, stream, args.steps)
+    replay_ms(graphs[:1], stream)  # untimed warm replay
     torch.cuda.synchronize()
 
     clocks = Clocks(local)
-    if world > 1:
-        dist.barrier()
+    barrier(world)
     torch.cuda.synchronize()
     clocks.start()
     time.sleep(0.3)
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    # CUDAGraph.replay launches on the current stream: keep events and
-    # replays on the same stream.
-    with torch.cuda.stream(stream):
-        start.record(stream)
-        for g in graphs:
-            g.replay()
-        end.record(stream)
-    stream.synchronize()
-    ms = start.elapsed_time(end)
-    t = torch.tensor([ms], device=device)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = max_over_ranks(replay_ms(graphs, stream), device, world)
     # Keep the GPU in the same loop until the clock sampler has seen >= 1.5 s
     # of it (untimed; only the first pass above is reported).  The count comes
     # from the slowest rank's time, so every rank replays the same exchanges.
@@ -442,7 +639,10 @@ def run_gpu(args):
     stream.synchronize()
     clk = clocks.stop()
     torch.cuda.synchronize()
-    kernel_ms = kernel_only_ms(wl, stream, args.steps) if args.workload in ("b3", "b1", "q8b3") else None
+    graphs.clear()
+    single = args.workload in ("b3", "b1", "q8b3")
+    kernel_ms = kernel_only_ms(wl, stream, args.steps) if single else None
+    reps_ms = fixed_call_ms(wl, stream, world) if not args.quick else None
     ms_per_step = ms_max / args.steps
     value = job_factor * nbytes * args.steps / (ms_max * 1e-3) / 1e9
 
@@ -463,8 +663,7 @@ def run_gpu(args):
             wl.step(i, stream, x=xh)
             qmr.ops.copy_f32(out, yh, out.numel(), stream=stream)
     stream.synchronize()
-    if world > 1:
-        dist.barrier()
+    barrier(world)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
@@ -474,33 +673,31 @@ def run_gpu(args):
             qmr.ops.copy_f32(out, yh, out.numel(), stream=stream)
         e1.record(stream)
     stream.synchronize()
-    te = torch.tensor([e0.elapsed_time(e1)], device=device)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = job_factor * nbytes * e2e_steps / (float(te.item()) * 1e-3) / 1e9
+    te = max_over_ranks(e0.elapsed_time(e1), device, world)
+    e2e_value = job_factor * nbytes * e2e_steps / (te * 1e-3) / 1e9
 
-    peak, peak_kind = load_peaks()
     if kernel_ms is not None:
-        kernel_nbytes = nbytes  # the streaming kernel reads weights, x' and writes y
-        achieved = kernel_nbytes / (kernel_ms * 1e-3) / 1e9
+        achieved = nbytes / (kernel_ms * 1e-3) / 1e9  # the streaming kernel reads weights, x' and writes y
         timing_note = "streaming kernel alone: activations prepared once, K launches in one graph"
     else:
         # per GPU: its share of the job's bytes over the step time
         achieved = job_factor * nbytes / world / (ms_per_step * 1e-3) / 1e9
         timing_note = "whole call" + (f", sharded step incl. the {wl.exchange} exchange" if wl.sharded else "")
     traffic = profile_traffic(args.workload)
+    config = config_of(spec)
+    config.update({"weight_copies": wl.copies, "l2_bytes": wl.l2,
+                   "l2_policy": f"{wl.copies} distinct weight copies rotated (> 4x L2)",
+                   "bytes_per_step": nbytes,
+                   "parallelism": (f"rowshard{world} ({'peer-memory exchange in the kernels' if wl.exchange == 'p2p' else 'NCCL all-gather'})"
+                                   if wl.sharded else f"replicas{world}" if world > 1 else "single")})
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 6), "higher_is_better": True,
         "scaling": "strong" if wl.sharded else "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; benchmark distributions)",
-        "config": {"workload": spec["desc"], "batch": spec["batch"], "rows": spec["rows"], "cols": spec["cols"],
-                   "bits": spec["bits"], "group": GROUP, "metadata": "bf16", "weight_copies": wl.copies,
-                   "l2_bytes": wl.l2, "l2_policy": f"{wl.copies} distinct weight copies rotated (> 4x L2)",
-                   "bytes_per_step": nbytes,
-                   "parallelism": (f"rowshard{world} ({'peer-memory exchange in the kernels' if wl.exchange == 'p2p' else 'NCCL all-gather'})"
-                                   if wl.sharded else
-                                   f"replicas{world}" if world > 1 else "single")},
+        "vs_baseline": None, "dtype": "f32", "arith": ARITH,
+        "data": "synthetic (seeded; benchmark distributions)",
+        "config": config,
+        "call_frac": round(job_factor * nbytes / world / (ms_per_step * 1e-3) / 1e9 / peak, 4),
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "steps": e2e_steps},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
@@ -510,8 +707,20 @@ def run_gpu(args):
         "gpu_launches": wl.launches_per_step * args.steps,
         "clocks": clk,
     }
+    if reps_ms is not None:
+        line["reps200"] = {"calls": FIXED_REPS, "us_per_call": round(reps_ms * 1e3, 3),
+                           "value": round(job_factor * nbytes / (reps_ms * 1e-3) / 1e9, 2)}
+    wl.close()
+    del wl
+
+    if args.workload == "b3" and not args.quick:
+        line["workloads"] = {n: single_record(n, device, 2000 + 17 * rank, stream, world, peak)
+                             for n in ("b1", "q8b3")}
+        line["sharded"] = {n: sharded_record(n, device, 3000, stream, world, rank, peak) for n in ("mlp", "head")}
+
     if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.quick):
         import oracle
+        oracle.set_threads(host_threads())
         rows = calibrate_rows(args.workload, spec, 2.0)
         secs, nb = 0.0, 0.0
         for i in range(5):
@@ -524,17 +733,9 @@ def run_gpu(args):
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
-        # Every graph that holds NCCL calls must be gone before the process
-        # group is destroyed (the loop variable above holds one too).
-        g = None
-        graphs.clear()
-        del graphs, g
         import gc
         gc.collect()
         torch.cuda.synchronize()
-        if wl.sharded:
-            for m in wl.mods:
-                m.close()
         dist.barrier()
         dist.destroy_process_group()
     return 0
@@ -551,7 +752,7 @@ def main():
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="sharded workloads: output exchange over peer memory in the kernels, or NCCL all-gathers")
     ap.add_argument("--quick", action="store_true",
-                    help="profiling runs: no clock-sampling loop, short e2e, no CPU baseline")
+                    help="profiling runs: no clock-sampling loop, no sub-records, short e2e, no CPU baseline")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -3,8 +3,8 @@
  *
  * This library replaces the matrix half of the reference engine's GPU
  * dispatch layer (rucin93/qwen-mlx-runner v0.7.3, src/gpu.rs).  The reference
- * engine binds to it through `extern "C"` declarations;
- * every entry point below names the reference interface it stands in for.
+ * engine binds to it through `extern "C"` declarations of the entry points
+ * below; each one names the reference interface it stands in for.
  *
  * Conventions shared by all entry points
  *   - Every pointer argument that names tensor data is a DEVICE pointer of
@@ -158,8 +158,11 @@ int qmr_embed_affine(const void *w, const void *scales, const void *biases, uint
  * larger shapes fail with QMR_ERANGE before any launch.  The array is shared
  * by all streams and threads, so calls that overlap in time race and must be
  * serialised by the caller.  The first call on each device does the set-up
- * (symbol lookup with the device current, clearing the array, which
- * synchronises the device) and should come before any stream capture. */
+ * (symbol lookup with the device current, clearing the array, then
+ * cudaDeviceSynchronize so the clear is finished before any stream uses it)
+ * and should come before any stream capture.  The array's address is kept
+ * for the life of the process: do not use this entry point after
+ * cudaDeviceReset. */
 int qmr_matmul_affine_static(const void *w, const void *scales, const void *biases, const float *x,
                              float *y, uint32_t rows, uint32_t cols, uint32_t bits, uint32_t group,
                              uint32_t batch, int meta_bf16, void *stream);

@@ -226,10 +226,14 @@ __global__ void __launch_bounds__(32) exchange_wait_kernel(const unsigned int *f
         }
     }
     if (!__all_sync(0xffffffffu, ok) || keys == nullptr || lane >= batch) return;
+    // The lanes that acquired the flags are not the lanes that read the keys:
+    // the keys are read with acquire semantics too, so each read is ordered
+    // after the publishing rank's release of the flag this warp observed.
+    __syncwarp();
     unsigned long long k = 0ull;
     for (int r = 0; r < world; ++r) {
         unsigned long long v;
-        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(keys + r * 4 + lane) : "memory");
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(keys + r * 4 + lane) : "memory");
         k = v > k ? v : k;
     }
     if (argmax) argmax[lane] = (int)(0xffffffffu - (uint32_t)(k & 0xffffffffu));

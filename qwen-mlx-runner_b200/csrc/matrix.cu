@@ -122,13 +122,13 @@ int acquire_scratch(cudaStream_t stream, size_t need, void **out) {
     }
     const size_t floor_bytes = scratch_bytes(4, 65536, 4);
     const size_t want = need > floor_bytes ? need : floor_bytes;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(stream, &cs);
+    if (cs != cudaStreamCaptureStatusNone)
+        return fail(QMR_EUNSUPPORTED,
+                    "activation scratch must be allocated or grown, which cannot happen during stream capture; "
+                    "make one call with the largest shape on this stream before capturing");
     if (s.base != nullptr) {
-        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-        cudaStreamIsCapturing(stream, &cs);
-        if (cs != cudaStreamCaptureStatusNone)
-            return fail(QMR_EUNSUPPORTED,
-                        "activation scratch must grow, which cannot happen during stream capture; "
-                        "make one call with the largest shape before capturing");
         if (cudaStreamSynchronize(stream) != cudaSuccess) return fail(QMR_ECUDA, "stream synchronize failed");
         cudaFree(s.base);
         s.base = nullptr;
@@ -139,6 +139,11 @@ int acquire_scratch(cudaStream_t stream, size_t need, void **out) {
     if (e != cudaSuccess) return fail(QMR_ECUDA, "cudaMalloc of activation scratch failed: %s", cudaGetErrorString(e));
     e = cudaMemset(p, 0, want);  // counters start at zero
     if (e != cudaSuccess) return fail(QMR_ECUDA, "cudaMemset of activation scratch failed: %s", cudaGetErrorString(e));
+    // The clear runs on the legacy stream, which does not order against a
+    // non-blocking caller stream: finish it before any kernel uses the
+    // buffer (cudaMalloc above has synchronised the device already).
+    e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return fail(QMR_ECUDA, "waiting for the scratch clear failed: %s", cudaGetErrorString(e));
     s.base = p;
     s.bytes = want;
     *out = p;

@@ -1,7 +1,8 @@
 // Packed-affine dequantise-and-multiply kernels for sm_100a: shared helpers,
 // the activation prep pass, the register-streaming fallback kernel, the
-// generic per-element kernel and the embed kernel.  The main streaming kernel
-// is rowlane.cuh.
+// generic per-element kernel and the embed kernel.  The default streaming
+// kernel is the tensor-core one in mma_stream.cuh; the FP32 TMA pipeline is
+// tile.cuh.
 //
 // Semantics follow the reference's matrix kernels (rucin93/qwen-mlx-runner
 // v0.7.3): y[b*rows+r] = sum_c (q[r,c]*s[r,g]+b[r,g]) * x[b*cols+c], with

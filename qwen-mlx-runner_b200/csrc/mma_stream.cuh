@@ -821,11 +821,13 @@ __global__ void __launch_bounds__(32 * NW, 1)
     const bool xchg = a.xworld > 1;
     if (EPI == 2 || xchg) {
         // Last CTA: this CTA's stores (peer stores included) are ordered
-        // before its count, the last CTA's epilogue after all counts.
-        if (xchg)
-            __threadfence_system();
-        else
-            __threadfence();
+        // before its count by a GPU-scope fence, the last CTA's epilogue after
+        // all counts.  With an exchange, the last CTA alone then fences at
+        // system scope before it releases the epoch: fences are cumulative, so
+        // that one fence orders every store the counts made visible to it
+        // before the flag a peer acquires.  (No CTA waits for its own NVLink
+        // stores to be acknowledged before counting.)
+        __threadfence();
         __syncthreads();
         if (threadIdx.x == 0) flag = (atomicAdd(a.done, 1u) == gridDim.x - 1) ? 1u : 0u;
         __syncthreads();

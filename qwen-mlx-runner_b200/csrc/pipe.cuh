@@ -1,6 +1,7 @@
 // Shared-memory pipeline primitives for sm_100a: mbarriers with waits bounded
-// by the global timer, L2 cache policies, TMA tensor and bulk copies (never
-// with cluster multicast), and Ampere-style cp.async with mbarrier arrival.
+// by the global timer, L2 cache policies, TMA tensor and bulk copies (each
+// into the issuing CTA's own shared memory only), and Ampere-style cp.async
+// with mbarrier arrival.
 #pragma once
 
 #include <cuda.h>

@@ -18,8 +18,12 @@
 //    that overlap in time (two streams, or two host threads) race on it and
 //    must be serialised by the caller;
 //  * the first call on each device does the set-up (it looks the array's
-//    address up with that device current and clears it, which synchronises
-//    the device), so it should come before any stream capture.
+//    address up with that device current, clears the array and waits for
+//    the device to finish the clear), so it should come before any stream
+//    capture;
+//  * the address is looked up once per device and kept for the life of the
+//    process: the entry point does not survive cudaDeviceReset (which
+//    unloads the module that holds the array).
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -41,7 +45,9 @@ void *g_static_addr[64] = {};
 
 // Address of this device's array, set up on first use: cudaGetSymbolAddress
 // with the device current, then the whole array cleared (the argmax keys and
-// the split-tile counters in it must start at zero).
+// the split-tile counters in it must start at zero) and the device
+// synchronised, so the clear has finished before any stream -- a
+// non-blocking one included -- runs a kernel on the array.
 int static_scratch(void **out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -57,6 +63,9 @@ int static_scratch(void **out) {
             return fail(QMR_ECUDA, "static scratch is not 256-byte aligned");
         e = cudaMemset(p, 0, kStaticScratchBytes);
         if (e != cudaSuccess) return fail(QMR_ECUDA, "clearing the static scratch: %s", cudaGetErrorString(e));
+        e = cudaDeviceSynchronize();
+        if (e != cudaSuccess)
+            return fail(QMR_ECUDA, "waiting for the static scratch clear: %s", cudaGetErrorString(e));
         g_static_addr[dev] = p;
     }
     *out = g_static_addr[dev];

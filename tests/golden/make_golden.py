@@ -88,4 +88,6 @@ def main(reference_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py REFERENCE_ROOT (a checkout of rucin93/qwen-mlx-runner v0.7.3)")
+    main(sys.argv[1])

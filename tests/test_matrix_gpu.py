@@ -270,14 +270,11 @@ def test_selective_mlp_r2_real_shapes_match_legacy_bits_and_fp64_with_guards(cud
         assert np.all(o[:4] == 12345.0) and np.all(o[rows * 3 + 4:] == 12345.0)
         assert np.all(np.isfinite(o[4:rows * 3 + 4]))
     assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
-    sample = sorted({s * (rows - 1) // 31 for s in range(32)})
-    for r in sample:
-        want, mag = oracle.matmul_f64(weights, high_half(scales), high_half(biases), x, rows, cols, 4, 64, batch=3,
-                                      row0=r, nrows=1)
-        for bi in range(3):
-            got = outs[0][4 + bi * rows + r]
-            assert abs(got - want[bi, r]) <= 4e-4 + abs(want[bi, r]) * 3e-5
-            assert_ns_bound([got], [want[bi, r]], [mag[bi, r]], f"R2 {rows}x{cols} row {r} rhs {bi}")
+    # Every row of every RHS against FP64: the reference's tolerance and the north-star bound.
+    want, mag = oracle.matmul_f64(weights, high_half(scales), high_half(biases), x, rows, cols, 4, 64, batch=3)
+    got = outs[0][4:rows * 3 + 4].reshape(3, rows).astype(np.float64)
+    assert np.all(np.abs(got - want) <= 4e-4 + np.abs(want) * 3e-5), f"R2 {rows}x{cols}"
+    assert_ns_bound(got, want, mag, f"R2 {rows}x{cols}")
     for buf in [wb, sb, bb, xb]:
         raw = buf.cpu().numpy()
         assert np.all(raw[:16] == 0xA5) and np.all(raw[-16:] == 0xA5)
@@ -287,16 +284,12 @@ def test_selective_mlp_r2_real_shapes_match_legacy_bits_and_fp64_with_guards(cud
 # Benchmark shapes (configs 0-3) with the benchmark distributions
 # ---------------------------------------------------------------------------
 
-def sampled_rows(rows, n=96):
-    return sorted({0, 1, rows - 2, rows - 1} | {int(v) for v in np.linspace(0, rows - 1, n)})
-
-
-def check_sampled(mat, m, x, y, batch, what):
-    """Compare sampled rows of y [batch, rows] with the FP64 oracle."""
-    for r in sampled_rows(m.rows):
-        want, mag = oracle.matmul_f64(mat["weight"], mat["scales"], mat["biases"], x, m.rows, m.cols, m.bits,
-                                      m.group, batch=batch, row0=r, nrows=1)
-        assert_ns_bound(y[:, r], want[:, r], mag[:, r], f"{what} row {r}")
+def check_all_rows(mat, m, x, y, batch, what):
+    """Compare every output row of y [batch, rows] with the FP64 oracle."""
+    want, mag = oracle.matmul_f64(mat["weight"], mat["scales"], mat["biases"], x, m.rows, m.cols, m.bits, m.group,
+                                  batch=batch)
+    assert_ns_bound(y, want, mag, what)
+    return want, mag
 
 
 @pytest.mark.parametrize("bits", [4, 8])
@@ -313,8 +306,11 @@ def test_config_shapes_b1_b3_parity_and_block_equals_gemv(cuda, bits):
         qmr.matvec_affine(m, xd[b * cols:(b + 1) * cols], y1[b])
     torch.cuda.synchronize()
     y3h = y3.cpu().numpy().reshape(3, rows)
-    assert np.array_equal(y3h.view(np.uint32), y1.cpu().numpy().view(np.uint32))
-    check_sampled(mat, m, x, y3h, 3, f"Q{bits} B3 {rows}x{cols}")
+    y1h = y1.cpu().numpy()
+    assert np.array_equal(y3h.view(np.uint32), y1h.view(np.uint32))
+    check_all_rows(mat, m, x, y3h, 3, f"Q{bits} B3 {rows}x{cols}")
+    # The B1 GEMV (config 0 for Q4) on its own, every row.
+    check_all_rows(mat, m, x[:1], y1h[:1], 1, f"Q{bits} B1 {rows}x{cols}")
 
 
 def test_gateup_swiglu_matches_oracle_and_separate_projections(cuda):
@@ -352,6 +348,30 @@ def test_gateup_swiglu_matches_oracle_and_separate_projections(cuda):
             assert np.array_equal(a[1].view(np.uint32), a1.cpu().numpy().view(np.uint32))
 
 
+@pytest.mark.parametrize("batch", [1, 3])
+def test_mlp_down_of_swiglu_every_row(cuda, batch):
+    """Config 2 end to end: y = down(silu(gate x) * (up x)) through the fused
+    gate/up kernel and the 5120x17408 down projection; every activation row
+    against FP64 swiglu, every output row against FP64 down of the device
+    activations (the down stage's own bound)."""
+    H, F = 5120, 17408
+    g = synth.affine_matrix(F, H, 4, 64, seed=81)
+    u = synth.affine_matrix(F, H, 4, 64, seed=82)
+    d = synth.affine_matrix(H, F, 4, 64, seed=83)
+    gm, um, dm = (synth.to_device(t, r, c, 4, 64) for t, r, c in ((g, F, H), (u, F, H), (d, H, F)))
+    x = synth.activations(batch, H, seed=84 + batch)
+    act = torch.empty(batch * F, dtype=torch.float32, device="cuda")
+    y = torch.empty(batch * H, dtype=torch.float32, device="cuda")
+    qmr.gateup_swiglu(gm, um, f32_tensor(x), act, batch)
+    qmr.matmul_affine(dm, act, y, batch)
+    torch.cuda.synchronize()
+    a = act.cpu().numpy().reshape(batch, F)
+    want_a, mag_a = oracle.swiglu_f64(g["weight"], g["scales"], g["biases"], u["weight"], u["scales"], u["biases"],
+                                      x, F, H, 4, 64, batch)
+    assert_ns_bound(a, want_a, mag_a + np.abs(want_a) * 0.05, f"MLP swiglu B{batch}")
+    check_all_rows(d, dm, a, y.cpu().numpy().reshape(batch, H), batch, f"MLP down B{batch}")
+
+
 def test_head_argmax_matches_logits_and_oracle(cuda):
     rows, cols = 152064, 5120
     mat = synth.affine_matrix(rows, cols, 4, 64, seed=41)
@@ -384,7 +404,7 @@ def test_head_argmax_matches_logits_and_oracle(cuda):
             if w[best] - second > 4 * NS_RTOL * mag[0, best]:
                 assert got[b] == best
             assert best in top
-        check_sampled(mat, m, x, lg, batch, f"head B{batch}")
+        check_all_rows(mat, m, x, lg, batch, f"head B{batch}")
 
 
 def test_head_argmax_ties_go_to_lowest_index(cuda):
@@ -501,10 +521,7 @@ def test_fresh_matrices_keep_blocks_equal_to_gemv(cuda, meta):
         torch.cuda.synchronize()
         got = y4.cpu().numpy().reshape(4, rows)
         assert np.array_equal(got[2].view(np.uint32), y1.cpu().numpy().view(np.uint32)), f"iteration {it}"
-        for r in sampled_rows(rows, 16):
-            want, mag = oracle.matmul_f64(mat["weight"], mat["scales"], mat["biases"], x_np, rows, cols, 4, 64,
-                                          batch=4, row0=r, nrows=1)
-            assert_ns_bound(got[:, r], want[:, r], mag[:, r], f"fresh {meta} it {it} row {r}")
+        check_all_rows(mat, m, x_np, got, 4, f"fresh {meta} it {it}")
         del m
 
 
@@ -523,6 +540,8 @@ def test_all_streaming_paths_meet_the_bound(cuda, bits, meta):
             m = synth.to_device(mat, rows, cols, bits, 64)
             x_np = synth.activations(4, cols, seed=rows)
             x = f32_tensor(x_np.ravel())
+            want, mag = oracle.matmul_f64(mat["weight"], mat["scales"], mat["biases"], x_np, rows, cols, bits, 64,
+                                          batch=4)
             for path in ("mma", "tma", "registers"):
                 qmr.ops.set_stream_path(path)
                 y4 = torch.full((4 * rows,), float("nan"), dtype=torch.float32, device="cuda")
@@ -532,14 +551,13 @@ def test_all_streaming_paths_meet_the_bound(cuda, bits, meta):
                 torch.cuda.synchronize()
                 got = y4.cpu().numpy().reshape(4, rows)
                 assert np.array_equal(got[2].view(np.uint32), y1.cpu().numpy().view(np.uint32)), (path, rows, cols)
-                for r in sampled_rows(rows, 24):
-                    want, mag = oracle.matmul_f64(mat["weight"], mat["scales"], mat["biases"], x_np, rows, cols,
-                                                  bits, 64, batch=4, row0=r, nrows=1)
-                    assert_ns_bound(got[:, r], want[:, r], mag[:, r], f"{path} {rows}x{cols} row {r}")
+                assert_ns_bound(got, want, mag, f"{path} {rows}x{cols}")
             if rows >= 1000 and bits == 4 and meta == "bf16":
                 upm = synth.affine_matrix(rows, cols, bits, 64, seed=7, meta=meta)
                 up = synth.to_device(upm, rows, cols, bits, 64)
                 x3 = x_np[:3]
+                want_a, amag = oracle.swiglu_f64(mat["weight"], mat["scales"], mat["biases"], upm["weight"],
+                                                 upm["scales"], upm["biases"], x3, rows, cols, bits, 64, 3)
                 for path in ("mma", "tma", "registers"):
                     qmr.ops.set_stream_path(path)
                     act = torch.empty(3 * rows, dtype=torch.float32, device="cuda")
@@ -551,13 +569,7 @@ def test_all_streaming_paths_meet_the_bound(cuda, bits, meta):
                     lgh = lg.cpu().numpy().reshape(3, rows)
                     assert [oracle.argmax_f32(lgh[b]) for b in range(3)] == idx.cpu().numpy().tolist()
                     a = act.cpu().numpy().reshape(3, rows)
-                    for r in sampled_rows(rows, 12):
-                        want, amag = oracle.swiglu_f64(mat["weight"][r:r + 1], mat["scales"][r:r + 1],
-                                                       mat["biases"][r:r + 1], upm["weight"][r:r + 1],
-                                                       upm["scales"][r:r + 1], upm["biases"][r:r + 1], x3, 1, cols,
-                                                       bits, 64, 3)
-                        assert_ns_bound(a[:, r], want[:, 0], amag[:, 0] + np.abs(want[:, 0]) * 0.1,
-                                        f"{path} swiglu row {r}")
+                    assert_ns_bound(a, want_a, amag + np.abs(want_a) * 0.1, f"{path} swiglu {rows}x{cols}")
         assert qmr.ops.device_error() == 0
     finally:
         qmr.ops.set_stream_path("mma")
