@@ -23,6 +23,7 @@ import numpy as np
 HERE = pathlib.Path(__file__).resolve().parent
 LIB = HERE / "liboracle.so"
 SRC = HERE / "oracle.c"
+SOURCES = [HERE / "oracle.c", HERE / "decode.c"]
 
 # -ffp-contract=off: Rust never fuses a*b+c, so neither may the restatement.
 CFLAGS = ["-O3", "-march=x86-64-v2", "-fPIC", "-ffp-contract=off", "-fopenmp", "-shared"]
@@ -31,9 +32,9 @@ _lib = None
 
 
 def build(force: bool = False) -> pathlib.Path:
-    if force or not LIB.exists() or LIB.stat().st_mtime < SRC.stat().st_mtime:
+    if force or not LIB.exists() or any(LIB.stat().st_mtime < src.stat().st_mtime for src in SOURCES):
         tmp = LIB.with_suffix(".so.tmp")
-        subprocess.run(["gcc", *CFLAGS, "-o", os.fspath(tmp), os.fspath(SRC), "-lm"], check=True)
+        subprocess.run(["gcc", *CFLAGS, "-o", os.fspath(tmp), *map(os.fspath, SOURCES), "-lm"], check=True)
         os.replace(tmp, LIB)
     return LIB
 
@@ -57,6 +58,18 @@ def lib() -> ctypes.CDLL:
         h.or_bf16_rne.restype = ctypes.c_uint16
         h.or_num_threads.restype = i32
         h.or_set_threads.argtypes = [i32]
+        h.or_model_new.restype = vp
+        h.or_model_new.argtypes = [vp, vp, vp, u32]
+        h.or_model_free.argtypes = [vp]
+        h.or_model_set_matrix.argtypes = [vp, i32, i32, vp, vp, vp, i32, u32, u32, u32, u32]
+        h.or_model_set_synth.argtypes = [vp, i32, i32, u64, u32, u32, u32]
+        h.or_model_set_vector.argtypes = [vp, i32, i32, vp]
+        h.or_model_reset.argtypes = [vp]
+        h.or_model_forward.argtypes = [vp, u32, vp]
+        h.or_model_forward.restype = i32
+        h.or_model_position.argtypes = [vp]
+        h.or_model_position.restype = u32
+        h.or_synth_matrix.argtypes = [u64, u32, u32, u32, vp, vp, vp]
         _lib = h
     return _lib
 
@@ -155,3 +168,79 @@ def tolerance_ratio(got, want, scale, rtol=2e-5, atol=0.0):
     ratio = np.where(np.isnan(ratio), np.inf, ratio)
     i = int(np.argmax(ratio)) if ratio.size else -1
     return (float(ratio[i]) if ratio.size else 0.0), i
+
+
+# ---------------------------------------------------------------------------
+# FP64 decode graph (decode.c)
+# ---------------------------------------------------------------------------
+
+MATRIX_SLOTS = {"qkv": 0, "z": 1, "a": 2, "b": 3, "out": 4, "q": 5, "k": 6, "v": 7, "o": 8, "gate": 9, "up": 10,
+                "down": 11}
+VECTOR_SLOTS = {"input_norm": 0, "post_norm": 1, "conv": 2, "A_log": 3, "dt_bias": 4, "delta_norm": 5,
+                "q_norm": 6, "k_norm": 7}
+
+
+def synth_matrix(seed: int, mid: int, rows: int, cols: int):
+    """The counter-based synthetic Q4/g64 matrix (words, BF16 scale and bias bits)."""
+    w = np.empty(rows * cols // 8, dtype=np.uint32)
+    s = np.empty(rows * cols // 64, dtype=np.uint16)
+    b = np.empty(rows * cols // 64, dtype=np.uint16)
+    lib().or_synth_matrix(seed, mid, rows, cols, w.ctypes.data, s.ctypes.data, b.ctypes.data)
+    return dict(weight=w.reshape(rows, cols // 8), scales=s.reshape(rows, cols // 64),
+                biases=b.reshape(rows, cols // 64))
+
+
+class DecodeOracle:
+    """FP64 restatement of the reference's per-token graph (decode.c).
+
+    cfg: dict with hidden, inter, layers, heads, kv_heads, head_dim, vocab,
+    lin_key_heads, lin_value_heads, lin_key_dim, lin_value_dim, conv_width,
+    rotary_dim, eps, theta, is_attn (list of bools), context."""
+
+    def __init__(self, cfg):
+        self.cfg = cfg
+        u = np.array([cfg["hidden"], cfg["inter"], cfg["layers"], cfg["heads"], cfg["kv_heads"], cfg["head_dim"],
+                      cfg["vocab"], cfg["lin_key_heads"], cfg["lin_value_heads"], cfg["lin_key_dim"],
+                      cfg["lin_value_dim"], cfg["conv_width"], cfg["rotary_dim"]], dtype=np.uint32)
+        f = np.array([cfg["eps"], cfg["theta"]], dtype=np.float64)
+        att = np.array([1 if a else 0 for a in cfg["is_attn"]], dtype=np.uint8)
+        self._keep = []
+        self.h = lib().or_model_new(u.ctypes.data, f.ctypes.data, att.ctypes.data, cfg["context"])
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().or_model_free(self.h)
+            self.h = None
+
+    def set_matrix(self, layer, which, mat, rows, cols, bits, group):
+        """layer -1: which "embed" / "head"; else a MATRIX_SLOTS name."""
+        slot = (0 if which == "embed" else 1) if layer < 0 else MATRIX_SLOTS[which]
+        w = np.ascontiguousarray(mat["weight"], dtype=np.uint32)
+        s, bf = _meta(mat["scales"])
+        b, _ = _meta(mat["biases"])
+        self._keep += [w, s, b]
+        lib().or_model_set_matrix(self.h, layer, slot, w.ctypes.data, s.ctypes.data, b.ctypes.data, bf, rows,
+                                  cols, bits, group)
+
+    def set_synth(self, layer, which, seed, mid, rows, cols):
+        slot = (0 if which == "embed" else 1) if layer < 0 else MATRIX_SLOTS[which]
+        lib().or_model_set_synth(self.h, layer, slot, seed, mid, rows, cols)
+
+    def set_vector(self, layer, which, values):
+        v = np.ascontiguousarray(values, dtype=np.float32)
+        self._keep.append(v)
+        lib().or_model_set_vector(self.h, layer, 0 if layer < 0 else VECTOR_SLOTS[which], v.ctypes.data)
+
+    def reset(self):
+        lib().or_model_reset(self.h)
+
+    @property
+    def position(self):
+        return int(lib().or_model_position(self.h))
+
+    def forward(self, token: int, logits: bool = True):
+        out = np.empty(self.cfg["vocab"], dtype=np.float64) if logits else None
+        rc = lib().or_model_forward(self.h, token, out.ctypes.data if logits else None)
+        if rc != 0:
+            raise ValueError("token outside the vocabulary or context full")
+        return out

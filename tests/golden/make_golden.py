@@ -5,6 +5,9 @@ double-precision scalar oracle for tiny hybrid models) in a scratch copy, then
 stores:
   * tiny-bf16/{model.safetensors,config.json,golden.json}: the packed Q4/g32
     checkpoint with BF16 metadata and the reference's golden logits;
+  * tiny-q4/{model.safetensors,config.json,golden.json}: the same model
+    quantised with F16 scale/bias (not all BF16-exact, so it loads with f32
+    metadata) and its golden logits;
   * matrices.npz: for several packed matrices of that checkpoint the packed
     words, BF16 scale/bias bits, the reference's dequantised values
     (q*scale+bias in f64) and y = mv(name, x) computed by the reference's own
@@ -57,11 +60,12 @@ def main(reference_root: str) -> None:
         (tmp / "scripts").mkdir()
         shutil.copy(script, tmp / "scripts" / "make_fixture.py")
         g = runpy.run_path(str(tmp / "scripts" / "make_fixture.py"), run_name="__main__")
+        for fixture in ("tiny-bf16", "tiny-q4"):
+            dst = HERE / fixture
+            dst.mkdir(exist_ok=True)
+            for f in ("model.safetensors", "config.json", "golden.json"):
+                shutil.copy(tmp / "tests" / "fixtures" / fixture / f, dst / f)
         src = tmp / "tests" / "fixtures" / "tiny-bf16"
-        dst = HERE / "tiny-bf16"
-        dst.mkdir(exist_ok=True)
-        for f in ("model.safetensors", "config.json", "golden.json"):
-            shutil.copy(src / f, dst / f)
         tensors = read_safetensors(src / "model.safetensors")
         weights, mv = g["weights"], g["mv"]
         arrays = {}
