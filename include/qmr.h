@@ -314,6 +314,87 @@ int qmr_head_argmax_exchange(const void *w, const void *scales, const void *bias
  * merged argmax (token ids, may be NULL) and keys (may be NULL) per RHS. */
 int qmr_exchange_wait(const QmrExchange *ex, uint32_t batch, int32_t *argmax, uint64_t *best_key, void *stream);
 
+/* ---- checkpoints and the decode engine ---------------------------------
+ * The per-token graph of the hybrid Qwen3.5 model (src/engine.rs:607-797):
+ * DeltaNet and gated-attention layers in the config's 3:1 pattern, SwiGLU
+ * MLPs, final norm and vocabulary head with greedy argmax.  All matrices run
+ * through this library's packed-affine kernels; the other decode-step work
+ * runs in this library's own kernels (one fused mixer launch per DeltaNet or
+ * attention layer; RMSNorm folded into the next matrix's activation prep and
+ * residual adds into the output epilogue where the tensor-core kernel takes
+ * the matrix).  Activations, recurrent state and the KV cache are FP32.
+ * Position and token live in device memory, so one captured CUDA graph per
+ * step kind is replayed for every token.
+ *
+ * A QmrModel is bound to the CUDA device that is current when it is created;
+ * its calls must come from one thread at a time (like the reference's
+ * single-threaded Gpu). */
+#define QMR_MAX_LAYERS 256
+
+/* ModelConfig (src/config.rs:4-25) as the engine uses it. */
+typedef struct QmrModelConfig {
+    uint32_t hidden_size, intermediate_size, num_layers, num_heads, num_kv_heads, head_dim, vocab_size;
+    uint32_t linear_key_heads, linear_value_heads, linear_key_dim, linear_value_dim, conv_width;
+    uint32_t rotary_dim;                    /* head_dim * partial_rotary_factor */
+    float rms_eps, rope_theta;
+    uint8_t is_attention[QMR_MAX_LAYERS];   /* 1: full attention, 0: DeltaNet */
+} QmrModelConfig;
+
+typedef struct QmrCheckpoint QmrCheckpoint;
+typedef struct QmrModel QmrModel;
+
+/* Checkpoint::open (src/weights.rs:53-289): config.json plus one
+ * .safetensors file or model.safetensors.index.json with its shards;
+ * validates the config (src/config.rs:29-235), the safetensors headers and
+ * the MLX affine quantisation metadata. */
+int qmr_checkpoint_open(const char *dir, QmrCheckpoint **out);
+void qmr_checkpoint_close(QmrCheckpoint *cp);
+int qmr_checkpoint_config(const QmrCheckpoint *cp, QmrModelConfig *cfg, uint32_t *max_position, int *tied);
+/* Checkpoint::matrix (src/weights.rs:292-351): shape and format of a packed
+ * matrix; when w/s/b are non-NULL also its data: rows*cols*bits/32 u32 words
+ * and rows*cols/group f32 scales and biases (F16/BF16/F32 widened). */
+int qmr_checkpoint_matrix(const QmrCheckpoint *cp, const char *name, uint32_t *rows, uint32_t *cols, uint32_t *bits,
+                          uint32_t *group, uint32_t *w, float *s, float *b);
+/* Checkpoint::vector (src/weights.rs:353-368): n elements; data into out when
+ * it is non-NULL and cap >= n. */
+int qmr_checkpoint_vector(const QmrCheckpoint *cp, const char *name, float *out, uint64_t cap, uint64_t *n);
+
+/* Engine::load (src/engine.rs:276-446): a checkpoint into device memory for
+ * `context` positions (1..max_position_embeddings).  Metadata is compacted
+ * to BF16 when QWEN_METAL_METADATA=bf16 and every value is BF16-exact
+ * (src/gpu.rs:479-490, metadata.rs:6-14), as the reference does. */
+int qmr_model_load(const char *dir, uint32_t context, QmrModel **out);
+/* Engine::synthetic_qwen27b (src/engine/synthetic.rs:92-281) with distinct
+ * seeded Q4/g64 BF16-metadata weights per layer and matrix (the counter
+ * generator of the test oracle) and the reference's synthetic constants for
+ * norms (1), conv (0.1), A_log and dt_bias (0). */
+int qmr_model_synthetic(const QmrModelConfig *cfg, uint64_t seed, uint32_t context, QmrModel **out);
+void qmr_model_free(QmrModel *m);
+int qmr_model_config(const QmrModel *m, QmrModelConfig *cfg, uint32_t *context);
+/* Engine::reset (src/engine.rs:561-584): clear recurrent state, position 0. */
+int qmr_model_reset(QmrModel *m);
+int qmr_model_position(const QmrModel *m, uint32_t *pos);
+/* Engine::forward (src/engine.rs:586-605): one token at the current
+ * position.  logits (host, vocab floats) and next (the greedy argmax,
+ * src/chat.rs:383-390) may be NULL.  Fails before any launch for a token
+ * outside the vocabulary or a full context. */
+int qmr_model_forward(QmrModel *m, uint32_t token, float *logits, int32_t *next);
+/* Prefill n prompt tokens then greedy-decode: out receives max_new tokens,
+ * the first from the prompt's last logits (the reference's prefill + sample +
+ * step loop, src/engine.rs:846-935, at temperature 0 and without EOS).  The
+ * steps run as graph replays with no host round trip in between;
+ * prefill_ms / decode_ms (may be NULL) are device times. */
+int qmr_model_generate(QmrModel *m, const uint32_t *prompt, uint32_t n_prompt, uint32_t max_new, uint32_t *out,
+                       double *prefill_ms, double *decode_ms);
+/* Engine::mlp_r2_eligible_matrices (src/engine.rs:454-468). */
+int qmr_model_mlp_r2_eligible(const QmrModel *m, uint32_t *count);
+/* Gpu::metadata_stats (src/gpu.rs:473-478): matrices loaded with compacted
+ * BF16 metadata and the bytes that saved. */
+int qmr_model_metadata_stats(const QmrModel *m, uint64_t *matrices, uint64_t *saved_bytes);
+/* Kernels the library launches per decode step with and without the head
+ * (the captured graphs' node counts). */
+int qmr_model_step_launches(const QmrModel *m, uint32_t *with_head, uint32_t *without_head);
+
 #ifdef __cplusplus
 }
 #endif

@@ -474,6 +474,11 @@ static int launch_matrix(const void *w, const void *s, const void *b, const floa
     return run_generic(w, s, b, x, y, rows, cols, bits, group, batch, bf16, stream);
 }
 
+// The current modes as the decode engine needs them.
+bool modes_meta_bf16() { return modes().meta_bf16; }
+bool modes_gemv_aligned() { return modes().gemv == QMR_GEMV_ALIGNED && !modes().reference; }
+int modes_stream_path() { return modes().stream_path; }
+
 }  // namespace qmr
 
 using namespace qmr;

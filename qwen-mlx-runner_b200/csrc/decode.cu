@@ -1,0 +1,494 @@
+// Decode-step kernels of the hybrid Qwen3.5 graph on sm_100a (everything
+// outside the packed matrix products, which run in the streaming kernels).
+//
+// Semantics follow the reference's kernels (rucin93/qwen-mlx-runner v0.7.3,
+// kernels/qwen.metal:78-258) as the per-token graph calls them
+// (src/engine.rs:607-797); the fusion and the work split are this file's:
+//  * delta_mixer_kernel: conv_silu + delta_norm + delta_step + gated_rms of
+//    one DeltaNet layer in one launch, one CTA per value head (the state
+//    rows of a head are prefetched into registers, so its 64 KiB streams
+//    once in each direction);
+//  * attention_kernel: split_q_gate + head_rms + rope + kv_append +
+//    attn_scores + softmax + attn_values (with the sigmoid gate) in one
+//    launch: one CTA per (64-position chunk, KV head) computes the
+//    partial softmax of the KV group's query heads over its chunk; the last
+//    CTA of each KV head merges the chunks in chunk order;
+//  * embed_token_kernel reads the step's token from the control block, so a
+//    captured step graph replays for every token; advance_kernel ends a step.
+// Reductions use a fixed order (xor shuffles, then warps in order), so a
+// step is reproducible run to run.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "decode.h"
+#include "matrix_kernels.cuh"
+#include "qmr_internal.h"
+
+namespace qmr {
+
+namespace {
+
+__host__ __device__ __forceinline__ uint64_t sg_mix(uint64_t z) {
+    z ^= z >> 30;
+    z *= 0xBF58476D1CE4E5B9ull;
+    z ^= z >> 27;
+    z *= 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    return z;
+}
+
+__host__ __device__ __forceinline__ uint64_t sg_key(uint64_t seed, uint64_t mid, uint64_t tag) {
+    return sg_mix(seed ^ (mid * 0x9E3779B97F4A7C15ull) ^ (tag * 0xD1B54A32D192ED03ull));
+}
+
+__device__ __forceinline__ uint16_t bf16_rne_bits(float v) {
+    const uint32_t u = __float_as_uint(v);
+    return (uint16_t)((u + 0x7fffu + ((u >> 16) & 1u)) >> 16);
+}
+
+// The synthetic generator of the test oracle, bit for bit: word pairs from a
+// counter hash; scale uniform [0.002, 0.02] -> BF16; bias = BF16(-8 scale +
+// 1e-3 * Irwin-Hall(4) normal approximation), all in explicitly rounded f64.
+__global__ void synth_words_kernel(uint32_t *w, uint64_t key, uint64_t first_pair, uint64_t npairs) {
+    for (uint64_t j = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; j < npairs;
+         j += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t h = sg_mix(key + (first_pair + j + 1) * 0x9E3779B97F4A7C15ull);
+        reinterpret_cast<uint2 *>(w)[j] = make_uint2((uint32_t)h, (uint32_t)(h >> 32));
+    }
+}
+
+__global__ void synth_meta_kernel(uint16_t *s, uint16_t *b, uint64_t key_m, uint64_t key_n, uint64_t first,
+                                  uint64_t n) {
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t g = first + i;
+        const uint64_t h = sg_mix(key_m + (g + 1) * 0x9E3779B97F4A7C15ull);
+        const double u = __dmul_rn((double)(h >> 11), 1.0 / 9007199254740992.0);
+        const float s32 = __double2float_rn(__dadd_rn(0.002, __dmul_rn(0.018, u)));
+        const uint16_t sb = bf16_rne_bits(s32);
+        const uint64_t h2 = sg_mix(h ^ key_n);
+        double nrm = 0.0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            nrm = __dadd_rn(nrm, __dmul_rn(__dadd_rn((double)((h2 >> (16 * k)) & 0xffffu), 0.5), 1.0 / 65536.0));
+        nrm = __dmul_rn(__dadd_rn(nrm, -2.0), 1.7320508075688772);
+        const double sv = (double)__uint_as_float((uint32_t)sb << 16);
+        const float b32 = __double2float_rn(__dadd_rn(__dmul_rn(-8.0, sv), __dmul_rn(1e-3, nrm)));
+        s[i] = sb;
+        b[i] = bf16_rne_bits(b32);
+    }
+}
+
+__global__ void fill_kernel(float *p, uint64_t n, float v) {
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+        p[i] = v;
+}
+
+__device__ __forceinline__ uint32_t step_token(const DecodeCtrl *ctrl, const int32_t *prompt) {
+    const uint32_t pos = ctrl->pos;
+    return pos < ctrl->n_prompt ? (uint32_t)prompt[pos] : (uint32_t)ctrl->token;
+}
+
+// embed_affine of the step's token (kernels/affine_bf16.metal:439-451):
+// float(q) * s + b with two roundings, bit-exact with the reference.
+template <bool BF16>
+__global__ void embed_token_kernel(const uint32_t *__restrict__ w, const void *__restrict__ s,
+                                   const void *__restrict__ bias, uint32_t cols, uint32_t bits, uint32_t group,
+                                   const DecodeCtrl *ctrl, const int32_t *prompt, float *__restrict__ x) {
+    const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= cols) return;
+    const uint64_t row = step_token(ctrl, prompt);
+    const uint32_t pack = 32u / bits;
+    const uint32_t word = __ldg(w + row * (cols / pack) + c / pack);
+    const uint32_t q = (word >> ((c % pack) * bits)) & ((1u << bits) - 1u);
+    const uint64_t gi = row * (cols / group) + c / group;
+    x[c] = __fadd_rn(__fmul_rn((float)q, load_meta<BF16>(s, gi)), load_meta<BF16>(bias, gi));
+}
+
+// Fixed-order sum over the block: xor shuffles inside each warp, then the
+// warps' sums in warp order by one thread; every thread gets the result.
+// `red` holds at least 33 floats.  Every thread of the block must call it.
+__device__ __forceinline__ float block_sum(float v, float *red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[warp] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+        for (int i = 0; i < nw; ++i) t = __fadd_rn(t, red[i]);
+        red[32] = t;
+    }
+    __syncthreads();
+    return red[32];
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ float sigmoid_f32(float x) { return __frcp_rn(__fadd_rn(1.0f, expf(-x))); }
+
+__device__ __forceinline__ float rsqrt_f32(float x) { return __fdiv_rn(1.0f, __fsqrt_rn(x)); }
+
+// rms_norm (kernels/qwen.metal:78-86): y = x * inv * w, one CTA.
+__global__ void rms_norm_kernel(const float *x, const float *w, float *y, uint32_t n, float eps) {
+    __shared__ float red[33];
+    float ss = 0.0f;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) ss = __fmaf_rn(x[i], x[i], ss);
+    const float inv = rsqrt_f32(__fadd_rn(__fdiv_rn(block_sum(ss, red), (float)n), eps));
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) y[i] = __fmul_rn(__fmul_rn(x[i], inv), w[i]);
+}
+
+// add (kernels/qwen.metal:87-90) in place: x = x + r.
+__global__ void add_kernel(float *x, const float *r, uint32_t n) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) x[i] = __fadd_rn(x[i], r[i]);
+}
+
+constexpr int kDeltaThreads = 512;
+constexpr int kDeltaRowsPerWarp = 8;
+
+// One DeltaNet layer's mixer for value head blockIdx.x.
+//  conv_silu (qwen.metal:95-106): y = silu(x*w[W-1] + sum_k state[k]*w[k])
+//    over the channels this head reads (its key head's q and k, its own v);
+//    the history is double-buffered by position parity (read parity pos&1,
+//    write the other), so CTAs sharing a key head never race on it: the
+//    first value head of each key group writes the shared q/k history.
+//  delta_norm (:107-116): q *= rsqrt(|q|^2 + 1e-6) * rsqrt(K),
+//    k *= rsqrt(|k|^2 + 1e-6).
+//  delta_step (:117-136): decay = exp(-exp(A_log) softplus(a + dt)),
+//    beta = sigmoid(b); per value row S = S*decay, delta = (v - S.k)*beta,
+//    S += k*delta, y = S.q.
+//  gated_rms (:184-194): out = y * rsqrt(mean(y^2) + eps) * w * silu(z).
+__global__ void __launch_bounds__(kDeltaThreads) delta_mixer_kernel(DeltaArgs a) {
+    extern __shared__ float dsm[];
+    const int K = a.K, V = a.V, W = a.W, KH = a.KH, VH = a.VH;
+    const int h = blockIdx.x, ratio = VH / KH, kh = h / ratio;
+    const bool rep = (h % ratio) == 0;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+    float *q = dsm, *k = q + K, *v = k + K, *y = v + V, *red = y + V;
+    const int qkv = 2 * KH * K + VH * V;
+    const int par = (int)(a.ctrl->pos & 1u);
+    const float *cs_old = a.conv_state + (size_t)par * qkv * (W - 1);
+    float *cs_new = a.conv_state + (size_t)(par ^ 1) * qkv * (W - 1);
+    for (int i = tid; i < 2 * K + V; i += blockDim.x) {
+        const int c = i < K ? kh * K + i : (i < 2 * K ? KH * K + kh * K + (i - K) : 2 * KH * K + h * V + (i - 2 * K));
+        const float xin = a.proj[c];
+        const float *w = a.conv_w + (size_t)c * W;
+        const float *st = cs_old + (size_t)c * (W - 1);
+        float sum = __fmul_rn(xin, w[W - 1]);
+        for (int j = 0; j + 1 < W; ++j) sum = __fadd_rn(sum, __fmul_rn(st[j], w[j]));
+        if (i >= 2 * K || rep) {
+            float *sn = cs_new + (size_t)c * (W - 1);
+            for (int j = 0; j + 2 < W; ++j) sn[j] = st[j + 1];
+            if (W > 1) sn[W - 2] = xin;
+        }
+        const float yv = silu_f32(sum);
+        if (i < K)
+            q[i] = yv;
+        else if (i < 2 * K)
+            k[i - K] = yv;
+        else
+            v[i - 2 * K] = yv;
+    }
+    __syncthreads();
+    float qs = 0.0f, ks = 0.0f;
+    for (int i = tid; i < K; i += blockDim.x) {
+        qs = __fmaf_rn(q[i], q[i], qs);
+        ks = __fmaf_rn(k[i], k[i], ks);
+    }
+    qs = block_sum(qs, red);
+    ks = block_sum(ks, red);
+    const float qi = __fmul_rn(rsqrt_f32(__fadd_rn(qs, 1e-6f)), rsqrt_f32((float)K));
+    const float ki = rsqrt_f32(__fadd_rn(ks, 1e-6f));
+    for (int i = tid; i < K; i += blockDim.x) {
+        q[i] = __fmul_rn(q[i], qi);
+        k[i] = __fmul_rn(k[i], ki);
+    }
+    __syncthreads();
+    const float *pa = a.proj + 2 * KH * K + 2 * VH * V;
+    const float av = __fadd_rn(pa[h], a.dt[h]);
+    const float sp = __fadd_rn(fmaxf(av, 0.0f), log1pf(expf(-fabsf(av))));  // softplus, stable
+    const float decay = expf(-__fmul_rn(expf(a.alog[h]), sp));
+    const float beta = sigmoid_f32(pa[VH + h]);
+    // Lane layout over K: column lane + 32*m, m < 4 (K <= 128).
+    float kr[4], qr[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const int j = lane + 32 * m;
+        kr[m] = j < K ? k[j] : 0.0f;
+        qr[m] = j < K ? q[j] : 0.0f;
+    }
+    float *S = a.state + (size_t)h * V * K;
+    for (int r0 = warp * kDeltaRowsPerWarp; r0 < V; r0 += nwarps * kDeltaRowsPerWarp) {
+        float sv[kDeltaRowsPerWarp][4];
+#pragma unroll
+        for (int rr = 0; rr < kDeltaRowsPerWarp; ++rr)
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                const int r = r0 + rr, j = lane + 32 * m;
+                sv[rr][m] = (r < V && j < K) ? S[(size_t)r * K + j] : 0.0f;
+            }
+#pragma unroll
+        for (int rr = 0; rr < kDeltaRowsPerWarp; ++rr) {
+            const int r = r0 + rr;
+            if (r >= V) break;
+            float p = 0.0f;
+#pragma unroll
+            for (int m = 0; m < 4; ++m) p = __fmaf_rn(__fmul_rn(sv[rr][m], decay), kr[m], p);
+            p = warp_sum(p);
+            const float delta = __fmul_rn(__fsub_rn(v[r], p), beta);
+            float o = 0.0f;
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                const float nx = __fmaf_rn(kr[m], delta, __fmul_rn(sv[rr][m], decay));
+                sv[rr][m] = nx;
+                o = __fmaf_rn(nx, qr[m], o);
+            }
+            o = warp_sum(o);
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                const int j = lane + 32 * m;
+                if (j < K) S[(size_t)r * K + j] = sv[rr][m];
+            }
+            if (lane == 0) y[r] = o;
+        }
+    }
+    __syncthreads();
+    float ys = 0.0f;
+    for (int i = tid; i < V; i += blockDim.x) ys = __fmaf_rn(y[i], y[i], ys);
+    const float inv = rsqrt_f32(__fadd_rn(__fdiv_rn(block_sum(ys, red), (float)V), a.eps));
+    const float *z = a.proj + 2 * KH * K + VH * V + (size_t)h * V;
+    for (int i = tid; i < V; i += blockDim.x)
+        a.out[(size_t)h * V + i] = __fmul_rn(__fmul_rn(__fmul_rn(y[i], inv), a.norm_w[i]), silu_f32(z[i]));
+}
+
+constexpr int kAttnThreads = 256;
+
+// head_rms (qwen.metal:204-212) then partial rotate-half RoPE (:213-221) of
+// one D-vector in shared memory t, weight w; every thread calls it.
+__device__ void rms_rope(float *t, const float *w, int D, int RD, float pos, float theta, float eps, float *red) {
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) ss = __fmaf_rn(t[i], t[i], ss);
+    const float inv = rsqrt_f32(__fadd_rn(__fdiv_rn(block_sum(ss, red), (float)D), eps));
+    for (int i = threadIdx.x; i < D; i += blockDim.x) t[i] = __fmul_rn(t[i], __fmul_rn(inv, w[i]));
+    __syncthreads();
+    const int half = RD / 2;
+    for (int j = threadIdx.x; j < half; j += blockDim.x) {
+        const float ang = __fmul_rn(pos, powf(theta, __fdiv_rn(-(float)(2 * j), (float)RD)));
+        float sn, cs;
+        sincosf(ang, &sn, &cs);
+        const float x0 = t[j], x1 = t[j + half];
+        t[j] = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+        t[j + half] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+    }
+    __syncthreads();
+}
+
+// Decode attention of one KV head over one 64-position chunk (see the file
+// comment).  Shared memory: q [G][D], k_new [D], v_new [D], p [G][64], red.
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a) {
+    extern __shared__ float asm_[];
+    const int D = a.D, NH = a.NH, NKV = a.NKV, G = NH / NKV;
+    const int c = blockIdx.x, kh = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+    float *qs = asm_, *kn = qs + G * D, *vn = kn + D, *ps = vn + D, *red = ps + G * kAttnChunk;
+    __shared__ unsigned int last;
+    const int pos = (int)a.ctrl->pos, len = pos + 1;
+    const int t0 = c * kAttnChunk, t1 = min(t0 + kAttnChunk, len);
+    const float fpos = (float)pos;
+    float *part = a.part + ((size_t)kh * a.nchunks + c) * G * (D + 2);
+    if (t0 < len) {
+        for (int g = 0; g < G; ++g) {
+            const float *src = a.proj + (size_t)(kh * G + g) * 2 * D;
+            for (int i = tid; i < D; i += blockDim.x) qs[g * D + i] = src[i];
+            __syncthreads();
+            rms_rope(qs + g * D, a.qnorm, D, a.RD, fpos, a.theta, a.eps, red);
+        }
+        const bool mine = t0 <= pos && pos < t0 + kAttnChunk;  // this chunk holds the new position
+        if (mine) {
+            const float *ksrc = a.proj + (size_t)NH * 2 * D + (size_t)kh * D;
+            const float *vsrc = a.proj + (size_t)NH * 2 * D + (size_t)NKV * D + (size_t)kh * D;
+            for (int i = tid; i < D; i += blockDim.x) {
+                kn[i] = ksrc[i];
+                vn[i] = vsrc[i];
+            }
+            __syncthreads();
+            rms_rope(kn, a.knorm, D, a.RD, fpos, a.theta, a.eps, red);
+            float *kd = a.kcache + ((size_t)pos * NKV + kh) * D, *vd = a.vcache + ((size_t)pos * NKV + kh) * D;
+            for (int i = tid; i < D; i += blockDim.x) {
+                kd[i] = kn[i];
+                vd[i] = vn[i];
+            }
+        }
+        // Scores q.k / sqrt(D) (attn_scores, qwen.metal:228-238), warps over positions.
+        const float rs = rsqrt_f32((float)D);
+        for (int t = t0 + warp; t < t1; t += nwarps) {
+            const float *kt = (t == pos) ? kn : a.kcache + ((size_t)t * NKV + kh) * D;
+            float kv[8];
+#pragma unroll
+            for (int m = 0; m < 8; ++m) {
+                const int d = lane + 32 * m;
+                kv[m] = d < D ? kt[d] : 0.0f;
+            }
+            for (int g = 0; g < G; ++g) {
+                float s = 0.0f;
+#pragma unroll
+                for (int m = 0; m < 8; ++m) {
+                    const int d = lane + 32 * m;
+                    if (d < D) s = __fmaf_rn(qs[g * D + d], kv[m], s);
+                }
+                s = warp_sum(s);
+                if (lane == 0) ps[g * kAttnChunk + (t - t0)] = __fmul_rn(s, rs);
+            }
+        }
+        __syncthreads();
+        // Chunk-local softmax per query head: warp g, lanes over positions.
+        for (int g = warp; g < G; g += nwarps) {
+            float mx = -INFINITY;
+            for (int t = lane; t < t1 - t0; t += 32) mx = fmaxf(mx, ps[g * kAttnChunk + t]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            float l = 0.0f;
+            for (int t = lane; t < t1 - t0; t += 32) {
+                const float e = expf(__fsub_rn(ps[g * kAttnChunk + t], mx));
+                ps[g * kAttnChunk + t] = e;
+                l = __fadd_rn(l, e);
+            }
+            l = warp_sum(l);
+            if (lane == 0) {
+                part[(size_t)g * (D + 2) + D] = mx;
+                part[(size_t)g * (D + 2) + D + 1] = l;
+            }
+        }
+        __syncthreads();
+        // Weighted values over the chunk: thread d, all query heads of the group.
+        for (int d = tid; d < D; d += blockDim.x) {
+            float acc[8];
+#pragma unroll
+            for (int g = 0; g < 8; ++g) acc[g] = 0.0f;
+            for (int t = t0; t < t1; ++t) {
+                const float vv = (t == pos) ? vn[d] : a.vcache[((size_t)t * NKV + kh) * D + d];
+#pragma unroll
+                for (int g = 0; g < 8; ++g)
+                    if (g < G) acc[g] = __fmaf_rn(ps[g * kAttnChunk + (t - t0)], vv, acc[g]);
+            }
+#pragma unroll
+            for (int g = 0; g < 8; ++g)
+                if (g < G) part[(size_t)g * (D + 2) + d] = acc[g];
+        }
+    }
+    // The last CTA of this KV head merges the used chunks in chunk order.
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last = (atomicAdd(a.count + kh, 1u) == (unsigned)a.nchunks - 1u) ? 1u : 0u;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    const int used = (len + kAttnChunk - 1) / kAttnChunk;
+    for (int i = tid; i < G * D; i += blockDim.x) {
+        const int g = i / D, d = i % D;
+        const float *pk = a.part + (size_t)kh * a.nchunks * G * (D + 2) + (size_t)g * (D + 2);
+        const size_t cstride = (size_t)G * (D + 2);
+        float M = -INFINITY;
+        for (int cc = 0; cc < used; ++cc) M = fmaxf(M, __ldcg(pk + cc * cstride + D));
+        float L = 0.0f, o = 0.0f;
+        for (int cc = 0; cc < used; ++cc) {
+            const float f = expf(__fsub_rn(__ldcg(pk + cc * cstride + D), M));
+            L = __fmaf_rn(__ldcg(pk + cc * cstride + D + 1), f, L);
+            o = __fmaf_rn(__ldcg(pk + cc * cstride + d), f, o);
+        }
+        const int h = kh * G + g;
+        const float gate = a.proj[(size_t)h * 2 * D + D + d];
+        a.out[(size_t)h * D + d] = __fmul_rn(__fdiv_rn(o, L), sigmoid_f32(gate));
+    }
+    if (tid == 0) a.count[kh] = 0u;
+}
+
+// End of a step: append the greedy token (when the step had a head) and
+// advance the position.
+__global__ void advance_kernel(DecodeCtrl *ctrl, int32_t *out, uint32_t cap, int record) {
+    if (threadIdx.x != 0) return;
+    if (record) {
+        if (ctrl->n_out < cap) out[ctrl->n_out] = ctrl->token;
+        ctrl->n_out += 1;
+    }
+    ctrl->pos += 1;
+}
+
+int launched(const char *what) {
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(QMR_ECUDA, "%s launch failed: %s", what, cudaGetErrorString(e));
+    return QMR_OK;
+}
+
+}  // namespace
+
+int launch_synth_q4(uint32_t *w, uint16_t *s, uint16_t *b, uint64_t seed, uint32_t mid, uint32_t rows, uint32_t cols,
+                    uint32_t row0, cudaStream_t stream) {
+    if (cols % 64 != 0) return fail(QMR_EINVAL, "synthetic matrices need cols divisible by 64");
+    const uint64_t wpr = cols / 8, gpr = cols / 64;
+    const uint64_t npairs = (uint64_t)rows * wpr / 2;
+    synth_words_kernel<<<1184, 256, 0, stream>>>(w + (uint64_t)row0 * wpr, sg_key(seed, mid, 1), 0, npairs);
+    int rc = launched("synthetic weights");
+    if (rc != QMR_OK) return rc;
+    synth_meta_kernel<<<592, 256, 0, stream>>>(s + (uint64_t)row0 * gpr, b + (uint64_t)row0 * gpr,
+                                               sg_key(seed, mid, 2), sg_key(seed, mid, 3), 0,
+                                               (uint64_t)rows * gpr);
+    return launched("synthetic metadata");
+}
+
+int launch_fill_f32(float *p, uint64_t n, float v, cudaStream_t stream) {
+    fill_kernel<<<296, 256, 0, stream>>>(p, n, v);
+    return launched("fill");
+}
+
+int launch_embed_token(const void *w, const void *s, const void *b, bool bf16, uint32_t cols, uint32_t bits,
+                       uint32_t group, const DecodeCtrl *ctrl, const int32_t *prompt, float *x, cudaStream_t stream) {
+    const unsigned grid = (cols + 255) / 256;
+    if (bf16)
+        embed_token_kernel<true><<<grid, 256, 0, stream>>>(static_cast<const uint32_t *>(w), s, b, cols, bits, group,
+                                                           ctrl, prompt, x);
+    else
+        embed_token_kernel<false><<<grid, 256, 0, stream>>>(static_cast<const uint32_t *>(w), s, b, cols, bits, group,
+                                                            ctrl, prompt, x);
+    return launched("embed");
+}
+
+int launch_rms_norm(const float *x, const float *w, float *y, uint32_t n, float eps, cudaStream_t stream) {
+    rms_norm_kernel<<<1, 512, 0, stream>>>(x, w, y, n, eps);
+    return launched("rms_norm");
+}
+
+int launch_add(float *x, const float *r, uint32_t n, cudaStream_t stream) {
+    add_kernel<<<(n + 255) / 256, 256, 0, stream>>>(x, r, n);
+    return launched("add");
+}
+
+int launch_delta_mixer(const DeltaArgs &a, cudaStream_t stream) {
+    if (a.K > 128 || a.K < 1 || a.V < 1 || a.KH < 1 || a.VH % a.KH != 0 || a.W < 1)
+        return fail(QMR_EUNSUPPORTED, "DeltaNet mixer needs key dim <= 128 and value heads a multiple of key heads");
+    const size_t smem = (size_t)(2 * a.K + 2 * a.V + 33) * sizeof(float);
+    delta_mixer_kernel<<<a.VH, kDeltaThreads, smem, stream>>>(a);
+    return launched("DeltaNet mixer");
+}
+
+int launch_attention(const AttnArgs &a, cudaStream_t stream) {
+    const int G = a.NH / a.NKV;
+    if (a.D > 256 || a.D < 1 || a.NKV < 1 || a.NH % a.NKV != 0 || G > 8 || a.RD > a.D || a.RD % 2 != 0)
+        return fail(QMR_EUNSUPPORTED, "decode attention needs head_dim <= 256 and at most 8 query heads per KV head");
+    const size_t smem = (size_t)(G * a.D + 2 * a.D + G * kAttnChunk + 33) * sizeof(float);
+    attention_kernel<<<dim3((unsigned)a.nchunks, (unsigned)a.NKV), kAttnThreads, smem, stream>>>(a);
+    return launched("attention");
+}
+
+int launch_advance(DecodeCtrl *ctrl, int32_t *out, uint32_t out_cap, bool record, cudaStream_t stream) {
+    advance_kernel<<<1, 32, 0, stream>>>(ctrl, out, out_cap, record ? 1 : 0);
+    return launched("advance");
+}
+
+}  // namespace qmr

@@ -1,0 +1,820 @@
+// The decode engine: the hybrid Qwen3.5 per-token graph on one B200.
+//
+// Restates the reference's Engine (rucin93/qwen-mlx-runner v0.7.3,
+// src/engine.rs): the layer graph of forward_inner (:607-797), load (:276-
+// 446), reset (:561-584), the synthetic 27B-shaped model
+// (src/engine/synthetic.rs:92-281) and mlp_r2_eligible_matrices
+// (:454-468).  The step is laid out for the GPU rather than after the
+// reference's dispatch list:
+//  * a DeltaNet layer's in-projections (qkv, z, a, b) are one concatenated
+//    matrix, an attention layer's (q|gate, k, v) likewise, so each layer
+//    streams its input-side weights in one call;
+//  * the input RMSNorm of every matrix call on a hidden vector rides in that
+//    call's activation prep and output factor, and the residual adds in the
+//    out/o/down epilogues, whenever the tensor-core kernel takes the matrix
+//    (otherwise separate rms_norm / add kernels run, as in the reference);
+//  * the DeltaNet and attention mixers are one launch each (decode.cu);
+//  * position and token are read on the device, so each kind of step (with
+//    and without the vocabulary head) is captured once as a CUDA graph and
+//    replayed for every token; prefill and greedy decode run as a sequence of
+//    replays with no host round trip.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "checkpoint.h"
+#include "decode.h"
+#include "qmr_internal.h"
+
+namespace qmr {
+
+// Matrix slots of a layer and of the model; the synthetic generator's matrix
+// id is slot-derived: layer * 16 + slot + 1, embedding 0x100000, head
+// 0x100001 (the test oracle uses the same ids).
+enum Slot { S_QKV, S_Z, S_A, S_B, S_OUT, S_Q, S_K, S_V, S_O, S_GATE, S_UP, S_DOWN };
+constexpr uint32_t kMidEmbed = 0x100000u, kMidHead = 0x100001u;
+inline uint32_t synth_mid(uint32_t layer, int slot) { return layer * 16u + (uint32_t)slot + 1u; }
+
+struct DevMat {
+    void *w = nullptr, *s = nullptr, *b = nullptr;
+    uint32_t rows = 0, cols = 0, bits = 4, group = 64;
+    bool bf16 = true;
+};
+
+struct LayerState {
+    bool attn = false;
+    DevMat in, out, gate, up, down;
+    float *in_norm = nullptr, *post_norm = nullptr;
+    float *conv_w = nullptr, *alog = nullptr, *dt = nullptr, *dnorm = nullptr;
+    float *qnorm = nullptr, *knorm = nullptr;
+    float *conv_state = nullptr, *state = nullptr;
+    float *kcache = nullptr, *vcache = nullptr;
+};
+
+}  // namespace qmr
+
+using namespace qmr;
+
+struct QmrModel {
+    int device = 0;
+    QmrModelConfig cfg{};
+    uint32_t context = 0;
+    std::vector<LayerState> layers;
+    DevMat embed, head;
+    float *final_norm = nullptr;
+    float *x = nullptr, *proj = nullptr, *mixed = nullptr, *act = nullptr, *logits = nullptr;
+    float *normed = nullptr, *tmp = nullptr;
+    float *attn_part = nullptr;
+    unsigned int *attn_count = nullptr;
+    int attn_chunks = 0;
+    void *scratch = nullptr;
+    size_t scratch_size = 0;
+    DecodeCtrl *ctrl = nullptr;
+    int32_t *prompt = nullptr, *out = nullptr;
+    uint32_t out_cap = 0;
+    int32_t *host_stage = nullptr;  // pinned: [0] token, [1] n_prompt
+    cudaStream_t stream = nullptr;
+    cudaGraph_t graph[2] = {nullptr, nullptr};
+    cudaGraphExec_t exec[2] = {nullptr, nullptr};  // [0] no head (prefill), [1] with head
+    uint32_t launches[2] = {0, 0};
+    uint32_t pos = 0;
+    std::vector<void *> allocs;
+    uint64_t compacted = 0, saved_bytes = 0;
+    size_t qkv_channels = 0;
+
+    ~QmrModel() {
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaSetDevice(device);
+        if (stream != nullptr) cudaStreamSynchronize(stream);
+        for (int i = 0; i < 2; ++i) {
+            if (exec[i] != nullptr) cudaGraphExecDestroy(exec[i]);
+            if (graph[i] != nullptr) cudaGraphDestroy(graph[i]);
+        }
+        for (void *p : allocs) cudaFree(p);
+        if (host_stage != nullptr) cudaFreeHost(host_stage);
+        if (stream != nullptr) cudaStreamDestroy(stream);
+        cudaSetDevice(prev);
+    }
+};
+
+namespace qmr {
+namespace {
+
+int cuda_check(cudaError_t e, const char *what) {
+    if (e != cudaSuccess) return fail(QMR_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+    return QMR_OK;
+}
+
+template <typename T>
+int dev_alloc(QmrModel *m, T **p, size_t count) {
+    void *v = nullptr;
+    const size_t bytes = count * sizeof(T) > 0 ? count * sizeof(T) : 16;
+    int rc = cuda_check(cudaMalloc(&v, bytes), "cudaMalloc of model memory");
+    if (rc != QMR_OK) return rc;
+    m->allocs.push_back(v);
+    rc = cuda_check(cudaMemsetAsync(v, 0, bytes, m->stream), "clearing model memory");
+    *p = static_cast<T *>(v);
+    return rc;
+}
+
+int upload(QmrModel *m, void *dst, const void *src, size_t bytes) {
+    return cuda_check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, m->stream), "uploading model data");
+}
+
+int dev_vector(QmrModel *m, float **p, const std::vector<float> &v) {
+    int rc = dev_alloc(m, p, v.size());
+    if (rc == QMR_OK) rc = upload(m, *p, v.data(), v.size() * sizeof(float));
+    if (rc == QMR_OK) rc = cuda_check(cudaStreamSynchronize(m->stream), "uploading model data");
+    return rc;
+}
+
+int dev_const(QmrModel *m, float **p, size_t n, float value) {
+    int rc = dev_alloc(m, p, n);
+    if (rc == QMR_OK) rc = launch_fill_f32(*p, n, value, m->stream);
+    return rc;
+}
+
+int alloc_matrix(QmrModel *m, DevMat *d, uint32_t rows, uint32_t cols, uint32_t bits, uint32_t group, bool bf16) {
+    d->rows = rows;
+    d->cols = cols;
+    d->bits = bits;
+    d->group = group;
+    d->bf16 = bf16;
+    const size_t wbytes = (size_t)rows * cols * bits / 8, groups = (size_t)rows * cols / group;
+    uint8_t *w = nullptr, *s = nullptr, *b = nullptr;
+    int rc = dev_alloc(m, &w, wbytes);
+    if (rc == QMR_OK) rc = dev_alloc(m, &s, groups * (bf16 ? 2 : 4));
+    if (rc == QMR_OK) rc = dev_alloc(m, &b, groups * (bf16 ? 2 : 4));
+    d->w = w;
+    d->s = s;
+    d->b = b;
+    return rc;
+}
+
+// Model-wide validation and the activations, state and control memory.
+int create_common(QmrModel *m, const QmrModelConfig &c, uint32_t context) {
+    if (c.num_layers == 0 || c.num_layers > QMR_MAX_LAYERS) return fail(QMR_EINVAL, "layer count out of range");
+    if (c.hidden_size == 0 || c.intermediate_size == 0 || c.vocab_size == 0 || c.num_heads == 0 ||
+        c.num_kv_heads == 0 || c.head_dim == 0 || c.linear_key_heads == 0 || c.linear_value_heads == 0 ||
+        c.linear_key_dim == 0 || c.linear_value_dim == 0 || c.conv_width == 0)
+        return fail(QMR_EINVAL, "model dimensions must be positive");
+    if (c.num_heads % c.num_kv_heads != 0 || c.num_heads / c.num_kv_heads > 8)
+        return fail(QMR_EUNSUPPORTED, "attention needs at most 8 query heads per KV head");
+    if (c.head_dim > 256 || c.rotary_dim == 0 || c.rotary_dim % 2 != 0 || c.rotary_dim > c.head_dim)
+        return fail(QMR_EUNSUPPORTED, "head_dim must be <= 256 with an even rotary dimension that fits it");
+    if (c.linear_key_dim > 128 || c.linear_value_heads % c.linear_key_heads != 0)
+        return fail(QMR_EUNSUPPORTED, "DeltaNet needs key dim <= 128 and value heads a multiple of key heads");
+    if (!(c.rms_eps > 0 && std::isfinite(c.rms_eps)) || !(c.rope_theta > 0 && std::isfinite(c.rope_theta)))
+        return fail(QMR_EINVAL, "invalid RMS epsilon or RoPE theta");
+    if (context == 0) return fail(QMR_EINVAL, "context must be positive");
+    // Metal-era 32-bit index limits kept as the reference checks them (engine.rs:286-304).
+    if ((uint64_t)c.num_heads * context * 32 > 0xffffffffull || (uint64_t)context * c.num_kv_heads * c.head_dim > 0xffffffffull)
+        return fail(QMR_ERANGE, "context exceeds 32-bit indexing");
+    m->cfg = c;
+    m->context = context;
+    int rc = cuda_check(cudaGetDevice(&m->device), "cudaGetDevice");
+    if (rc == QMR_OK) rc = cuda_check(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking), "stream");
+    if (rc != QMR_OK) return rc;
+    const size_t H = c.hidden_size, F = c.intermediate_size;
+    const size_t KD = (size_t)c.linear_key_heads * c.linear_key_dim, VD = (size_t)c.linear_value_heads * c.linear_value_dim;
+    const size_t QD = (size_t)c.num_heads * c.head_dim, KVD = (size_t)c.num_kv_heads * c.head_dim;
+    m->qkv_channels = 2 * KD + VD;
+    const size_t delta_in = 2 * KD + 2 * VD + 2 * c.linear_value_heads, attn_in = 2 * QD + 2 * KVD;
+    size_t widest = H;
+    for (size_t v : {F, VD, QD}) widest = v > widest ? v : widest;
+    const size_t proj = delta_in > attn_in ? delta_in : attn_in;
+    rc = dev_alloc(m, &m->x, H);
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->normed, widest);
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->tmp, H);
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->proj, proj);
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->mixed, VD > QD ? VD : QD);
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->act, F);
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->logits, c.vocab_size);
+    m->attn_chunks = (int)((context + kAttnChunk - 1) / kAttnChunk);
+    const size_t G = c.num_heads / c.num_kv_heads;
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->attn_part, (size_t)c.num_kv_heads * m->attn_chunks * G * (c.head_dim + 2));
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->attn_count, c.num_kv_heads);
+    m->scratch_size = scratch_bytes(8, (uint32_t)widest, 4);
+    uint8_t *scr = nullptr;
+    if (rc == QMR_OK) rc = dev_alloc(m, &scr, m->scratch_size);
+    m->scratch = scr;
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->ctrl, 1);
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->prompt, context);
+    m->out_cap = context;
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->out, context);
+    if (rc == QMR_OK) rc = cuda_check(cudaMallocHost(&m->host_stage, 64), "pinned staging");
+    if (rc != QMR_OK) return rc;
+    m->layers.resize(c.num_layers);
+    for (uint32_t l = 0; l < c.num_layers; ++l) {
+        LayerState &L = m->layers[l];
+        L.attn = c.is_attention[l] != 0;
+        if (L.attn) {
+            rc = dev_alloc(m, &L.kcache, (size_t)context * KVD);
+            if (rc == QMR_OK) rc = dev_alloc(m, &L.vcache, (size_t)context * KVD);
+        } else {
+            rc = dev_alloc(m, &L.conv_state, 2 * m->qkv_channels * (c.conv_width - 1));
+            if (rc == QMR_OK) rc = dev_alloc(m, &L.state, VD * c.linear_key_dim);
+        }
+        if (rc != QMR_OK) return rc;
+    }
+    return QMR_OK;
+}
+
+// Rows of the concatenated in-projection: DeltaNet [qkv; z; a; b], attention [q|gate; k; v].
+uint32_t in_rows(const QmrModelConfig &c, bool attn) {
+    if (attn) return 2 * c.num_heads * c.head_dim + 2 * c.num_kv_heads * c.head_dim;
+    return 2 * c.linear_key_heads * c.linear_key_dim + 2 * c.linear_value_heads * c.linear_value_dim +
+           2 * c.linear_value_heads;
+}
+
+// ---- one step --------------------------------------------------------------
+
+struct StepCounter {
+    uint32_t n = 0;
+};
+
+// y = W x for the engine, with the optional fused input RMSNorm (norm_w) and
+// residual (resid == y), gate/up SwiGLU (epi 1, up = second matrix) or head
+// argmax (epi 2, into argmax).
+int mat_call(QmrModel *m, const DevMat &W, const float *x, float *y, const float *norm_w, const float *resid, int epi,
+             const DevMat *up, int32_t *argmax, StepCounter *cnt) {
+    FastCall c = {};
+    c.w = W.w;
+    c.s = W.s;
+    c.b = W.b;
+    if (epi == 1) {
+        c.w2 = up->w;
+        c.s2 = up->s;
+        c.b2 = up->b;
+    }
+    c.x = x;
+    c.y = y;
+    c.argmax = argmax;
+    c.rows = W.rows;
+    c.cols = W.cols;
+    c.bits = W.bits;
+    c.group = W.group;
+    c.batch = 1;
+    c.bf16 = W.bf16;
+    c.epilogue = epi;
+    c.path = modes_stream_path();
+    c.scratch = m->scratch;
+    c.scratch_bytes = m->scratch_size;
+    c.eps = m->cfg.rms_eps;
+    if (norm_w != nullptr || resid != nullptr) {
+        FastCall f = c;
+        f.norm_w = norm_w;
+        f.resid = resid;
+        if (fused_supported(f)) {
+            cnt->n += 2;  // activation prep + streaming kernel
+            return run_fast(f, m->stream);
+        }
+    }
+    int rc = QMR_OK;
+    if (norm_w != nullptr) {
+        rc = launch_rms_norm(x, norm_w, m->normed, W.cols, m->cfg.rms_eps, m->stream);
+        if (rc != QMR_OK) return rc;
+        ++cnt->n;
+        c.x = m->normed;
+    }
+    if (resid != nullptr) c.y = m->tmp;
+    if (fast_eligible(W.w, W.cols, W.bits, W.group)) {
+        rc = run_fast(c, m->stream);
+        cnt->n += 2;
+    } else if (epi == 0) {
+        rc = run_generic(W.w, W.s, W.b, c.x, c.y, W.rows, W.cols, W.bits, W.group, 1, W.bf16, m->stream);
+        cnt->n += 1;
+    } else {
+        rc = fail(QMR_EUNSUPPORTED, "fused gate/up and head need a packed shape the streaming kernels take");
+    }
+    if (rc != QMR_OK) return rc;
+    if (resid != nullptr) {
+        rc = launch_add(y, m->tmp, W.rows, m->stream);
+        ++cnt->n;
+    }
+    return rc;
+}
+
+int record_step(QmrModel *m, bool with_head, StepCounter *cnt) {
+    const QmrModelConfig &c = m->cfg;
+    int rc = launch_embed_token(m->embed.w, m->embed.s, m->embed.b, m->embed.bf16, m->embed.cols, m->embed.bits,
+                                m->embed.group, m->ctrl, m->prompt, m->x, m->stream);
+    ++cnt->n;
+    for (uint32_t l = 0; l < c.num_layers && rc == QMR_OK; ++l) {
+        LayerState &L = m->layers[l];
+        rc = mat_call(m, L.in, m->x, m->proj, L.in_norm, nullptr, 0, nullptr, nullptr, cnt);
+        if (rc != QMR_OK) break;
+        if (L.attn) {
+            AttnArgs a = {};
+            a.proj = m->proj;
+            a.qnorm = L.qnorm;
+            a.knorm = L.knorm;
+            a.kcache = L.kcache;
+            a.vcache = L.vcache;
+            a.part = m->attn_part;
+            a.count = m->attn_count;
+            a.out = m->mixed;
+            a.ctrl = m->ctrl;
+            a.NH = (int)c.num_heads;
+            a.NKV = (int)c.num_kv_heads;
+            a.D = (int)c.head_dim;
+            a.RD = (int)c.rotary_dim;
+            a.context = (int)m->context;
+            a.nchunks = m->attn_chunks;
+            a.eps = c.rms_eps;
+            a.theta = c.rope_theta;
+            rc = launch_attention(a, m->stream);
+        } else {
+            DeltaArgs a = {};
+            a.proj = m->proj;
+            a.conv_w = L.conv_w;
+            a.conv_state = L.conv_state;
+            a.state = L.state;
+            a.alog = L.alog;
+            a.dt = L.dt;
+            a.norm_w = L.dnorm;
+            a.out = m->mixed;
+            a.ctrl = m->ctrl;
+            a.KH = (int)c.linear_key_heads;
+            a.VH = (int)c.linear_value_heads;
+            a.K = (int)c.linear_key_dim;
+            a.V = (int)c.linear_value_dim;
+            a.W = (int)c.conv_width;
+            a.eps = c.rms_eps;
+            rc = launch_delta_mixer(a, m->stream);
+        }
+        ++cnt->n;
+        if (rc == QMR_OK) rc = mat_call(m, L.out, m->mixed, m->x, nullptr, m->x, 0, nullptr, nullptr, cnt);
+        if (rc == QMR_OK) rc = mat_call(m, L.gate, m->x, m->act, L.post_norm, nullptr, 1, &L.up, nullptr, cnt);
+        if (rc == QMR_OK) rc = mat_call(m, L.down, m->act, m->x, nullptr, m->x, 0, nullptr, nullptr, cnt);
+    }
+    if (rc == QMR_OK && with_head)
+        rc = mat_call(m, m->head, m->x, m->logits, m->final_norm, nullptr, 2, nullptr, &m->ctrl->token, cnt);
+    if (rc == QMR_OK) {
+        rc = launch_advance(m->ctrl, m->out, m->out_cap, with_head, m->stream);
+        ++cnt->n;
+    }
+    return rc;
+}
+
+int clear_state(QmrModel *m) {
+    const QmrModelConfig &c = m->cfg;
+    const size_t VD = (size_t)c.linear_value_heads * c.linear_value_dim;
+    int rc = QMR_OK;
+    for (LayerState &L : m->layers) {
+        if (L.attn) continue;
+        if (rc == QMR_OK)
+            rc = cuda_check(cudaMemsetAsync(L.conv_state, 0, 2 * m->qkv_channels * (c.conv_width - 1) * sizeof(float),
+                                            m->stream), "reset");
+        if (rc == QMR_OK) rc = cuda_check(cudaMemsetAsync(L.state, 0, VD * c.linear_key_dim * sizeof(float), m->stream), "reset");
+    }
+    if (rc == QMR_OK) rc = cuda_check(cudaMemsetAsync(m->ctrl, 0, sizeof(DecodeCtrl), m->stream), "reset");
+    if (rc == QMR_OK) rc = cuda_check(cudaStreamSynchronize(m->stream), "reset");
+    m->pos = 0;
+    return rc;
+}
+
+// One eager step of each kind (per-device kernel attributes and occupancy
+// queries happen outside capture), then the two graphs, then a clean state.
+int build_graphs(QmrModel *m) {
+    int rc = QMR_OK;
+    for (int head = 0; head < 2 && rc == QMR_OK; ++head) {
+        StepCounter cnt;
+        rc = record_step(m, head == 1, &cnt);
+        if (rc == QMR_OK) rc = cuda_check(cudaStreamSynchronize(m->stream), "warm-up step");
+    }
+    for (int head = 0; head < 2 && rc == QMR_OK; ++head) {
+        StepCounter cnt;
+        rc = cuda_check(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+        if (rc != QMR_OK) break;
+        const int rs = record_step(m, head == 1, &cnt);
+        cudaGraph_t g = nullptr;
+        const cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+        if (rs != QMR_OK) {
+            if (g != nullptr) cudaGraphDestroy(g);
+            return rs;
+        }
+        rc = cuda_check(e, "end capture");
+        if (rc != QMR_OK) break;
+        m->graph[head] = g;
+        rc = cuda_check(cudaGraphInstantiate(&m->exec[head], g, 0), "graph instantiate");
+        m->launches[head] = cnt.n;
+    }
+    if (rc == QMR_OK) rc = clear_state(m);
+    return rc;
+}
+
+int check_device_error() {
+    int code = 0;
+    const int rc = device_error(&code, false);
+    if (rc != QMR_OK) return rc;
+    if (code != 0) return fail(QMR_ETIMEOUT, "a bounded device wait ran out (code %d)", code);
+    return QMR_OK;
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+// ---- building from a checkpoint -----------------------------------------------
+
+// Upload one or more checkpoint matrices as one concatenated device matrix
+// (rows stacked).  Metadata is stored as BF16 when the library's metadata
+// mode is bf16 and every part is BF16-exact (compact_metadata,
+// src/gpu.rs:479-490), else as f32.
+int load_matrix(QmrModel *m, const Checkpoint &cp, const std::vector<std::string> &names, DevMat *d) {
+    std::vector<HostMatrix> parts(names.size());
+    uint32_t rows = 0;
+    for (size_t i = 0; i < names.size(); ++i) {
+        const int rc = cp.matrix(names[i], &parts[i]);
+        if (rc != QMR_OK) return rc;
+        if (i > 0 && (parts[i].cols != parts[0].cols || parts[i].bits != parts[0].bits ||
+                      parts[i].group != parts[0].group))
+            return fail(QMR_EINVAL, "%s: parts of one projection differ in width or quantisation", names[i].c_str());
+        rows += parts[i].rows;
+    }
+    const HostMatrix &p0 = parts[0];
+    const bool supported = (p0.bits == 4 || p0.bits == 8) && (p0.group == 32 || p0.group == 64 || p0.group == 128);
+    std::vector<std::vector<uint16_t>> cs(parts.size()), cb(parts.size());
+    bool bf16 = modes_meta_bf16() && supported;
+    for (size_t i = 0; i < parts.size() && bf16; ++i) {
+        cs[i].resize(parts[i].scales.size());
+        cb[i].resize(parts[i].biases.size());
+        bf16 = qmr_pack_bf16_exact(parts[i].scales.data(), parts[i].scales.size(), cs[i].data()) == 1 &&
+               qmr_pack_bf16_exact(parts[i].biases.data(), parts[i].biases.size(), cb[i].data()) == 1;
+    }
+    int rc = alloc_matrix(m, d, rows, p0.cols, p0.bits, p0.group, bf16);
+    size_t woff = 0, moff = 0;
+    for (size_t i = 0; i < parts.size() && rc == QMR_OK; ++i) {
+        const HostMatrix &p = parts[i];
+        rc = upload(m, static_cast<uint8_t *>(d->w) + woff, p.words.data(), p.words.size() * 4);
+        const size_t esz = bf16 ? 2 : 4;
+        const void *sp = bf16 ? (const void *)cs[i].data() : (const void *)p.scales.data();
+        const void *bp = bf16 ? (const void *)cb[i].data() : (const void *)p.biases.data();
+        if (rc == QMR_OK) rc = upload(m, static_cast<uint8_t *>(d->s) + moff, sp, p.scales.size() * esz);
+        if (rc == QMR_OK) rc = upload(m, static_cast<uint8_t *>(d->b) + moff, bp, p.biases.size() * esz);
+        if (rc == QMR_OK) rc = cuda_check(cudaStreamSynchronize(m->stream), "uploading a matrix");
+        woff += p.words.size() * 4;
+        moff += p.scales.size() * esz;
+        if (bf16) {
+            m->compacted += 1;
+            m->saved_bytes += (p.scales.size() + p.biases.size()) * 2;
+        }
+    }
+    return rc;
+}
+
+int load_vector(QmrModel *m, const Checkpoint &cp, const std::string &name, size_t n, float **out) {
+    std::vector<float> v;
+    int rc = cp.vector(name, &v);
+    if (rc != QMR_OK) return rc;
+    if (v.size() != n) return fail(QMR_EINVAL, "%s: expected %zu elements, got %zu", name.c_str(), n, v.size());
+    return dev_vector(m, out, v);
+}
+
+int load_model(QmrModel *m, const std::string &dir, uint32_t context) {
+    std::unique_ptr<Checkpoint> cp;
+    int rc = Checkpoint::open(dir, &cp);
+    if (rc != QMR_OK) return rc;
+    const QmrModelConfig &c = cp->config();
+    if (context == 0 || context > cp->max_position())
+        return fail(QMR_EINVAL, "context must be in 1..=%u", cp->max_position());
+    rc = create_common(m, c, context);
+    if (rc != QMR_OK) return rc;
+    const size_t H = c.hidden_size;
+    rc = load_matrix(m, *cp, {"model.embed_tokens"}, &m->embed);
+    if (rc == QMR_OK && (m->embed.rows != c.vocab_size || m->embed.cols != H))
+        rc = fail(QMR_EINVAL, "model.embed_tokens: expected [%u,%zu]", c.vocab_size, H);
+    for (uint32_t l = 0; l < c.num_layers && rc == QMR_OK; ++l) {
+        LayerState &L = m->layers[l];
+        const std::string p = "model.layers." + std::to_string(l);
+        rc = load_vector(m, *cp, p + ".input_layernorm", H, &L.in_norm);
+        if (rc == QMR_OK) rc = load_vector(m, *cp, p + ".post_attention_layernorm", H, &L.post_norm);
+        if (rc == QMR_OK && L.attn) {
+            const std::string a = p + ".self_attn.";
+            rc = load_matrix(m, *cp, {a + "q_proj", a + "k_proj", a + "v_proj"}, &L.in);
+            if (rc == QMR_OK) rc = load_matrix(m, *cp, {a + "o_proj"}, &L.out);
+            if (rc == QMR_OK) rc = load_vector(m, *cp, a + "q_norm", c.head_dim, &L.qnorm);
+            if (rc == QMR_OK) rc = load_vector(m, *cp, a + "k_norm", c.head_dim, &L.knorm);
+        } else if (rc == QMR_OK) {
+            const std::string a = p + ".linear_attn.";
+            rc = load_matrix(m, *cp, {a + "in_proj_qkv", a + "in_proj_z", a + "in_proj_a", a + "in_proj_b"}, &L.in);
+            if (rc == QMR_OK) rc = load_matrix(m, *cp, {a + "out_proj"}, &L.out);
+            std::vector<float> conv;
+            if (rc == QMR_OK) rc = cp->conv(a + "conv1d", (uint32_t)m->qkv_channels, c.conv_width, &conv);
+            if (rc == QMR_OK) rc = dev_vector(m, &L.conv_w, conv);
+            if (rc == QMR_OK) rc = load_vector(m, *cp, a + "A_log", c.linear_value_heads, &L.alog);
+            if (rc == QMR_OK) rc = load_vector(m, *cp, a + "dt_bias", c.linear_value_heads, &L.dt);
+            if (rc == QMR_OK) rc = load_vector(m, *cp, a + "norm", c.linear_value_dim, &L.dnorm);
+        }
+        if (rc == QMR_OK) rc = load_matrix(m, *cp, {p + ".mlp.gate_proj"}, &L.gate);
+        if (rc == QMR_OK) rc = load_matrix(m, *cp, {p + ".mlp.up_proj"}, &L.up);
+        if (rc == QMR_OK) rc = load_matrix(m, *cp, {p + ".mlp.down_proj"}, &L.down);
+        if (rc == QMR_OK && (L.in.rows != in_rows(c, L.attn) || L.in.cols != H || L.out.rows != H ||
+                             L.gate.rows != c.intermediate_size || L.gate.cols != H || L.up.rows != c.intermediate_size ||
+                             L.down.rows != H || L.down.cols != c.intermediate_size ||
+                             L.gate.bf16 != L.up.bf16 || L.gate.bits != L.up.bits || L.gate.group != L.up.group))
+            rc = fail(QMR_EINVAL, "layer %u: matrix shapes do not match the config", l);
+    }
+    if (rc == QMR_OK) rc = load_vector(m, *cp, "model.norm", H, &m->final_norm);
+    // A tied head is the embedding matrix itself (engine.rs:426-431).
+    if (rc == QMR_OK) {
+        if (cp->tied())
+            m->head = m->embed;
+        else
+            rc = load_matrix(m, *cp, {"lm_head"}, &m->head);
+    }
+    if (rc == QMR_OK && (m->head.rows != c.vocab_size || m->head.cols != H))
+        rc = fail(QMR_EINVAL, "lm_head: expected [%u,%zu]", c.vocab_size, H);
+    return rc;
+}
+
+// ---- the synthetic model --------------------------------------------------------
+
+int synth_matrix(QmrModel *m, DevMat *d, uint64_t seed, const std::vector<std::pair<uint32_t, uint32_t>> &parts,
+                 uint32_t cols) {
+    uint32_t rows = 0;
+    for (const auto &p : parts) rows += p.second;
+    int rc = alloc_matrix(m, d, rows, cols, 4, 64, true);
+    uint32_t r0 = 0;
+    for (const auto &p : parts) {
+        if (rc != QMR_OK) break;
+        rc = launch_synth_q4(static_cast<uint32_t *>(d->w), static_cast<uint16_t *>(d->s),
+                             static_cast<uint16_t *>(d->b), seed, p.first, p.second, cols, r0, m->stream);
+        r0 += p.second;
+    }
+    return rc;
+}
+
+int synth_model(QmrModel *m, const QmrModelConfig &c, uint64_t seed, uint32_t context) {
+    int rc = create_common(m, c, context);
+    if (rc != QMR_OK) return rc;
+    if (c.hidden_size % 64 || c.intermediate_size % 64 || (c.linear_value_heads * c.linear_value_dim) % 64 ||
+        (c.num_heads * c.head_dim) % 64)
+        return fail(QMR_EINVAL, "synthetic Q4/g64 matrices need widths divisible by 64");
+    const uint32_t H = c.hidden_size, F = c.intermediate_size;
+    const uint32_t KD = c.linear_key_heads * c.linear_key_dim, VD = c.linear_value_heads * c.linear_value_dim;
+    const uint32_t QD = c.num_heads * c.head_dim, KVD = c.num_kv_heads * c.head_dim;
+    rc = synth_matrix(m, &m->embed, seed, {{kMidEmbed, c.vocab_size}}, H);
+    if (rc == QMR_OK) rc = synth_matrix(m, &m->head, seed, {{kMidHead, c.vocab_size}}, H);
+    if (rc == QMR_OK) rc = dev_const(m, &m->final_norm, H, 1.0f);
+    for (uint32_t l = 0; l < c.num_layers && rc == QMR_OK; ++l) {
+        LayerState &L = m->layers[l];
+        rc = dev_const(m, &L.in_norm, H, 1.0f);
+        if (rc == QMR_OK) rc = dev_const(m, &L.post_norm, H, 1.0f);
+        if (rc == QMR_OK && L.attn) {
+            rc = synth_matrix(m, &L.in, seed,
+                              {{synth_mid(l, S_Q), 2 * QD}, {synth_mid(l, S_K), KVD}, {synth_mid(l, S_V), KVD}}, H);
+            if (rc == QMR_OK) rc = synth_matrix(m, &L.out, seed, {{synth_mid(l, S_O), H}}, QD);
+            if (rc == QMR_OK) rc = dev_const(m, &L.qnorm, c.head_dim, 1.0f);
+            if (rc == QMR_OK) rc = dev_const(m, &L.knorm, c.head_dim, 1.0f);
+        } else if (rc == QMR_OK) {
+            rc = synth_matrix(m, &L.in, seed,
+                              {{synth_mid(l, S_QKV), 2 * KD + VD}, {synth_mid(l, S_Z), VD},
+                               {synth_mid(l, S_A), c.linear_value_heads}, {synth_mid(l, S_B), c.linear_value_heads}},
+                              H);
+            if (rc == QMR_OK) rc = synth_matrix(m, &L.out, seed, {{synth_mid(l, S_OUT), H}}, VD);
+            if (rc == QMR_OK) rc = dev_const(m, &L.conv_w, m->qkv_channels * c.conv_width, 0.1f);
+            if (rc == QMR_OK) rc = dev_const(m, &L.alog, c.linear_value_heads, 0.0f);
+            if (rc == QMR_OK) rc = dev_const(m, &L.dt, c.linear_value_heads, 0.0f);
+            if (rc == QMR_OK) rc = dev_const(m, &L.dnorm, c.linear_value_dim, 1.0f);
+        }
+        if (rc == QMR_OK) rc = synth_matrix(m, &L.gate, seed, {{synth_mid(l, S_GATE), F}}, H);
+        if (rc == QMR_OK) rc = synth_matrix(m, &L.up, seed, {{synth_mid(l, S_UP), F}}, H);
+        if (rc == QMR_OK) rc = synth_matrix(m, &L.down, seed, {{synth_mid(l, S_DOWN), H}}, F);
+    }
+    if (rc == QMR_OK) rc = cuda_check(cudaStreamSynchronize(m->stream), "generating the synthetic model");
+    return rc;
+}
+
+int finish_create(QmrModel *m, QmrModel **out) {
+    int rc = build_graphs(m);
+    if (rc == QMR_OK) rc = check_device_error();
+    if (rc != QMR_OK) {
+        delete m;
+        return rc;
+    }
+    *out = m;
+    return QMR_OK;
+}
+
+int replay(QmrModel *m, int kind, uint32_t times) {
+    for (uint32_t i = 0; i < times; ++i) {
+        const int rc = cuda_check(cudaGraphLaunch(m->exec[kind], m->stream), "graph launch");
+        if (rc != QMR_OK) return rc;
+    }
+    return QMR_OK;
+}
+
+}  // namespace
+}  // namespace qmr
+
+extern "C" {
+
+int qmr_checkpoint_open(const char *dir, QmrCheckpoint **out) {
+    if (dir == nullptr || out == nullptr) return fail(QMR_EINVAL, "null argument");
+    std::unique_ptr<Checkpoint> cp;
+    const int rc = Checkpoint::open(dir, &cp);
+    if (rc != QMR_OK) return rc;
+    *out = reinterpret_cast<QmrCheckpoint *>(cp.release());
+    return QMR_OK;
+}
+
+void qmr_checkpoint_close(QmrCheckpoint *cp) { delete reinterpret_cast<Checkpoint *>(cp); }
+
+int qmr_checkpoint_config(const QmrCheckpoint *cp, QmrModelConfig *cfg, uint32_t *max_position, int *tied) {
+    if (cp == nullptr) return fail(QMR_EINVAL, "null checkpoint");
+    const Checkpoint *c = reinterpret_cast<const Checkpoint *>(cp);
+    if (cfg) *cfg = c->config();
+    if (max_position) *max_position = c->max_position();
+    if (tied) *tied = c->tied() ? 1 : 0;
+    return QMR_OK;
+}
+
+int qmr_checkpoint_matrix(const QmrCheckpoint *cp, const char *name, uint32_t *rows, uint32_t *cols, uint32_t *bits,
+                          uint32_t *group, uint32_t *w, float *s, float *b) {
+    if (cp == nullptr || name == nullptr) return fail(QMR_EINVAL, "null argument");
+    HostMatrix m;
+    const int rc = reinterpret_cast<const Checkpoint *>(cp)->matrix(name, &m);
+    if (rc != QMR_OK) return rc;
+    if (rows) *rows = m.rows;
+    if (cols) *cols = m.cols;
+    if (bits) *bits = m.bits;
+    if (group) *group = m.group;
+    if (w) memcpy(w, m.words.data(), m.words.size() * 4);
+    if (s) memcpy(s, m.scales.data(), m.scales.size() * 4);
+    if (b) memcpy(b, m.biases.data(), m.biases.size() * 4);
+    return QMR_OK;
+}
+
+int qmr_checkpoint_vector(const QmrCheckpoint *cp, const char *name, float *out, uint64_t cap, uint64_t *n) {
+    if (cp == nullptr || name == nullptr) return fail(QMR_EINVAL, "null argument");
+    std::vector<float> v;
+    const int rc = reinterpret_cast<const Checkpoint *>(cp)->vector(name, &v);
+    if (rc != QMR_OK) return rc;
+    if (n) *n = v.size();
+    if (out != nullptr) {
+        if (cap < v.size()) return fail(QMR_ERANGE, "vector of %zu elements does not fit %llu", v.size(), (unsigned long long)cap);
+        memcpy(out, v.data(), v.size() * 4);
+    }
+    return QMR_OK;
+}
+
+int qmr_model_load(const char *dir, uint32_t context, QmrModel **out) {
+    if (dir == nullptr || out == nullptr) return fail(QMR_EINVAL, "null argument");
+    QmrModel *m = new QmrModel();
+    const int rc = load_model(m, dir, context);
+    if (rc != QMR_OK) {
+        delete m;
+        return rc;
+    }
+    return finish_create(m, out);
+}
+
+int qmr_model_synthetic(const QmrModelConfig *cfg, uint64_t seed, uint32_t context, QmrModel **out) {
+    if (cfg == nullptr || out == nullptr) return fail(QMR_EINVAL, "null argument");
+    QmrModel *m = new QmrModel();
+    const int rc = synth_model(m, *cfg, seed, context);
+    if (rc != QMR_OK) {
+        delete m;
+        return rc;
+    }
+    return finish_create(m, out);
+}
+
+void qmr_model_free(QmrModel *m) { delete m; }
+
+int qmr_model_config(const QmrModel *m, QmrModelConfig *cfg, uint32_t *context) {
+    if (m == nullptr) return fail(QMR_EINVAL, "null model");
+    if (cfg) *cfg = m->cfg;
+    if (context) *context = m->context;
+    return QMR_OK;
+}
+
+int qmr_model_reset(QmrModel *m) {
+    if (m == nullptr) return fail(QMR_EINVAL, "null model");
+    DeviceGuard g(m->device);
+    return clear_state(m);
+}
+
+int qmr_model_position(const QmrModel *m, uint32_t *pos) {
+    if (m == nullptr || pos == nullptr) return fail(QMR_EINVAL, "null argument");
+    *pos = m->pos;
+    return QMR_OK;
+}
+
+int qmr_model_forward(QmrModel *m, uint32_t token, float *logits, int32_t *next) {
+    if (m == nullptr) return fail(QMR_EINVAL, "null model");
+    if (token >= m->cfg.vocab_size) return fail(QMR_EINVAL, "token %u outside vocabulary", token);
+    if (m->pos >= m->context) return fail(QMR_ERANGE, "context capacity %u exhausted", m->context);
+    DeviceGuard g(m->device);
+    m->host_stage[0] = (int32_t)token;
+    m->host_stage[1] = 0;  // n_prompt: the token comes from ctrl->token
+    int rc = cuda_check(cudaMemcpyAsync(&m->ctrl->token, m->host_stage, 8, cudaMemcpyHostToDevice, m->stream),
+                        "writing the step token");
+    if (rc == QMR_OK) rc = replay(m, 1, 1);
+    if (rc == QMR_OK && logits != nullptr)
+        rc = cuda_check(cudaMemcpyAsync(logits, m->logits, (size_t)m->cfg.vocab_size * 4, cudaMemcpyDeviceToHost,
+                                        m->stream), "reading logits");
+    if (rc == QMR_OK)
+        rc = cuda_check(cudaMemcpyAsync(m->host_stage + 2, &m->ctrl->token, 4, cudaMemcpyDeviceToHost, m->stream),
+                        "reading the argmax");
+    if (rc == QMR_OK) rc = cuda_check(cudaStreamSynchronize(m->stream), "forward");
+    if (rc == QMR_OK) rc = check_device_error();
+    if (rc != QMR_OK) {
+        // A failed step may have updated recurrent state; never reuse it (engine.rs:591-595).
+        clear_state(m);
+        return rc;
+    }
+    if (next) *next = m->host_stage[2];
+    m->pos += 1;
+    return QMR_OK;
+}
+
+int qmr_model_generate(QmrModel *m, const uint32_t *prompt, uint32_t n_prompt, uint32_t max_new, uint32_t *out,
+                       double *prefill_ms, double *decode_ms) {
+    if (m == nullptr || prompt == nullptr || out == nullptr) return fail(QMR_EINVAL, "null argument");
+    if (n_prompt == 0 || max_new == 0) return fail(QMR_EINVAL, "empty prompt or max_new = 0");
+    for (uint32_t i = 0; i < n_prompt; ++i)
+        if (prompt[i] >= m->cfg.vocab_size) return fail(QMR_EINVAL, "prompt token %u outside vocabulary", prompt[i]);
+    if ((uint64_t)m->pos + n_prompt + max_new - 1 > m->context)
+        return fail(QMR_ERANGE, "prompt (%u tokens) plus max_new (%u) exceeds context %u", n_prompt, max_new, m->context);
+    DeviceGuard g(m->device);
+    std::vector<int32_t> p(prompt, prompt + n_prompt);
+    int rc = cuda_check(cudaMemcpyAsync(m->prompt + m->pos, p.data(), (size_t)n_prompt * 4, cudaMemcpyHostToDevice,
+                                        m->stream), "uploading the prompt");
+    const uint32_t hdr[2] = {m->pos + n_prompt, 0u};  // n_prompt (absolute), n_out
+    if (rc == QMR_OK)
+        rc = cuda_check(cudaMemcpyAsync(&m->ctrl->n_prompt, hdr, 8, cudaMemcpyHostToDevice, m->stream), "control block");
+    cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+    for (int i = 0; i < 3 && rc == QMR_OK; ++i) rc = cuda_check(cudaEventCreate(&ev[i]), "event");
+    if (rc == QMR_OK) rc = cuda_check(cudaEventRecord(ev[0], m->stream), "event");
+    if (rc == QMR_OK) rc = replay(m, 0, n_prompt - 1);
+    if (rc == QMR_OK) rc = replay(m, 1, 1);
+    if (rc == QMR_OK) rc = cuda_check(cudaEventRecord(ev[1], m->stream), "event");
+    if (rc == QMR_OK) rc = replay(m, 1, max_new - 1);
+    if (rc == QMR_OK) rc = cuda_check(cudaEventRecord(ev[2], m->stream), "event");
+    std::vector<int32_t> toks(max_new);
+    if (rc == QMR_OK)
+        rc = cuda_check(cudaMemcpyAsync(toks.data(), m->out, (size_t)max_new * 4, cudaMemcpyDeviceToHost, m->stream),
+                        "reading tokens");
+    if (rc == QMR_OK) rc = cuda_check(cudaStreamSynchronize(m->stream), "generate");
+    if (rc == QMR_OK) rc = check_device_error();
+    float t01 = 0, t12 = 0;
+    if (rc == QMR_OK) rc = cuda_check(cudaEventElapsedTime(&t01, ev[0], ev[1]), "event time");
+    if (rc == QMR_OK) rc = cuda_check(cudaEventElapsedTime(&t12, ev[1], ev[2]), "event time");
+    for (auto e : ev)
+        if (e != nullptr) cudaEventDestroy(e);
+    if (rc != QMR_OK) {
+        clear_state(m);
+        return rc;
+    }
+    for (uint32_t i = 0; i < max_new; ++i) out[i] = (uint32_t)toks[i];
+    if (prefill_ms) *prefill_ms = t01;
+    if (decode_ms) *decode_ms = t12;
+    m->pos += n_prompt + max_new - 1;
+    return QMR_OK;
+}
+
+int qmr_model_mlp_r2_eligible(const QmrModel *m, uint32_t *count) {
+    if (m == nullptr || count == nullptr) return fail(QMR_EINVAL, "null argument");
+    uint32_t n = 0;
+    if (modes_gemv_aligned())
+        for (const LayerState &L : m->layers)
+            for (const DevMat *d : {&L.gate, &L.up, &L.down})
+                if (d->bf16 && d->bits == 4 && d->group == 64 &&
+                    ((d->rows == 17408 && d->cols == 5120) || (d->rows == 5120 && d->cols == 17408)))
+                    ++n;
+    *count = n;
+    return QMR_OK;
+}
+
+int qmr_model_metadata_stats(const QmrModel *m, uint64_t *matrices, uint64_t *saved_bytes) {
+    if (m == nullptr) return fail(QMR_EINVAL, "null model");
+    if (matrices) *matrices = m->compacted;
+    if (saved_bytes) *saved_bytes = m->saved_bytes;
+    return QMR_OK;
+}
+
+int qmr_model_step_launches(const QmrModel *m, uint32_t *with_head, uint32_t *without_head) {
+    if (m == nullptr) return fail(QMR_EINVAL, "null model");
+    if (with_head) *with_head = m->launches[1];
+    if (without_head) *without_head = m->launches[0];
+    return QMR_OK;
+}
+
+}  // extern "C"

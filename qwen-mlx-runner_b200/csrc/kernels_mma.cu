@@ -188,6 +188,8 @@ int QMR_MMA_LAUNCH(const FastCall &c, const MmaPlan &p, const ScratchView &sv, c
     a.off_part = p.off_part;
     a.off_bars = p.off_bars;
     a.zero = 0u;
+    a.row_scale = c.norm_w != nullptr ? v.row_scale : nullptr;
+    a.resid = c.resid;
     switch (c.epilogue) {
         case 0: return launch_e<0>(maps, a, p, c.bf16, c.group, c.batch, c.overlap, stream);
         case 1: return launch_e<1>(maps, a, p, c.bf16, c.group, c.batch, c.overlap, stream);

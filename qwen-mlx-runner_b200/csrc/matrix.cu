@@ -62,7 +62,8 @@ size_t prepared_region(int bits, uint32_t cols, uint32_t batch) {
 // The shape-dependent prepared activations follow it.
 size_t fixed_region() {
     return align_up(8 * sizeof(float)) + align_up(4 * sizeof(unsigned long long) + sizeof(unsigned int)) +
-           align_up(kCounterCount * sizeof(unsigned int)) + align_up(kPartialFloats * sizeof(float));
+           align_up(kCounterCount * sizeof(unsigned int)) + align_up(kPartialFloats * sizeof(float)) +
+           align_up(4 * sizeof(float));
 }
 
 void scratch_layout(void *base, int bits, uint32_t cols, uint32_t batch, ScratchView *v, MmaImageView *mv = nullptr) {
@@ -77,8 +78,13 @@ void scratch_layout(void *base, int bits, uint32_t cols, uint32_t batch, Scratch
     p += align_up(kCounterCount * sizeof(unsigned int));
     v->partial = reinterpret_cast<float *>(p);
     p += align_up(kPartialFloats * sizeof(float));
+    float *row_scale = reinterpret_cast<float *>(p);  // fused RMSNorm factors, one per RHS
+    p += align_up(4 * sizeof(float));
     v->xp = reinterpret_cast<float *>(p);
     if (mv != nullptr) {
+        mv->norm_w = nullptr;
+        mv->eps = 0.0f;
+        mv->row_scale = row_scale;
         const size_t padded = ((size_t)cols + 1023) / 1024 * 1024;
         mv->image = reinterpret_cast<__half *>(p);
         mv->table = reinterpret_cast<float *>(p + align_up(padded * 4 * batch));
@@ -322,10 +328,18 @@ bool mma_takes(const FastCall &c, MmaPlan *p) {
     if (!mma_plan(c.bits, c.group, c.rows, c.cols, c.batch, c.epilogue, c.bf16, p)) return false;
     if (!aligned16(c.w) || !aligned16(c.s) || !aligned16(c.b)) return false;
     if (c.epilogue == 1 && (!aligned16(c.w2) || !aligned16(c.s2) || !aligned16(c.b2))) return false;
+    // The fused RMSNorm needs the whole row in one prep CTA per RHS.
+    if (c.norm_w != nullptr && p->ngroups_pad > kPrepGroupsPerCta) return false;
     return true;
 }
 
 }  // namespace
+
+bool fused_supported(const FastCall &c) {
+    if (!fast_eligible(c.w, c.cols, c.bits, c.group)) return false;
+    MmaPlan p;
+    return mma_takes(c, &p);
+}
 
 int run_prepare(const float *x, uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch, void *base, int path,
                 cudaStream_t stream) {
@@ -395,6 +409,10 @@ int run_fast(const FastCall &c, cudaStream_t stream) {
         if (!mma_takes(call, &plan))
             return fail(QMR_EUNSUPPORTED, "the exchange calls need a shape the tensor-core kernel takes");
     }
+    const bool fused = call.norm_w != nullptr || call.resid != nullptr;
+    if (fused && !mma_takes(call, &plan))
+        return fail(QMR_EUNSUPPORTED, "the fused RMSNorm/residual epilogue needs a shape the tensor-core kernel takes");
+    if (fused) call.path = kPathMma;
     if (call.path == kPathMma && !mma_takes(call, &plan)) call.path = kPathTile;  // FP32 kernels take the rest
     if (call.path == kPathMma) {
         // Prep kernel, then the streaming kernel behind it (programmatic
@@ -402,6 +420,8 @@ int run_fast(const FastCall &c, cudaStream_t stream) {
         ScratchView sv;
         MmaImageView mv;
         scratch_layout(base, (int)call.bits, call.cols, call.batch, &sv, &mv);
+        mv.norm_w = call.norm_w;
+        mv.eps = call.eps;
         const int rc = launch_mma_prep_bits((int)call.bits, call.x, call.cols, call.group, call.batch,
                                             plan.ngroups_pad, mv, stream);
         if (rc != QMR_OK) return rc;

@@ -125,6 +125,13 @@ struct MmaImageView {
     float *table;
     unsigned long long *keys;  // argmax keys, cleared by the prep
     unsigned int *done;        // CTA counter, cleared by the prep
+    // Fused RMSNorm (optional): the image holds x * norm_w, and the prep
+    // writes row_scale[b] = 1 / sqrt(mean(x_b^2) + eps), which the streaming
+    // kernel multiplies into every output of RHS b.  Needs one prep CTA per
+    // RHS (ngroups_pad <= kPrepGroupsPerCta).
+    const float *norm_w;
+    float eps;
+    float *row_scale;
 };
 
 // ---- activation image arithmetic (the prep kernel's) ----
@@ -259,6 +266,7 @@ __global__ void __launch_bounds__(4 * kPrepGroupsPerCta) mma_prep_kernel(const f
     float v_[CPL];
 #pragma unroll
     for (int k = 0; k < CPL; ++k) v_[k] = 0.0f;
+    float ss = 0.0f;  // sum of x^2 over this thread's columns (fused RMSNorm)
     if (real) {
         const float *xl = xb + (size_t)g * G + t * CPL;
         if ((reinterpret_cast<uintptr_t>(xl) & 15) == 0) {
@@ -273,6 +281,28 @@ __global__ void __launch_bounds__(4 * kPrepGroupsPerCta) mma_prep_kernel(const f
         } else {
 #pragma unroll
             for (int k = 0; k < CPL; ++k) v_[k] = __ldcg(xl + k);
+        }
+        if (v.norm_w != nullptr) {
+            const float *wl = v.norm_w + (size_t)g * G + t * CPL;
+#pragma unroll
+            for (int k = 0; k < CPL; ++k) {
+                ss = __fmaf_rn(v_[k], v_[k], ss);
+                v_[k] = __fmul_rn(v_[k], __ldg(wl + k));
+            }
+        }
+    }
+    if (v.norm_w != nullptr) {
+        // 1 / rms of the whole row: this CTA holds every group of RHS b.
+        // Fixed-order reduction: lanes by xor shuffle, then warps in order.
+        __shared__ float warp_ss[4 * kPrepGroupsPerCta / 32];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+        if ((tid & 31) == 0) warp_ss[tid >> 5] = ss;
+        __syncthreads();
+        if (tid == 0) {
+            float total = 0.0f;
+            for (int w = 0; w < (int)(blockDim.x >> 5); ++w) total = __fadd_rn(total, warp_ss[w]);
+            v.row_scale[b] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)cols), v.eps)));
         }
     }
     int E;
@@ -393,6 +423,8 @@ struct MmaArgs {
     int rows, ngroups, ngroups_pad, ystride, row_base;
     int tiles, nwin, kc, clusters, pieces, stages;
     uint32_t zero;                         // always 0 (an opaque operand, see the slot refill)
+    const float *row_scale;                // per-RHS output factor (fused RMSNorm), or null
+    const float *resid;                    // residual added to every output (same index as y), or null
     uint32_t off_image, off_table, off_pieces, off_part, off_bars;  // offsets into the 1024-aligned dynamic smem
     // Output exchange over peer memory (xworld > 1): rows also go to every
     // rank's output (peer_y, same index as y; not for EPI 2, whose keys go to
@@ -554,8 +586,15 @@ __global__ void __launch_bounds__(32 * NW, 1)
                 const int row = T * kTileRows + gq + 8 * h;
                 if (row < a.rows) {
                     float val = v[0][h];
-                    if constexpr (EPI == 1) val = __fmul_rn(silu_f32(val), v[NM - 1][h]);
+                    float up = v[NM - 1][h];
+                    if (a.row_scale != nullptr) {
+                        const float rs = a.row_scale[t];
+                        val = __fmul_rn(val, rs);
+                        up = __fmul_rn(up, rs);
+                    }
+                    if constexpr (EPI == 1) val = __fmul_rn(silu_f32(val), up);
                     const size_t yi = (size_t)t * a.ystride + row;
+                    if (a.resid != nullptr) val = __fadd_rn(a.resid[yi], val);
                     a.y[yi] = val;
                     if constexpr (EPI != 2) {
                         for (int p = 0; p < a.xworld; ++p)  // xworld is 0 without an exchange

@@ -31,7 +31,16 @@ struct FastCall {
     size_t scratch_bytes;
     uint32_t ystride;          // output row stride per RHS (0: rows)
     const QmrExchange *ex;     // output exchange over peer memory, or nullptr
+    // Fused decode-step work (tensor-core path only): RMSNorm of x with
+    // weight norm_w folded into the activation prep and the output factor,
+    // and a residual added to every output (resid may equal y).
+    const float *norm_w;
+    float eps;
+    const float *resid;
 };
+// The tensor-core path takes this call with the fused RMSNorm / residual
+// epilogue (false: the caller must run them as separate kernels).
+bool fused_supported(const FastCall &c);
 
 // Streaming kernels of the fast path.
 constexpr int kPathMma = 0;        // tensor-core weight streaming (default)
@@ -58,6 +67,11 @@ int device_error(int *code, bool clear);
 // The bounded wait for every rank's current exchange epoch (+ key merge).
 int launch_exchange_wait(const QmrExchange &ex, uint32_t batch, int32_t *argmax, uint64_t *best_key,
                          cudaStream_t stream);
+// Library modes (abi.cpp): QWEN_METAL_METADATA=bf16, QWEN_METAL_GEMV=aligned
+// (and not reference mode), the selected streaming kernel.
+bool modes_meta_bf16();
+bool modes_gemv_aligned();
+int modes_stream_path();
 // qmr_matmul_affine on the fixed per-device static scratch (static_scratch.cu).
 int matmul_static(const void *w, const void *s, const void *b, const float *x, float *y, uint32_t rows,
                   uint32_t cols, uint32_t bits, uint32_t group, uint32_t batch, bool bf16, bool r2, int path,

@@ -68,6 +68,19 @@ _int = ctypes.c_int
 _sz = ctypes.c_size_t
 _cstr = ctypes.c_char_p
 
+QMR_MAX_LAYERS = 256
+
+
+class QmrModelConfig(ctypes.Structure):
+    """struct QmrModelConfig (include/qmr.h): ModelConfig (src/config.rs:4-25)."""
+    _fields_ = [("hidden_size", ctypes.c_uint32), ("intermediate_size", ctypes.c_uint32),
+                ("num_layers", ctypes.c_uint32), ("num_heads", ctypes.c_uint32), ("num_kv_heads", ctypes.c_uint32),
+                ("head_dim", ctypes.c_uint32), ("vocab_size", ctypes.c_uint32),
+                ("linear_key_heads", ctypes.c_uint32), ("linear_value_heads", ctypes.c_uint32),
+                ("linear_key_dim", ctypes.c_uint32), ("linear_value_dim", ctypes.c_uint32),
+                ("conv_width", ctypes.c_uint32), ("rotary_dim", ctypes.c_uint32), ("rms_eps", ctypes.c_float),
+                ("rope_theta", ctypes.c_float), ("is_attention", ctypes.c_uint8 * QMR_MAX_LAYERS)]
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     "qmr_abi_version": (_int, []),
@@ -110,6 +123,25 @@ SIGNATURES = {
     "qmr_head_argmax_exchange": (_int, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _int,
                                         ctypes.POINTER(QmrExchange), _vp]),
     "qmr_exchange_wait": (_int, [ctypes.POINTER(QmrExchange), _u32, _vp, _vp, _vp]),
+    "qmr_checkpoint_open": (_int, [_cstr, ctypes.POINTER(_vp)]),
+    "qmr_checkpoint_close": (None, [_vp]),
+    "qmr_checkpoint_config": (_int, [_vp, ctypes.POINTER(QmrModelConfig), ctypes.POINTER(_u32),
+                                     ctypes.POINTER(_int)]),
+    "qmr_checkpoint_matrix": (_int, [_vp, _cstr, ctypes.POINTER(_u32), ctypes.POINTER(_u32), ctypes.POINTER(_u32),
+                                     ctypes.POINTER(_u32), _vp, _vp, _vp]),
+    "qmr_checkpoint_vector": (_int, [_vp, _cstr, _vp, _u64, ctypes.POINTER(_u64)]),
+    "qmr_model_load": (_int, [_cstr, _u32, ctypes.POINTER(_vp)]),
+    "qmr_model_synthetic": (_int, [ctypes.POINTER(QmrModelConfig), _u64, _u32, ctypes.POINTER(_vp)]),
+    "qmr_model_free": (None, [_vp]),
+    "qmr_model_config": (_int, [_vp, ctypes.POINTER(QmrModelConfig), ctypes.POINTER(_u32)]),
+    "qmr_model_reset": (_int, [_vp]),
+    "qmr_model_position": (_int, [_vp, ctypes.POINTER(_u32)]),
+    "qmr_model_forward": (_int, [_vp, _u32, _vp, _vp]),
+    "qmr_model_generate": (_int, [_vp, _vp, _u32, _u32, _vp, ctypes.POINTER(ctypes.c_double),
+                                  ctypes.POINTER(ctypes.c_double)]),
+    "qmr_model_mlp_r2_eligible": (_int, [_vp, ctypes.POINTER(_u32)]),
+    "qmr_model_metadata_stats": (_int, [_vp, ctypes.POINTER(_u64), ctypes.POINTER(_u64)]),
+    "qmr_model_step_launches": (_int, [_vp, ctypes.POINTER(_u32), ctypes.POINTER(_u32)]),
 }
 
 

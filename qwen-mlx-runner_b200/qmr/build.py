@@ -27,9 +27,13 @@ UNITS = [
     ("kernels_mma.cu", ["-DQMR_MMA_BITS=4"], "kernels_mma4.o"),
     ("kernels_mma.cu", ["-DQMR_MMA_BITS=8"], "kernels_mma8.o"),
     ("static_scratch.cu", [], "static_scratch.o"),
+    ("decode.cu", [], "decode.o"),
+    ("engine.cpp", [], "engine.o"),
+    ("checkpoint.cpp", [], "checkpoint.o"),
 ]
 SOURCES = sorted({u[0] for u in UNITS})
-HEADERS = ["matrix_kernels.cuh", "qmr_internal.h", "tile.cuh", "mma_stream.cuh", "launch.h", "pipe.cuh"]
+HEADERS = ["matrix_kernels.cuh", "qmr_internal.h", "tile.cuh", "mma_stream.cuh", "launch.h", "pipe.cuh", "decode.h",
+           "checkpoint.h"]
 OBJ_DIR = PKG_ROOT / "_build"
 
 NVCC_FLAGS = [
