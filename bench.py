@@ -18,7 +18,11 @@ The same JSON line also carries, measured in the same run:
     inside the kernels), timed as the max over ranks, and checked against the
     1-GPU call on rank 0;
   * `reps200`: the headline call timed over a fixed 200 calls, comparable
-    between runs whatever --steps is.
+    between runs whatever --steps is;
+  * `decode`: config 4, the synthetic 64-layer 27B-shaped hybrid: prefill a
+    seeded 512-token prompt and greedily decode 128 tokens at context 4096
+    through the engine (qmr_model_generate), decode tokens/s; under
+    torchrun one replica per rank.
 
 Multi-GPU headline: one process per GPU (torchrun); each rank runs the b3
 call on its own weights (independent matrices, no data-path collective),
@@ -593,6 +597,81 @@ def sharded_record(name, device, seed, stream, world, rank, peak):
     return rec
 
 
+# ---- config 4: the synthetic 64-layer hybrid decode -------------------------
+
+DECODE_PROMPT, DECODE_NEW, DECODE_CONTEXT = 512, 128, 4096
+
+
+def decode_bytes_per_token(cfg):
+    """Algorithmic bytes of one decode step: every packed matrix once (Q4
+    words + BF16 scale and bias per 64 columns), the embedding row, the
+    DeltaNet state read and written, the conv history."""
+    H, F, V = cfg["hidden"], cfg["inter"], cfg["vocab"]
+    KD, VD = cfg["lin_key_heads"] * cfg["lin_key_dim"], cfg["lin_value_heads"] * cfg["lin_value_dim"]
+    QD, KVD = cfg["heads"] * cfg["head_dim"], cfg["kv_heads"] * cfg["head_dim"]
+    mat = lambda r, c: r * c // 2 + r * c // 64 * 4  # noqa: E731
+    total = mat(V, H) + H * 4 // 8  # head, embedding row
+    for att in cfg["is_attn"]:
+        total += 3 * mat(F, H)
+        if att:
+            total += mat(2 * QD + 2 * KVD, H) + mat(H, QD)
+        else:
+            total += mat(2 * KD + 2 * VD + 2 * cfg["lin_value_heads"], H) + mat(H, VD)
+            total += 2 * cfg["lin_value_heads"] * cfg["lin_value_dim"] * cfg["lin_key_dim"] * 4
+    return total
+
+
+def decode_record(device, world, rank, peak, cpu_baseline):
+    """Config 4 on each rank's GPU: prefill a seeded 512-token prompt, then
+    greedily decode 128 tokens at context 4096 (one replica per rank; the
+    head-sharded multi-GPU decode is not built)."""
+    import torch
+
+    import qmr
+    from qmr import engine as qeng
+    from qmr import synth
+    torch.cuda.empty_cache()
+    cfg = qeng.qwen27b_config()
+    eng = qmr.Engine.synthetic(cfg, 4242, DECODE_CONTEXT)
+    prompt = [int(v % cfg["vocab"]) for v in synth.splitmix64(77, DECODE_PROMPT)]
+    eng.generate(prompt[:16], 8)  # untimed warm-up
+    eng.reset()
+    barrier(world)
+    toks, pre_ms, dec_ms = eng.generate(prompt, DECODE_NEW)
+    pre_max = max_over_ranks(pre_ms, device, world)
+    dec_max = max_over_ranks(dec_ms, device, world)
+    with_head, without = eng.step_launches()
+    eng.close()
+    nbytes = decode_bytes_per_token(cfg)
+    per_gpu_tps = (DECODE_NEW - 1) / (dec_max * 1e-3)
+    rec = {"workload": "synthetic 64-layer Qwen3.5-27B-shaped hybrid (3:1 DeltaNet:attention), Q4/g64 BF16 "
+                       "metadata, distinct seeded weights, vocabulary 152064, FP32 activations/state/KV",
+           "prompt_tokens": DECODE_PROMPT, "new_tokens": DECODE_NEW, "context": DECODE_CONTEXT,
+           "decode_tok_s": round(world * per_gpu_tps, 2), "decode_tok_s_per_gpu": round(per_gpu_tps, 2),
+           "ms_per_token": round(dec_max / (DECODE_NEW - 1), 4),
+           "prefill_tok_s": round(world * DECODE_PROMPT / (pre_max * 1e-3), 2),
+           "bytes_per_token": nbytes, "gbs_per_gpu": round(nbytes * per_gpu_tps / 1e9, 2),
+           "frac_per_gpu": round(nbytes * per_gpu_tps / 1e9 / peak, 4),
+           "launches_per_token": with_head, "launches_per_prefill_token": without,
+           "parallelism": f"replicas{world}" if world > 1 else "single",
+           "first_tokens": toks[:8]}
+    if cpu_baseline and rank == 0 and world == 1:
+        # The reference's CPU arithmetic for this graph: the FP64 oracle on the
+        # same synthetic model, all host cores, two steps of the prompt.
+        import oracle
+        oracle.set_threads(host_threads())
+        o = oracle.synthetic_decode_oracle(cfg, 4242, 8, qeng.synthetic_mid, qeng.MID_EMBED, qeng.MID_HEAD)
+        t0 = time.perf_counter()
+        for t in prompt[:2]:
+            o.forward(t)
+        secs = (time.perf_counter() - t0) / 2
+        rec["cpu_baseline"] = {"value": round(1.0 / secs, 5), "unit": "tok/s", "cores": oracle.threads(),
+                               "kind": "port", "s_per_token": round(secs, 3),
+                               "sample": "2 decode steps (positions 0-1) of the same model, FP64 oracle "
+                                         "(oracle/decode.c), OpenMP over matrix rows"}
+    return rec
+
+
 def run_gpu(args):
     import torch
     import torch.distributed as dist
@@ -717,6 +796,8 @@ def run_gpu(args):
         line["workloads"] = {n: single_record(n, device, 2000 + 17 * rank, stream, world, peak)
                              for n in ("b1", "q8b3")}
         line["sharded"] = {n: sharded_record(n, device, 3000, stream, world, rank, peak) for n in ("mlp", "head")}
+        line["decode"] = decode_record(device, world, rank, peak, not args.no_cpu_baseline)
+        line["gpu_launches_decode_per_token"] = line["decode"]["launches_per_token"]
 
     if rank == 0 and world == 1 and not (args.no_cpu_baseline or args.quick):
         import oracle

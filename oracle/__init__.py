@@ -244,3 +244,44 @@ class DecodeOracle:
         if rc != 0:
             raise ValueError("token outside the vocabulary or context full")
         return out
+
+
+def synthetic_decode_oracle(cfg, seed, context, mid, mid_embed, mid_head):
+    """DecodeOracle of the engine's synthetic model: every matrix generated on
+    the fly from (seed, mid(layer, slot)), norms 1, conv 0.1, A_log and
+    dt_bias 0 (the reference's synthetic constants, src/engine/synthetic.rs:220-225)."""
+    o = DecodeOracle(dict(cfg, context=context))
+    H, F = cfg["hidden"], cfg["inter"]
+    KD, VD = cfg["lin_key_heads"] * cfg["lin_key_dim"], cfg["lin_value_heads"] * cfg["lin_value_dim"]
+    QD, KVD = cfg["heads"] * cfg["head_dim"], cfg["kv_heads"] * cfg["head_dim"]
+    o.set_synth(-1, "embed", seed, mid_embed, cfg["vocab"], H)
+    o.set_synth(-1, "head", seed, mid_head, cfg["vocab"], H)
+    ones_h, ones_v = np.ones(H, np.float32), np.ones(cfg["lin_value_dim"], np.float32)
+    ones_d = np.ones(cfg["head_dim"], np.float32)
+    conv = np.full((2 * KD + VD) * cfg["conv_width"], 0.1, np.float32)
+    zeros = np.zeros(cfg["lin_value_heads"], np.float32)
+    o.set_vector(-1, None, ones_h)
+    for l, att in enumerate(cfg["is_attn"]):
+        o.set_vector(l, "input_norm", ones_h)
+        o.set_vector(l, "post_norm", ones_h)
+        o.set_synth(l, "gate", seed, mid(l, "gate"), F, H)
+        o.set_synth(l, "up", seed, mid(l, "up"), F, H)
+        o.set_synth(l, "down", seed, mid(l, "down"), H, F)
+        if att:
+            o.set_synth(l, "q", seed, mid(l, "q"), 2 * QD, H)
+            o.set_synth(l, "k", seed, mid(l, "k"), KVD, H)
+            o.set_synth(l, "v", seed, mid(l, "v"), KVD, H)
+            o.set_synth(l, "o", seed, mid(l, "o"), H, QD)
+            o.set_vector(l, "q_norm", ones_d)
+            o.set_vector(l, "k_norm", ones_d)
+        else:
+            o.set_synth(l, "qkv", seed, mid(l, "qkv"), 2 * KD + VD, H)
+            o.set_synth(l, "z", seed, mid(l, "z"), VD, H)
+            o.set_synth(l, "a", seed, mid(l, "a"), cfg["lin_value_heads"], H)
+            o.set_synth(l, "b", seed, mid(l, "b"), cfg["lin_value_heads"], H)
+            o.set_synth(l, "out", seed, mid(l, "out"), H, VD)
+            o.set_vector(l, "conv", conv)
+            o.set_vector(l, "A_log", zeros)
+            o.set_vector(l, "dt_bias", zeros)
+            o.set_vector(l, "delta_norm", ones_v)
+    return o

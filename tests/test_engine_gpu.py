@@ -125,41 +125,7 @@ def small_config():
 
 
 def synthetic_oracle(cfg, seed, context):
-    o = oracle.DecodeOracle(dict(cfg, context=context))
-    H, F = cfg["hidden"], cfg["inter"]
-    KD, VD = cfg["lin_key_heads"] * cfg["lin_key_dim"], cfg["lin_value_heads"] * cfg["lin_value_dim"]
-    QD, KVD = cfg["heads"] * cfg["head_dim"], cfg["kv_heads"] * cfg["head_dim"]
-    o.set_synth(-1, "embed", seed, qeng.MID_EMBED, cfg["vocab"], H)
-    o.set_synth(-1, "head", seed, qeng.MID_HEAD, cfg["vocab"], H)
-    keep = [np.ones(H, np.float32), np.ones(cfg["lin_value_dim"], np.float32), np.ones(cfg["head_dim"], np.float32),
-            np.full((2 * KD + VD) * cfg["conv_width"], 0.1, np.float32), np.zeros(cfg["lin_value_heads"], np.float32)]
-    o.set_vector(-1, None, keep[0])
-    for l, att in enumerate(cfg["is_attn"]):
-        mid = lambda s: qeng.synthetic_mid(l, s)  # noqa: E731
-        o.set_vector(l, "input_norm", keep[0])
-        o.set_vector(l, "post_norm", keep[0])
-        o.set_synth(l, "gate", seed, mid("gate"), F, H)
-        o.set_synth(l, "up", seed, mid("up"), F, H)
-        o.set_synth(l, "down", seed, mid("down"), H, F)
-        if att:
-            o.set_synth(l, "q", seed, mid("q"), 2 * QD, H)
-            o.set_synth(l, "k", seed, mid("k"), KVD, H)
-            o.set_synth(l, "v", seed, mid("v"), KVD, H)
-            o.set_synth(l, "o", seed, mid("o"), H, QD)
-            o.set_vector(l, "q_norm", keep[2])
-            o.set_vector(l, "k_norm", keep[2])
-        else:
-            o.set_synth(l, "qkv", seed, mid("qkv"), 2 * KD + VD, H)
-            o.set_synth(l, "z", seed, mid("z"), VD, H)
-            o.set_synth(l, "a", seed, mid("a"), cfg["lin_value_heads"], H)
-            o.set_synth(l, "b", seed, mid("b"), cfg["lin_value_heads"], H)
-            o.set_synth(l, "out", seed, mid("out"), H, VD)
-            o.set_vector(l, "conv", keep[3])
-            o.set_vector(l, "A_log", keep[4])
-            o.set_vector(l, "dt_bias", keep[4])
-            o.set_vector(l, "delta_norm", keep[1])
-    o._keep += keep
-    return o
+    return oracle.synthetic_decode_oracle(cfg, seed, context, qeng.synthetic_mid, qeng.MID_EMBED, qeng.MID_HEAD)
 
 
 def prompt_tokens(seed, n, vocab):
@@ -199,3 +165,44 @@ def test_synthetic_engine_matches_fp64_oracle_logits_and_greedy_ids(cuda):
         assert qmr.ops.device_error() == 0
     finally:
         eng.close()
+
+
+def test_qwen27b_shaped_synthetic_model_gives_the_oracle_greedy_ids(cuda):
+    """Config 4's model (64 layers, 3:1 DeltaNet : attention, hidden 5120, MLP
+    17408, vocabulary 152064, distinct seeded Q4/g64 weights per matrix) on a
+    short window: the last prompt token's logits against the FP64 oracle, and
+    the greedy continuation identical to the oracle's."""
+    import os
+    cfg = qeng.qwen27b_config()
+    seed, context = 2026, 64
+    oracle.set_threads(len(os.sched_getaffinity(0)))
+    eng = qmr.Engine.synthetic(cfg, seed, context)
+    o = synthetic_oracle(cfg, seed, context)
+    try:
+        assert eng.mlp_r2_eligible_matrices() == (192 if "gemv=aligned" in modes() else 0)
+        prompt = prompt_tokens(7, 3, cfg["vocab"])
+        toks, _, _ = eng.generate(prompt, 3)
+        seq = []
+        for i, t in enumerate(prompt):
+            want = o.forward(t)
+        seq.append(oracle.argmax_f64(want))
+        eng.reset()
+        for t in prompt:
+            got, nxt = eng.forward(t)
+        scale = np.max(np.abs(want))
+        err = np.max(np.abs(got - want))
+        assert err <= 1e-3 * scale, (err, scale)
+        assert nxt == seq[0]
+        for _ in range(2):
+            seq.append(oracle.argmax_f64(o.forward(seq[-1])))
+        assert toks == seq, (toks, seq)
+        assert qmr.ops.device_error() == 0
+    finally:
+        eng.close()
+
+
+def modes():
+    import ctypes
+    buf = ctypes.create_string_buffer(256)
+    qmr.lib().qmr_get_modes(buf, 256)
+    return buf.value.decode()
