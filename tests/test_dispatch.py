@@ -16,8 +16,8 @@ U32_MAX = 0xFFFFFFFF
 
 def test_library_exports_every_header_symbol():
     header = (ROOT / "include" / "qmr.h").read_text()
-    names = set(re.findall(r"^(?:int|const char \*)\s*(qmr_\w+)\(", header, flags=re.M))
-    assert len(names) >= 18
+    names = set(re.findall(r"^(?:int|void|uint64_t|const char \*)\s*(qmr_\w+)\(", header, flags=re.M))
+    assert len(names) >= 49
     lib = qmr.lib()
     for n in sorted(names):
         assert hasattr(lib, n), n
