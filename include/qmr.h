@@ -386,6 +386,32 @@ int qmr_model_forward(QmrModel *m, uint32_t token, float *logits, int32_t *next)
  * prefill_ms / decode_ms (may be NULL) are device times. */
 int qmr_model_generate(QmrModel *m, const uint32_t *prompt, uint32_t n_prompt, uint32_t max_new, uint32_t *out,
                        double *prefill_ms, double *decode_ms);
+/* Engine::verify_block (src/engine/block.rs:296-333): evaluate inputs
+ * tokens[0..n) (n = 1..4; the anchor and its drafts) at positions pos ..
+ * pos+n-1 as one batch-n pass over every layer, matrices streamed once for
+ * all inputs, DeltaNet state and convolution history saved before every
+ * input.  logits (host, n*vocab, may be NULL) and argmax (host, n, may be
+ * NULL) receive every row.  The state is tentative until
+ * qmr_model_commit_block; no other step may run in between. */
+int qmr_model_verify_block(QmrModel *m, const uint32_t *tokens, uint32_t n, float *logits, int32_t *argmax);
+/* Engine::commit_block_prefix (src/engine/block.rs:335-390): keep the first
+ * `consumed` inputs of the pending block; DeltaNet state and convolution
+ * history are restored on the GPU, attention entries past the new position
+ * are masked by it. */
+int qmr_model_commit_block(QmrModel *m, uint32_t consumed);
+/* Prefill, then greedy MTP-style decoding in verification rounds of `block`
+ * inputs (2..4): each round evaluates [last token, drafts for the next
+ * block-1 positions] with the drafts read from `drafts` (the draft token for
+ * each absolute position; this library has no drafter), accepts drafts while
+ * each equals the argmax of the row before it (src/speculative.rs:212-264 at
+ * temperature 0), emits the accepted drafts plus the next argmax and rolls
+ * the state back to the consumed prefix -- all on the device, one graph
+ * replay per round.  out receives max_new tokens, the same tokens as
+ * qmr_model_generate whatever the drafts; rounds and accepted (may be NULL)
+ * count verification rounds and accepted drafts. */
+int qmr_model_mtp_generate(QmrModel *m, const uint32_t *prompt, uint32_t n_prompt, uint32_t block, uint32_t max_new,
+                           const uint32_t *drafts, uint32_t n_drafts, uint32_t *out, uint32_t *rounds,
+                           uint32_t *accepted, double *prefill_ms, double *decode_ms);
 /* Engine::mlp_r2_eligible_matrices (src/engine.rs:454-468). */
 int qmr_model_mlp_r2_eligible(const QmrModel *m, uint32_t *count);
 /* Gpu::metadata_stats (src/gpu.rs:473-478): matrices loaded with compacted

@@ -149,136 +149,207 @@ __global__ void add_kernel(float *x, const float *r, uint32_t n) {
     if (i < n) x[i] = __fadd_rn(x[i], r[i]);
 }
 
-constexpr int kDeltaThreads = 512;
-constexpr int kDeltaRowsPerWarp = 8;
+constexpr int kDeltaThreads = 256;
+constexpr int kDeltaRowsPerWarp = 4;
+constexpr int kMaxTokens = 4;   // tokens of one mixer or attention launch
+constexpr int kMaxConvHist = 7; // conv width <= 8
 
-// One DeltaNet layer's mixer for value head blockIdx.x.
-//  conv_silu (qwen.metal:95-106): y = silu(x*w[W-1] + sum_k state[k]*w[k])
-//    over the channels this head reads (its key head's q and k, its own v);
-//    the history is double-buffered by position parity (read parity pos&1,
-//    write the other), so CTAs sharing a key head never race on it: the
-//    first value head of each key group writes the shared q/k history.
+// One DeltaNet layer's mixer for nq tokens, CTA blockIdx.x = value head h *
+// kDeltaSplit + part; the part owns value rows [part*V/S, (part+1)*V/S).
+//  conv_silu (qwen.metal:95-106): y = silu(x*w[W-1] + sum_k hist[k]*w[k])
+//    over the channels this CTA reads (its key head's q and k, its own v
+//    rows), token after token.  Single tokens double-buffer the live history
+//    by position parity (read pos&1, write the other), so CTAs sharing q/k
+//    channels never race: part 0 of the first value head of each key group
+//    writes them.  A verification block only reads the live history and
+//    leaves the history after every prefix in conv_snap.
 //  delta_norm (:107-116): q *= rsqrt(|q|^2 + 1e-6) * rsqrt(K),
 //    k *= rsqrt(|k|^2 + 1e-6).
-//  delta_step (:117-136): decay = exp(-exp(A_log) softplus(a + dt)),
-//    beta = sigmoid(b); per value row S = S*decay, delta = (v - S.k)*beta,
-//    S += k*delta, y = S.q.
-//  gated_rms (:184-194): out = y * rsqrt(mean(y^2) + eps) * w * silu(z).
+//  delta_step / delta_step_block (:117-183): decay = exp(-exp(A_log)
+//    softplus(a + dt)), beta = sigmoid(b); per value row S = S*decay,
+//    delta = (v - S.k)*beta, S += k*delta, y = S.q; the warp's rows stay in
+//    registers across the block's tokens, and a block stores S before each
+//    token in state_snap.
+//  gated_rms (:184-194): out = y * rsqrt(mean(y^2) + eps) * w * silu(z):
+//    every part stores its rows' y and sums of squares; the last part of the
+//    head to finish adds the parts' sums in part order and writes the head.
 __global__ void __launch_bounds__(kDeltaThreads) delta_mixer_kernel(DeltaArgs a) {
     extern __shared__ float dsm[];
-    const int K = a.K, V = a.V, W = a.W, KH = a.KH, VH = a.VH;
-    const int h = blockIdx.x, ratio = VH / KH, kh = h / ratio;
-    const bool rep = (h % ratio) == 0;
+    __shared__ unsigned int last;
+    const int K = a.K, V = a.V, W = a.W, KH = a.KH, VH = a.VH, nq = a.nq, P = a.proj_stride;
+    const int h = blockIdx.x / kDeltaSplit, part = blockIdx.x % kDeltaSplit;
+    const int ratio = VH / KH, kh = h / ratio;
+    const bool rep = (h % ratio) == 0 && part == 0;
+    const int r_begin = part * V / kDeltaSplit, r_end = (part + 1) * V / kDeltaSplit, nr = r_end - r_begin;
+    const int nrp = nr > 0 ? nr : 1;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
-    float *q = dsm, *k = q + K, *v = k + K, *y = v + V, *red = y + V;
+    float *q = dsm, *k = q + nq * K, *v = k + nq * K, *y = v + nq * nrp, *red = y + nq * nrp;
     const int qkv = 2 * KH * K + VH * V;
+    const int H1 = W - 1;
     const int par = (int)(a.ctrl->pos & 1u);
-    const float *cs_old = a.conv_state + (size_t)par * qkv * (W - 1);
-    float *cs_new = a.conv_state + (size_t)(par ^ 1) * qkv * (W - 1);
-    for (int i = tid; i < 2 * K + V; i += blockDim.x) {
-        const int c = i < K ? kh * K + i : (i < 2 * K ? KH * K + kh * K + (i - K) : 2 * KH * K + h * V + (i - 2 * K));
-        const float xin = a.proj[c];
+    const float *cs_old = a.conv_state + (size_t)par * qkv * H1;
+    float *cs_new = a.conv_state + (size_t)(par ^ 1) * qkv * H1;
+    for (int i = tid; i < 2 * K + nr; i += blockDim.x) {
+        const int c = i < K ? kh * K + i
+                            : (i < 2 * K ? KH * K + kh * K + (i - K) : 2 * KH * K + h * V + r_begin + (i - 2 * K));
+        const bool owner = i >= 2 * K || rep;
         const float *w = a.conv_w + (size_t)c * W;
-        const float *st = cs_old + (size_t)c * (W - 1);
-        float sum = __fmul_rn(xin, w[W - 1]);
-        for (int j = 0; j + 1 < W; ++j) sum = __fadd_rn(sum, __fmul_rn(st[j], w[j]));
-        if (i >= 2 * K || rep) {
-            float *sn = cs_new + (size_t)c * (W - 1);
-            for (int j = 0; j + 2 < W; ++j) sn[j] = st[j + 1];
-            if (W > 1) sn[W - 2] = xin;
-        }
-        const float yv = silu_f32(sum);
-        if (i < K)
-            q[i] = yv;
-        else if (i < 2 * K)
-            k[i - K] = yv;
-        else
-            v[i - 2 * K] = yv;
-    }
-    __syncthreads();
-    float qs = 0.0f, ks = 0.0f;
-    for (int i = tid; i < K; i += blockDim.x) {
-        qs = __fmaf_rn(q[i], q[i], qs);
-        ks = __fmaf_rn(k[i], k[i], ks);
-    }
-    qs = block_sum(qs, red);
-    ks = block_sum(ks, red);
-    const float qi = __fmul_rn(rsqrt_f32(__fadd_rn(qs, 1e-6f)), rsqrt_f32((float)K));
-    const float ki = rsqrt_f32(__fadd_rn(ks, 1e-6f));
-    for (int i = tid; i < K; i += blockDim.x) {
-        q[i] = __fmul_rn(q[i], qi);
-        k[i] = __fmul_rn(k[i], ki);
-    }
-    __syncthreads();
-    const float *pa = a.proj + 2 * KH * K + 2 * VH * V;
-    const float av = __fadd_rn(pa[h], a.dt[h]);
-    const float sp = __fadd_rn(fmaxf(av, 0.0f), log1pf(expf(-fabsf(av))));  // softplus, stable
-    const float decay = expf(-__fmul_rn(expf(a.alog[h]), sp));
-    const float beta = sigmoid_f32(pa[VH + h]);
-    // Lane layout over K: column lane + 32*m, m < 4 (K <= 128).
-    float kr[4], qr[4];
+        const float *st = cs_old + (size_t)c * H1;
+        float hist[kMaxConvHist];
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
-        const int j = lane + 32 * m;
-        kr[m] = j < K ? k[j] : 0.0f;
-        qr[m] = j < K ? q[j] : 0.0f;
+        for (int j = 0; j < kMaxConvHist; ++j) hist[j] = j < H1 ? st[j] : 0.0f;
+        if (owner && a.conv_snap != nullptr)
+            for (int j = 0; j < H1; ++j) a.conv_snap[(size_t)c * H1 + j] = hist[j];
+        for (int t = 0; t < nq; ++t) {
+            const float xin = a.proj[(size_t)t * P + c];
+            float sum = __fmul_rn(xin, w[W - 1]);
+            for (int j = 0; j < H1; ++j) sum = __fadd_rn(sum, __fmul_rn(hist[j], w[j]));
+#pragma unroll
+            for (int j = 0; j + 1 < kMaxConvHist; ++j)
+                if (j + 1 < H1) hist[j] = hist[j + 1];
+            if (H1 > 0) {
+#pragma unroll
+                for (int j = 0; j < kMaxConvHist; ++j)
+                    if (j == H1 - 1) hist[j] = xin;
+            }
+            if (owner && a.conv_snap != nullptr)
+                for (int j = 0; j < H1; ++j) a.conv_snap[((size_t)(t + 1) * qkv + c) * H1 + j] = hist[j];
+            const float yv = silu_f32(sum);
+            if (i < K)
+                q[t * K + i] = yv;
+            else if (i < 2 * K)
+                k[t * K + i - K] = yv;
+            else
+                v[t * nrp + i - 2 * K] = yv;
+        }
+        if (owner && a.conv_snap == nullptr) {
+            float *sn = cs_new + (size_t)c * H1;
+            for (int j = 0; j < H1; ++j) sn[j] = hist[j];
+        }
     }
+    __syncthreads();
+    float qi[kMaxTokens], ki[kMaxTokens], decay[kMaxTokens], beta[kMaxTokens];
+    for (int t = 0; t < nq; ++t) {
+        float qs = 0.0f, ks = 0.0f;
+        for (int i = tid; i < K; i += blockDim.x) {
+            qs = __fmaf_rn(q[t * K + i], q[t * K + i], qs);
+            ks = __fmaf_rn(k[t * K + i], k[t * K + i], ks);
+        }
+        qs = block_sum(qs, red);
+        ks = block_sum(ks, red);
+        qi[t] = __fmul_rn(rsqrt_f32(__fadd_rn(qs, 1e-6f)), rsqrt_f32((float)K));
+        ki[t] = rsqrt_f32(__fadd_rn(ks, 1e-6f));
+        const float *pa = a.proj + (size_t)t * P + 2 * KH * K + 2 * VH * V;
+        const float av = __fadd_rn(pa[h], a.dt[h]);
+        const float sp = __fadd_rn(fmaxf(av, 0.0f), log1pf(expf(-fabsf(av))));  // softplus, stable
+        decay[t] = expf(-__fmul_rn(expf(a.alog[h]), sp));
+        beta[t] = sigmoid_f32(pa[VH + h]);
+    }
+    // Lane layout over K: column lane + 32*m, m < 4 (K <= 128).
     float *S = a.state + (size_t)h * V * K;
-    for (int r0 = warp * kDeltaRowsPerWarp; r0 < V; r0 += nwarps * kDeltaRowsPerWarp) {
+    for (int r0 = r_begin + warp * kDeltaRowsPerWarp; r0 < r_end; r0 += nwarps * kDeltaRowsPerWarp) {
         float sv[kDeltaRowsPerWarp][4];
 #pragma unroll
         for (int rr = 0; rr < kDeltaRowsPerWarp; ++rr)
 #pragma unroll
             for (int m = 0; m < 4; ++m) {
                 const int r = r0 + rr, j = lane + 32 * m;
-                sv[rr][m] = (r < V && j < K) ? S[(size_t)r * K + j] : 0.0f;
+                sv[rr][m] = (r < r_end && j < K) ? S[(size_t)r * K + j] : 0.0f;
             }
+        for (int t = 0; t < nq; ++t) {
+            float kr[4], qr[4];
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                const int j = lane + 32 * m;
+                kr[m] = j < K ? __fmul_rn(k[t * K + j], ki[t]) : 0.0f;
+                qr[m] = j < K ? __fmul_rn(q[t * K + j], qi[t]) : 0.0f;
+            }
+#pragma unroll
+            for (int rr = 0; rr < kDeltaRowsPerWarp; ++rr) {
+                const int r = r0 + rr;
+                if (r >= r_end) break;
+                if (a.state_snap != nullptr) {
+                    float *sn = a.state_snap + ((size_t)t * VH + h) * V * K + (size_t)r * K;
+#pragma unroll
+                    for (int m = 0; m < 4; ++m) {
+                        const int j = lane + 32 * m;
+                        if (j < K) sn[j] = sv[rr][m];
+                    }
+                }
+                float pr = 0.0f;
+#pragma unroll
+                for (int m = 0; m < 4; ++m) pr = __fmaf_rn(__fmul_rn(sv[rr][m], decay[t]), kr[m], pr);
+                pr = warp_sum(pr);
+                const float delta = __fmul_rn(__fsub_rn(v[t * nrp + r - r_begin], pr), beta[t]);
+                float o = 0.0f;
+#pragma unroll
+                for (int m = 0; m < 4; ++m) {
+                    const float nx = __fmaf_rn(kr[m], delta, __fmul_rn(sv[rr][m], decay[t]));
+                    sv[rr][m] = nx;
+                    o = __fmaf_rn(nx, qr[m], o);
+                }
+                o = warp_sum(o);
+                if (lane == 0) y[t * nrp + r - r_begin] = o;
+            }
+        }
 #pragma unroll
         for (int rr = 0; rr < kDeltaRowsPerWarp; ++rr) {
             const int r = r0 + rr;
-            if (r >= V) break;
-            float p = 0.0f;
-#pragma unroll
-            for (int m = 0; m < 4; ++m) p = __fmaf_rn(__fmul_rn(sv[rr][m], decay), kr[m], p);
-            p = warp_sum(p);
-            const float delta = __fmul_rn(__fsub_rn(v[r], p), beta);
-            float o = 0.0f;
-#pragma unroll
-            for (int m = 0; m < 4; ++m) {
-                const float nx = __fmaf_rn(kr[m], delta, __fmul_rn(sv[rr][m], decay));
-                sv[rr][m] = nx;
-                o = __fmaf_rn(nx, qr[m], o);
-            }
-            o = warp_sum(o);
+            if (r >= r_end) break;
 #pragma unroll
             for (int m = 0; m < 4; ++m) {
                 const int j = lane + 32 * m;
                 if (j < K) S[(size_t)r * K + j] = sv[rr][m];
             }
-            if (lane == 0) y[r] = o;
         }
     }
     __syncthreads();
-    float ys = 0.0f;
-    for (int i = tid; i < V; i += blockDim.x) ys = __fmaf_rn(y[i], y[i], ys);
-    const float inv = rsqrt_f32(__fadd_rn(__fdiv_rn(block_sum(ys, red), (float)V), a.eps));
-    const float *z = a.proj + 2 * KH * K + VH * V + (size_t)h * V;
-    for (int i = tid; i < V; i += blockDim.x)
-        a.out[(size_t)h * V + i] = __fmul_rn(__fmul_rn(__fmul_rn(y[i], inv), a.norm_w[i]), silu_f32(z[i]));
+    for (int t = 0; t < nq; ++t) {
+        float ys = 0.0f;
+        for (int i = tid; i < nr; i += blockDim.x) {
+            const float yy = y[t * nrp + i];
+            ys = __fmaf_rn(yy, yy, ys);
+            a.ybuf[(size_t)t * VH * V + (size_t)h * V + r_begin + i] = yy;
+        }
+        ys = block_sum(ys, red);
+        if (tid == 0) a.ssq[(h * kDeltaSplit + part) * kMaxTokens + t] = ys;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last = (atomicAdd(a.count + h, 1u) == (unsigned)kDeltaSplit - 1u) ? 1u : 0u;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    for (int t = 0; t < nq; ++t) {
+        float total = 0.0f;
+        for (int p2 = 0; p2 < kDeltaSplit; ++p2)
+            total = __fadd_rn(total, __ldcg(a.ssq + (h * kDeltaSplit + p2) * kMaxTokens + t));
+        const float inv = rsqrt_f32(__fadd_rn(__fdiv_rn(total, (float)V), a.eps));
+        const float *z = a.proj + (size_t)t * P + 2 * KH * K + VH * V + (size_t)h * V;
+        const size_t o0 = (size_t)t * VH * V + (size_t)h * V;
+        for (int i = tid; i < V; i += blockDim.x)
+            a.out[o0 + i] = __fmul_rn(__fmul_rn(__fmul_rn(__ldcg(a.ybuf + o0 + i), inv), a.norm_w[i]), silu_f32(z[i]));
+    }
+    if (tid == 0) a.count[h] = 0u;
 }
 
 constexpr int kAttnThreads = 256;
 
 // head_rms (qwen.metal:204-212) then partial rotate-half RoPE (:213-221) of
-// one D-vector in shared memory t, weight w; every thread calls it.
-__device__ void rms_rope(float *t, const float *w, int D, int RD, float pos, float theta, float eps, float *red) {
+// one D-vector, by one warp: src (global) -> t (shared), weight w.
+__device__ void warp_rms_rope(const float *src, float *t, const float *w, int D, int RD, float pos, float theta,
+                              float eps, int lane) {
     float ss = 0.0f;
-    for (int i = threadIdx.x; i < D; i += blockDim.x) ss = __fmaf_rn(t[i], t[i], ss);
-    const float inv = rsqrt_f32(__fadd_rn(__fdiv_rn(block_sum(ss, red), (float)D), eps));
-    for (int i = threadIdx.x; i < D; i += blockDim.x) t[i] = __fmul_rn(t[i], __fmul_rn(inv, w[i]));
-    __syncthreads();
+    for (int i = lane; i < D; i += 32) {
+        const float v = src[i];
+        t[i] = v;
+        ss = __fmaf_rn(v, v, ss);
+    }
+    const float inv = rsqrt_f32(__fadd_rn(__fdiv_rn(warp_sum(ss), (float)D), eps));
+    for (int i = lane; i < D; i += 32) t[i] = __fmul_rn(t[i], __fmul_rn(inv, w[i]));
+    __syncwarp();
     const int half = RD / 2;
-    for (int j = threadIdx.x; j < half; j += blockDim.x) {
+    for (int j = lane; j < half; j += 32) {
         const float ang = __fmul_rn(pos, powf(theta, __fdiv_rn(-(float)(2 * j), (float)RD)));
         float sn, cs;
         sincosf(ang, &sn, &cs);
@@ -286,114 +357,118 @@ __device__ void rms_rope(float *t, const float *w, int D, int RD, float pos, flo
         t[j] = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
         t[j + half] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
     }
-    __syncthreads();
+    __syncwarp();
 }
 
-// Decode attention of one KV head over one 64-position chunk (see the file
-// comment).  Shared memory: q [G][D], k_new [D], v_new [D], p [G][64], red.
+// Decode attention of one KV head over one 64-position chunk for nq query
+// tokens at positions pos + i (see the file comment).  Shared memory:
+// q [nq][G][D], new keys and values [nq][D] each, p [nq][G][64].
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a) {
     extern __shared__ float asm_[];
-    const int D = a.D, NH = a.NH, NKV = a.NKV, G = NH / NKV;
+    const int D = a.D, NH = a.NH, NKV = a.NKV, G = NH / NKV, nq = a.nq, P = a.proj_stride;
     const int c = blockIdx.x, kh = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
-    float *qs = asm_, *kn = qs + G * D, *vn = kn + D, *ps = vn + D, *red = ps + G * kAttnChunk;
+    float *qs = asm_, *kn = qs + nq * G * D, *vn = kn + nq * D, *ps = vn + nq * D;
     __shared__ unsigned int last;
-    const int pos = (int)a.ctrl->pos, len = pos + 1;
+    const int pos = (int)a.ctrl->pos, len = pos + nq;  // keys 0 .. pos+nq-1
     const int t0 = c * kAttnChunk, t1 = min(t0 + kAttnChunk, len);
-    const float fpos = (float)pos;
-    float *part = a.part + ((size_t)kh * a.nchunks + c) * G * (D + 2);
+    float *part = a.part + ((size_t)kh * a.nchunks + c) * nq * G * (D + 2);
     if (t0 < len) {
-        for (int g = 0; g < G; ++g) {
-            const float *src = a.proj + (size_t)(kh * G + g) * 2 * D;
-            for (int i = tid; i < D; i += blockDim.x) qs[g * D + i] = src[i];
-            __syncthreads();
-            rms_rope(qs + g * D, a.qnorm, D, a.RD, fpos, a.theta, a.eps, red);
-        }
-        const bool mine = t0 <= pos && pos < t0 + kAttnChunk;  // this chunk holds the new position
-        if (mine) {
-            const float *ksrc = a.proj + (size_t)NH * 2 * D + (size_t)kh * D;
-            const float *vsrc = a.proj + (size_t)NH * 2 * D + (size_t)NKV * D + (size_t)kh * D;
-            for (int i = tid; i < D; i += blockDim.x) {
-                kn[i] = ksrc[i];
-                vn[i] = vsrc[i];
-            }
-            __syncthreads();
-            rms_rope(kn, a.knorm, D, a.RD, fpos, a.theta, a.eps, red);
-            float *kd = a.kcache + ((size_t)pos * NKV + kh) * D, *vd = a.vcache + ((size_t)pos * NKV + kh) * D;
-            for (int i = tid; i < D; i += blockDim.x) {
-                kd[i] = kn[i];
-                vd[i] = vn[i];
+        // One warp per (query token, head) of the group and per new key in
+        // this chunk: split, head RMS, RoPE at that token's position.
+        const int n0 = max(t0, pos), n1 = min(t0 + kAttnChunk, pos + nq);  // new positions in this chunk
+        const int nnew = n1 > n0 ? n1 - n0 : 0;
+        for (int job = warp; job < nq * G + nnew; job += nwarps) {
+            if (job < nq * G) {
+                const int i = job / G, g = job % G;
+                warp_rms_rope(a.proj + (size_t)i * P + (size_t)(kh * G + g) * 2 * D, qs + job * D, a.qnorm, D, a.RD,
+                              (float)(pos + i), a.theta, a.eps, lane);
+            } else {
+                const int i = n0 + (job - nq * G) - pos;
+                const float *base = a.proj + (size_t)i * P + (size_t)NH * 2 * D;
+                warp_rms_rope(base + (size_t)kh * D, kn + i * D, a.knorm, D, a.RD, (float)(pos + i), a.theta, a.eps,
+                              lane);
+                for (int d = lane; d < D; d += 32) vn[i * D + d] = base[(size_t)NKV * D + (size_t)kh * D + d];
             }
         }
-        // Scores q.k / sqrt(D) (attn_scores, qwen.metal:228-238), warps over positions.
+        __syncthreads();
+        for (int e = tid; e < nnew * D; e += blockDim.x) {
+            const int i = n0 - pos + e / D, d = e % D;
+            a.kcache[((size_t)(pos + i) * NKV + kh) * D + d] = kn[i * D + d];
+            a.vcache[((size_t)(pos + i) * NKV + kh) * D + d] = vn[i * D + d];
+        }
+        // Scores q.k / sqrt(D) (attn_scores, qwen.metal:228-238), warps over
+        // positions; query i sees positions <= pos + i.
         const float rs = rsqrt_f32((float)D);
         for (int t = t0 + warp; t < t1; t += nwarps) {
-            const float *kt = (t == pos) ? kn : a.kcache + ((size_t)t * NKV + kh) * D;
+            const float *kt = (t >= pos) ? kn + (t - pos) * D : a.kcache + ((size_t)t * NKV + kh) * D;
             float kv[8];
 #pragma unroll
             for (int m = 0; m < 8; ++m) {
                 const int d = lane + 32 * m;
                 kv[m] = d < D ? kt[d] : 0.0f;
             }
-            for (int g = 0; g < G; ++g) {
-                float s = 0.0f;
+            for (int j = 0; j < nq * G; ++j) {
+                float sc = 0.0f;
 #pragma unroll
                 for (int m = 0; m < 8; ++m) {
                     const int d = lane + 32 * m;
-                    if (d < D) s = __fmaf_rn(qs[g * D + d], kv[m], s);
+                    if (d < D) sc = __fmaf_rn(qs[j * D + d], kv[m], sc);
                 }
-                s = warp_sum(s);
-                if (lane == 0) ps[g * kAttnChunk + (t - t0)] = __fmul_rn(s, rs);
+                sc = warp_sum(sc);
+                if (lane == 0) ps[j * kAttnChunk + (t - t0)] = (t <= pos + j / G) ? __fmul_rn(sc, rs) : -INFINITY;
             }
         }
         __syncthreads();
-        // Chunk-local softmax per query head: warp g, lanes over positions.
-        for (int g = warp; g < G; g += nwarps) {
+        // Chunk-local softmax per (query, head): warp j, lanes over positions.
+        for (int j = warp; j < nq * G; j += nwarps) {
             float mx = -INFINITY;
-            for (int t = lane; t < t1 - t0; t += 32) mx = fmaxf(mx, ps[g * kAttnChunk + t]);
+            for (int t = lane; t < t1 - t0; t += 32) mx = fmaxf(mx, ps[j * kAttnChunk + t]);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
             float l = 0.0f;
             for (int t = lane; t < t1 - t0; t += 32) {
-                const float e = expf(__fsub_rn(ps[g * kAttnChunk + t], mx));
-                ps[g * kAttnChunk + t] = e;
+                const float sc = ps[j * kAttnChunk + t];
+                const float e = sc == -INFINITY ? 0.0f : expf(__fsub_rn(sc, mx));
+                ps[j * kAttnChunk + t] = e;
                 l = __fadd_rn(l, e);
             }
             l = warp_sum(l);
             if (lane == 0) {
-                part[(size_t)g * (D + 2) + D] = mx;
-                part[(size_t)g * (D + 2) + D + 1] = l;
+                part[(size_t)j * (D + 2) + D] = mx;
+                part[(size_t)j * (D + 2) + D + 1] = l;
             }
         }
         __syncthreads();
-        // Weighted values over the chunk: thread d, all query heads of the group.
+        // Weighted values over the chunk: thread d, every (query, head).
         for (int d = tid; d < D; d += blockDim.x) {
-            float acc[8];
+            float acc[kMaxTokens * 8];
 #pragma unroll
-            for (int g = 0; g < 8; ++g) acc[g] = 0.0f;
+            for (int j = 0; j < kMaxTokens * 8; ++j) acc[j] = 0.0f;
             for (int t = t0; t < t1; ++t) {
-                const float vv = (t == pos) ? vn[d] : a.vcache[((size_t)t * NKV + kh) * D + d];
+                const float vv = (t >= pos) ? vn[(t - pos) * D + d] : a.vcache[((size_t)t * NKV + kh) * D + d];
 #pragma unroll
-                for (int g = 0; g < 8; ++g)
-                    if (g < G) acc[g] = __fmaf_rn(ps[g * kAttnChunk + (t - t0)], vv, acc[g]);
+                for (int j = 0; j < kMaxTokens * 8; ++j)
+                    if (j < nq * G) acc[j] = __fmaf_rn(ps[j * kAttnChunk + (t - t0)], vv, acc[j]);
             }
 #pragma unroll
-            for (int g = 0; g < 8; ++g)
-                if (g < G) part[(size_t)g * (D + 2) + d] = acc[g];
+            for (int j = 0; j < kMaxTokens * 8; ++j)
+                if (j < nq * G) part[(size_t)j * (D + 2) + d] = acc[j];
         }
     }
-    // The last CTA of this KV head merges the used chunks in chunk order.
+    // The last CTA of this KV head merges, per query, the chunks that hold
+    // its positions, in chunk order.
     __threadfence();
     __syncthreads();
     if (tid == 0) last = (atomicAdd(a.count + kh, 1u) == (unsigned)a.nchunks - 1u) ? 1u : 0u;
     __syncthreads();
     if (!last) return;
     __threadfence();
-    const int used = (len + kAttnChunk - 1) / kAttnChunk;
-    for (int i = tid; i < G * D; i += blockDim.x) {
-        const int g = i / D, d = i % D;
-        const float *pk = a.part + (size_t)kh * a.nchunks * G * (D + 2) + (size_t)g * (D + 2);
-        const size_t cstride = (size_t)G * (D + 2);
+    const size_t cstride = (size_t)nq * G * (D + 2);
+    for (int e = tid; e < nq * G * D; e += blockDim.x) {
+        const int j = e / D, d = e % D, i = j / G, g = j % G;
+        const int used = (pos + i) / kAttnChunk + 1;
+        const float *pk = a.part + (size_t)kh * a.nchunks * cstride + (size_t)j * (D + 2);
         float M = -INFINITY;
         for (int cc = 0; cc < used; ++cc) M = fmaxf(M, __ldcg(pk + cc * cstride + D));
         float L = 0.0f, o = 0.0f;
@@ -403,10 +478,72 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a) {
             o = __fmaf_rn(__ldcg(pk + cc * cstride + d), f, o);
         }
         const int h = kh * G + g;
-        const float gate = a.proj[(size_t)h * 2 * D + D + d];
-        a.out[(size_t)h * D + d] = __fmul_rn(__fdiv_rn(o, L), sigmoid_f32(gate));
+        const float gate = a.proj[(size_t)i * P + (size_t)h * 2 * D + D + d];
+        a.out[(size_t)i * NH * D + (size_t)h * D + d] = __fmul_rn(__fdiv_rn(o, L), sigmoid_f32(gate));
     }
     if (tid == 0) a.count[kh] = 0u;
+}
+
+// Embed a verification block: input 0 is the anchor (the last emitted
+// token), input i >= 1 the draft for position pos + i.
+template <bool BF16>
+__global__ void embed_block_kernel(const uint32_t *__restrict__ w, const void *__restrict__ s,
+                                   const void *__restrict__ bias, uint32_t cols, uint32_t bits, uint32_t group,
+                                   const DecodeCtrl *ctrl, const int32_t *drafts, BlockCtrl *bctrl,
+                                   float *__restrict__ x) {
+    const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+    const int i = blockIdx.y;
+    const uint32_t pos = ctrl->pos;
+    if (c == 0 && i == 0) bctrl->pos_base = pos;
+    if (c >= cols) return;
+    const uint64_t row = i == 0 ? (uint32_t)ctrl->token : (uint32_t)drafts[pos + i];
+    const uint32_t pack = 32u / bits;
+    const uint32_t word = __ldg(w + row * (cols / pack) + c / pack);
+    const uint32_t q = (word >> ((c % pack) * bits)) & ((1u << bits) - 1u);
+    const uint64_t gi = row * (cols / group) + c / group;
+    x[(size_t)i * cols + c] = __fadd_rn(__fmul_rn((float)q, load_meta<BF16>(s, gi)), load_meta<BF16>(bias, gi));
+}
+
+// Greedy verification of one block (one warp; lane 0 decides).
+__global__ void verify_kernel(DecodeCtrl *ctrl, BlockCtrl *bctrl, const int32_t *argmax, const int32_t *drafts, int nq,
+                              int32_t *out, uint32_t cap) {
+    if (threadIdx.x != 0) return;
+    const uint32_t pos = bctrl->pos_base;
+    int acc = 0;
+    while (acc < nq - 1 && drafts[pos + 1 + acc] == argmax[acc]) ++acc;
+    uint32_t n = ctrl->n_out;
+    for (int j = 0; j < acc; ++j, ++n)
+        if (n < cap) out[n] = drafts[pos + 1 + j];
+    if (n < cap) out[n] = argmax[acc];
+    ctrl->n_out = n + 1;
+    ctrl->token = argmax[acc];
+    ctrl->pos = pos + (uint32_t)acc + 1u;
+    bctrl->consumed = (uint32_t)acc + 1u;
+    bctrl->accepted = (uint32_t)acc;
+    bctrl->rounds += 1u;
+    bctrl->drafts_accepted += (uint32_t)acc;
+}
+
+// Roll every DeltaNet layer back to the consumed prefix: the convolution
+// history after `consumed` inputs into the live buffer of that position's
+// parity, and (when inputs were rejected) the recurrent state before input
+// `consumed`.  Grid: (chunks, layers).
+__global__ void commit_kernel(const BlockCtrl *bctrl, float *const *layer_ptrs, int nq, size_t conv_elems,
+                              size_t state_elems) {
+    const int layer = blockIdx.y;
+    const uint32_t consumed = bctrl->consumed, pos_next = bctrl->pos_base + consumed;
+    float *conv = layer_ptrs[4 * layer + 0], *state = layer_ptrs[4 * layer + 1];
+    const float *csnap = layer_ptrs[4 * layer + 2], *ssnap = layer_ptrs[4 * layer + 3];
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    const size_t i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    float *live = conv + (size_t)(pos_next & 1u) * conv_elems;
+    const float *src = csnap + (size_t)consumed * conv_elems;
+    for (size_t i = i0; i < conv_elems; i += stride) live[i] = src[i];
+    if ((int)consumed < nq) {
+        const float4 *ss = reinterpret_cast<const float4 *>(ssnap + (size_t)consumed * state_elems);
+        float4 *sd = reinterpret_cast<float4 *>(state);
+        for (size_t i = i0; i < state_elems / 4; i += stride) sd[i] = ss[i];
+    }
 }
 
 // End of a step: append the greedy token (when the step had a head) and
@@ -470,20 +607,59 @@ int launch_add(float *x, const float *r, uint32_t n, cudaStream_t stream) {
 }
 
 int launch_delta_mixer(const DeltaArgs &a, cudaStream_t stream) {
-    if (a.K > 128 || a.K < 1 || a.V < 1 || a.KH < 1 || a.VH % a.KH != 0 || a.W < 1)
-        return fail(QMR_EUNSUPPORTED, "DeltaNet mixer needs key dim <= 128 and value heads a multiple of key heads");
-    const size_t smem = (size_t)(2 * a.K + 2 * a.V + 33) * sizeof(float);
-    delta_mixer_kernel<<<a.VH, kDeltaThreads, smem, stream>>>(a);
+    if (a.K > 128 || a.K < 1 || a.V < 1 || a.KH < 1 || a.VH % a.KH != 0 || a.W < 1 || a.W > kMaxConvHist + 1 ||
+        a.nq < 1 || a.nq > kMaxTokens || (a.nq > 1 && a.conv_snap == nullptr))
+        return fail(QMR_EUNSUPPORTED,
+                    "DeltaNet mixer needs key dim <= 128, value heads a multiple of key heads, conv width <= 8 and "
+                    "1..4 tokens (more than one only as a verification block)");
+    const int rows = (a.V + kDeltaSplit - 1) / kDeltaSplit;
+    const size_t smem = (size_t)(a.nq * (2 * a.K + 2 * rows) + 33) * sizeof(float);
+    delta_mixer_kernel<<<a.VH * kDeltaSplit, kDeltaThreads, smem, stream>>>(a);
     return launched("DeltaNet mixer");
 }
 
 int launch_attention(const AttnArgs &a, cudaStream_t stream) {
     const int G = a.NH / a.NKV;
-    if (a.D > 256 || a.D < 1 || a.NKV < 1 || a.NH % a.NKV != 0 || G > 8 || a.RD > a.D || a.RD % 2 != 0)
-        return fail(QMR_EUNSUPPORTED, "decode attention needs head_dim <= 256 and at most 8 query heads per KV head");
-    const size_t smem = (size_t)(G * a.D + 2 * a.D + G * kAttnChunk + 33) * sizeof(float);
+    if (a.D > 256 || a.D < 1 || a.NKV < 1 || a.NH % a.NKV != 0 || G > 8 || a.RD > a.D || a.RD % 2 != 0 || a.nq < 1 ||
+        a.nq > kMaxTokens)
+        return fail(QMR_EUNSUPPORTED,
+                    "decode attention needs head_dim <= 256, at most 8 query heads per KV head and 1..4 tokens");
+    const size_t smem = (size_t)(a.nq * G * a.D + 2 * a.nq * a.D + a.nq * G * kAttnChunk) * sizeof(float);
+    static bool opted[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (smem > 48 * 1024 && dev >= 0 && dev < 64 && !opted[dev]) {
+        cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+        opted[dev] = true;
+    }
     attention_kernel<<<dim3((unsigned)a.nchunks, (unsigned)a.NKV), kAttnThreads, smem, stream>>>(a);
     return launched("attention");
+}
+
+int launch_embed_block(const void *w, const void *s, const void *b, bool bf16, uint32_t cols, uint32_t bits,
+                       uint32_t group, const DecodeCtrl *ctrl, const int32_t *drafts, BlockCtrl *bctrl, int nq,
+                       float *x, cudaStream_t stream) {
+    const dim3 grid((cols + 255) / 256, (unsigned)nq);
+    if (bf16)
+        embed_block_kernel<true><<<grid, 256, 0, stream>>>(static_cast<const uint32_t *>(w), s, b, cols, bits, group,
+                                                           ctrl, drafts, bctrl, x);
+    else
+        embed_block_kernel<false><<<grid, 256, 0, stream>>>(static_cast<const uint32_t *>(w), s, b, cols, bits, group,
+                                                            ctrl, drafts, bctrl, x);
+    return launched("block embed");
+}
+
+int launch_verify(DecodeCtrl *ctrl, BlockCtrl *bctrl, const int32_t *argmax, const int32_t *drafts, int nq,
+                  int32_t *out, uint32_t out_cap, cudaStream_t stream) {
+    verify_kernel<<<1, 32, 0, stream>>>(ctrl, bctrl, argmax, drafts, nq, out, out_cap);
+    return launched("verify");
+}
+
+int launch_commit(const BlockCtrl *bctrl, float *const *layer_ptrs, int nlayers, int nq, size_t conv_elems,
+                  size_t state_elems, cudaStream_t stream) {
+    if (nlayers == 0) return QMR_OK;
+    commit_kernel<<<dim3(64, (unsigned)nlayers), 256, 0, stream>>>(bctrl, layer_ptrs, nq, conv_elems, state_elems);
+    return launched("commit");
 }
 
 int launch_advance(DecodeCtrl *ctrl, int32_t *out, uint32_t out_cap, bool record, cudaStream_t stream) {

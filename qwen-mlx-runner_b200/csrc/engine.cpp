@@ -45,8 +45,11 @@ struct DevMat {
     bool bf16 = true;
 };
 
+constexpr int kMaxBlock = 4;  // inputs of one verification block (src/engine/block.rs:12)
+
 struct LayerState {
     bool attn = false;
+    float *conv_snap = nullptr, *state_snap = nullptr;  // verification-block prefixes
     DevMat in, out, gate, up, down;
     float *in_norm = nullptr, *post_norm = nullptr;
     float *conv_w = nullptr, *alog = nullptr, *dt = nullptr, *dnorm = nullptr;
@@ -70,6 +73,21 @@ struct QmrModel {
     float *normed = nullptr, *tmp = nullptr;
     float *attn_part = nullptr;
     unsigned int *attn_count = nullptr;
+    float *delta_y = nullptr, *delta_ssq = nullptr;
+    unsigned int *delta_count = nullptr;
+    // Verification blocks (allocated on first use): snapshots per DeltaNet
+    // layer, the round's control words, the per-row argmax, the draft table
+    // (draft token for each position), device pointer table of the layers.
+    bool block_ready = false;
+    BlockCtrl *bctrl = nullptr;
+    int32_t *block_argmax = nullptr;
+    int32_t *drafts = nullptr;
+    float **layer_ptrs = nullptr;
+    int ndelta = 0;
+    cudaGraph_t bgraph[2][kMaxBlock + 1] = {};
+    cudaGraphExec_t bexec[2][kMaxBlock + 1] = {};  // [0] evaluate only, [1] round (evaluate, verify, commit)
+    bool pending = false;  // an evaluated block awaits commit_block_prefix
+    uint32_t pending_width = 0;
     int attn_chunks = 0;
     void *scratch = nullptr;
     size_t scratch_size = 0;
@@ -94,6 +112,10 @@ struct QmrModel {
         for (int i = 0; i < 2; ++i) {
             if (exec[i] != nullptr) cudaGraphExecDestroy(exec[i]);
             if (graph[i] != nullptr) cudaGraphDestroy(graph[i]);
+            for (int b = 0; b <= kMaxBlock; ++b) {
+                if (bexec[i][b] != nullptr) cudaGraphExecDestroy(bexec[i][b]);
+                if (bgraph[i][b] != nullptr) cudaGraphDestroy(bgraph[i][b]);
+            }
         }
         for (void *p : allocs) cudaFree(p);
         if (host_stage != nullptr) cudaFreeHost(host_stage);
@@ -188,22 +210,31 @@ int create_common(QmrModel *m, const QmrModelConfig &c, uint32_t context) {
     size_t widest = H;
     for (size_t v : {F, VD, QD}) widest = v > widest ? v : widest;
     const size_t proj = delta_in > attn_in ? delta_in : attn_in;
-    rc = dev_alloc(m, &m->x, H);
-    if (rc == QMR_OK) rc = dev_alloc(m, &m->normed, widest);
-    if (rc == QMR_OK) rc = dev_alloc(m, &m->tmp, H);
-    if (rc == QMR_OK) rc = dev_alloc(m, &m->proj, proj);
-    if (rc == QMR_OK) rc = dev_alloc(m, &m->mixed, VD > QD ? VD : QD);
-    if (rc == QMR_OK) rc = dev_alloc(m, &m->act, F);
-    if (rc == QMR_OK) rc = dev_alloc(m, &m->logits, c.vocab_size);
+    // Activations for up to kMaxBlock tokens (token-major).
+    const size_t T = kMaxBlock;
+    rc = dev_alloc(m, &m->x, T * H);
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->normed, T * widest);
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->tmp, T * H);
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->proj, T * proj);
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->mixed, T * (VD > QD ? VD : QD));
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->act, T * F);
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->logits, T * c.vocab_size);
     m->attn_chunks = (int)((context + kAttnChunk - 1) / kAttnChunk);
     const size_t G = c.num_heads / c.num_kv_heads;
-    if (rc == QMR_OK) rc = dev_alloc(m, &m->attn_part, (size_t)c.num_kv_heads * m->attn_chunks * G * (c.head_dim + 2));
+    if (rc == QMR_OK)
+        rc = dev_alloc(m, &m->attn_part, (size_t)c.num_kv_heads * m->attn_chunks * T * G * (c.head_dim + 2));
     if (rc == QMR_OK) rc = dev_alloc(m, &m->attn_count, c.num_kv_heads);
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->delta_y, T * VD);
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->delta_ssq, (size_t)c.linear_value_heads * kDeltaSplit * 4);
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->delta_count, c.linear_value_heads);
     m->scratch_size = scratch_bytes(8, (uint32_t)widest, 4);
     uint8_t *scr = nullptr;
     if (rc == QMR_OK) rc = dev_alloc(m, &scr, m->scratch_size);
     m->scratch = scr;
     if (rc == QMR_OK) rc = dev_alloc(m, &m->ctrl, 1);
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->bctrl, 1);
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->block_argmax, T);
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->drafts, (size_t)context + T);
     if (rc == QMR_OK) rc = dev_alloc(m, &m->prompt, context);
     m->out_cap = context;
     if (rc == QMR_OK) rc = dev_alloc(m, &m->out, context);
@@ -242,7 +273,7 @@ struct StepCounter {
 // residual (resid == y), gate/up SwiGLU (epi 1, up = second matrix) or head
 // argmax (epi 2, into argmax).
 int mat_call(QmrModel *m, const DevMat &W, const float *x, float *y, const float *norm_w, const float *resid, int epi,
-             const DevMat *up, int32_t *argmax, StepCounter *cnt) {
+             const DevMat *up, int32_t *argmax, StepCounter *cnt, int nq = 1) {
     FastCall c = {};
     c.w = W.w;
     c.s = W.s;
@@ -259,7 +290,7 @@ int mat_call(QmrModel *m, const DevMat &W, const float *x, float *y, const float
     c.cols = W.cols;
     c.bits = W.bits;
     c.group = W.group;
-    c.batch = 1;
+    c.batch = (uint32_t)nq;
     c.bf16 = W.bf16;
     c.epilogue = epi;
     c.path = modes_stream_path();
@@ -277,9 +308,12 @@ int mat_call(QmrModel *m, const DevMat &W, const float *x, float *y, const float
     }
     int rc = QMR_OK;
     if (norm_w != nullptr) {
-        rc = launch_rms_norm(x, norm_w, m->normed, W.cols, m->cfg.rms_eps, m->stream);
+        for (int t = 0; t < nq && rc == QMR_OK; ++t) {
+            rc = launch_rms_norm(x + (size_t)t * W.cols, norm_w, m->normed + (size_t)t * W.cols, W.cols,
+                                 m->cfg.rms_eps, m->stream);
+            ++cnt->n;
+        }
         if (rc != QMR_OK) return rc;
-        ++cnt->n;
         c.x = m->normed;
     }
     if (resid != nullptr) c.y = m->tmp;
@@ -287,27 +321,39 @@ int mat_call(QmrModel *m, const DevMat &W, const float *x, float *y, const float
         rc = run_fast(c, m->stream);
         cnt->n += 2;
     } else if (epi == 0) {
-        rc = run_generic(W.w, W.s, W.b, c.x, c.y, W.rows, W.cols, W.bits, W.group, 1, W.bf16, m->stream);
+        rc = run_generic(W.w, W.s, W.b, c.x, c.y, W.rows, W.cols, W.bits, W.group, (uint32_t)nq, W.bf16, m->stream);
         cnt->n += 1;
     } else {
         rc = fail(QMR_EUNSUPPORTED, "fused gate/up and head need a packed shape the streaming kernels take");
     }
     if (rc != QMR_OK) return rc;
     if (resid != nullptr) {
-        rc = launch_add(y, m->tmp, W.rows, m->stream);
+        rc = launch_add(y, m->tmp, W.rows * (uint32_t)nq, m->stream);
         ++cnt->n;
     }
     return rc;
 }
 
-int record_step(QmrModel *m, bool with_head, StepCounter *cnt) {
+// Kinds of recorded step: one token without / with the head, a
+// verification block evaluated, or a full verification round (evaluate,
+// greedy verify, roll back to the consumed prefix).
+enum StepKind { kStepPlain, kStepHead, kStepBlockEval, kStepBlockRound };
+
+int record_step(QmrModel *m, StepKind kind, int nq, StepCounter *cnt) {
     const QmrModelConfig &c = m->cfg;
-    int rc = launch_embed_token(m->embed.w, m->embed.s, m->embed.b, m->embed.bf16, m->embed.cols, m->embed.bits,
+    const bool block = kind == kStepBlockEval || kind == kStepBlockRound;
+    int rc;
+    if (block)
+        rc = launch_embed_block(m->embed.w, m->embed.s, m->embed.b, m->embed.bf16, m->embed.cols, m->embed.bits,
+                                m->embed.group, m->ctrl, m->drafts, m->bctrl, nq, m->x, m->stream);
+    else
+        rc = launch_embed_token(m->embed.w, m->embed.s, m->embed.b, m->embed.bf16, m->embed.cols, m->embed.bits,
                                 m->embed.group, m->ctrl, m->prompt, m->x, m->stream);
     ++cnt->n;
     for (uint32_t l = 0; l < c.num_layers && rc == QMR_OK; ++l) {
         LayerState &L = m->layers[l];
-        rc = mat_call(m, L.in, m->x, m->proj, L.in_norm, nullptr, 0, nullptr, nullptr, cnt);
+        // The in-projection writes [nq][in rows]; the mixers read it with that stride.
+        rc = mat_call(m, L.in, m->x, m->proj, L.in_norm, nullptr, 0, nullptr, nullptr, cnt, nq);
         if (rc != QMR_OK) break;
         if (L.attn) {
             AttnArgs a = {};
@@ -326,6 +372,8 @@ int record_step(QmrModel *m, bool with_head, StepCounter *cnt) {
             a.RD = (int)c.rotary_dim;
             a.context = (int)m->context;
             a.nchunks = m->attn_chunks;
+            a.nq = nq;
+            a.proj_stride = (int)L.in.rows;
             a.eps = c.rms_eps;
             a.theta = c.rope_theta;
             rc = launch_attention(a, m->stream);
@@ -339,25 +387,43 @@ int record_step(QmrModel *m, bool with_head, StepCounter *cnt) {
             a.dt = L.dt;
             a.norm_w = L.dnorm;
             a.out = m->mixed;
+            a.ybuf = m->delta_y;
+            a.ssq = m->delta_ssq;
+            a.count = m->delta_count;
+            a.conv_snap = block ? L.conv_snap : nullptr;
+            a.state_snap = block ? L.state_snap : nullptr;
             a.ctrl = m->ctrl;
             a.KH = (int)c.linear_key_heads;
             a.VH = (int)c.linear_value_heads;
             a.K = (int)c.linear_key_dim;
             a.V = (int)c.linear_value_dim;
             a.W = (int)c.conv_width;
+            a.nq = nq;
+            a.proj_stride = (int)L.in.rows;
             a.eps = c.rms_eps;
             rc = launch_delta_mixer(a, m->stream);
         }
         ++cnt->n;
-        if (rc == QMR_OK) rc = mat_call(m, L.out, m->mixed, m->x, nullptr, m->x, 0, nullptr, nullptr, cnt);
-        if (rc == QMR_OK) rc = mat_call(m, L.gate, m->x, m->act, L.post_norm, nullptr, 1, &L.up, nullptr, cnt);
-        if (rc == QMR_OK) rc = mat_call(m, L.down, m->act, m->x, nullptr, m->x, 0, nullptr, nullptr, cnt);
+        if (rc == QMR_OK) rc = mat_call(m, L.out, m->mixed, m->x, nullptr, m->x, 0, nullptr, nullptr, cnt, nq);
+        if (rc == QMR_OK) rc = mat_call(m, L.gate, m->x, m->act, L.post_norm, nullptr, 1, &L.up, nullptr, cnt, nq);
+        if (rc == QMR_OK) rc = mat_call(m, L.down, m->act, m->x, nullptr, m->x, 0, nullptr, nullptr, cnt, nq);
     }
-    if (rc == QMR_OK && with_head)
-        rc = mat_call(m, m->head, m->x, m->logits, m->final_norm, nullptr, 2, nullptr, &m->ctrl->token, cnt);
-    if (rc == QMR_OK) {
-        rc = launch_advance(m->ctrl, m->out, m->out_cap, with_head, m->stream);
+    if (rc == QMR_OK && kind != kStepPlain)
+        rc = mat_call(m, m->head, m->x, m->logits, m->final_norm, nullptr, 2, nullptr,
+                      block ? m->block_argmax : &m->ctrl->token, cnt, nq);
+    if (rc == QMR_OK && !block) {
+        rc = launch_advance(m->ctrl, m->out, m->out_cap, kind == kStepHead, m->stream);
         ++cnt->n;
+    }
+    if (rc == QMR_OK && kind == kStepBlockRound) {
+        rc = launch_verify(m->ctrl, m->bctrl, m->block_argmax, m->drafts, nq, m->out, m->out_cap, m->stream);
+        ++cnt->n;
+        if (rc == QMR_OK && m->ndelta > 0) {
+            const size_t VD = (size_t)c.linear_value_heads * c.linear_value_dim;
+            rc = launch_commit(m->bctrl, m->layer_ptrs, m->ndelta, nq, m->qkv_channels * (c.conv_width - 1),
+                               VD * c.linear_key_dim, m->stream);
+            ++cnt->n;
+        }
     }
     return rc;
 }
@@ -376,6 +442,7 @@ int clear_state(QmrModel *m) {
     if (rc == QMR_OK) rc = cuda_check(cudaMemsetAsync(m->ctrl, 0, sizeof(DecodeCtrl), m->stream), "reset");
     if (rc == QMR_OK) rc = cuda_check(cudaStreamSynchronize(m->stream), "reset");
     m->pos = 0;
+    m->pending = false;
     return rc;
 }
 
@@ -385,14 +452,14 @@ int build_graphs(QmrModel *m) {
     int rc = QMR_OK;
     for (int head = 0; head < 2 && rc == QMR_OK; ++head) {
         StepCounter cnt;
-        rc = record_step(m, head == 1, &cnt);
+        rc = record_step(m, head == 1 ? kStepHead : kStepPlain, 1, &cnt);
         if (rc == QMR_OK) rc = cuda_check(cudaStreamSynchronize(m->stream), "warm-up step");
     }
     for (int head = 0; head < 2 && rc == QMR_OK; ++head) {
         StepCounter cnt;
         rc = cuda_check(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
         if (rc != QMR_OK) break;
-        const int rs = record_step(m, head == 1, &cnt);
+        const int rs = record_step(m, head == 1 ? kStepHead : kStepPlain, 1, &cnt);
         cudaGraph_t g = nullptr;
         const cudaError_t e = cudaStreamEndCapture(m->stream, &g);
         if (rs != QMR_OK) {
@@ -406,6 +473,65 @@ int build_graphs(QmrModel *m) {
         m->launches[head] = cnt.n;
     }
     if (rc == QMR_OK) rc = clear_state(m);
+    return rc;
+}
+
+// Verification-block resources (BlockState::new, src/engine/block.rs:45-135):
+// prefix snapshots per DeltaNet layer, the device table of layer pointers,
+// then the evaluate and round graphs of width nq.  The per-width kernels are
+// first run eagerly on the matrices alone (they touch activations and
+// scratch, never model state), so the capture sees no first-use set-up.
+int ensure_block(QmrModel *m, int nq) {
+    const QmrModelConfig &c = m->cfg;
+    int rc = QMR_OK;
+    if (!m->block_ready) {
+        const size_t conv = m->qkv_channels * (c.conv_width - 1);
+        const size_t st = (size_t)c.linear_value_heads * c.linear_value_dim * c.linear_key_dim;
+        std::vector<float *> ptrs;
+        for (LayerState &L : m->layers) {
+            if (L.attn) continue;
+            rc = dev_alloc(m, &L.conv_snap, (size_t)(kMaxBlock + 1) * conv);
+            if (rc == QMR_OK) rc = dev_alloc(m, &L.state_snap, (size_t)kMaxBlock * st);
+            if (rc != QMR_OK) return rc;
+            ptrs.insert(ptrs.end(), {L.conv_state, L.state, L.conv_snap, L.state_snap});
+        }
+        m->ndelta = (int)(ptrs.size() / 4);
+        rc = dev_alloc(m, &m->layer_ptrs, ptrs.size() > 0 ? ptrs.size() : 1);
+        if (rc == QMR_OK && !ptrs.empty()) rc = upload(m, m->layer_ptrs, ptrs.data(), ptrs.size() * sizeof(float *));
+        if (rc == QMR_OK) rc = cuda_check(cudaStreamSynchronize(m->stream), "block set-up");
+        if (rc != QMR_OK) return rc;
+        m->block_ready = true;
+    }
+    if (m->bexec[1][nq] != nullptr) return QMR_OK;
+    StepCounter warm;
+    bool seen[2] = {false, false};
+    for (LayerState &L : m->layers) {
+        if (seen[L.attn]) continue;
+        seen[L.attn] = true;
+        rc = mat_call(m, L.in, m->x, m->proj, L.in_norm, nullptr, 0, nullptr, nullptr, &warm, nq);
+        if (rc == QMR_OK) rc = mat_call(m, L.out, m->mixed, m->x, nullptr, m->x, 0, nullptr, nullptr, &warm, nq);
+        if (rc == QMR_OK) rc = mat_call(m, L.gate, m->x, m->act, L.post_norm, nullptr, 1, &L.up, nullptr, &warm, nq);
+        if (rc == QMR_OK) rc = mat_call(m, L.down, m->act, m->x, nullptr, m->x, 0, nullptr, nullptr, &warm, nq);
+        if (rc != QMR_OK) return rc;
+    }
+    rc = mat_call(m, m->head, m->x, m->logits, m->final_norm, nullptr, 2, nullptr, m->block_argmax, &warm, nq);
+    if (rc == QMR_OK) rc = cuda_check(cudaStreamSynchronize(m->stream), "block warm-up");
+    for (int kind = 0; kind < 2 && rc == QMR_OK; ++kind) {
+        StepCounter cnt;
+        rc = cuda_check(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+        if (rc != QMR_OK) break;
+        const int rs = record_step(m, kind == 0 ? kStepBlockEval : kStepBlockRound, nq, &cnt);
+        cudaGraph_t g = nullptr;
+        const cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+        if (rs != QMR_OK) {
+            if (g != nullptr) cudaGraphDestroy(g);
+            return rs;
+        }
+        rc = cuda_check(e, "end capture");
+        if (rc != QMR_OK) break;
+        m->bgraph[kind][nq] = g;
+        rc = cuda_check(cudaGraphInstantiate(&m->bexec[kind][nq], g, 0), "graph instantiate");
+    }
     return rc;
 }
 
@@ -719,6 +845,7 @@ int qmr_model_position(const QmrModel *m, uint32_t *pos) {
 
 int qmr_model_forward(QmrModel *m, uint32_t token, float *logits, int32_t *next) {
     if (m == nullptr) return fail(QMR_EINVAL, "null model");
+    if (m->pending) return fail(QMR_EINVAL, "commit or reset the pending verification block before a normal forward");
     if (token >= m->cfg.vocab_size) return fail(QMR_EINVAL, "token %u outside vocabulary", token);
     if (m->pos >= m->context) return fail(QMR_ERANGE, "context capacity %u exhausted", m->context);
     DeviceGuard g(m->device);
@@ -749,6 +876,7 @@ int qmr_model_generate(QmrModel *m, const uint32_t *prompt, uint32_t n_prompt, u
                        double *prefill_ms, double *decode_ms) {
     if (m == nullptr || prompt == nullptr || out == nullptr) return fail(QMR_EINVAL, "null argument");
     if (n_prompt == 0 || max_new == 0) return fail(QMR_EINVAL, "empty prompt or max_new = 0");
+    if (m->pending) return fail(QMR_EINVAL, "commit or reset the pending verification block first");
     for (uint32_t i = 0; i < n_prompt; ++i)
         if (prompt[i] >= m->cfg.vocab_size) return fail(QMR_EINVAL, "prompt token %u outside vocabulary", prompt[i]);
     if ((uint64_t)m->pos + n_prompt + max_new - 1 > m->context)
@@ -787,6 +915,152 @@ int qmr_model_generate(QmrModel *m, const uint32_t *prompt, uint32_t n_prompt, u
     if (prefill_ms) *prefill_ms = t01;
     if (decode_ms) *decode_ms = t12;
     m->pos += n_prompt + max_new - 1;
+    return QMR_OK;
+}
+
+int qmr_model_verify_block(QmrModel *m, const uint32_t *tokens, uint32_t n, float *logits, int32_t *argmax) {
+    if (m == nullptr || tokens == nullptr) return fail(QMR_EINVAL, "null argument");
+    if (m->pending) return fail(QMR_EINVAL, "commit or reset the pending verification block before another block");
+    if (n < 1 || n > (uint32_t)kMaxBlock) return fail(QMR_EINVAL, "verification block width must be 1..=4");
+    for (uint32_t i = 0; i < n; ++i)
+        if (tokens[i] >= m->cfg.vocab_size) return fail(QMR_EINVAL, "verification block contains a token outside vocabulary");
+    if ((uint64_t)m->pos + n > m->context)
+        return fail(QMR_ERANGE, "verification block exceeds context capacity %u", m->context);
+    DeviceGuard g(m->device);
+    int rc = ensure_block(m, (int)n);
+    // Input 0 is the anchor (ctrl->token); inputs 1.. come from the draft table.
+    std::vector<int32_t> t(tokens, tokens + n);
+    m->host_stage[0] = t[0];
+    m->host_stage[1] = 0;
+    if (rc == QMR_OK)
+        rc = cuda_check(cudaMemcpyAsync(&m->ctrl->token, m->host_stage, 8, cudaMemcpyHostToDevice, m->stream),
+                        "block anchor");
+    if (rc == QMR_OK && n > 1)
+        rc = cuda_check(cudaMemcpyAsync(m->drafts + m->pos + 1, t.data() + 1, (size_t)(n - 1) * 4,
+                                        cudaMemcpyHostToDevice, m->stream), "block inputs");
+    if (rc == QMR_OK) rc = cuda_check(cudaGraphLaunch(m->bexec[0][n], m->stream), "graph launch");
+    if (rc == QMR_OK && logits != nullptr)
+        rc = cuda_check(cudaMemcpyAsync(logits, m->logits, (size_t)n * m->cfg.vocab_size * 4, cudaMemcpyDeviceToHost,
+                                        m->stream), "reading logits");
+    if (rc == QMR_OK && argmax != nullptr)
+        rc = cuda_check(cudaMemcpyAsync(argmax, m->block_argmax, (size_t)n * 4, cudaMemcpyDeviceToHost, m->stream),
+                        "reading argmax");
+    if (rc == QMR_OK) rc = cuda_check(cudaStreamSynchronize(m->stream), "verify block");
+    if (rc == QMR_OK) rc = check_device_error();
+    if (rc != QMR_OK) {
+        clear_state(m);
+        return rc;
+    }
+    m->pending = true;
+    m->pending_width = n;
+    m->pos += n;
+    return QMR_OK;
+}
+
+int qmr_model_commit_block(QmrModel *m, uint32_t consumed) {
+    if (m == nullptr) return fail(QMR_EINVAL, "null model");
+    if (!m->pending) return fail(QMR_EINVAL, "there is no pending verification block");
+    if (consumed > m->pending_width) return fail(QMR_EINVAL, "accepted prefix exceeds pending block length");
+    DeviceGuard g(m->device);
+    const uint32_t base = m->pos - m->pending_width;
+    const QmrModelConfig &c = m->cfg;
+    m->host_stage[0] = (int32_t)consumed;
+    m->host_stage[4] = (int32_t)(base + consumed);
+    int rc = cuda_check(cudaMemcpyAsync(&m->bctrl->consumed, m->host_stage, 4, cudaMemcpyHostToDevice, m->stream),
+                        "commit");
+    if (rc == QMR_OK)
+        rc = cuda_check(cudaMemcpyAsync(&m->ctrl->pos, m->host_stage + 4, 4, cudaMemcpyHostToDevice, m->stream), "commit");
+    if (rc == QMR_OK)
+        rc = launch_commit(m->bctrl, m->layer_ptrs, m->ndelta, (int)m->pending_width, m->qkv_channels * (c.conv_width - 1),
+                           (size_t)c.linear_value_heads * c.linear_value_dim * c.linear_key_dim, m->stream);
+    if (rc == QMR_OK) rc = cuda_check(cudaStreamSynchronize(m->stream), "commit");
+    if (rc != QMR_OK) {
+        clear_state(m);
+        return rc;
+    }
+    m->pending = false;
+    m->pos = base + consumed;
+    return QMR_OK;
+}
+
+int qmr_model_mtp_generate(QmrModel *m, const uint32_t *prompt, uint32_t n_prompt, uint32_t block, uint32_t max_new,
+                           const uint32_t *drafts, uint32_t n_drafts, uint32_t *out, uint32_t *rounds,
+                           uint32_t *accepted, double *prefill_ms, double *decode_ms) {
+    if (m == nullptr || prompt == nullptr || out == nullptr || drafts == nullptr) return fail(QMR_EINVAL, "null argument");
+    if (block < 2 || block > (uint32_t)kMaxBlock) return fail(QMR_EINVAL, "MTP block width must be 2..=4");
+    if (n_prompt == 0 || max_new == 0) return fail(QMR_EINVAL, "empty prompt or max_new = 0");
+    if (m->pending) return fail(QMR_EINVAL, "commit or reset the pending verification block first");
+    for (uint32_t i = 0; i < n_prompt; ++i)
+        if (prompt[i] >= m->cfg.vocab_size) return fail(QMR_EINVAL, "prompt token %u outside vocabulary", prompt[i]);
+    for (uint32_t i = 0; i < n_drafts; ++i)
+        if (drafts[i] >= m->cfg.vocab_size) return fail(QMR_EINVAL, "draft token %u outside vocabulary", drafts[i]);
+    if ((uint64_t)m->pos + n_prompt + max_new - 1 + block > m->context)
+        return fail(QMR_ERANGE, "prompt (%u) plus max_new (%u) plus a block (%u) exceeds context %u", n_prompt, max_new,
+                    block, m->context);
+    DeviceGuard g(m->device);
+    int rc = ensure_block(m, (int)block);
+    const uint32_t base = m->pos;
+    std::vector<int32_t> p(prompt, prompt + n_prompt);
+    if (rc == QMR_OK)
+        rc = cuda_check(cudaMemcpyAsync(m->prompt + base, p.data(), (size_t)n_prompt * 4, cudaMemcpyHostToDevice,
+                                        m->stream), "uploading the prompt");
+    const uint32_t hdr[2] = {base + n_prompt, 0u};
+    if (rc == QMR_OK)
+        rc = cuda_check(cudaMemcpyAsync(&m->ctrl->n_prompt, hdr, 8, cudaMemcpyHostToDevice, m->stream), "control block");
+    std::vector<int32_t> table(m->context + kMaxBlock, 0);
+    for (uint32_t i = 0; i < n_drafts && i < m->context; ++i) table[i] = (int32_t)drafts[i];
+    if (rc == QMR_OK)
+        rc = cuda_check(cudaMemcpyAsync(m->drafts, table.data(), table.size() * 4, cudaMemcpyHostToDevice, m->stream),
+                        "uploading the draft table");
+    if (rc == QMR_OK) rc = cuda_check(cudaMemsetAsync(m->bctrl, 0, sizeof(BlockCtrl), m->stream), "block control");
+    cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+    for (int i = 0; i < 3 && rc == QMR_OK; ++i) rc = cuda_check(cudaEventCreate(&ev[i]), "event");
+    if (rc == QMR_OK) rc = cuda_check(cudaEventRecord(ev[0], m->stream), "event");
+    if (rc == QMR_OK) rc = replay(m, 0, n_prompt - 1);
+    if (rc == QMR_OK) rc = replay(m, 1, 1);  // the prompt's last token emits the first output
+    if (rc == QMR_OK) rc = cuda_check(cudaEventRecord(ev[1], m->stream), "event");
+    // Rounds of verification, replayed in batches; every round emits 1..block
+    // tokens, so a batch sized for full acceptance never overshoots by more
+    // than one round.
+    uint32_t n_out = 1, pos = base + n_prompt;
+    while (rc == QMR_OK && n_out < max_new && (uint64_t)pos + block <= m->context) {
+        uint32_t k = (max_new - n_out + block - 1) / block;
+        const uint32_t room = (m->context - pos) / block;
+        if (k > room) k = room;
+        if (k == 0) break;
+        for (uint32_t i = 0; i < k && rc == QMR_OK; ++i)
+            rc = cuda_check(cudaGraphLaunch(m->bexec[1][block], m->stream), "graph launch");
+        if (rc == QMR_OK)
+            rc = cuda_check(cudaMemcpyAsync(m->host_stage, m->ctrl, 16, cudaMemcpyDeviceToHost, m->stream), "control");
+        if (rc == QMR_OK) rc = cuda_check(cudaStreamSynchronize(m->stream), "verification rounds");
+        pos = (uint32_t)m->host_stage[0];
+        n_out = (uint32_t)m->host_stage[3];
+    }
+    if (rc == QMR_OK) rc = cuda_check(cudaEventRecord(ev[2], m->stream), "event");
+    std::vector<int32_t> toks(n_out);
+    BlockCtrl bc{};
+    if (rc == QMR_OK)
+        rc = cuda_check(cudaMemcpyAsync(toks.data(), m->out, (size_t)n_out * 4, cudaMemcpyDeviceToHost, m->stream),
+                        "reading tokens");
+    if (rc == QMR_OK) rc = cuda_check(cudaMemcpyAsync(&bc, m->bctrl, sizeof bc, cudaMemcpyDeviceToHost, m->stream), "stats");
+    if (rc == QMR_OK) rc = cuda_check(cudaStreamSynchronize(m->stream), "mtp generate");
+    if (rc == QMR_OK) rc = check_device_error();
+    float t01 = 0, t12 = 0;
+    if (rc == QMR_OK) rc = cuda_check(cudaEventElapsedTime(&t01, ev[0], ev[1]), "event time");
+    if (rc == QMR_OK) rc = cuda_check(cudaEventElapsedTime(&t12, ev[1], ev[2]), "event time");
+    for (auto e : ev)
+        if (e != nullptr) cudaEventDestroy(e);
+    if (rc != QMR_OK) {
+        clear_state(m);
+        return rc;
+    }
+    if (n_out < max_new) return fail(QMR_ERANGE, "context filled after %u of %u tokens", n_out, max_new);
+    for (uint32_t i = 0; i < max_new; ++i) out[i] = (uint32_t)toks[i];
+    if (rounds) *rounds = bc.rounds;
+    if (accepted) *accepted = bc.drafts_accepted;
+    if (prefill_ms) *prefill_ms = t01;
+    if (decode_ms) *decode_ms = t12;
+    m->pos = pos;
     return QMR_OK;
 }
 

@@ -139,6 +139,11 @@ SIGNATURES = {
     "qmr_model_forward": (_int, [_vp, _u32, _vp, _vp]),
     "qmr_model_generate": (_int, [_vp, _vp, _u32, _u32, _vp, ctypes.POINTER(ctypes.c_double),
                                   ctypes.POINTER(ctypes.c_double)]),
+    "qmr_model_verify_block": (_int, [_vp, _vp, _u32, _vp, _vp]),
+    "qmr_model_commit_block": (_int, [_vp, _u32]),
+    "qmr_model_mtp_generate": (_int, [_vp, _vp, _u32, _u32, _u32, _vp, _u32, _vp, ctypes.POINTER(_u32),
+                                      ctypes.POINTER(_u32), ctypes.POINTER(ctypes.c_double),
+                                      ctypes.POINTER(ctypes.c_double)]),
     "qmr_model_mlp_r2_eligible": (_int, [_vp, ctypes.POINTER(_u32)]),
     "qmr_model_metadata_stats": (_int, [_vp, ctypes.POINTER(_u64), ctypes.POINTER(_u64)]),
     "qmr_model_step_launches": (_int, [_vp, ctypes.POINTER(_u32), ctypes.POINTER(_u32)]),

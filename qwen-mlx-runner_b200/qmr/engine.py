@@ -168,6 +168,35 @@ class Engine:
                                             ctypes.byref(pre), ctypes.byref(dec)))
         return out.tolist(), pre.value, dec.value
 
+    def verify_block(self, tokens: Sequence[int], logits: bool = True):
+        """Engine::verify_block (src/engine/block.rs:296-333): (logits [n, vocab] or
+        None, greedy argmax per row); the state stays tentative until commit_block_prefix."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        n = t.size
+        lg = np.empty((n, self.config["vocab"]), dtype=np.float32) if logits else None
+        am = np.empty(n, dtype=np.int32)
+        check(_lib.lib().qmr_model_verify_block(self._h, t.ctypes.data, n, lg.ctypes.data if logits else None,
+                                                am.ctypes.data))
+        return lg, am.tolist()
+
+    def commit_block_prefix(self, consumed: int) -> None:
+        """Engine::commit_block_prefix (src/engine/block.rs:335-390)."""
+        check(_lib.lib().qmr_model_commit_block(self._h, consumed))
+
+    def mtp_generate(self, prompt: Sequence[int], max_new: int, block: int, drafts: Sequence[int]):
+        """Greedy decoding in verification rounds of `block` inputs with drafts
+        from a per-position table.  Returns (tokens, rounds, accepted drafts,
+        prefill_ms, decode_ms)."""
+        p = np.ascontiguousarray(prompt, dtype=np.uint32)
+        d = np.ascontiguousarray(drafts, dtype=np.uint32)
+        out = np.empty(max_new, dtype=np.uint32)
+        r, a = ctypes.c_uint32(), ctypes.c_uint32()
+        pre, dec = ctypes.c_double(), ctypes.c_double()
+        check(_lib.lib().qmr_model_mtp_generate(self._h, p.ctypes.data, p.size, block, max_new, d.ctypes.data, d.size,
+                                                out.ctypes.data, ctypes.byref(r), ctypes.byref(a),
+                                                ctypes.byref(pre), ctypes.byref(dec)))
+        return out.tolist(), r.value, a.value, pre.value, dec.value
+
     def mlp_r2_eligible_matrices(self) -> int:
         n = ctypes.c_uint32()
         check(_lib.lib().qmr_model_mlp_r2_eligible(self._h, ctypes.byref(n)))
