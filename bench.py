@@ -599,7 +599,7 @@ def sharded_record(name, device, seed, stream, world, rank, peak):
 
 # ---- config 4: the synthetic 64-layer hybrid decode -------------------------
 
-DECODE_PROMPT, DECODE_NEW, DECODE_CONTEXT = 512, 128, 4096
+DECODE_CONTEXT = 4096
 
 
 def decode_bytes_per_token(cfg):
@@ -621,10 +621,11 @@ def decode_bytes_per_token(cfg):
     return total
 
 
-def decode_record(device, world, rank, peak, cpu_baseline):
+def decode_record(device, world, rank, peak, cpu_baseline, n_prompt=512, n_new=128):
     """Config 4 on each rank's GPU: prefill a seeded 512-token prompt, then
     greedily decode 128 tokens at context 4096 (one replica per rank; the
     head-sharded multi-GPU decode is not built)."""
+    DECODE_PROMPT, DECODE_NEW = n_prompt, n_new
     import torch
 
     import qmr
@@ -641,6 +642,23 @@ def decode_record(device, world, rank, peak, cpu_baseline):
     pre_max = max_over_ranks(pre_ms, device, world)
     dec_max = max_over_ranks(dec_ms, device, world)
     with_head, without = eng.step_launches()
+    # B3 verification rounds (MTP-style decoding): the synthetic model has no
+    # trained drafter, so the drafts are (i) the greedy continuation just
+    # decoded (every draft accepted: 3 tokens per round) and (ii) wrong
+    # tokens (every draft rejected: 1 token per round).  Both must emit the
+    # plain greedy tokens.
+    table = [0] * DECODE_CONTEXT
+    for k, t in enumerate(toks):
+        table[DECODE_PROMPT + k] = t
+    mtp = {}
+    for label, drafts in (("drafts_accepted", table), ("drafts_rejected", [(t + 1) % cfg["vocab"] for t in table])):
+        eng.reset()
+        barrier(world)
+        m_toks, rounds, acc, _, m_dec = eng.mtp_generate(prompt, DECODE_NEW, 3, drafts)
+        m_max = max_over_ranks(m_dec, device, world)
+        mtp[label] = {"rounds": rounds, "drafts_accepted": acc, "rounds_per_s": round(rounds / (m_max * 1e-3), 2),
+                      "tok_s": round(world * (DECODE_NEW - 1) / (m_max * 1e-3), 2),
+                      "ms_per_round": round(m_max / rounds, 4), "same_tokens_as_plain": m_toks == toks}
     eng.close()
     nbytes = decode_bytes_per_token(cfg)
     per_gpu_tps = (DECODE_NEW - 1) / (dec_max * 1e-3)
@@ -654,7 +672,9 @@ def decode_record(device, world, rank, peak, cpu_baseline):
            "frac_per_gpu": round(nbytes * per_gpu_tps / 1e9 / peak, 4),
            "launches_per_token": with_head, "launches_per_prefill_token": without,
            "parallelism": f"replicas{world}" if world > 1 else "single",
-           "first_tokens": toks[:8]}
+           "first_tokens": toks[:8],
+           "mtp_b3": dict(mtp, block=3, note="tok/s counts the 127 tokens after the first (the prompt's last step "
+                                             "emits it); timed over the verification rounds")}
     if cpu_baseline and rank == 0 and world == 1:
         # The reference's CPU arithmetic for this graph: the FP64 oracle on the
         # same synthetic model, all host cores, two steps of the prompt.
@@ -672,11 +692,38 @@ def decode_record(device, world, rank, peak, cpu_baseline):
     return rec
 
 
+def run_decode(args):
+    """--workload decode: the config-4 record alone (profiling runs)."""
+    import torch
+    import torch.distributed as dist
+
+    import qmr
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+    qmr.ops.init(local)
+    peak, _ = load_peaks()
+    rec = decode_record(device, world, rank, peak, not (args.no_cpu_baseline or args.quick), args.decode_prompt,
+                        args.decode_new)
+    if rank == 0:
+        print(json.dumps({"metric": "synthetic decode tokens/s", "value": rec["decode_tok_s"], "unit": "tok/s",
+                          "n_gpus": world, "higher_is_better": True, "scaling": "weak", "decode": rec}), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def run_gpu(args):
     import torch
     import torch.distributed as dist
 
     import qmr
+    if args.workload == "decode":
+        return run_decode(args)
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
@@ -828,7 +875,9 @@ def main():
     ap.add_argument("--steps", type=int, default=4000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="qmr", choices=["qmr", "reference"])
-    ap.add_argument("--workload", default="b3", choices=["b3", "b1", "q8b3", "mlp", "head"])
+    ap.add_argument("--workload", default="b3", choices=["b3", "b1", "q8b3", "mlp", "head", "decode"])
+    ap.add_argument("--decode-prompt", type=int, default=512, help="config-4 prompt tokens")
+    ap.add_argument("--decode-new", type=int, default=128, help="config-4 generated tokens")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="sharded workloads: output exchange over peer memory in the kernels, or NCCL all-gathers")
@@ -838,6 +887,8 @@ def main():
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
+        if args.workload == "decode":
+            args.workload = "b3"
         return run_reference(args)
     return run_gpu(args)
 

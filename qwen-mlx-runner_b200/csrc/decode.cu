@@ -363,9 +363,11 @@ __device__ void warp_rms_rope(const float *src, float *t, const float *w, int D,
 // Decode attention of one KV head over one 64-position chunk for nq query
 // tokens at positions pos + i (see the file comment).  Shared memory:
 // q [nq][G][D], new keys and values [nq][D] each, p [nq][G][64].
+template <int NQ>
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a) {
     extern __shared__ float asm_[];
-    const int D = a.D, NH = a.NH, NKV = a.NKV, G = NH / NKV, nq = a.nq, P = a.proj_stride;
+    const int D = a.D, NH = a.NH, NKV = a.NKV, G = NH / NKV, P = a.proj_stride;
+    constexpr int nq = NQ;
     const int c = blockIdx.x, kh = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
     float *qs = asm_, *kn = qs + nq * G * D, *vn = kn + nq * D, *ps = vn + nq * D;
@@ -441,19 +443,23 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a) {
         }
         __syncthreads();
         // Weighted values over the chunk: thread d, every (query, head).
+        // Query heads in groups of 8 accumulators (G <= 8 per token).
         for (int d = tid; d < D; d += blockDim.x) {
-            float acc[kMaxTokens * 8];
 #pragma unroll
-            for (int j = 0; j < kMaxTokens * 8; ++j) acc[j] = 0.0f;
-            for (int t = t0; t < t1; ++t) {
-                const float vv = (t >= pos) ? vn[(t - pos) * D + d] : a.vcache[((size_t)t * NKV + kh) * D + d];
+            for (int i = 0; i < NQ; ++i) {
+                float acc[8];
 #pragma unroll
-                for (int j = 0; j < kMaxTokens * 8; ++j)
-                    if (j < nq * G) acc[j] = __fmaf_rn(ps[j * kAttnChunk + (t - t0)], vv, acc[j]);
+                for (int g = 0; g < 8; ++g) acc[g] = 0.0f;
+                for (int t = t0; t < min(t1, pos + i + 1); ++t) {
+                    const float vv = (t >= pos) ? vn[(t - pos) * D + d] : a.vcache[((size_t)t * NKV + kh) * D + d];
+#pragma unroll
+                    for (int g = 0; g < 8; ++g)
+                        if (g < G) acc[g] = __fmaf_rn(ps[(i * G + g) * kAttnChunk + (t - t0)], vv, acc[g]);
+                }
+#pragma unroll
+                for (int g = 0; g < 8; ++g)
+                    if (g < G) part[(size_t)(i * G + g) * (D + 2) + d] = acc[g];
             }
-#pragma unroll
-            for (int j = 0; j < kMaxTokens * 8; ++j)
-                if (j < nq * G) part[(size_t)j * (D + 2) + d] = acc[j];
         }
     }
     // The last CTA of this KV head merges, per query, the chunks that hold
@@ -625,14 +631,14 @@ int launch_attention(const AttnArgs &a, cudaStream_t stream) {
         return fail(QMR_EUNSUPPORTED,
                     "decode attention needs head_dim <= 256, at most 8 query heads per KV head and 1..4 tokens");
     const size_t smem = (size_t)(a.nq * G * a.D + 2 * a.nq * a.D + a.nq * G * kAttnChunk) * sizeof(float);
-    static bool opted[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (smem > 48 * 1024 && dev >= 0 && dev < 64 && !opted[dev]) {
-        cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-        opted[dev] = true;
+    if (smem > 48 * 1024) return fail(QMR_EUNSUPPORTED, "decode attention block needs %zu bytes of shared memory", smem);
+    const dim3 grid((unsigned)a.nchunks, (unsigned)a.NKV);
+    switch (a.nq) {
+        case 1: attention_kernel<1><<<grid, kAttnThreads, smem, stream>>>(a); break;
+        case 2: attention_kernel<2><<<grid, kAttnThreads, smem, stream>>>(a); break;
+        case 3: attention_kernel<3><<<grid, kAttnThreads, smem, stream>>>(a); break;
+        default: attention_kernel<4><<<grid, kAttnThreads, smem, stream>>>(a); break;
     }
-    attention_kernel<<<dim3((unsigned)a.nchunks, (unsigned)a.NKV), kAttnThreads, smem, stream>>>(a);
     return launched("attention");
 }
 
