@@ -421,6 +421,34 @@ int qmr_model_metadata_stats(const QmrModel *m, uint64_t *matrices, uint64_t *sa
  * (the captured graphs' node counts). */
 int qmr_model_step_launches(const QmrModel *m, uint32_t *with_head, uint32_t *without_head);
 
+/* ---- tensor-parallel decode over several GPUs --------------------------
+ * No single reference counterpart (the reference decodes on one GPU): the
+ * synthetic model of qmr_model_synthetic split over `world` processes, one
+ * per GPU.  Rank r holds 1/world of the DeltaNet key and value heads, the
+ * attention query heads (KV heads split too, or each replicated on the
+ * world / num_kv_heads ranks that use it), the MLP rows and the vocabulary
+ * rows; the residual stream is replicated.  out_proj, o_proj and down_proj
+ * are split by input columns and their partial sums all-reduced over NVLink
+ * by the streaming kernel's own output exchange (peer stores into every
+ * rank's slot buffer, epoch release, bounded wait, a rank-ordered sum), so
+ * every rank holds the same residual bits and emits the same tokens.  The
+ * head's shard argmax keys are merged with the single-GPU rule.
+ *
+ * Set-up, every rank in lock step: qmr_model_synthetic_sharded (this
+ * rank's weights and its exchange memory), qmr_model_exchange_handle
+ * (QMR_IPC_HANDLE_BYTES to share with the other ranks), then
+ * qmr_model_exchange_open with all ranks' handles in rank order (maps the
+ * peers' memory and captures the step graphs; its warm-up steps exchange
+ * with the peers).  After that every rank makes the same qmr_model_* calls
+ * with the same arguments; logits are this rank's vocabulary rows
+ * (qmr_model_shard).  A rank that falls more than 2 s behind makes the
+ * others' waits run out (QMR_ETIMEOUT).  world = 1 is qmr_model_synthetic. */
+int qmr_model_synthetic_sharded(const QmrModelConfig *cfg, uint64_t seed, uint32_t context, uint32_t world,
+                                uint32_t rank, QmrModel **out);
+int qmr_model_exchange_handle(const QmrModel *m, void *handle /* QMR_IPC_HANDLE_BYTES */);
+int qmr_model_exchange_open(QmrModel *m, const void *handles /* world * QMR_IPC_HANDLE_BYTES */);
+int qmr_model_shard(const QmrModel *m, uint32_t *world, uint32_t *rank, uint32_t *vocab_base, uint32_t *vocab_rows);
+
 #ifdef __cplusplus
 }
 #endif

@@ -79,6 +79,54 @@ __global__ void synth_meta_kernel(uint16_t *s, uint16_t *b, uint64_t key_m, uint
     }
 }
 
+// A region of the synthetic matrix (seed-derived keys, full width
+// full_cols): rows [r0, r0 + nr), columns [c0, c0 + nc), written row by row
+// from destination row dst_row0 with the destination's own word and metadata
+// strides (so row shards and column shards of one matrix come from the same
+// generator stream as the whole matrix).
+__global__ void synth_region_kernel(uint32_t *w, uint16_t *s, uint16_t *b, uint64_t key_w, uint64_t key_m,
+                                    uint64_t key_n, uint32_t full_cols, uint32_t r0, uint32_t nr, uint32_t c0,
+                                    uint32_t nc, uint32_t dst_wstride, uint32_t dst_mstride, uint32_t dst_row0) {
+    const uint64_t wpr = full_cols / 8, gpr = full_cols / 64;
+    const uint64_t nw = (uint64_t)nr * (nc / 8), ng = (uint64_t)nr * (nc / 64);
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < nw; i += stride) {
+        const uint64_t r = i / (nc / 8), j = i % (nc / 8);
+        const uint64_t gw = (r0 + r) * wpr + c0 / 8 + j;
+        const uint64_t h = sg_mix(key_w + (gw / 2 + 1) * 0x9E3779B97F4A7C15ull);
+        w[(dst_row0 + r) * dst_wstride + j] = (gw & 1) ? (uint32_t)(h >> 32) : (uint32_t)h;
+    }
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < ng; i += stride) {
+        const uint64_t r = i / (nc / 64), g = i % (nc / 64);
+        const uint64_t gg = (r0 + r) * gpr + c0 / 64 + g;
+        const uint64_t h = sg_mix(key_m + (gg + 1) * 0x9E3779B97F4A7C15ull);
+        const double u = __dmul_rn((double)(h >> 11), 1.0 / 9007199254740992.0);
+        const float s32 = __double2float_rn(__dadd_rn(0.002, __dmul_rn(0.018, u)));
+        const uint16_t sb = bf16_rne_bits(s32);
+        const uint64_t h2 = sg_mix(h ^ key_n);
+        double nrm = 0.0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            nrm = __dadd_rn(nrm, __dmul_rn(__dadd_rn((double)((h2 >> (16 * k)) & 0xffffu), 0.5), 1.0 / 65536.0));
+        nrm = __dmul_rn(__dadd_rn(nrm, -2.0), 1.7320508075688772);
+        const double sv = (double)__uint_as_float((uint32_t)sb << 16);
+        const float b32 = __double2float_rn(__dadd_rn(__dmul_rn(-8.0, sv), __dmul_rn(1e-3, nrm)));
+        s[(dst_row0 + r) * dst_mstride + g] = sb;
+        b[(dst_row0 + r) * dst_mstride + g] = bf16_rne_bits(b32);
+    }
+}
+
+// Sharded decode: x[t][i] += sum over ranks (in rank order) of the partial
+// products the ranks pushed into this rank's slots [t][world][H].
+__global__ void partial_sum_kernel(float *x, const float *slots, int world, int H, int nq) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x, t = blockIdx.y;
+    if (i >= H || t >= nq) return;
+    const float *src = slots + (size_t)t * world * H + i;
+    float acc = __ldcg(src);
+    for (int r = 1; r < world; ++r) acc = __fadd_rn(acc, __ldcg(src + (size_t)r * H));
+    x[(size_t)t * H + i] = __fadd_rn(x[(size_t)t * H + i], acc);
+}
+
 __global__ void fill_kernel(float *p, uint64_t n, float v) {
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
         p[i] = v;
@@ -583,6 +631,22 @@ int launch_synth_q4(uint32_t *w, uint16_t *s, uint16_t *b, uint64_t seed, uint32
                                                sg_key(seed, mid, 2), sg_key(seed, mid, 3), 0,
                                                (uint64_t)rows * gpr);
     return launched("synthetic metadata");
+}
+
+int launch_synth_region(uint32_t *w, uint16_t *s, uint16_t *b, uint64_t seed, uint32_t mid, uint32_t full_cols,
+                        uint32_t r0, uint32_t nr, uint32_t c0, uint32_t nc, uint32_t dst_wstride, uint32_t dst_mstride,
+                        uint32_t dst_row0, cudaStream_t stream) {
+    if (full_cols % 64 != 0 || c0 % 64 != 0 || nc % 64 != 0 || c0 + nc > full_cols)
+        return fail(QMR_EINVAL, "synthetic regions need 64-column alignment");
+    synth_region_kernel<<<1184, 256, 0, stream>>>(w, s, b, sg_key(seed, mid, 1), sg_key(seed, mid, 2),
+                                                  sg_key(seed, mid, 3), full_cols, r0, nr, c0, nc, dst_wstride,
+                                                  dst_mstride, dst_row0);
+    return launched("synthetic region");
+}
+
+int launch_partial_sum(float *x, const float *slots, int world, int H, int nq, cudaStream_t stream) {
+    partial_sum_kernel<<<dim3((unsigned)((H + 255) / 256), (unsigned)nq), 256, 0, stream>>>(x, slots, world, H, nq);
+    return launched("partial sum");
 }
 
 int launch_fill_f32(float *p, uint64_t n, float v, cudaStream_t stream) {

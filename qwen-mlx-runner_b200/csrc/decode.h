@@ -76,6 +76,13 @@ constexpr int kDeltaSplit = 4;  // CTAs per DeltaNet value head
 // stride is `cols` with the counter-based synthetic matrix (seed, mid).
 int launch_synth_q4(uint32_t *w, uint16_t *s, uint16_t *b, uint64_t seed, uint32_t mid, uint32_t rows, uint32_t cols,
                     uint32_t row0, cudaStream_t stream);
+// Rows [r0, r0+nr) x columns [c0, c0+nc) of the synthetic matrix (seed,
+// mid) of width full_cols into a destination with its own strides.
+int launch_synth_region(uint32_t *w, uint16_t *s, uint16_t *b, uint64_t seed, uint32_t mid, uint32_t full_cols,
+                        uint32_t r0, uint32_t nr, uint32_t c0, uint32_t nc, uint32_t dst_wstride, uint32_t dst_mstride,
+                        uint32_t dst_row0, cudaStream_t stream);
+// x[t][i] += the ranks' partial products in rank order (slots [t][world][H]).
+int launch_partial_sum(float *x, const float *slots, int world, int H, int nq, cudaStream_t stream);
 int launch_fill_f32(float *p, uint64_t n, float v, cudaStream_t stream);
 int launch_embed_token(const void *w, const void *s, const void *b, bool bf16, uint32_t cols, uint32_t bits,
                        uint32_t group, const DecodeCtrl *ctrl, const int32_t *prompt, float *x, cudaStream_t stream);

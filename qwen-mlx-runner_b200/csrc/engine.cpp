@@ -18,6 +18,21 @@
 //    and without the vocabulary head) is captured once as a CUDA graph and
 //    replayed for every token; prefill and greedy decode run as a sequence of
 //    replays with no host round trip.
+//
+// Tensor-parallel decode over `world` GPUs (one process per GPU, the
+// synthetic model): rank r holds 1/world of the DeltaNet key and value
+// heads, of the attention query heads (KV heads split too, or replicated
+// when there are fewer KV heads than ranks), of the MLP rows and of the
+// vocabulary.  The residual stream x is replicated.  The in-projections and
+// gate/up are split by output rows, so they read the full x and write local
+// activations; out_proj, o_proj and down_proj are split along their input
+// columns, so each rank's product is a partial sum of the full hidden
+// vector.  Those partial sums are all-reduced by the streaming kernel's own
+// exchange epilogue (every rank's partial row goes into slot `rank` of every
+// rank's slot buffer over NVLink peer stores, then an epoch release), a
+// bounded wait for every rank's epoch, and one kernel that adds the slots in
+// rank order into x, so every rank keeps bit-identical x.  The head's shard
+// argmax keys are exchanged the same way and merged by the wait kernel.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -42,6 +57,7 @@ inline uint32_t synth_mid(uint32_t layer, int slot) { return layer * 16u + (uint
 struct DevMat {
     void *w = nullptr, *s = nullptr, *b = nullptr;
     uint32_t rows = 0, cols = 0, bits = 4, group = 64;
+    uint32_t mstride = 0;  // metadata elements per row (0: cols / group); column slices pad it to 8
     bool bf16 = true;
 };
 
@@ -64,7 +80,23 @@ using namespace qmr;
 
 struct QmrModel {
     int device = 0;
-    QmrModelConfig cfg{};
+    QmrModelConfig cfg{};  // the model's configuration
+    // This rank's shapes: cfg with the head counts, the MLP width and the
+    // vocabulary divided among the ranks (cfg itself when world == 1).
+    QmrModelConfig lc{};
+    uint32_t world = 1, rank = 0;
+    uint32_t kv0 = 0;     // first global KV head of this rank
+    uint32_t vbase = 0;   // first vocabulary row of this rank
+    // Exchange memory (world > 1): one IPC-shareable allocation holding two
+    // slot buffers [kMaxBlock][world][hidden] f32, the flag arrays of the
+    // partial-sum and head exchanges, the head key array [world][4] and the
+    // two epoch words; the peers' copies are mapped in `peers`.
+    uint8_t *xbuf = nullptr;
+    size_t xslot = 0;     // bytes of one slot buffer (256-aligned)
+    void *peers[QMR_MAX_RANKS] = {};
+    QmrExchange xch[2] = {}, hxch = {};
+    bool opened = true;   // sharded models are usable after qmr_model_exchange_open
+    int xpar = 0;         // slot buffer of the next partial-sum exchange while recording
     uint32_t context = 0;
     std::vector<LayerState> layers;
     DevMat embed, head;
@@ -117,6 +149,9 @@ struct QmrModel {
                 if (bgraph[i][b] != nullptr) cudaGraphDestroy(bgraph[i][b]);
             }
         }
+        for (uint32_t r = 0; r < QMR_MAX_RANKS; ++r)
+            if (peers[r] != nullptr) qmr_ipc_close(peers[r]);
+        if (xbuf != nullptr) qmr_exchange_free(xbuf);
         for (void *p : allocs) cudaFree(p);
         if (host_stage != nullptr) cudaFreeHost(host_stage);
         if (stream != nullptr) cudaStreamDestroy(stream);
@@ -161,13 +196,16 @@ int dev_const(QmrModel *m, float **p, size_t n, float value) {
     return rc;
 }
 
-int alloc_matrix(QmrModel *m, DevMat *d, uint32_t rows, uint32_t cols, uint32_t bits, uint32_t group, bool bf16) {
+int alloc_matrix(QmrModel *m, DevMat *d, uint32_t rows, uint32_t cols, uint32_t bits, uint32_t group, bool bf16,
+                 uint32_t mstride = 0) {
     d->rows = rows;
     d->cols = cols;
     d->bits = bits;
     d->group = group;
     d->bf16 = bf16;
-    const size_t wbytes = (size_t)rows * cols * bits / 8, groups = (size_t)rows * cols / group;
+    d->mstride = mstride;
+    const size_t wbytes = (size_t)rows * cols * bits / 8;
+    const size_t groups = (size_t)rows * (mstride != 0 ? mstride : cols / group);
     uint8_t *w = nullptr, *s = nullptr, *b = nullptr;
     int rc = dev_alloc(m, &w, wbytes);
     if (rc == QMR_OK) rc = dev_alloc(m, &s, groups * (bf16 ? 2 : 4));
@@ -178,31 +216,12 @@ int alloc_matrix(QmrModel *m, DevMat *d, uint32_t rows, uint32_t cols, uint32_t 
     return rc;
 }
 
-// Model-wide validation and the activations, state and control memory.
-int create_common(QmrModel *m, const QmrModelConfig &c, uint32_t context) {
-    if (c.num_layers == 0 || c.num_layers > QMR_MAX_LAYERS) return fail(QMR_EINVAL, "layer count out of range");
-    if (c.hidden_size == 0 || c.intermediate_size == 0 || c.vocab_size == 0 || c.num_heads == 0 ||
-        c.num_kv_heads == 0 || c.head_dim == 0 || c.linear_key_heads == 0 || c.linear_value_heads == 0 ||
-        c.linear_key_dim == 0 || c.linear_value_dim == 0 || c.conv_width == 0)
-        return fail(QMR_EINVAL, "model dimensions must be positive");
-    if (c.num_heads % c.num_kv_heads != 0 || c.num_heads / c.num_kv_heads > 8)
-        return fail(QMR_EUNSUPPORTED, "attention needs at most 8 query heads per KV head");
-    if (c.head_dim > 256 || c.rotary_dim == 0 || c.rotary_dim % 2 != 0 || c.rotary_dim > c.head_dim)
-        return fail(QMR_EUNSUPPORTED, "head_dim must be <= 256 with an even rotary dimension that fits it");
-    if (c.linear_key_dim > 128 || c.linear_value_heads % c.linear_key_heads != 0)
-        return fail(QMR_EUNSUPPORTED, "DeltaNet needs key dim <= 128 and value heads a multiple of key heads");
-    if (!(c.rms_eps > 0 && std::isfinite(c.rms_eps)) || !(c.rope_theta > 0 && std::isfinite(c.rope_theta)))
-        return fail(QMR_EINVAL, "invalid RMS epsilon or RoPE theta");
-    if (context == 0) return fail(QMR_EINVAL, "context must be positive");
-    // Metal-era 32-bit index limits kept as the reference checks them (engine.rs:286-304).
-    if ((uint64_t)c.num_heads * context * 32 > 0xffffffffull || (uint64_t)context * c.num_kv_heads * c.head_dim > 0xffffffffull)
-        return fail(QMR_ERANGE, "context exceeds 32-bit indexing");
-    m->cfg = c;
-    m->context = context;
-    int rc = cuda_check(cudaGetDevice(&m->device), "cudaGetDevice");
-    if (rc == QMR_OK) rc = cuda_check(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking), "stream");
-    if (rc != QMR_OK) return rc;
+// Activations, recurrent state, KV cache and control memory for this
+// rank's shapes.
+int alloc_buffers(QmrModel *m, uint32_t context) {
+    const QmrModelConfig &c = m->lc;
     const size_t H = c.hidden_size, F = c.intermediate_size;
+    int rc = QMR_OK;
     const size_t KD = (size_t)c.linear_key_heads * c.linear_key_dim, VD = (size_t)c.linear_value_heads * c.linear_value_dim;
     const size_t QD = (size_t)c.num_heads * c.head_dim, KVD = (size_t)c.num_kv_heads * c.head_dim;
     m->qkv_channels = 2 * KD + VD;
@@ -256,6 +275,72 @@ int create_common(QmrModel *m, const QmrModelConfig &c, uint32_t context) {
     return QMR_OK;
 }
 
+// This rank's shapes for a split over `world` ranks (see the file comment).
+int shard_config(QmrModel *m, const QmrModelConfig &c, uint32_t world, uint32_t rank) {
+    m->world = world;
+    m->rank = rank;
+    m->lc = c;
+    m->kv0 = 0;
+    m->vbase = 0;
+    if (world == 1) return QMR_OK;
+    if (world > QMR_MAX_RANKS || rank >= world) return fail(QMR_EINVAL, "world must be 1..%d and rank < world", QMR_MAX_RANKS);
+    const uint32_t VD = c.linear_value_heads * c.linear_value_dim, QD = c.num_heads * c.head_dim;
+    if (c.linear_key_heads % world || c.linear_value_heads % world || c.num_heads % world)
+        return fail(QMR_EUNSUPPORTED, "DeltaNet key/value heads and attention heads must divide among %u ranks", world);
+    if (c.num_kv_heads % world != 0 && world % c.num_kv_heads != 0)
+        return fail(QMR_EUNSUPPORTED, "KV heads must divide among the ranks or the ranks among the KV heads");
+    if (c.intermediate_size % (world * 64) || VD % (world * 64) || QD % (world * 64))
+        return fail(QMR_EUNSUPPORTED, "MLP, DeltaNet value and attention widths must split into 64-column groups");
+    if (c.vocab_size % (world * 16)) return fail(QMR_EUNSUPPORTED, "the vocabulary must split into 16-row tiles");
+    QmrModelConfig &l = m->lc;
+    l.linear_key_heads = c.linear_key_heads / world;
+    l.linear_value_heads = c.linear_value_heads / world;
+    l.num_heads = c.num_heads / world;
+    if (c.num_kv_heads % world == 0) {
+        l.num_kv_heads = c.num_kv_heads / world;
+        m->kv0 = rank * l.num_kv_heads;
+    } else {
+        // Fewer KV heads than ranks: each KV head is replicated on the
+        // world / num_kv_heads ranks whose query heads use it.
+        l.num_kv_heads = 1;
+        m->kv0 = rank / (world / c.num_kv_heads);
+    }
+    l.intermediate_size = c.intermediate_size / world;
+    l.vocab_size = c.vocab_size / world;
+    m->vbase = rank * l.vocab_size;
+    return QMR_OK;
+}
+
+// Model-wide validation and the activations, state and control memory
+// (sized for this rank's shapes, m->lc).
+int create_common(QmrModel *m, const QmrModelConfig &gc, uint32_t context, uint32_t world = 1, uint32_t rank = 0) {
+    const QmrModelConfig &c = gc;
+    if (c.num_layers == 0 || c.num_layers > QMR_MAX_LAYERS) return fail(QMR_EINVAL, "layer count out of range");
+    if (c.hidden_size == 0 || c.intermediate_size == 0 || c.vocab_size == 0 || c.num_heads == 0 ||
+        c.num_kv_heads == 0 || c.head_dim == 0 || c.linear_key_heads == 0 || c.linear_value_heads == 0 ||
+        c.linear_key_dim == 0 || c.linear_value_dim == 0 || c.conv_width == 0)
+        return fail(QMR_EINVAL, "model dimensions must be positive");
+    if (c.num_heads % c.num_kv_heads != 0 || c.num_heads / c.num_kv_heads > 8)
+        return fail(QMR_EUNSUPPORTED, "attention needs at most 8 query heads per KV head");
+    if (c.head_dim > 256 || c.rotary_dim == 0 || c.rotary_dim % 2 != 0 || c.rotary_dim > c.head_dim)
+        return fail(QMR_EUNSUPPORTED, "head_dim must be <= 256 with an even rotary dimension that fits it");
+    if (c.linear_key_dim > 128 || c.linear_value_heads % c.linear_key_heads != 0)
+        return fail(QMR_EUNSUPPORTED, "DeltaNet needs key dim <= 128 and value heads a multiple of key heads");
+    if (!(c.rms_eps > 0 && std::isfinite(c.rms_eps)) || !(c.rope_theta > 0 && std::isfinite(c.rope_theta)))
+        return fail(QMR_EINVAL, "invalid RMS epsilon or RoPE theta");
+    if (context == 0) return fail(QMR_EINVAL, "context must be positive");
+    // Metal-era 32-bit index limits kept as the reference checks them (engine.rs:286-304).
+    if ((uint64_t)c.num_heads * context * 32 > 0xffffffffull || (uint64_t)context * c.num_kv_heads * c.head_dim > 0xffffffffull)
+        return fail(QMR_ERANGE, "context exceeds 32-bit indexing");
+    m->cfg = gc;
+    m->context = context;
+    int rc = shard_config(m, gc, world, rank);
+    if (rc != QMR_OK) return rc;
+    rc = cuda_check(cudaGetDevice(&m->device), "cudaGetDevice");
+    if (rc == QMR_OK) rc = cuda_check(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking), "stream");
+    if (rc != QMR_OK) return rc;
+    return alloc_buffers(m, context);
+}
 // Rows of the concatenated in-projection: DeltaNet [qkv; z; a; b], attention [q|gate; k; v].
 uint32_t in_rows(const QmrModelConfig &c, bool attn) {
     if (attn) return 2 * c.num_heads * c.head_dim + 2 * c.num_kv_heads * c.head_dim;
@@ -297,6 +382,7 @@ int mat_call(QmrModel *m, const DevMat &W, const float *x, float *y, const float
     c.scratch = m->scratch;
     c.scratch_bytes = m->scratch_size;
     c.eps = m->cfg.rms_eps;
+    c.meta_stride = W.mstride;
     if (norm_w != nullptr || resid != nullptr) {
         FastCall f = c;
         f.norm_w = norm_w;
@@ -334,13 +420,86 @@ int mat_call(QmrModel *m, const DevMat &W, const float *x, float *y, const float
     return rc;
 }
 
+// x += W in for the matrices that feed the residual stream (out_proj,
+// o_proj, down_proj).  One GPU: the residual epilogue.  Split over ranks:
+// W is this rank's column slice, its partial product goes through the
+// exchange into slot `rank` of every rank's slot buffer (the two buffers
+// alternate, so a rank one exchange ahead never overwrites slots a peer
+// has not summed yet), then the bounded wait for every rank's epoch and the
+// rank-ordered sum into x.
+int mat_reduce(QmrModel *m, const DevMat &W, const float *in, StepCounter *cnt, int nq) {
+    if (m->world == 1) return mat_call(m, W, in, m->x, nullptr, m->x, 0, nullptr, nullptr, cnt, nq);
+    const QmrExchange &ex = m->xch[m->xpar];
+    m->xpar ^= 1;
+    FastCall c = {};
+    c.w = W.w;
+    c.s = W.s;
+    c.b = W.b;
+    c.x = in;
+    c.y = ex.out[ex.rank] + ex.row_base;
+    c.ystride = ex.total_rows;
+    c.rows = W.rows;
+    c.cols = W.cols;
+    c.bits = W.bits;
+    c.group = W.group;
+    c.batch = (uint32_t)nq;
+    c.bf16 = W.bf16;
+    c.path = kPathMma;
+    c.scratch = m->scratch;
+    c.scratch_bytes = m->scratch_size;
+    c.meta_stride = W.mstride;
+    c.ex = &ex;
+    int rc = run_fast(c, m->stream);
+    cnt->n += 2;
+    if (rc == QMR_OK) rc = launch_exchange_wait(ex, (uint32_t)nq, nullptr, nullptr, m->stream);
+    ++cnt->n;
+    if (rc == QMR_OK) rc = launch_partial_sum(m->x, ex.out[ex.rank], (int)m->world, (int)m->lc.hidden_size, nq, m->stream);
+    ++cnt->n;
+    return rc;
+}
+
+// Final norm + head + greedy argmax into `argmax` (nq entries).  Split over
+// ranks: each rank's vocabulary rows, its logits stay local, and the wait
+// kernel merges the ranks' best keys (highest logit, ties to the lowest
+// vocabulary index).
+int head_call(QmrModel *m, int32_t *argmax, StepCounter *cnt, int nq) {
+    if (m->world == 1)
+        return mat_call(m, m->head, m->x, m->logits, m->final_norm, nullptr, 2, nullptr, argmax, cnt, nq);
+    const DevMat &W = m->head;
+    FastCall c = {};
+    c.w = W.w;
+    c.s = W.s;
+    c.b = W.b;
+    c.x = m->x;
+    c.y = m->logits;
+    c.rows = W.rows;
+    c.cols = W.cols;
+    c.bits = W.bits;
+    c.group = W.group;
+    c.batch = (uint32_t)nq;
+    c.row_base = m->vbase;
+    c.bf16 = W.bf16;
+    c.epilogue = 2;
+    c.path = kPathMma;
+    c.scratch = m->scratch;
+    c.scratch_bytes = m->scratch_size;
+    c.norm_w = m->final_norm;
+    c.eps = m->cfg.rms_eps;
+    c.ex = &m->hxch;
+    int rc = run_fast(c, m->stream);
+    cnt->n += 2;
+    if (rc == QMR_OK) rc = launch_exchange_wait(m->hxch, (uint32_t)nq, argmax, nullptr, m->stream);
+    ++cnt->n;
+    return rc;
+}
+
 // Kinds of recorded step: one token without / with the head, a
 // verification block evaluated, or a full verification round (evaluate,
 // greedy verify, roll back to the consumed prefix).
 enum StepKind { kStepPlain, kStepHead, kStepBlockEval, kStepBlockRound };
 
 int record_step(QmrModel *m, StepKind kind, int nq, StepCounter *cnt) {
-    const QmrModelConfig &c = m->cfg;
+    const QmrModelConfig &c = m->lc;
     const bool block = kind == kStepBlockEval || kind == kStepBlockRound;
     int rc;
     if (block)
@@ -404,13 +563,11 @@ int record_step(QmrModel *m, StepKind kind, int nq, StepCounter *cnt) {
             rc = launch_delta_mixer(a, m->stream);
         }
         ++cnt->n;
-        if (rc == QMR_OK) rc = mat_call(m, L.out, m->mixed, m->x, nullptr, m->x, 0, nullptr, nullptr, cnt, nq);
+        if (rc == QMR_OK) rc = mat_reduce(m, L.out, m->mixed, cnt, nq);
         if (rc == QMR_OK) rc = mat_call(m, L.gate, m->x, m->act, L.post_norm, nullptr, 1, &L.up, nullptr, cnt, nq);
-        if (rc == QMR_OK) rc = mat_call(m, L.down, m->act, m->x, nullptr, m->x, 0, nullptr, nullptr, cnt, nq);
+        if (rc == QMR_OK) rc = mat_reduce(m, L.down, m->act, cnt, nq);
     }
-    if (rc == QMR_OK && kind != kStepPlain)
-        rc = mat_call(m, m->head, m->x, m->logits, m->final_norm, nullptr, 2, nullptr,
-                      block ? m->block_argmax : &m->ctrl->token, cnt, nq);
+    if (rc == QMR_OK && kind != kStepPlain) rc = head_call(m, block ? m->block_argmax : &m->ctrl->token, cnt, nq);
     if (rc == QMR_OK && !block) {
         rc = launch_advance(m->ctrl, m->out, m->out_cap, kind == kStepHead, m->stream);
         ++cnt->n;
@@ -429,7 +586,7 @@ int record_step(QmrModel *m, StepKind kind, int nq, StepCounter *cnt) {
 }
 
 int clear_state(QmrModel *m) {
-    const QmrModelConfig &c = m->cfg;
+    const QmrModelConfig &c = m->lc;
     const size_t VD = (size_t)c.linear_value_heads * c.linear_value_dim;
     int rc = QMR_OK;
     for (LayerState &L : m->layers) {
@@ -482,7 +639,7 @@ int build_graphs(QmrModel *m) {
 // first run eagerly on the matrices alone (they touch activations and
 // scratch, never model state), so the capture sees no first-use set-up.
 int ensure_block(QmrModel *m, int nq) {
-    const QmrModelConfig &c = m->cfg;
+    const QmrModelConfig &c = m->lc;
     int rc = QMR_OK;
     if (!m->block_ready) {
         const size_t conv = m->qkv_channels * (c.conv_width - 1);
@@ -509,12 +666,12 @@ int ensure_block(QmrModel *m, int nq) {
         if (seen[L.attn]) continue;
         seen[L.attn] = true;
         rc = mat_call(m, L.in, m->x, m->proj, L.in_norm, nullptr, 0, nullptr, nullptr, &warm, nq);
-        if (rc == QMR_OK) rc = mat_call(m, L.out, m->mixed, m->x, nullptr, m->x, 0, nullptr, nullptr, &warm, nq);
+        if (rc == QMR_OK) rc = mat_reduce(m, L.out, m->mixed, &warm, nq);
         if (rc == QMR_OK) rc = mat_call(m, L.gate, m->x, m->act, L.post_norm, nullptr, 1, &L.up, nullptr, &warm, nq);
-        if (rc == QMR_OK) rc = mat_call(m, L.down, m->act, m->x, nullptr, m->x, 0, nullptr, nullptr, &warm, nq);
+        if (rc == QMR_OK) rc = mat_reduce(m, L.down, m->act, &warm, nq);
         if (rc != QMR_OK) return rc;
     }
-    rc = mat_call(m, m->head, m->x, m->logits, m->final_norm, nullptr, 2, nullptr, m->block_argmax, &warm, nq);
+    rc = head_call(m, m->block_argmax, &warm, nq);
     if (rc == QMR_OK) rc = cuda_check(cudaStreamSynchronize(m->stream), "block warm-up");
     for (int kind = 0; kind < 2 && rc == QMR_OK; ++kind) {
         StepCounter cnt;
@@ -671,60 +828,133 @@ int load_model(QmrModel *m, const std::string &dir, uint32_t context) {
 
 // ---- the synthetic model --------------------------------------------------------
 
-int synth_matrix(QmrModel *m, DevMat *d, uint64_t seed, const std::vector<std::pair<uint32_t, uint32_t>> &parts,
-                 uint32_t cols) {
+// Rows [r0, r0 + nr) of synthetic matrix `mid` (full width `cols`), the
+// parts stacked in order into one device matrix.
+struct RowPart {
+    uint32_t mid, r0, nr;
+};
+
+int synth_rows(QmrModel *m, DevMat *d, uint64_t seed, const std::vector<RowPart> &parts, uint32_t cols) {
     uint32_t rows = 0;
-    for (const auto &p : parts) rows += p.second;
+    for (const RowPart &p : parts) rows += p.nr;
     int rc = alloc_matrix(m, d, rows, cols, 4, 64, true);
-    uint32_t r0 = 0;
-    for (const auto &p : parts) {
+    uint32_t dst = 0;
+    for (const RowPart &p : parts) {
         if (rc != QMR_OK) break;
-        rc = launch_synth_q4(static_cast<uint32_t *>(d->w), static_cast<uint16_t *>(d->s),
-                             static_cast<uint16_t *>(d->b), seed, p.first, p.second, cols, r0, m->stream);
-        r0 += p.second;
+        rc = launch_synth_region(static_cast<uint32_t *>(d->w), static_cast<uint16_t *>(d->s),
+                                 static_cast<uint16_t *>(d->b), seed, p.mid, cols, p.r0, p.nr, 0, cols, cols / 8,
+                                 cols / 64, dst, m->stream);
+        dst += p.nr;
     }
     return rc;
 }
 
-int synth_model(QmrModel *m, const QmrModelConfig &c, uint64_t seed, uint32_t context) {
-    int rc = create_common(m, c, context);
-    if (rc != QMR_OK) return rc;
+// Columns [c0, c0 + nc) of synthetic matrix `mid` (rows x full_cols): the
+// input-side slice of a column-split matrix.  Its metadata rows are padded
+// to a multiple of 8 groups (16-byte rows for the kernel's tensor maps).
+int synth_cols(QmrModel *m, DevMat *d, uint64_t seed, uint32_t mid, uint32_t rows, uint32_t full_cols, uint32_t c0,
+               uint32_t nc) {
+    const uint32_t ng = nc / 64, mstride = (ng + 7) / 8 * 8;
+    int rc = alloc_matrix(m, d, rows, nc, 4, 64, true, mstride == ng ? 0 : mstride);
+    if (rc == QMR_OK)
+        rc = launch_synth_region(static_cast<uint32_t *>(d->w), static_cast<uint16_t *>(d->s),
+                                 static_cast<uint16_t *>(d->b), seed, mid, full_cols, 0, rows, c0, nc, nc / 8, mstride,
+                                 0, m->stream);
+    return rc;
+}
+
+// The synthetic model, or rank `rank`'s shard of it (the file comment gives
+// the split); the matrices are regions of the same seeded matrices either way.
+int synth_model(QmrModel *m, const QmrModelConfig &c, uint64_t seed, uint32_t context, uint32_t world = 1,
+                uint32_t rank = 0) {
     if (c.hidden_size % 64 || c.intermediate_size % 64 || (c.linear_value_heads * c.linear_value_dim) % 64 ||
         (c.num_heads * c.head_dim) % 64)
         return fail(QMR_EINVAL, "synthetic Q4/g64 matrices need widths divisible by 64");
-    const uint32_t H = c.hidden_size, F = c.intermediate_size;
+    int rc = create_common(m, c, context, world, rank);
+    if (rc != QMR_OK) return rc;
+    const QmrModelConfig &l = m->lc;
+    const uint32_t H = c.hidden_size, F = c.intermediate_size, Fl = l.intermediate_size;
     const uint32_t KD = c.linear_key_heads * c.linear_key_dim, VD = c.linear_value_heads * c.linear_value_dim;
-    const uint32_t QD = c.num_heads * c.head_dim, KVD = c.num_kv_heads * c.head_dim;
-    rc = synth_matrix(m, &m->embed, seed, {{kMidEmbed, c.vocab_size}}, H);
-    if (rc == QMR_OK) rc = synth_matrix(m, &m->head, seed, {{kMidHead, c.vocab_size}}, H);
+    const uint32_t KDl = l.linear_key_heads * l.linear_key_dim, VDl = l.linear_value_heads * l.linear_value_dim;
+    const uint32_t QD = c.num_heads * c.head_dim, QDl = l.num_heads * l.head_dim;
+    const uint32_t KVD = c.num_kv_heads * c.head_dim, KVDl = l.num_kv_heads * l.head_dim;
+    const uint32_t VHl = l.linear_value_heads, r = rank, kvr0 = m->kv0 * c.head_dim;
+    (void)KVD;
+    rc = synth_rows(m, &m->embed, seed, {{kMidEmbed, 0, c.vocab_size}}, H);
+    if (rc == QMR_OK) rc = synth_rows(m, &m->head, seed, {{kMidHead, m->vbase, l.vocab_size}}, H);
     if (rc == QMR_OK) rc = dev_const(m, &m->final_norm, H, 1.0f);
-    for (uint32_t l = 0; l < c.num_layers && rc == QMR_OK; ++l) {
-        LayerState &L = m->layers[l];
+    for (uint32_t li = 0; li < c.num_layers && rc == QMR_OK; ++li) {
+        LayerState &L = m->layers[li];
         rc = dev_const(m, &L.in_norm, H, 1.0f);
         if (rc == QMR_OK) rc = dev_const(m, &L.post_norm, H, 1.0f);
         if (rc == QMR_OK && L.attn) {
-            rc = synth_matrix(m, &L.in, seed,
-                              {{synth_mid(l, S_Q), 2 * QD}, {synth_mid(l, S_K), KVD}, {synth_mid(l, S_V), KVD}}, H);
-            if (rc == QMR_OK) rc = synth_matrix(m, &L.out, seed, {{synth_mid(l, S_O), H}}, QD);
+            // q|gate rows of this rank's query heads ([head][2][D]), k and v rows of its KV heads.
+            rc = synth_rows(m, &L.in, seed,
+                            {{synth_mid(li, S_Q), r * 2 * QDl, 2 * QDl}, {synth_mid(li, S_K), kvr0, KVDl},
+                             {synth_mid(li, S_V), kvr0, KVDl}}, H);
+            if (rc == QMR_OK) rc = synth_cols(m, &L.out, seed, synth_mid(li, S_O), H, QD, r * QDl, QDl);
             if (rc == QMR_OK) rc = dev_const(m, &L.qnorm, c.head_dim, 1.0f);
             if (rc == QMR_OK) rc = dev_const(m, &L.knorm, c.head_dim, 1.0f);
         } else if (rc == QMR_OK) {
-            rc = synth_matrix(m, &L.in, seed,
-                              {{synth_mid(l, S_QKV), 2 * KD + VD}, {synth_mid(l, S_Z), VD},
-                               {synth_mid(l, S_A), c.linear_value_heads}, {synth_mid(l, S_B), c.linear_value_heads}},
-                              H);
-            if (rc == QMR_OK) rc = synth_matrix(m, &L.out, seed, {{synth_mid(l, S_OUT), H}}, VD);
+            // q, k, v channels of this rank's key / value heads, then z, a, b of its value heads.
+            rc = synth_rows(m, &L.in, seed,
+                            {{synth_mid(li, S_QKV), r * KDl, KDl}, {synth_mid(li, S_QKV), KD + r * KDl, KDl},
+                             {synth_mid(li, S_QKV), 2 * KD + r * VDl, VDl}, {synth_mid(li, S_Z), r * VDl, VDl},
+                             {synth_mid(li, S_A), r * VHl, VHl}, {synth_mid(li, S_B), r * VHl, VHl}},
+                            H);
+            if (rc == QMR_OK) rc = synth_cols(m, &L.out, seed, synth_mid(li, S_OUT), H, VD, r * VDl, VDl);
             if (rc == QMR_OK) rc = dev_const(m, &L.conv_w, m->qkv_channels * c.conv_width, 0.1f);
-            if (rc == QMR_OK) rc = dev_const(m, &L.alog, c.linear_value_heads, 0.0f);
-            if (rc == QMR_OK) rc = dev_const(m, &L.dt, c.linear_value_heads, 0.0f);
+            if (rc == QMR_OK) rc = dev_const(m, &L.alog, VHl, 0.0f);
+            if (rc == QMR_OK) rc = dev_const(m, &L.dt, VHl, 0.0f);
             if (rc == QMR_OK) rc = dev_const(m, &L.dnorm, c.linear_value_dim, 1.0f);
         }
-        if (rc == QMR_OK) rc = synth_matrix(m, &L.gate, seed, {{synth_mid(l, S_GATE), F}}, H);
-        if (rc == QMR_OK) rc = synth_matrix(m, &L.up, seed, {{synth_mid(l, S_UP), F}}, H);
-        if (rc == QMR_OK) rc = synth_matrix(m, &L.down, seed, {{synth_mid(l, S_DOWN), H}}, F);
+        if (rc == QMR_OK) rc = synth_rows(m, &L.gate, seed, {{synth_mid(li, S_GATE), r * Fl, Fl}}, H);
+        if (rc == QMR_OK) rc = synth_rows(m, &L.up, seed, {{synth_mid(li, S_UP), r * Fl, Fl}}, H);
+        if (rc == QMR_OK) rc = synth_cols(m, &L.down, seed, synth_mid(li, S_DOWN), H, F, r * Fl, Fl);
     }
     if (rc == QMR_OK) rc = cuda_check(cudaStreamSynchronize(m->stream), "generating the synthetic model");
     return rc;
+}
+
+// Exchange memory of a sharded model: its own allocation (IPC-shareable).
+constexpr size_t kFlagsOff = 0, kHFlagsOff = 256, kKeysOff = 512, kEpochOff = 768, kHEpochOff = 772, kCtlBytes = 1024;
+
+int alloc_exchange(QmrModel *m) {
+    m->xslot = ((size_t)kMaxBlock * m->world * m->lc.hidden_size * 4 + 255) / 256 * 256;
+    void *p = nullptr;
+    const int rc = qmr_exchange_alloc(2 * m->xslot + kCtlBytes, &p);
+    m->xbuf = static_cast<uint8_t *>(p);
+    return rc;
+}
+
+// Fill the two partial-sum exchanges and the head exchange from every
+// rank's exchange memory (this rank's own and the mapped peers').
+void wire_exchanges(QmrModel *m, uint8_t *const *base) {
+    const uint32_t H = m->lc.hidden_size;
+    for (int par = 0; par < 2; ++par) {
+        QmrExchange &x = m->xch[par];
+        x = QmrExchange{};
+        x.world = m->world;
+        x.rank = m->rank;
+        x.total_rows = m->world * H;
+        x.row_base = m->rank * H;
+        for (uint32_t p = 0; p < m->world; ++p) {
+            x.out[p] = reinterpret_cast<float *>(base[p] + par * m->xslot);
+            x.flags[p] = reinterpret_cast<uint32_t *>(base[p] + 2 * m->xslot + kFlagsOff);
+        }
+        x.epoch = reinterpret_cast<uint32_t *>(m->xbuf + 2 * m->xslot + kEpochOff);
+    }
+    QmrExchange &h = m->hxch;
+    h = QmrExchange{};
+    h.world = m->world;
+    h.rank = m->rank;
+    h.total_rows = m->cfg.vocab_size;
+    h.row_base = m->vbase;
+    for (uint32_t p = 0; p < m->world; ++p) {
+        h.flags[p] = reinterpret_cast<uint32_t *>(base[p] + 2 * m->xslot + kHFlagsOff);
+        h.keys[p] = reinterpret_cast<uint64_t *>(base[p] + 2 * m->xslot + kKeysOff);
+    }
+    h.epoch = reinterpret_cast<uint32_t *>(m->xbuf + 2 * m->xslot + kHEpochOff);
 }
 
 int finish_create(QmrModel *m, QmrModel **out) {
@@ -822,6 +1052,68 @@ int qmr_model_synthetic(const QmrModelConfig *cfg, uint64_t seed, uint32_t conte
     return finish_create(m, out);
 }
 
+int qmr_model_synthetic_sharded(const QmrModelConfig *cfg, uint64_t seed, uint32_t context, uint32_t world,
+                                uint32_t rank, QmrModel **out) {
+    if (cfg == nullptr || out == nullptr) return fail(QMR_EINVAL, "null argument");
+    if (world == 0 || world > QMR_MAX_RANKS || rank >= world)
+        return fail(QMR_EINVAL, "world must be 1..%d and rank < world", QMR_MAX_RANKS);
+    if (world == 1) return qmr_model_synthetic(cfg, seed, context, out);
+    QmrModel *m = new QmrModel();
+    int rc = synth_model(m, *cfg, seed, context, world, rank);
+    if (rc == QMR_OK) rc = alloc_exchange(m);
+    if (rc != QMR_OK) {
+        delete m;
+        return rc;
+    }
+    m->opened = false;
+    *out = m;
+    return QMR_OK;
+}
+
+int qmr_model_exchange_handle(const QmrModel *m, void *handle) {
+    if (m == nullptr || handle == nullptr) return fail(QMR_EINVAL, "null argument");
+    if (m->world < 2 || m->xbuf == nullptr) return fail(QMR_EINVAL, "the model is not sharded");
+    DeviceGuard g(m->device);
+    return qmr_ipc_handle(m->xbuf, handle);
+}
+
+int qmr_model_exchange_open(QmrModel *m, const void *handles) {
+    if (m == nullptr || handles == nullptr) return fail(QMR_EINVAL, "null argument");
+    if (m->world < 2 || m->xbuf == nullptr) return fail(QMR_EINVAL, "the model is not sharded");
+    if (m->opened) return fail(QMR_EINVAL, "the exchange is already open");
+    DeviceGuard g(m->device);
+    uint8_t *base[QMR_MAX_RANKS] = {};
+    const uint8_t *h = static_cast<const uint8_t *>(handles);
+    int rc = QMR_OK;
+    for (uint32_t r = 0; r < m->world && rc == QMR_OK; ++r) {
+        if (r == m->rank) {
+            base[r] = m->xbuf;
+            continue;
+        }
+        void *p = nullptr;
+        rc = qmr_ipc_open(h + (size_t)r * QMR_IPC_HANDLE_BYTES, &p);
+        m->peers[r] = p;
+        base[r] = static_cast<uint8_t *>(p);
+    }
+    if (rc != QMR_OK) return rc;
+    wire_exchanges(m, base);
+    m->opened = true;
+    // The warm-up steps exchange with the peers: every rank opens together.
+    rc = build_graphs(m);
+    if (rc == QMR_OK) rc = check_device_error();
+    if (rc != QMR_OK) m->opened = false;
+    return rc;
+}
+
+int qmr_model_shard(const QmrModel *m, uint32_t *world, uint32_t *rank, uint32_t *vocab_base, uint32_t *vocab_rows) {
+    if (m == nullptr) return fail(QMR_EINVAL, "null model");
+    if (world) *world = m->world;
+    if (rank) *rank = m->rank;
+    if (vocab_base) *vocab_base = m->vbase;
+    if (vocab_rows) *vocab_rows = m->lc.vocab_size;
+    return QMR_OK;
+}
+
 void qmr_model_free(QmrModel *m) { delete m; }
 
 int qmr_model_config(const QmrModel *m, QmrModelConfig *cfg, uint32_t *context) {
@@ -833,6 +1125,7 @@ int qmr_model_config(const QmrModel *m, QmrModelConfig *cfg, uint32_t *context) 
 
 int qmr_model_reset(QmrModel *m) {
     if (m == nullptr) return fail(QMR_EINVAL, "null model");
+    if (!m->opened) return fail(QMR_EINVAL, "open the sharded model's exchange first");
     DeviceGuard g(m->device);
     return clear_state(m);
 }
@@ -845,6 +1138,7 @@ int qmr_model_position(const QmrModel *m, uint32_t *pos) {
 
 int qmr_model_forward(QmrModel *m, uint32_t token, float *logits, int32_t *next) {
     if (m == nullptr) return fail(QMR_EINVAL, "null model");
+    if (!m->opened) return fail(QMR_EINVAL, "open the sharded model's exchange first");
     if (m->pending) return fail(QMR_EINVAL, "commit or reset the pending verification block before a normal forward");
     if (token >= m->cfg.vocab_size) return fail(QMR_EINVAL, "token %u outside vocabulary", token);
     if (m->pos >= m->context) return fail(QMR_ERANGE, "context capacity %u exhausted", m->context);
@@ -855,7 +1149,7 @@ int qmr_model_forward(QmrModel *m, uint32_t token, float *logits, int32_t *next)
                         "writing the step token");
     if (rc == QMR_OK) rc = replay(m, 1, 1);
     if (rc == QMR_OK && logits != nullptr)
-        rc = cuda_check(cudaMemcpyAsync(logits, m->logits, (size_t)m->cfg.vocab_size * 4, cudaMemcpyDeviceToHost,
+        rc = cuda_check(cudaMemcpyAsync(logits, m->logits, (size_t)m->lc.vocab_size * 4, cudaMemcpyDeviceToHost,
                                         m->stream), "reading logits");
     if (rc == QMR_OK)
         rc = cuda_check(cudaMemcpyAsync(m->host_stage + 2, &m->ctrl->token, 4, cudaMemcpyDeviceToHost, m->stream),
@@ -876,6 +1170,7 @@ int qmr_model_generate(QmrModel *m, const uint32_t *prompt, uint32_t n_prompt, u
                        double *prefill_ms, double *decode_ms) {
     if (m == nullptr || prompt == nullptr || out == nullptr) return fail(QMR_EINVAL, "null argument");
     if (n_prompt == 0 || max_new == 0) return fail(QMR_EINVAL, "empty prompt or max_new = 0");
+    if (!m->opened) return fail(QMR_EINVAL, "open the sharded model's exchange first");
     if (m->pending) return fail(QMR_EINVAL, "commit or reset the pending verification block first");
     for (uint32_t i = 0; i < n_prompt; ++i)
         if (prompt[i] >= m->cfg.vocab_size) return fail(QMR_EINVAL, "prompt token %u outside vocabulary", prompt[i]);
@@ -920,6 +1215,7 @@ int qmr_model_generate(QmrModel *m, const uint32_t *prompt, uint32_t n_prompt, u
 
 int qmr_model_verify_block(QmrModel *m, const uint32_t *tokens, uint32_t n, float *logits, int32_t *argmax) {
     if (m == nullptr || tokens == nullptr) return fail(QMR_EINVAL, "null argument");
+    if (!m->opened) return fail(QMR_EINVAL, "open the sharded model's exchange first");
     if (m->pending) return fail(QMR_EINVAL, "commit or reset the pending verification block before another block");
     if (n < 1 || n > (uint32_t)kMaxBlock) return fail(QMR_EINVAL, "verification block width must be 1..=4");
     for (uint32_t i = 0; i < n; ++i)
@@ -940,7 +1236,7 @@ int qmr_model_verify_block(QmrModel *m, const uint32_t *tokens, uint32_t n, floa
                                         cudaMemcpyHostToDevice, m->stream), "block inputs");
     if (rc == QMR_OK) rc = cuda_check(cudaGraphLaunch(m->bexec[0][n], m->stream), "graph launch");
     if (rc == QMR_OK && logits != nullptr)
-        rc = cuda_check(cudaMemcpyAsync(logits, m->logits, (size_t)n * m->cfg.vocab_size * 4, cudaMemcpyDeviceToHost,
+        rc = cuda_check(cudaMemcpyAsync(logits, m->logits, (size_t)n * m->lc.vocab_size * 4, cudaMemcpyDeviceToHost,
                                         m->stream), "reading logits");
     if (rc == QMR_OK && argmax != nullptr)
         rc = cuda_check(cudaMemcpyAsync(argmax, m->block_argmax, (size_t)n * 4, cudaMemcpyDeviceToHost, m->stream),
@@ -959,11 +1255,12 @@ int qmr_model_verify_block(QmrModel *m, const uint32_t *tokens, uint32_t n, floa
 
 int qmr_model_commit_block(QmrModel *m, uint32_t consumed) {
     if (m == nullptr) return fail(QMR_EINVAL, "null model");
+    if (!m->opened) return fail(QMR_EINVAL, "open the sharded model's exchange first");
     if (!m->pending) return fail(QMR_EINVAL, "there is no pending verification block");
     if (consumed > m->pending_width) return fail(QMR_EINVAL, "accepted prefix exceeds pending block length");
     DeviceGuard g(m->device);
     const uint32_t base = m->pos - m->pending_width;
-    const QmrModelConfig &c = m->cfg;
+    const QmrModelConfig &c = m->lc;
     m->host_stage[0] = (int32_t)consumed;
     m->host_stage[4] = (int32_t)(base + consumed);
     int rc = cuda_check(cudaMemcpyAsync(&m->bctrl->consumed, m->host_stage, 4, cudaMemcpyHostToDevice, m->stream),
@@ -987,6 +1284,7 @@ int qmr_model_mtp_generate(QmrModel *m, const uint32_t *prompt, uint32_t n_promp
                            const uint32_t *drafts, uint32_t n_drafts, uint32_t *out, uint32_t *rounds,
                            uint32_t *accepted, double *prefill_ms, double *decode_ms) {
     if (m == nullptr || prompt == nullptr || out == nullptr || drafts == nullptr) return fail(QMR_EINVAL, "null argument");
+    if (!m->opened) return fail(QMR_EINVAL, "open the sharded model's exchange first");
     if (block < 2 || block > (uint32_t)kMaxBlock) return fail(QMR_EINVAL, "MTP block width must be 2..=4");
     if (n_prompt == 0 || max_new == 0) return fail(QMR_EINVAL, "empty prompt or max_new = 0");
     if (m->pending) return fail(QMR_EINVAL, "commit or reset the pending verification block first");

@@ -142,8 +142,8 @@ int QMR_MMA_LAUNCH(const FastCall &c, const MmaPlan &p, const ScratchView &sv, c
         const bool second = q == 1 && nm == 2;
         const void *w = second ? c.w2 : c.w, *s = second ? c.s2 : c.s, *b = second ? c.b2 : c.b;
         int rc = tensor_map_2d(&maps.w[q], w, 4, row_words, c.rows, 32, kTileRows, true);
-        if (rc == QMR_OK) rc = tensor_map_2d(&maps.s[q], s, msz, ngroups, c.rows, wg, kTileRows, false);
-        if (rc == QMR_OK) rc = tensor_map_2d(&maps.b[q], b, msz, ngroups, c.rows, wg, kTileRows, false);
+        if (rc == QMR_OK) rc = tensor_map_2d(&maps.s[q], s, msz, ngroups, c.rows, wg, kTileRows, false, c.meta_stride);
+        if (rc == QMR_OK) rc = tensor_map_2d(&maps.b[q], b, msz, ngroups, c.rows, wg, kTileRows, false, c.meta_stride);
         if (rc != QMR_OK) return rc;
     }
     MmaArgs a = {};

@@ -34,7 +34,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // Encoded maps cached by (address, kind, shape, box): the engine and the
 // benchmarks reuse a handful of matrices, so encoding happens once each.
-using MapKey = std::tuple<const void *, int, uint64_t, uint64_t, uint32_t, uint32_t, bool>;
+using MapKey = std::tuple<const void *, int, uint64_t, uint64_t, uint32_t, uint32_t, bool, uint64_t>;
 std::mutex g_map_mu;
 std::map<MapKey, CUtensorMap> g_maps;
 
@@ -44,8 +44,9 @@ std::map<MapKey, CUtensorMap> g_maps;
 // `esize` bytes, box = box_x elements x box_y rows, zero fill out of range,
 // optionally with the 128-byte shared-memory swizzle.
 int tensor_map_2d(CUtensorMap *out, const void *base, int esize, uint64_t row_elems, uint64_t rows, uint32_t box_x,
-                  uint32_t box_y, bool swizzle128) {
-    const MapKey key{base, esize, row_elems, rows, box_x, box_y, swizzle128};
+                  uint32_t box_y, bool swizzle128, uint64_t row_stride_elems) {
+    if (row_stride_elems == 0) row_stride_elems = row_elems;
+    const MapKey key{base, esize, row_elems, rows, box_x, box_y, swizzle128, row_stride_elems};
     {
         std::lock_guard<std::mutex> lock(g_map_mu);
         auto it = g_maps.find(key);
@@ -58,7 +59,7 @@ int tensor_map_2d(CUtensorMap *out, const void *base, int esize, uint64_t row_el
     if (fn == nullptr) return fail(QMR_ECUDA, "cuTensorMapEncodeTiled is unavailable");
     const CUtensorMapDataType dt = esize == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32;
     const cuuint64_t dims[2] = {row_elems, rows};
-    const cuuint64_t strides[1] = {row_elems * (uint64_t)esize};
+    const cuuint64_t strides[1] = {row_stride_elems * (uint64_t)esize};
     const cuuint32_t box[2] = {box_x, box_y};
     const cuuint32_t es[2] = {1, 1};
     CUtensorMap m;

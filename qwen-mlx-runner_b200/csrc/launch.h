@@ -30,8 +30,9 @@ int launch_reg(const StreamArgs &a, int bits, bool bf16, uint32_t batch, int epi
 // kernels_tile.cu
 bool tile_eligible(const FastCall &c);
 int launch_tile_call(const FastCall &c, const ScratchView &sv, cudaStream_t stream);
+// row_stride_elems: elements from one row to the next (0: row_elems).
 int tensor_map_2d(CUtensorMap *out, const void *base, int esize, uint64_t row_elems, uint64_t rows, uint32_t box_x,
-                  uint32_t box_y, bool swizzle128);
+                  uint32_t box_y, bool swizzle128, uint64_t row_stride_elems = 0);
 unsigned int *device_error_word();
 
 // Launch shape of the tensor-core kernel for one call (matrix.cu).
@@ -47,8 +48,10 @@ struct MmaPlan {
     int warps;        // warps per CTA
     uint32_t smem, off_image, off_table, off_pieces, off_part, off_bars;
 };
+// meta_stride: metadata elements per row (0: cols / group); it must be a
+// multiple of 8 (16-byte rows for the metadata tensor maps).
 bool mma_plan(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint32_t batch, int epi, bool bf16,
-              MmaPlan *p);
+              MmaPlan *p, uint32_t meta_stride = 0);
 
 // kernels_mma.cu (one translation unit per bit width)
 int launch_mma_prep_bits(int bits, const float *x, uint32_t cols, uint32_t group, uint32_t batch, int ngroups_pad,

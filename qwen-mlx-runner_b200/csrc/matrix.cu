@@ -173,7 +173,7 @@ constexpr size_t kMmaImageBudget = 96 * 1024;
 namespace {
 
 bool mma_plan_b(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint32_t batch, int epi, bool bf16,
-                int only_kc, int only_warps, MmaPlan *p);
+                int only_kc, int only_warps, MmaPlan *p, uint32_t meta_stride);
 
 }  // namespace
 
@@ -181,10 +181,10 @@ bool mma_plan_b(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uin
 // at B = 4, and the column slicing does not depend on B, so every block width
 // of one matrix runs the same kernel with the same summation order.
 bool mma_plan(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint32_t batch, int epi, bool bf16,
-              MmaPlan *p) {
+              MmaPlan *p, uint32_t meta_stride) {
     MmaPlan widest;
-    if (!mma_plan_b(bits, group, rows, cols, 4, epi, bf16, 0, 0, &widest)) return false;
-    return mma_plan_b(bits, group, rows, cols, batch, epi, bf16, widest.kc, widest.warps, p);
+    if (!mma_plan_b(bits, group, rows, cols, 4, epi, bf16, 0, 0, &widest, meta_stride)) return false;
+    return mma_plan_b(bits, group, rows, cols, batch, epi, bf16, widest.kc, widest.warps, p, meta_stride);
 }
 
 namespace {
@@ -192,13 +192,14 @@ namespace {
 // only_kc / only_warps: 0 searches the slice count / warps per CTA,
 // otherwise the plan must use that one.
 bool mma_plan_b(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uint32_t batch, int epi, bool bf16,
-                int only_kc, int only_warps, MmaPlan *p) {
+                int only_kc, int only_warps, MmaPlan *p, uint32_t meta_stride) {
     if (bits != 4 && bits != 8) return false;
     if (group != 32 && group != 64 && group != 128) return false;
     if (bits == 8 && group == 128) return false;
     if (rows == 0 || cols == 0 || cols % group != 0 || batch < 1 || batch > 4) return false;
     const uint32_t ngroups = cols / group;
-    if (ngroups % 8 != 0) return false;  // 16-byte metadata rows for cp.async
+    const uint32_t mstride = meta_stride != 0 ? meta_stride : ngroups;
+    if (mstride % 8 != 0 || mstride < ngroups) return false;  // 16-byte metadata rows for the tensor maps
     const uint32_t win_cols = 8 * group > 512 ? 8 * group : 512;
     const uint32_t wg = win_cols / group;
     const int nwin = (int)((cols + win_cols - 1) / win_cols);
@@ -325,7 +326,7 @@ int mma_layout_groups(uint32_t bits, uint32_t group, uint32_t cols, uint32_t bat
 // The tensor-core kernel takes this call: a launch plan and 16-byte aligned
 // weights and metadata (TMA and cp.async sources).
 bool mma_takes(const FastCall &c, MmaPlan *p) {
-    if (!mma_plan(c.bits, c.group, c.rows, c.cols, c.batch, c.epilogue, c.bf16, p)) return false;
+    if (!mma_plan(c.bits, c.group, c.rows, c.cols, c.batch, c.epilogue, c.bf16, p, c.meta_stride)) return false;
     if (!aligned16(c.w) || !aligned16(c.s) || !aligned16(c.b)) return false;
     if (c.epilogue == 1 && (!aligned16(c.w2) || !aligned16(c.s2) || !aligned16(c.b2))) return false;
     // The fused RMSNorm needs the whole row in one prep CTA per RHS.
@@ -409,7 +410,7 @@ int run_fast(const FastCall &c, cudaStream_t stream) {
         if (!mma_takes(call, &plan))
             return fail(QMR_EUNSUPPORTED, "the exchange calls need a shape the tensor-core kernel takes");
     }
-    const bool fused = call.norm_w != nullptr || call.resid != nullptr;
+    const bool fused = call.norm_w != nullptr || call.resid != nullptr || call.meta_stride != 0;
     if (fused && !mma_takes(call, &plan))
         return fail(QMR_EUNSUPPORTED, "the fused RMSNorm/residual epilogue needs a shape the tensor-core kernel takes");
     if (fused) call.path = kPathMma;

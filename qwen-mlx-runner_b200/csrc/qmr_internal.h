@@ -37,6 +37,10 @@ struct FastCall {
     const float *norm_w;
     float eps;
     const float *resid;
+    // Metadata elements per row (0: cols / group).  A larger, 8-aligned
+    // stride lets a column slice of a matrix keep 16-byte metadata rows;
+    // tensor-core path only.
+    uint32_t meta_stride;
 };
 // The tensor-core path takes this call with the fused RMSNorm / residual
 // epilogue (false: the caller must run them as separate kernels).

@@ -147,6 +147,12 @@ SIGNATURES = {
     "qmr_model_mlp_r2_eligible": (_int, [_vp, ctypes.POINTER(_u32)]),
     "qmr_model_metadata_stats": (_int, [_vp, ctypes.POINTER(_u64), ctypes.POINTER(_u64)]),
     "qmr_model_step_launches": (_int, [_vp, ctypes.POINTER(_u32), ctypes.POINTER(_u32)]),
+    "qmr_model_synthetic_sharded": (_int, [ctypes.POINTER(QmrModelConfig), _u64, _u32, _u32, _u32,
+                                           ctypes.POINTER(_vp)]),
+    "qmr_model_exchange_handle": (_int, [_vp, _vp]),
+    "qmr_model_exchange_open": (_int, [_vp, _vp]),
+    "qmr_model_shard": (_int, [_vp, ctypes.POINTER(_u32), ctypes.POINTER(_u32), ctypes.POINTER(_u32),
+                               ctypes.POINTER(_u32)]),
 }
 
 

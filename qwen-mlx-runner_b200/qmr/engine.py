@@ -135,12 +135,56 @@ class Engine:
         check(_lib.lib().qmr_model_synthetic(ctypes.byref(s), seed, context, ctypes.byref(h)))
         return cls(h)
 
+    @classmethod
+    def synthetic_sharded(cls, cfg: dict, seed: int, context: int, group=None) -> "Engine":
+        """The synthetic model split over the ranks of a torch.distributed
+        group, one process per GPU (tensor-parallel decode, include/qmr.h
+        "tensor-parallel decode"): every rank calls this together; the IPC
+        handles of the ranks' exchange memory travel through
+        all_gather_object.  Afterwards every rank makes the same calls and
+        gets the same tokens; logits are the rank's vocabulary rows."""
+        import torch.distributed as dist
+        L = _lib.lib()
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        h = ctypes.c_void_p()
+        s = to_struct(cfg)
+        check(L.qmr_model_synthetic_sharded(ctypes.byref(s), seed, context, world, rank, ctypes.byref(h)))
+        eng = cls(h)
+        eng._group, eng._sharded = group, world > 1
+        if world > 1:
+            mine = ctypes.create_string_buffer(_lib.QMR_IPC_HANDLE_BYTES)
+            check(L.qmr_model_exchange_handle(h, mine))
+            handles = [None] * world
+            dist.all_gather_object(handles, mine.raw, group=group)
+            dist.barrier(group)
+            allh = ctypes.create_string_buffer(b"".join(handles), world * _lib.QMR_IPC_HANDLE_BYTES)
+            check(L.qmr_model_exchange_open(h, allh))
+        return eng
+
+    @property
+    def shard(self):
+        """(world, rank, first vocabulary row, vocabulary rows) of this rank."""
+        a, b, c, d = (ctypes.c_uint32() for _ in range(4))
+        check(_lib.lib().qmr_model_shard(self._h, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c), ctypes.byref(d)))
+        return a.value, b.value, c.value, d.value
+
     def close(self):
+        """Free the model.  A sharded model's peers may still be writing into
+        its exchange memory until they finish their last step, so its ranks
+        synchronise (device, then a barrier of its group) first."""
         if getattr(self, "_h", None):
+            if getattr(self, "_sharded", False):
+                import torch
+                import torch.distributed as dist
+                torch.cuda.synchronize()
+                dist.barrier(self._group)
             _lib.lib().qmr_model_free(self._h)
             self._h = None
 
-    __del__ = close
+    def __del__(self):
+        if getattr(self, "_h", None):
+            _lib.lib().qmr_model_free(self._h)
+            self._h = None
 
     def reset(self) -> None:
         check(_lib.lib().qmr_model_reset(self._h))
@@ -152,8 +196,9 @@ class Engine:
         return p.value
 
     def forward(self, token: int, logits: bool = True):
-        """Engine::forward: (logits f32 [vocab] or None, greedy next token)."""
-        out = np.empty(self.config["vocab"], dtype=np.float32) if logits else None
+        """Engine::forward: (logits f32 [vocab] or None, greedy next token);
+        a sharded model returns its vocabulary rows."""
+        out = np.empty(self.shard[3], dtype=np.float32) if logits else None
         nxt = ctypes.c_int32()
         check(_lib.lib().qmr_model_forward(self._h, token, out.ctypes.data if logits else None, ctypes.byref(nxt)))
         return out, nxt.value
@@ -173,7 +218,7 @@ class Engine:
         None, greedy argmax per row); the state stays tentative until commit_block_prefix."""
         t = np.ascontiguousarray(tokens, dtype=np.uint32)
         n = t.size
-        lg = np.empty((n, self.config["vocab"]), dtype=np.float32) if logits else None
+        lg = np.empty((n, self.shard[3]), dtype=np.float32) if logits else None
         am = np.empty(n, dtype=np.int32)
         check(_lib.lib().qmr_model_verify_block(self._h, t.ctypes.data, n, lg.ctypes.data if logits else None,
                                                 am.ctypes.data))
