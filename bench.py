@@ -22,7 +22,8 @@ The same JSON line also carries, measured in the same run:
   * `decode`: config 4, the synthetic 64-layer 27B-shaped hybrid: prefill a
     seeded 512-token prompt and greedily decode 128 tokens at context 4096
     through the engine (qmr_model_generate), decode tokens/s; under
-    torchrun one replica per rank.
+    torchrun the model split tensor-parallel over the ranks (one token
+    stream for the job, strong scaling).
 
 Multi-GPU headline: one process per GPU (torchrun); each rank runs the b3
 call on its own weights (independent matrices, no data-path collective),
@@ -622,9 +623,12 @@ def decode_bytes_per_token(cfg):
 
 
 def decode_record(device, world, rank, peak, cpu_baseline, n_prompt=512, n_new=128):
-    """Config 4 on each rank's GPU: prefill a seeded 512-token prompt, then
-    greedily decode 128 tokens at context 4096 (one replica per rank; the
-    head-sharded multi-GPU decode is not built)."""
+    """Config 4: prefill a seeded 512-token prompt, then greedily decode 128
+    tokens at context 4096.  One GPU: the whole model.  N GPUs: the model
+    split tensor-parallel over the N ranks (qmr_model_synthetic_sharded:
+    heads, MLP rows and vocabulary divided, partial sums all-reduced by the
+    streaming kernels' peer-memory exchange), one token stream for the job,
+    so tokens/s is strong-scaling."""
     DECODE_PROMPT, DECODE_NEW = n_prompt, n_new
     import torch
 
@@ -633,7 +637,10 @@ def decode_record(device, world, rank, peak, cpu_baseline, n_prompt=512, n_new=1
     from qmr import synth
     torch.cuda.empty_cache()
     cfg = qeng.qwen27b_config()
-    eng = qmr.Engine.synthetic(cfg, 4242, DECODE_CONTEXT)
+    if world > 1:
+        eng = qmr.Engine.synthetic_sharded(cfg, 4242, DECODE_CONTEXT)
+    else:
+        eng = qmr.Engine.synthetic(cfg, 4242, DECODE_CONTEXT)
     prompt = [int(v % cfg["vocab"]) for v in synth.splitmix64(77, DECODE_PROMPT)]
     eng.generate(prompt[:16], 8)  # untimed warm-up
     eng.reset()
@@ -657,21 +664,27 @@ def decode_record(device, world, rank, peak, cpu_baseline, n_prompt=512, n_new=1
         m_toks, rounds, acc, _, m_dec = eng.mtp_generate(prompt, DECODE_NEW, 3, drafts)
         m_max = max_over_ranks(m_dec, device, world)
         mtp[label] = {"rounds": rounds, "drafts_accepted": acc, "rounds_per_s": round(rounds / (m_max * 1e-3), 2),
-                      "tok_s": round(world * (DECODE_NEW - 1) / (m_max * 1e-3), 2),
+                      "tok_s": round((DECODE_NEW - 1) / (m_max * 1e-3), 2),
                       "ms_per_round": round(m_max / rounds, 4), "same_tokens_as_plain": m_toks == toks}
+    same_tokens = True
+    if world > 1:
+        import torch.distributed as dist
+        every = [None] * world
+        dist.all_gather_object(every, toks)
+        same_tokens = all(t == every[0] for t in every)
     eng.close()
     nbytes = decode_bytes_per_token(cfg)
-    per_gpu_tps = (DECODE_NEW - 1) / (dec_max * 1e-3)
+    tps = (DECODE_NEW - 1) / (dec_max * 1e-3)
     rec = {"workload": "synthetic 64-layer Qwen3.5-27B-shaped hybrid (3:1 DeltaNet:attention), Q4/g64 BF16 "
                        "metadata, distinct seeded weights, vocabulary 152064, FP32 activations/state/KV",
            "prompt_tokens": DECODE_PROMPT, "new_tokens": DECODE_NEW, "context": DECODE_CONTEXT,
-           "decode_tok_s": round(world * per_gpu_tps, 2), "decode_tok_s_per_gpu": round(per_gpu_tps, 2),
-           "ms_per_token": round(dec_max / (DECODE_NEW - 1), 4),
-           "prefill_tok_s": round(world * DECODE_PROMPT / (pre_max * 1e-3), 2),
-           "bytes_per_token": nbytes, "gbs_per_gpu": round(nbytes * per_gpu_tps / 1e9, 2),
-           "frac_per_gpu": round(nbytes * per_gpu_tps / 1e9 / peak, 4),
+           "decode_tok_s": round(tps, 2), "ms_per_token": round(dec_max / (DECODE_NEW - 1), 4),
+           "prefill_tok_s": round(DECODE_PROMPT / (pre_max * 1e-3), 2),
+           "bytes_per_token": nbytes, "gbs_per_gpu": round(nbytes / world * tps / 1e9, 2),
+           "frac_per_gpu": round(nbytes / world * tps / 1e9 / peak, 4),
            "launches_per_token": with_head, "launches_per_prefill_token": without,
-           "parallelism": f"replicas{world}" if world > 1 else "single",
+           "parallelism": f"tp{world}" if world > 1 else "single", "scaling": "strong",
+           "tokens_identical_across_ranks": same_tokens,
            "first_tokens": toks[:8],
            "mtp_b3": dict(mtp, block=3, note="tok/s counts the 127 tokens after the first (the prompt's last step "
                                              "emits it); timed over the verification rounds")}
@@ -710,7 +723,7 @@ def run_decode(args):
                         args.decode_new)
     if rank == 0:
         print(json.dumps({"metric": "synthetic decode tokens/s", "value": rec["decode_tok_s"], "unit": "tok/s",
-                          "n_gpus": world, "higher_is_better": True, "scaling": "weak", "decode": rec}), flush=True)
+                          "n_gpus": world, "higher_is_better": True, "scaling": "strong", "decode": rec}), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

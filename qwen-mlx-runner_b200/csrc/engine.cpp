@@ -97,6 +97,9 @@ struct QmrModel {
     QmrExchange xch[2] = {}, hxch = {};
     bool opened = true;   // sharded models are usable after qmr_model_exchange_open
     int xpar = 0;         // slot buffer of the next partial-sum exchange while recording
+    // While recording: the partial-sum exchange whose all-reduce into x is
+    // still to come (folded into the prep of the next matrix that reads x).
+    const QmrExchange *pending_reduce = nullptr;
     uint32_t context = 0;
     std::vector<LayerState> layers;
     DevMat embed, head;
@@ -357,6 +360,8 @@ struct StepCounter {
 // y = W x for the engine, with the optional fused input RMSNorm (norm_w) and
 // residual (resid == y), gate/up SwiGLU (epi 1, up = second matrix) or head
 // argmax (epi 2, into argmax).
+int flush_reduce(QmrModel *m, StepCounter *cnt, int nq);
+
 int mat_call(QmrModel *m, const DevMat &W, const float *x, float *y, const float *norm_w, const float *resid, int epi,
              const DevMat *up, int32_t *argmax, StepCounter *cnt, int nq = 1) {
     FastCall c = {};
@@ -383,16 +388,20 @@ int mat_call(QmrModel *m, const DevMat &W, const float *x, float *y, const float
     c.scratch_bytes = m->scratch_size;
     c.eps = m->cfg.rms_eps;
     c.meta_stride = W.mstride;
-    if (norm_w != nullptr || resid != nullptr) {
+    const bool reduce = m->pending_reduce != nullptr && x == m->x;
+    if (norm_w != nullptr || resid != nullptr || reduce) {
         FastCall f = c;
         f.norm_w = norm_w;
         f.resid = resid;
+        f.reduce = reduce ? m->pending_reduce : nullptr;
         if (fused_supported(f)) {
-            cnt->n += 2;  // activation prep + streaming kernel
+            if (reduce) m->pending_reduce = nullptr;
+            cnt->n += 2;  // activation prep (with the all-reduce) + streaming kernel
             return run_fast(f, m->stream);
         }
     }
-    int rc = QMR_OK;
+    int rc = reduce ? flush_reduce(m, cnt, nq) : QMR_OK;
+    if (rc != QMR_OK) return rc;
     if (norm_w != nullptr) {
         for (int t = 0; t < nq && rc == QMR_OK; ++t) {
             rc = launch_rms_norm(x + (size_t)t * W.cols, norm_w, m->normed + (size_t)t * W.cols, W.cols,
@@ -420,15 +429,33 @@ int mat_call(QmrModel *m, const DevMat &W, const float *x, float *y, const float
     return rc;
 }
 
+// The pending all-reduce as its own launches: the bounded wait for every
+// rank's epoch, then the rank-ordered sum of the slots into x.
+int flush_reduce(QmrModel *m, StepCounter *cnt, int nq) {
+    const QmrExchange *ex = m->pending_reduce;
+    if (ex == nullptr) return QMR_OK;
+    m->pending_reduce = nullptr;
+    int rc = launch_exchange_wait(*ex, (uint32_t)nq, nullptr, nullptr, m->stream);
+    ++cnt->n;
+    if (rc == QMR_OK) rc = launch_partial_sum(m->x, ex->out[ex->rank], (int)m->world, (int)m->lc.hidden_size, nq, m->stream);
+    ++cnt->n;
+    return rc;
+}
+
 // x += W in for the matrices that feed the residual stream (out_proj,
 // o_proj, down_proj).  One GPU: the residual epilogue.  Split over ranks:
 // W is this rank's column slice, its partial product goes through the
-// exchange into slot `rank` of every rank's slot buffer (the two buffers
-// alternate, so a rank one exchange ahead never overwrites slots a peer
-// has not summed yet), then the bounded wait for every rank's epoch and the
-// rank-ordered sum into x.
+// exchange into slot `rank` of every rank's slot buffer; the all-reduce
+// into x (bounded wait for every rank's epoch, rank-ordered sum of the
+// slots) is folded into the prep of the next matrix that reads x, or runs
+// as its own launches at the end of the step.  Every exchange is thus
+// waited for before the next one is issued, and the two slot buffers
+// alternate, so a rank one exchange ahead never overwrites slots that a
+// peer has not summed yet.
 int mat_reduce(QmrModel *m, const DevMat &W, const float *in, StepCounter *cnt, int nq) {
     if (m->world == 1) return mat_call(m, W, in, m->x, nullptr, m->x, 0, nullptr, nullptr, cnt, nq);
+    int rc = flush_reduce(m, cnt, nq);  // none pending in the step's order (in -> out, gate/up -> down)
+    if (rc != QMR_OK) return rc;
     const QmrExchange &ex = m->xch[m->xpar];
     m->xpar ^= 1;
     FastCall c = {};
@@ -449,12 +476,9 @@ int mat_reduce(QmrModel *m, const DevMat &W, const float *in, StepCounter *cnt, 
     c.scratch_bytes = m->scratch_size;
     c.meta_stride = W.mstride;
     c.ex = &ex;
-    int rc = run_fast(c, m->stream);
+    rc = run_fast(c, m->stream);
     cnt->n += 2;
-    if (rc == QMR_OK) rc = launch_exchange_wait(ex, (uint32_t)nq, nullptr, nullptr, m->stream);
-    ++cnt->n;
-    if (rc == QMR_OK) rc = launch_partial_sum(m->x, ex.out[ex.rank], (int)m->world, (int)m->lc.hidden_size, nq, m->stream);
-    ++cnt->n;
+    m->pending_reduce = &ex;
     return rc;
 }
 
@@ -486,6 +510,8 @@ int head_call(QmrModel *m, int32_t *argmax, StepCounter *cnt, int nq) {
     c.norm_w = m->final_norm;
     c.eps = m->cfg.rms_eps;
     c.ex = &m->hxch;
+    c.reduce = m->pending_reduce;
+    m->pending_reduce = nullptr;
     int rc = run_fast(c, m->stream);
     cnt->n += 2;
     if (rc == QMR_OK) rc = launch_exchange_wait(m->hxch, (uint32_t)nq, argmax, nullptr, m->stream);
@@ -568,6 +594,8 @@ int record_step(QmrModel *m, StepKind kind, int nq, StepCounter *cnt) {
         if (rc == QMR_OK) rc = mat_reduce(m, L.down, m->act, cnt, nq);
     }
     if (rc == QMR_OK && kind != kStepPlain) rc = head_call(m, block ? m->block_argmax : &m->ctrl->token, cnt, nq);
+    if (rc == QMR_OK) rc = flush_reduce(m, cnt, nq);  // a step without the head: the last down's all-reduce
+    m->pending_reduce = nullptr;
     if (rc == QMR_OK && !block) {
         rc = launch_advance(m->ctrl, m->out, m->out_cap, kind == kStepHead, m->stream);
         ++cnt->n;
@@ -672,6 +700,7 @@ int ensure_block(QmrModel *m, int nq) {
         if (rc != QMR_OK) return rc;
     }
     rc = head_call(m, m->block_argmax, &warm, nq);
+    if (rc == QMR_OK) rc = flush_reduce(m, &warm, nq);
     if (rc == QMR_OK) rc = cuda_check(cudaStreamSynchronize(m->stream), "block warm-up");
     for (int kind = 0; kind < 2 && rc == QMR_OK; ++kind) {
         StepCounter cnt;

@@ -85,6 +85,12 @@ void scratch_layout(void *base, int bits, uint32_t cols, uint32_t batch, Scratch
         mv->norm_w = nullptr;
         mv->eps = 0.0f;
         mv->row_scale = row_scale;
+        mv->red_slots = nullptr;
+        mv->red_x = nullptr;
+        mv->red_flags = nullptr;
+        mv->red_epoch = nullptr;
+        mv->red_err = nullptr;
+        mv->red_world = 0;
         const size_t padded = ((size_t)cols + 1023) / 1024 * 1024;
         mv->image = reinterpret_cast<__half *>(p);
         mv->table = reinterpret_cast<float *>(p + align_up(padded * 4 * batch));
@@ -410,7 +416,7 @@ int run_fast(const FastCall &c, cudaStream_t stream) {
         if (!mma_takes(call, &plan))
             return fail(QMR_EUNSUPPORTED, "the exchange calls need a shape the tensor-core kernel takes");
     }
-    const bool fused = call.norm_w != nullptr || call.resid != nullptr || call.meta_stride != 0;
+    const bool fused = call.norm_w != nullptr || call.resid != nullptr || call.meta_stride != 0 || call.reduce != nullptr;
     if (fused && !mma_takes(call, &plan))
         return fail(QMR_EUNSUPPORTED, "the fused RMSNorm/residual epilogue needs a shape the tensor-core kernel takes");
     if (fused) call.path = kPathMma;
@@ -423,6 +429,18 @@ int run_fast(const FastCall &c, cudaStream_t stream) {
         scratch_layout(base, (int)call.bits, call.cols, call.batch, &sv, &mv);
         mv.norm_w = call.norm_w;
         mv.eps = call.eps;
+        if (call.reduce != nullptr) {
+            const QmrExchange &r = *call.reduce;
+            if (r.total_rows != r.world * call.cols || call.batch > 4)
+                return fail(QMR_EINVAL, "the folded all-reduce needs slots of [batch][world][cols]");
+            mv.red_slots = r.out[r.rank];
+            mv.red_x = const_cast<float *>(call.x);
+            mv.red_flags = r.flags[r.rank];
+            mv.red_epoch = r.epoch;
+            mv.red_err = device_error_word();
+            mv.red_world = (int)r.world;
+            if (mv.red_err == nullptr) return fail(QMR_ECUDA, "device error word is unavailable");
+        }
         const int rc = launch_mma_prep_bits((int)call.bits, call.x, call.cols, call.group, call.batch,
                                             plan.ngroups_pad, mv, stream);
         if (rc != QMR_OK) return rc;

@@ -132,6 +132,17 @@ struct MmaImageView {
     const float *norm_w;
     float eps;
     float *row_scale;
+    // An all-reduce of partial sums folded in front of the prep (red_slots
+    // null: none): wait, bounded, until every one of red_world ranks has
+    // published epoch *red_epoch in red_flags, then x[b] += slots[b][r] for
+    // r = 0 .. red_world-1 in rank order (slots [batch][red_world][cols]),
+    // written back to x (red_x) before the prep uses it.
+    const float *red_slots;
+    float *red_x;
+    const unsigned int *red_flags;
+    const unsigned int *red_epoch;
+    unsigned int *red_err;
+    int red_world;
 };
 
 // ---- activation image arithmetic (the prep kernel's) ----
@@ -238,8 +249,8 @@ __device__ __forceinline__ float2 act_table_entry(int E, float sum, bool zero) {
 constexpr int kPrepGroupsPerCta = 128;
 
 template <int BITS, int G>
-__global__ void __launch_bounds__(4 * kPrepGroupsPerCta) mma_prep_kernel(const float *__restrict__ x, int cols,
-                                                                         int batch, int ngroups_pad, MmaImageView v) {
+__global__ void __launch_bounds__(4 * kPrepGroupsPerCta) mma_prep_kernel(const float *x, int cols, int batch,
+                                                                         int ngroups_pad, MmaImageView v) {
     // Launched behind the previous kernel (programmatic dependent launch): let
     // the streaming kernel launch now, then wait for x and for the previous
     // user of this scratch before touching either.
@@ -263,6 +274,38 @@ __global__ void __launch_bounds__(4 * kPrepGroupsPerCta) mma_prep_kernel(const f
     // Every lane takes part in the quad shuffles of act_quad_stats.
     const int g = blockIdx.x * kPrepGroupsPerCta + (tid >> 2), t = tid & 3;
     const bool here = g < ngroups_pad, real = g < ngroups;
+    if (v.red_slots != nullptr) {
+        // The ranks' epochs: the first warp acquires them (bounded; after a
+        // wait has run out anywhere, later waits return at once), the CTA
+        // barrier then orders every thread's slot reads after the acquire.
+        if (tid < 32 && *(volatile unsigned int *)v.red_err == 0u) {
+            const unsigned int e = *v.red_epoch;
+            if (tid < v.red_world) {
+                const unsigned long long start = global_ns();
+                for (;;) {
+                    unsigned int f;
+                    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(v.red_flags + tid) : "memory");
+                    if ((int)(f - e) >= 0) break;
+                    if (global_ns() - start > kWaitLimitNs) {
+                        atomicCAS(v.red_err, 0u, kErrTimeoutPeer);
+                        break;
+                    }
+                    __nanosleep(100);
+                }
+            }
+        }
+        __syncthreads();
+        if (real) {
+            float *xl = v.red_x + (size_t)b * cols + (size_t)g * G + t * CPL;
+            const float *sl = v.red_slots + ((size_t)b * v.red_world * cols) + (size_t)g * G + t * CPL;
+#pragma unroll
+            for (int k = 0; k < CPL; ++k) {
+                float acc = __ldcg(sl + k);
+                for (int r = 1; r < v.red_world; ++r) acc = __fadd_rn(acc, __ldcg(sl + (size_t)r * cols + k));
+                xl[k] = __fadd_rn(xl[k], acc);
+            }
+        }
+    }
     float v_[CPL];
 #pragma unroll
     for (int k = 0; k < CPL; ++k) v_[k] = 0.0f;

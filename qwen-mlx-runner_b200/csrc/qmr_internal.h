@@ -41,6 +41,10 @@ struct FastCall {
     // stride lets a column slice of a matrix keep 16-byte metadata rows;
     // tensor-core path only.
     uint32_t meta_stride;
+    // An exchange of partial sums to all-reduce into x before it is used
+    // (the prep waits for every rank's epoch and adds the slots [batch]
+    // [world][cols] in rank order, writing x back); tensor-core path only.
+    const QmrExchange *reduce;
 };
 // The tensor-core path takes this call with the fused RMSNorm / residual
 // epilogue (false: the caller must run them as separate kernels).

@@ -11,8 +11,8 @@ What must hold:
   the single-GPU engine's bound (the all-reduce sums the ranks' partial
   products in rank order, a different order from one GPU's, so the bits
   are not required to equal the unsharded engine's);
-* the step graph holds the extra wait and sum launches of the 2 all-reduces
-  per layer and the head's key wait.
+* the step graph holds the one-GPU launches plus the head's key wait: the
+  all-reduces ride in the activation prep of the next matrix that reads x.
 
 Each world size is skipped when the box has fewer GPUs.  Shapes: the small
 layer graph at 2 ranks (column slices of 4 groups, padded metadata rows),
@@ -142,7 +142,8 @@ def test_sharded_decode_gives_the_oracle_tokens_on_every_rank(name, world):
         scale = np.max(np.abs(want_lgs), axis=1, keepdims=True)
         err = np.max(np.abs(x["lgs"] - want) / scale)
         assert err <= tol, (r, err)
-        # embed + per layer (in-proj, mixer, 2 x (K-split matmul, wait, sum), gate/up)
-        # + head (prep, matmul, key wait) + advance.
+        # embed + per layer (in-proj, mixer, out, gate/up, down: prep + matmul each; the
+        # all-reduces ride in the next prep) + head (prep, matmul, key wait) + advance;
+        # without the head, the last all-reduce runs as wait + sum.
         with_head, without = x["launches"].tolist()
-        assert with_head == 1 + 13 * L + 3 + 1 and without == with_head - 3
+        assert with_head == 1 + 9 * L + 3 + 1 and without == with_head - 1
