@@ -296,14 +296,17 @@ class Workload:
             self.mats = [(_clone(g0), _clone(u0), _clone(d0)) for _ in range(self.copies)]
             self.act = torch.empty(b * ROWS, dtype=torch.float32, device=device)
             self.y = torch.empty(b * COLS, dtype=torch.float32, device=device)
-            self.launches_per_step = 4  # prep + fused gate/up, prep + down
+            # fused gate/up, down: each streaming kernel builds its activation image
+            self.launches_per_step = 2
         else:
             m0 = _synth_matrix(spec["rows"], spec["cols"], bits, seed + 10, device)
             self.copies = _copies(self.l2, m0.nbytes)
             self.mats = [_clone(m0) for _ in range(self.copies)]
             self.y = torch.empty(b * spec["rows"], dtype=torch.float32, device=device)
             self.idx = torch.empty(b, dtype=torch.int32, device=device)
-            self.launches_per_step = 2  # activation prep + streaming kernel
+            # the streaming kernel (building its activation image); the head's
+            # argmax epilogue keeps the separate activation prep
+            self.launches_per_step = 2 if name == "head" else 1
 
     def shard_seed(self, r):
         return self.seed + 100 * r
@@ -325,8 +328,9 @@ class Workload:
             self.mods = [parallel.ShardedMLP(_clone(g0), _clone(u0), _clone(d0), COLS, ROWS, qmr.ops,
                                              exchange=self.exchange) for _ in range(self.copies)]
             self.y = torch.empty(b * COLS, dtype=torch.float32, device=dev)
-            # prep + gate/up + exchange wait, prep + down + exchange wait (p2p)
-            self.launches_per_step = 6 if self.exchange == "p2p" else 4
+            # p2p: prep + gate/up + exchange wait, prep + down + exchange wait;
+            # nccl: gate/up and down, each building its image (+ NCCL's own kernels)
+            self.launches_per_step = 6 if self.exchange == "p2p" else 2
         else:
             v0, v1 = parallel.shard_range(VOCAB, world, rank)
             h = _synth_matrix(v1 - v0, COLS, 4, s + 10, dev)

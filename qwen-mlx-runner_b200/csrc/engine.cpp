@@ -396,7 +396,7 @@ int mat_call(QmrModel *m, const DevMat &W, const float *x, float *y, const float
         f.reduce = reduce ? m->pending_reduce : nullptr;
         if (fused_supported(f)) {
             if (reduce) m->pending_reduce = nullptr;
-            cnt->n += 2;  // activation prep (with the all-reduce) + streaming kernel
+            f.launch_count = &cnt->n;
             return run_fast(f, m->stream);
         }
     }
@@ -413,8 +413,8 @@ int mat_call(QmrModel *m, const DevMat &W, const float *x, float *y, const float
     }
     if (resid != nullptr) c.y = m->tmp;
     if (fast_eligible(W.w, W.cols, W.bits, W.group)) {
+        c.launch_count = &cnt->n;
         rc = run_fast(c, m->stream);
-        cnt->n += 2;
     } else if (epi == 0) {
         rc = run_generic(W.w, W.s, W.b, c.x, c.y, W.rows, W.cols, W.bits, W.group, (uint32_t)nq, W.bf16, m->stream);
         cnt->n += 1;
@@ -476,8 +476,8 @@ int mat_reduce(QmrModel *m, const DevMat &W, const float *in, StepCounter *cnt, 
     c.scratch_bytes = m->scratch_size;
     c.meta_stride = W.mstride;
     c.ex = &ex;
+    c.launch_count = &cnt->n;
     rc = run_fast(c, m->stream);
-    cnt->n += 2;
     m->pending_reduce = &ex;
     return rc;
 }
@@ -512,8 +512,8 @@ int head_call(QmrModel *m, int32_t *argmax, StepCounter *cnt, int nq) {
     c.ex = &m->hxch;
     c.reduce = m->pending_reduce;
     m->pending_reduce = nullptr;
+    c.launch_count = &cnt->n;
     int rc = run_fast(c, m->stream);
-    cnt->n += 2;
     if (rc == QMR_OK) rc = launch_exchange_wait(m->hxch, (uint32_t)nq, argmax, nullptr, m->stream);
     ++cnt->n;
     return rc;

@@ -190,6 +190,10 @@ int QMR_MMA_LAUNCH(const FastCall &c, const MmaPlan &p, const ScratchView &sv, c
     a.zero = 0u;
     a.row_scale = c.norm_w != nullptr ? v.row_scale : nullptr;
     a.resid = c.resid;
+    a.x = c.x;
+    a.norm_w = c.norm_w;
+    a.eps = c.eps;
+    a.build = c.build ? 1 : 0;
     switch (c.epilogue) {
         case 0: return launch_e<0>(maps, a, p, c.bf16, c.group, c.batch, c.overlap, stream);
         case 1: return launch_e<1>(maps, a, p, c.bf16, c.group, c.batch, c.overlap, stream);

@@ -399,6 +399,17 @@ int run_stream(const FastCall &c, void *base, cudaStream_t stream) {
     return launch_reg(a, (int)c.bits, c.bf16, c.batch, c.epilogue, c.overlap, stream);
 }
 
+// x in device memory (every streaming CTA may read it); pinned host
+// activations are read once, by the prep kernel.
+bool device_resident(const void *p) {
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return false;
+    }
+    return at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
+}
+
 int run_fast(const FastCall &c, cudaStream_t stream) {
     const size_t need = scratch_bytes((int)c.bits, c.cols, c.batch);
     void *base = c.scratch;
@@ -422,11 +433,23 @@ int run_fast(const FastCall &c, cudaStream_t stream) {
     if (fused) call.path = kPathMma;
     if (call.path == kPathMma && !mma_takes(call, &plan)) call.path = kPathTile;  // FP32 kernels take the rest
     if (call.path == kPathMma) {
-        // Prep kernel, then the streaming kernel behind it (programmatic
-        // dependent launch: the prep writes no weights), one plan for both.
         ScratchView sv;
         MmaImageView mv;
         scratch_layout(base, (int)call.bits, call.cols, call.batch, &sv, &mv);
+        // Calls without an argmax or exchange epilogue and without a folded
+        // all-reduce: the streaming CTAs build the image themselves, one
+        // launch behind the producer of x.  (The argmax and exchange
+        // epilogues count CTAs on scratch words that the prep clears.)
+        call.build = call.epilogue != 2 && call.ex == nullptr && call.reduce == nullptr &&
+                     (call.norm_w == nullptr || plan.kc == 1) && device_resident(call.x);
+        if (call.build) {
+            call.overlap = true;
+            if (call.launch_count != nullptr) *call.launch_count += 1;
+            return call.bits == 4 ? launch_mma4(call, plan, sv, mv, stream) : launch_mma8(call, plan, sv, mv, stream);
+        }
+        if (call.launch_count != nullptr) *call.launch_count += 2;
+        // Prep kernel, then the streaming kernel behind it (programmatic
+        // dependent launch: the prep writes no weights), one plan for both.
         mv.norm_w = call.norm_w;
         mv.eps = call.eps;
         if (call.reduce != nullptr) {
@@ -447,6 +470,7 @@ int run_fast(const FastCall &c, cudaStream_t stream) {
         call.overlap = true;
         return call.bits == 4 ? launch_mma4(call, plan, sv, mv, stream) : launch_mma8(call, plan, sv, mv, stream);
     }
+    if (call.launch_count != nullptr) *call.launch_count += 2;
     const int rc = run_prepare(call.x, call.cols, call.bits, call.group, call.batch, base, call.path, stream);
     if (rc != QMR_OK) return rc;
     call.overlap = true;  // the preceding kernel is our prep, which writes no weights

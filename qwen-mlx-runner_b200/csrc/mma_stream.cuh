@@ -357,6 +357,95 @@ __global__ void __launch_bounds__(4 * kPrepGroupsPerCta) mma_prep_kernel(const f
     }
 }
 
+// The same image built by a streaming CTA in its own prologue, for the
+// groups of its column slice [g0, g0 + ng) and RHS 0..B-1, straight into its
+// shared memory (image blocks from the slice's first group; table rows
+// [B][ngroups_pad] at the global group index), with the functions the prep
+// kernel uses, so the image bits are the prep's.  The quads of the CTA take
+// the (group, RHS) items in turn.  norm_w (optional): the image holds
+// x * norm_w and rs[b] receives 1 / sqrt(mean(x_b^2) + eps) (the slice must
+// be the whole row).  Every thread of the CTA calls this; the caller
+// synchronises the CTA afterwards.
+template <int BITS, int G, int B, int NW>
+__device__ __forceinline__ void mma_build_image(const float *x, const float *norm_w, float eps, int ngroups,
+                                                int ngroups_pad, int g0, int ng, unsigned char *img_s,
+                                                unsigned char *tab_s, float *red, float *rs) {
+    using S = MmaShape<BITS, G>;
+    constexpr int CPL = S::CPL;
+    constexpr int NB = 2 * B;
+    constexpr int NQ = NW * 8;
+    const int tid = threadIdx.x, t = tid & 3, quad = tid >> 2;
+    const int cols = ngroups * G;
+    const int items = ng * B;
+    uint32_t *img = reinterpret_cast<uint32_t *>(img_s);
+    float2 *tab = reinterpret_cast<float2 *>(tab_s);
+    float ss[B];
+#pragma unroll
+    for (int k = 0; k < B; ++k) ss[k] = 0.0f;
+    for (int base = 0; base < items; base += NQ) {  // the same trip count in every warp
+        const int i = base + quad;
+        const bool here = i < items;
+        const int gl = here ? i / B : 0, b = here ? i % B : 0;
+        const int g = g0 + gl;
+        const bool real = here && g < ngroups;
+        float v[CPL];
+#pragma unroll
+        for (int k = 0; k < CPL; ++k) v[k] = 0.0f;
+        if (real) {
+            const float *xl = x + (size_t)b * cols + (size_t)g * G + t * CPL;
+            if ((reinterpret_cast<uintptr_t>(xl) & 15) == 0) {
+#pragma unroll
+                for (int k = 0; k < CPL / 4; ++k) {
+                    const float4 q = __ldcg(reinterpret_cast<const float4 *>(xl) + k);
+                    v[4 * k] = q.x;
+                    v[4 * k + 1] = q.y;
+                    v[4 * k + 2] = q.z;
+                    v[4 * k + 3] = q.w;
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < CPL; ++k) v[k] = __ldcg(xl + k);
+            }
+            if (norm_w != nullptr) {
+                const float *wl = norm_w + (size_t)g * G + t * CPL;
+                float sq = 0.0f;
+#pragma unroll
+                for (int k = 0; k < CPL; ++k) {
+                    sq = __fmaf_rn(v[k], v[k], sq);
+                    v[k] = __fmul_rn(v[k], __ldg(wl + k));
+                }
+#pragma unroll
+                for (int k = 0; k < B; ++k)
+                    if (k == b) ss[k] = __fadd_rn(ss[k], sq);
+            }
+        }
+        int E;
+        float sum;
+        act_quad_stats<CPL>(v, &E, &sum);
+        if (here) {
+            act_quad_store<BITS, G>(v, E, !real, img + (size_t)gl * S::NCH * NB * 16, NB, 2 * b, t);
+            if (t == 0) tab[(size_t)b * ngroups_pad + g] = act_table_entry(E, sum, !real);
+        }
+    }
+    if (norm_w != nullptr) {
+        // Fixed-order reduction: lanes by xor shuffle, then warps in order.
+        const int warp = tid >> 5;
+#pragma unroll
+        for (int k = 0; k < B; ++k) {
+            float r = ss[k];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, o));
+            if ((tid & 31) == 0) red[warp * 4 + k] = r;
+        }
+        __syncthreads();
+        if (tid < B) {
+            float total = 0.0f;
+            for (int w = 0; w < NW; ++w) total = __fadd_rn(total, red[w * 4 + tid]);
+            rs[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)cols), eps)));
+        }
+    }
+}
+
 // D = A * B + D and D = A * B (zero accumulator) for m16n8k16 f16 -> f32.
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                           uint32_t b0, uint32_t b1) {
@@ -457,6 +546,14 @@ struct MmaArgs {
     const unsigned char *s, *b, *s2, *b2;  // metadata [rows][ngroups] (f32 or bf16 bits)
     const __half *image;                   // prepared activation image
     const float *table;                    // [4][ngroups_pad] x (2^(24 - E_g), group sum)
+    // build != 0: no prepared image; every CTA builds its slice of the image
+    // in its prologue from x [B][cols] (mma_build_image), with the fused
+    // RMSNorm weight norm_w (optional; the output factor stays in shared
+    // memory; the plan must have kc == 1 then).
+    const float *x;
+    const float *norm_w;
+    float eps;
+    int build;
     float *y;
     unsigned long long *keys;              // [B] packed argmax (EPI 2)
     unsigned int *done;                    // CTAs finished (EPI 2)
@@ -587,10 +684,25 @@ __global__ void __launch_bounds__(32 * NW, 1)
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
 
-    // The activation image arrives window by window (the group-sum table with
-    // the first), so each warp starts as soon as its first window is in.
+    // The activation image: built here from x (the weights keep streaming
+    // into the rings meanwhile), or copied window by window from the
+    // prepared image (the group-sum table with the first window), so each
+    // warp starts as soon as its first window is in.
     bool ok = true;
-    if (U > 0 && threadIdx.x == 0) {
+    __shared__ float build_red[NW * 4];
+    __shared__ float build_rs[4];
+    // Windows of the image this warp has waited for (bit 0 also covers the
+    // table); all of them when the CTA built the image itself.
+    uint32_t img_ready = 0u;
+    if (a.build) {
+        if (U > 0) {  // CTA-uniform
+            mma_build_image<BITS, G, B, NW>(a.x, a.norm_w, a.eps, a.ngroups, a.ngroups_pad, win0 * S::WG,
+                                            nh * S::WG, smem + a.off_image, smem + a.off_table, build_red, build_rs);
+            fence_proxy_async();  // generic-proxy image writes before any later async-proxy use of shared memory
+            __syncthreads();
+        }
+        img_ready = ~0u;
+    } else if (U > 0 && threadIdx.x == 0) {
         const uint32_t chunk = (uint32_t)S::WG * XG;
         const uint32_t tab_bytes = 4u * (uint32_t)a.ngroups_pad * 8u;  // [4][ngroups_pad] float2
         const unsigned char *src = reinterpret_cast<const unsigned char *>(a.image) + (size_t)win0 * chunk;
@@ -600,9 +712,8 @@ __global__ void __launch_bounds__(32 * NW, 1)
             bulk_g2s(smem + a.off_image + (size_t)i * chunk, src + (size_t)i * chunk, chunk, &ibar[i], pol_keep);
         }
     }
-    // Windows of the image this warp has waited for (bit 0 also covers the
-    // table).
-    uint32_t img_ready = 0u;
+    // The output factor of the fused RMSNorm, per RHS (null: none).
+    const float *row_scale = a.build ? (a.norm_w != nullptr ? build_rs : nullptr) : a.row_scale;
 
     // Per-lane byte offsets: A words of row gq for the GPB groups of a box
     // line (128-byte swizzle: 16-byte unit u of row r at u ^ (r & 7)), the
@@ -630,8 +741,8 @@ __global__ void __launch_bounds__(32 * NW, 1)
                 if (row < a.rows) {
                     float val = v[0][h];
                     float up = v[NM - 1][h];
-                    if (a.row_scale != nullptr) {
-                        const float rs = a.row_scale[t];
+                    if (row_scale != nullptr) {
+                        const float rs = row_scale[t];
                         val = __fmul_rn(val, rs);
                         up = __fmul_rn(up, rs);
                     }
@@ -826,8 +937,9 @@ __global__ void __launch_bounds__(32 * NW, 1)
     }
 
     // Every image copy has landed before the CTA can exit (normally already
-    // waited for by the warps that read the window).
-    if (U > 0 && threadIdx.x == 0)
+    // waited for by the warps that read the window).  A CTA that built its
+    // image issued none.
+    if (U > 0 && threadIdx.x == 0 && !a.build)
         for (int i = 0; i < nh; ++i)
             if (!mbar_wait(&ibar[i], 0)) {
                 atomicCAS(a.err, 0u, kErrTimeoutDrain);

@@ -45,6 +45,11 @@ struct FastCall {
     // (the prep waits for every rank's epoch and adds the slots [batch]
     // [world][cols] in rank order, writing x back); tensor-core path only.
     const QmrExchange *reduce;
+    // Set by run_fast: the streaming CTAs build the activation image in
+    // their prologue from x (no prep kernel, no prepared image).
+    bool build;
+    // Optional: run_fast adds the number of kernels it launched.
+    uint32_t *launch_count;
 };
 // The tensor-core path takes this call with the fused RMSNorm / residual
 // epilogue (false: the caller must run them as separate kernels).

@@ -488,6 +488,31 @@ def test_prepared_activations_feed_several_matrices_bit_exactly(cuda):
             assert np.array_equal(a.cpu().numpy().view(np.uint32), b.cpu().numpy().view(np.uint32))
 
 
+@pytest.mark.parametrize("rows,cols", [(1024, 5120), (512, 17408)])
+def test_in_kernel_image_equals_the_prep_kernel_image(cuda, rows, cols):
+    """Device-resident x: every streaming CTA builds its slice of the
+    activation image in its prologue (one CTA per row slice at 5120 columns,
+    4-CTA clusters at 17408).  Pinned host x: the prep kernel builds it once.
+    Same image bits, same kernel and plan: the outputs agree bit for bit, for
+    the plain product and for the fused gate/up SwiGLU."""
+    g = synth.to_device(synth.affine_matrix(rows, cols, 4, 64, seed=61), rows, cols, 4, 64)
+    u = synth.to_device(synth.affine_matrix(rows, cols, 4, 64, seed=62), rows, cols, 4, 64)
+    for batch in (1, 4):
+        xs = synth.activations(batch, cols, seed=63 + batch).ravel()
+        xd = f32_tensor(xs)
+        xh = torch.from_numpy(xs.copy()).pin_memory()
+        outs = []
+        for x in (xd, xh):
+            y = torch.empty(batch * rows, dtype=torch.float32, device="cuda")
+            a = torch.empty(batch * rows, dtype=torch.float32, device="cuda")
+            qmr.matmul_affine(g, x, y, batch)
+            qmr.ops.gateup_swiglu(g, u, x, a, batch)
+            torch.cuda.synchronize()
+            outs.append((y.cpu().numpy().view(np.uint32), a.cpu().numpy().view(np.uint32)))
+        assert np.array_equal(outs[0][0], outs[1][0]), batch
+        assert np.array_equal(outs[0][1], outs[1][1]), batch
+
+
 def test_typed_wrappers_reject_undersized_views_before_launch(cuda):
     rows, cols = 64, 512
     m = synth.to_device(synth.affine_matrix(rows, cols, 4, 64, seed=3), rows, cols, 4, 64)

@@ -142,8 +142,9 @@ def test_sharded_decode_gives_the_oracle_tokens_on_every_rank(name, world):
         scale = np.max(np.abs(want_lgs), axis=1, keepdims=True)
         err = np.max(np.abs(x["lgs"] - want) / scale)
         assert err <= tol, (r, err)
-        # embed + per layer (in-proj, mixer, out, gate/up, down: prep + matmul each; the
-        # all-reduces ride in the next prep) + head (prep, matmul, key wait) + advance;
-        # without the head, the last all-reduce runs as wait + sum.
+        # embed + per layer (in-proj, mixer, out, gate/up, down: prep + matmul each, the
+        # all-reduces riding in the next prep; layer 0's in-proj has none to fold and builds
+        # its own image) + head (prep, matmul, key wait) + advance; without the head, the
+        # last all-reduce runs as wait + sum.
         with_head, without = x["launches"].tolist()
-        assert with_head == 1 + 9 * L + 3 + 1 and without == with_head - 1
+        assert with_head == 1 + 9 * L - 1 + 3 + 1 and without == with_head - 1
