@@ -212,15 +212,14 @@ bool mma_plan_b(uint32_t bits, uint32_t group, uint32_t rows, uint32_t cols, uin
     const int tiles = (int)((rows + kTileRows - 1) / kTileRows);
     const int nm = epi == 1 ? 2 : 1;
     const int sms = sm_count();
-    // Warps per CTA: 12 for long Q4 streams (groups of 32 or 64), where the per-unit instruction
-    // latency of 8 warps (2 per scheduler) limits the rate; 8 otherwise, where
-    // the deeper rings that 8 warps leave room for matter more (they fill
-    // while the call waits for its activations).  Chosen from the shape only.
+    // Warps per CTA: 12 for Q4 streams with groups of 32 or 64, where the
+    // per-unit instruction latency of 8 warps (2 per scheduler) limits the
+    // rate at every size (measured on dependent B1 chains, 1.5 to 50 MB per
+    // call); 8 for the gate/up pair (twice the registers per thread) and for
+    // Q8 and g128, whose deeper rings matter more.  Chosen from the shape only.
     for (int warps : {kMmaWarpsLong, kMmaWarps}) {
         if (only_warps != 0 && warps != only_warps) continue;
-        if (only_warps == 0 && warps == kMmaWarpsLong &&
-            (epi == 1 || bits != 4 || group > 64 || (long long)tiles * nwin < (long long)kLongUnitsPerCta * sms))
-            continue;
+        if (only_warps == 0 && warps == kMmaWarpsLong && (epi == 1 || bits != 4 || group > 64)) continue;
         // Column slices (= cluster size): the smallest kc whose activation slice
         // fits the image budget and whose whole plan (rings of at least two
         // stages, image, table, pieces) fits the shared memory of one SM.  Two
@@ -440,8 +439,7 @@ int run_fast(const FastCall &c, cudaStream_t stream) {
         // all-reduce: the streaming CTAs build the image themselves, one
         // launch behind the producer of x.  (The argmax and exchange
         // epilogues count CTAs on scratch words that the prep clears.)
-        call.build = call.epilogue != 2 && call.ex == nullptr && call.reduce == nullptr &&
-                     (call.norm_w == nullptr || plan.kc == 1) && device_resident(call.x);
+        call.build = call.epilogue != 2 && call.ex == nullptr && call.reduce == nullptr && device_resident(call.x);
         if (call.build) {
             call.overlap = true;
             if (call.launch_count != nullptr) *call.launch_count += 1;

@@ -45,10 +45,12 @@
 // completing on the slot's mbarrier, plus the tile's scales and biases for
 // the window's groups by 16-byte cp.async (zero-filled out of range) in one
 // commit group per unit, waited for with cp.async.wait_group and a warp
-// barrier.  The CTA's activation image (its slice of the prepared image
-// plus the table of group sums) arrives once by bulk copy.  Weight loads are
-// issued before `griddepcontrol.wait`, so they overlap the producer of the
-// activations under programmatic dependent launch.  Every wait is bounded by
+// barrier.  The CTA's activation image (its slice of the image plus the
+// table of group sums) is built by the CTA itself from x in its prologue, or
+// (argmax and exchange epilogues, host-resident x, the prepared-activation
+// API) arrives once by bulk copy from the prep kernel's image.  Weight loads
+// are issued before `griddepcontrol.wait`, so they overlap the producer of
+// the activations under programmatic dependent launch.  Every wait is bounded by
 // %globaltimer; on timeout the kernel records an error code and drains the
 // copies it issued (also bounded) before exiting.
 #pragma once
@@ -64,8 +66,7 @@
 namespace qmr {
 
 constexpr int kMmaWarps = 8;     // warps per CTA, each with its own copy ring
-constexpr int kMmaWarpsLong = 12;  // warps per CTA for long streams (shallower rings, more issue slots)
-constexpr int kLongUnitsPerCta = 128;  // (tile, window) units per CTA from which the long plan is tried
+constexpr int kMmaWarpsLong = 12;  // warps per CTA for Q4 g32/g64 (shallower rings, more issue slots)
 constexpr int kTileRows = 16;    // rows of one MMA tile
 constexpr int kMaxPieces = 4;    // tile pieces one warp may leave in shared memory
 constexpr int kMmaMaxStages = 6;
@@ -363,8 +364,9 @@ __global__ void __launch_bounds__(4 * kPrepGroupsPerCta) mma_prep_kernel(const f
 // [B][ngroups_pad] at the global group index), with the functions the prep
 // kernel uses, so the image bits are the prep's.  The quads of the CTA take
 // the (group, RHS) items in turn.  norm_w (optional): the image holds
-// x * norm_w and rs[b] receives 1 / sqrt(mean(x_b^2) + eps) (the slice must
-// be the whole row).  Every thread of the CTA calls this; the caller
+// x * norm_w and rs[b] receives 1 / sqrt(mean(x_b^2) + eps), summed over the
+// whole row in an order that does not depend on the slice, so every CTA of a
+// call gets the same factor.  Every thread of the CTA calls this; the caller
 // synchronises the CTA afterwards.
 template <int BITS, int G, int B, int NW>
 __device__ __forceinline__ void mma_build_image(const float *x, const float *norm_w, float eps, int ngroups,
@@ -380,8 +382,6 @@ __device__ __forceinline__ void mma_build_image(const float *x, const float *nor
     uint32_t *img = reinterpret_cast<uint32_t *>(img_s);
     float2 *tab = reinterpret_cast<float2 *>(tab_s);
     float ss[B];
-#pragma unroll
-    for (int k = 0; k < B; ++k) ss[k] = 0.0f;
     for (int base = 0; base < items; base += NQ) {  // the same trip count in every warp
         const int i = base + quad;
         const bool here = i < items;
@@ -408,15 +408,8 @@ __device__ __forceinline__ void mma_build_image(const float *x, const float *nor
             }
             if (norm_w != nullptr) {
                 const float *wl = norm_w + (size_t)g * G + t * CPL;
-                float sq = 0.0f;
 #pragma unroll
-                for (int k = 0; k < CPL; ++k) {
-                    sq = __fmaf_rn(v[k], v[k], sq);
-                    v[k] = __fmul_rn(v[k], __ldg(wl + k));
-                }
-#pragma unroll
-                for (int k = 0; k < B; ++k)
-                    if (k == b) ss[k] = __fadd_rn(ss[k], sq);
+                for (int k = 0; k < CPL; ++k) v[k] = __fmul_rn(v[k], __ldg(wl + k));
             }
         }
         int E;
@@ -428,7 +421,19 @@ __device__ __forceinline__ void mma_build_image(const float *x, const float *nor
         }
     }
     if (norm_w != nullptr) {
-        // Fixed-order reduction: lanes by xor shuffle, then warps in order.
+        // Sum of squares of the whole row: thread i takes columns i, i + NT,
+        // ... in order, then lanes by xor shuffle, then warps in order.
+        constexpr int NT = NW * 32;
+#pragma unroll
+        for (int k = 0; k < B; ++k) {
+            const float *xb = x + (size_t)k * cols;
+            float sq = 0.0f;
+            for (int c = tid; c < cols; c += NT) {
+                const float xv = __ldcg(xb + c);
+                sq = __fmaf_rn(xv, xv, sq);
+            }
+            ss[k] = sq;
+        }
         const int warp = tid >> 5;
 #pragma unroll
         for (int k = 0; k < B; ++k) {
@@ -548,8 +553,8 @@ struct MmaArgs {
     const float *table;                    // [4][ngroups_pad] x (2^(24 - E_g), group sum)
     // build != 0: no prepared image; every CTA builds its slice of the image
     // in its prologue from x [B][cols] (mma_build_image), with the fused
-    // RMSNorm weight norm_w (optional; the output factor stays in shared
-    // memory; the plan must have kc == 1 then).
+    // RMSNorm weight norm_w (optional; every CTA computes the whole row's
+    // output factor and keeps it in shared memory).
     const float *x;
     const float *norm_w;
     float eps;
