@@ -105,6 +105,11 @@ struct QmrModel {
     DevMat embed, head;
     float *final_norm = nullptr;
     float *x = nullptr, *proj = nullptr, *mixed = nullptr, *act = nullptr, *logits = nullptr;
+    // The residual stream's second buffer: an all-reduce folded into a
+    // streaming kernel's image build writes the reduced x to the other
+    // buffer (its CTAs still read the old one).  xc: the buffer holding x at
+    // the current point of a recording (the embedding writes x).
+    float *x2 = nullptr, *xc = nullptr;
     float *normed = nullptr, *tmp = nullptr;
     float *attn_part = nullptr;
     unsigned int *attn_count = nullptr;
@@ -235,6 +240,8 @@ int alloc_buffers(QmrModel *m, uint32_t context) {
     // Activations for up to kMaxBlock tokens (token-major).
     const size_t T = kMaxBlock;
     rc = dev_alloc(m, &m->x, T * H);
+    if (rc == QMR_OK) rc = dev_alloc(m, &m->x2, T * H);
+    m->xc = m->x;
     if (rc == QMR_OK) rc = dev_alloc(m, &m->normed, T * widest);
     if (rc == QMR_OK) rc = dev_alloc(m, &m->tmp, T * H);
     if (rc == QMR_OK) rc = dev_alloc(m, &m->proj, T * proj);
@@ -362,6 +369,8 @@ struct StepCounter {
 // argmax (epi 2, into argmax).
 int flush_reduce(QmrModel *m, StepCounter *cnt, int nq);
 
+float *other_x(QmrModel *m) { return m->xc == m->x ? m->x2 : m->x; }
+
 int mat_call(QmrModel *m, const DevMat &W, const float *x, float *y, const float *norm_w, const float *resid, int epi,
              const DevMat *up, int32_t *argmax, StepCounter *cnt, int nq = 1) {
     FastCall c = {};
@@ -383,21 +392,27 @@ int mat_call(QmrModel *m, const DevMat &W, const float *x, float *y, const float
     c.batch = (uint32_t)nq;
     c.bf16 = W.bf16;
     c.epilogue = epi;
+    c.counted_build = true;  // clear_state clears the scratch after any failed call
     c.path = modes_stream_path();
     c.scratch = m->scratch;
     c.scratch_bytes = m->scratch_size;
     c.eps = m->cfg.rms_eps;
     c.meta_stride = W.mstride;
-    const bool reduce = m->pending_reduce != nullptr && x == m->x;
+    const bool reduce = m->pending_reduce != nullptr && x == m->xc;
     if (norm_w != nullptr || resid != nullptr || reduce) {
         FastCall f = c;
         f.norm_w = norm_w;
         f.resid = resid;
         f.reduce = reduce ? m->pending_reduce : nullptr;
+        f.x_out = reduce ? other_x(m) : nullptr;
         if (fused_supported(f)) {
-            if (reduce) m->pending_reduce = nullptr;
             f.launch_count = &cnt->n;
-            return run_fast(f, m->stream);
+            const int rc = run_fast(f, m->stream);
+            if (reduce) {
+                m->pending_reduce = nullptr;
+                m->xc = f.x_out;
+            }
+            return rc;
         }
     }
     int rc = reduce ? flush_reduce(m, cnt, nq) : QMR_OK;
@@ -437,7 +452,7 @@ int flush_reduce(QmrModel *m, StepCounter *cnt, int nq) {
     m->pending_reduce = nullptr;
     int rc = launch_exchange_wait(*ex, (uint32_t)nq, nullptr, nullptr, m->stream);
     ++cnt->n;
-    if (rc == QMR_OK) rc = launch_partial_sum(m->x, ex->out[ex->rank], (int)m->world, (int)m->lc.hidden_size, nq, m->stream);
+    if (rc == QMR_OK) rc = launch_partial_sum(m->xc, ex->out[ex->rank], (int)m->world, (int)m->lc.hidden_size, nq, m->stream);
     ++cnt->n;
     return rc;
 }
@@ -453,7 +468,7 @@ int flush_reduce(QmrModel *m, StepCounter *cnt, int nq) {
 // alternate, so a rank one exchange ahead never overwrites slots that a
 // peer has not summed yet.
 int mat_reduce(QmrModel *m, const DevMat &W, const float *in, StepCounter *cnt, int nq) {
-    if (m->world == 1) return mat_call(m, W, in, m->x, nullptr, m->x, 0, nullptr, nullptr, cnt, nq);
+    if (m->world == 1) return mat_call(m, W, in, m->xc, nullptr, m->xc, 0, nullptr, nullptr, cnt, nq);
     int rc = flush_reduce(m, cnt, nq);  // none pending in the step's order (in -> out, gate/up -> down)
     if (rc != QMR_OK) return rc;
     const QmrExchange &ex = m->xch[m->xpar];
@@ -476,6 +491,7 @@ int mat_reduce(QmrModel *m, const DevMat &W, const float *in, StepCounter *cnt, 
     c.scratch_bytes = m->scratch_size;
     c.meta_stride = W.mstride;
     c.ex = &ex;
+    c.counted_build = true;
     c.launch_count = &cnt->n;
     rc = run_fast(c, m->stream);
     m->pending_reduce = &ex;
@@ -488,13 +504,13 @@ int mat_reduce(QmrModel *m, const DevMat &W, const float *in, StepCounter *cnt, 
 // vocabulary index).
 int head_call(QmrModel *m, int32_t *argmax, StepCounter *cnt, int nq) {
     if (m->world == 1)
-        return mat_call(m, m->head, m->x, m->logits, m->final_norm, nullptr, 2, nullptr, argmax, cnt, nq);
+        return mat_call(m, m->head, m->xc, m->logits, m->final_norm, nullptr, 2, nullptr, argmax, cnt, nq);
     const DevMat &W = m->head;
     FastCall c = {};
     c.w = W.w;
     c.s = W.s;
     c.b = W.b;
-    c.x = m->x;
+    c.x = m->xc;
     c.y = m->logits;
     c.rows = W.rows;
     c.cols = W.cols;
@@ -511,9 +527,12 @@ int head_call(QmrModel *m, int32_t *argmax, StepCounter *cnt, int nq) {
     c.eps = m->cfg.rms_eps;
     c.ex = &m->hxch;
     c.reduce = m->pending_reduce;
-    m->pending_reduce = nullptr;
+    c.x_out = c.reduce != nullptr ? other_x(m) : nullptr;
+    c.counted_build = true;
     c.launch_count = &cnt->n;
     int rc = run_fast(c, m->stream);
+    if (c.reduce != nullptr) m->xc = c.x_out;
+    m->pending_reduce = nullptr;
     if (rc == QMR_OK) rc = launch_exchange_wait(m->hxch, (uint32_t)nq, argmax, nullptr, m->stream);
     ++cnt->n;
     return rc;
@@ -527,6 +546,7 @@ enum StepKind { kStepPlain, kStepHead, kStepBlockEval, kStepBlockRound };
 int record_step(QmrModel *m, StepKind kind, int nq, StepCounter *cnt) {
     const QmrModelConfig &c = m->lc;
     const bool block = kind == kStepBlockEval || kind == kStepBlockRound;
+    m->xc = m->x;  // the embedding writes x
     int rc;
     if (block)
         rc = launch_embed_block(m->embed.w, m->embed.s, m->embed.b, m->embed.bf16, m->embed.cols, m->embed.bits,
@@ -538,7 +558,7 @@ int record_step(QmrModel *m, StepKind kind, int nq, StepCounter *cnt) {
     for (uint32_t l = 0; l < c.num_layers && rc == QMR_OK; ++l) {
         LayerState &L = m->layers[l];
         // The in-projection writes [nq][in rows]; the mixers read it with that stride.
-        rc = mat_call(m, L.in, m->x, m->proj, L.in_norm, nullptr, 0, nullptr, nullptr, cnt, nq);
+        rc = mat_call(m, L.in, m->xc, m->proj, L.in_norm, nullptr, 0, nullptr, nullptr, cnt, nq);
         if (rc != QMR_OK) break;
         if (L.attn) {
             AttnArgs a = {};
@@ -590,7 +610,7 @@ int record_step(QmrModel *m, StepKind kind, int nq, StepCounter *cnt) {
         }
         ++cnt->n;
         if (rc == QMR_OK) rc = mat_reduce(m, L.out, m->mixed, cnt, nq);
-        if (rc == QMR_OK) rc = mat_call(m, L.gate, m->x, m->act, L.post_norm, nullptr, 1, &L.up, nullptr, cnt, nq);
+        if (rc == QMR_OK) rc = mat_call(m, L.gate, m->xc, m->act, L.post_norm, nullptr, 1, &L.up, nullptr, cnt, nq);
         if (rc == QMR_OK) rc = mat_reduce(m, L.down, m->act, cnt, nq);
     }
     if (rc == QMR_OK && kind != kStepPlain) rc = head_call(m, block ? m->block_argmax : &m->ctrl->token, cnt, nq);
@@ -625,6 +645,9 @@ int clear_state(QmrModel *m) {
         if (rc == QMR_OK) rc = cuda_check(cudaMemsetAsync(L.state, 0, VD * c.linear_key_dim * sizeof(float), m->stream), "reset");
     }
     if (rc == QMR_OK) rc = cuda_check(cudaMemsetAsync(m->ctrl, 0, sizeof(DecodeCtrl), m->stream), "reset");
+    // The streaming kernels' CTA counters and argmax keys (the engine's
+    // calls build their images in-kernel, without the prep that clears them).
+    if (rc == QMR_OK) rc = cuda_check(cudaMemsetAsync(m->scratch, 0, m->scratch_size, m->stream), "reset");
     if (rc == QMR_OK) rc = cuda_check(cudaStreamSynchronize(m->stream), "reset");
     m->pos = 0;
     m->pending = false;
@@ -689,13 +712,14 @@ int ensure_block(QmrModel *m, int nq) {
     }
     if (m->bexec[1][nq] != nullptr) return QMR_OK;
     StepCounter warm;
+    m->xc = m->x;
     bool seen[2] = {false, false};
     for (LayerState &L : m->layers) {
         if (seen[L.attn]) continue;
         seen[L.attn] = true;
-        rc = mat_call(m, L.in, m->x, m->proj, L.in_norm, nullptr, 0, nullptr, nullptr, &warm, nq);
+        rc = mat_call(m, L.in, m->xc, m->proj, L.in_norm, nullptr, 0, nullptr, nullptr, &warm, nq);
         if (rc == QMR_OK) rc = mat_reduce(m, L.out, m->mixed, &warm, nq);
-        if (rc == QMR_OK) rc = mat_call(m, L.gate, m->x, m->act, L.post_norm, nullptr, 1, &L.up, nullptr, &warm, nq);
+        if (rc == QMR_OK) rc = mat_call(m, L.gate, m->xc, m->act, L.post_norm, nullptr, 1, &L.up, nullptr, &warm, nq);
         if (rc == QMR_OK) rc = mat_reduce(m, L.down, m->act, &warm, nq);
         if (rc != QMR_OK) return rc;
     }

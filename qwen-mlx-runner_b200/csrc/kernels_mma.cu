@@ -194,6 +194,19 @@ int QMR_MMA_LAUNCH(const FastCall &c, const MmaPlan &p, const ScratchView &sv, c
     a.norm_w = c.norm_w;
     a.eps = c.eps;
     a.build = c.build ? 1 : 0;
+    a.red_slots = nullptr;
+    a.red_flags = nullptr;
+    a.red_epoch = nullptr;
+    a.red_world = 0;
+    a.x_out = nullptr;
+    if (c.build && c.reduce != nullptr) {
+        const QmrExchange &r = *c.reduce;
+        a.red_slots = r.out[r.rank];
+        a.red_flags = r.flags[r.rank];
+        a.red_epoch = r.epoch;
+        a.red_world = (int)r.world;
+        a.x_out = c.x_out;
+    }
     switch (c.epilogue) {
         case 0: return launch_e<0>(maps, a, p, c.bf16, c.group, c.batch, c.overlap, stream);
         case 1: return launch_e<1>(maps, a, p, c.bf16, c.group, c.batch, c.overlap, stream);

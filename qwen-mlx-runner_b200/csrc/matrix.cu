@@ -435,11 +435,19 @@ int run_fast(const FastCall &c, cudaStream_t stream) {
         ScratchView sv;
         MmaImageView mv;
         scratch_layout(base, (int)call.bits, call.cols, call.batch, &sv, &mv);
-        // Calls without an argmax or exchange epilogue and without a folded
-        // all-reduce: the streaming CTAs build the image themselves, one
-        // launch behind the producer of x.  (The argmax and exchange
-        // epilogues count CTAs on scratch words that the prep clears.)
-        call.build = call.epilogue != 2 && call.ex == nullptr && call.reduce == nullptr && device_resident(call.x);
+        if (call.reduce != nullptr) {
+            const QmrExchange &r = *call.reduce;
+            if (r.total_rows != r.world * call.cols || call.batch > 4 || call.x_out == nullptr)
+                return fail(QMR_EINVAL, "the folded all-reduce needs slots of [batch][world][cols] and an x output");
+        }
+        // Device-resident x: the streaming CTAs build the image themselves,
+        // one launch behind the producer of x.  The argmax and exchange
+        // epilogues count CTAs on scratch words that the prep clears at the
+        // start of a call; they build in-kernel only for a caller that clears
+        // its scratch after any failed call (counted_build).
+        call.build = (call.epilogue != 2 && call.ex == nullptr) || call.counted_build;
+        call.build = call.build && device_resident(call.x);
+        if (call.reduce != nullptr && call.x_out == call.x) call.build = false;  // its CTAs read x while CTA 0 writes
         if (call.build) {
             call.overlap = true;
             if (call.launch_count != nullptr) *call.launch_count += 1;
@@ -452,10 +460,8 @@ int run_fast(const FastCall &c, cudaStream_t stream) {
         mv.eps = call.eps;
         if (call.reduce != nullptr) {
             const QmrExchange &r = *call.reduce;
-            if (r.total_rows != r.world * call.cols || call.batch > 4)
-                return fail(QMR_EINVAL, "the folded all-reduce needs slots of [batch][world][cols]");
             mv.red_slots = r.out[r.rank];
-            mv.red_x = const_cast<float *>(call.x);
+            mv.red_x = call.x_out;
             mv.red_flags = r.flags[r.rank];
             mv.red_epoch = r.epoch;
             mv.red_err = device_error_word();

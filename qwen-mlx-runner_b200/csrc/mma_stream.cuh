@@ -135,9 +135,10 @@ struct MmaImageView {
     float *row_scale;
     // An all-reduce of partial sums folded in front of the prep (red_slots
     // null: none): wait, bounded, until every one of red_world ranks has
-    // published epoch *red_epoch in red_flags, then x[b] += slots[b][r] for
-    // r = 0 .. red_world-1 in rank order (slots [batch][red_world][cols]),
-    // written back to x (red_x) before the prep uses it.
+    // published epoch *red_epoch in red_flags, then x_new[b] = x[b] +
+    // (slots[b][0] + slots[b][1] + ...) in rank order (slots
+    // [batch][red_world][cols]), written to red_x (may be x itself) and used
+    // by the prep in place of x.
     const float *red_slots;
     float *red_x;
     const unsigned int *red_flags;
@@ -249,6 +250,71 @@ __device__ __forceinline__ float2 act_table_entry(int E, float sum, bool zero) {
 // load of the CTA is in flight at once).
 constexpr int kPrepGroupsPerCta = 128;
 
+// Threads 0..world-1 of the calling warp wait, bounded, until every rank has
+// published this rank's current epoch in `flags` (acquire); after a wait has
+// run out anywhere (the error word is set), later waits return at once.
+__device__ __forceinline__ void wait_rank_epochs(const unsigned int *flags, const unsigned int *epoch, int world,
+                                                 unsigned int *err) {
+    const int lane = threadIdx.x & 31;
+    if (*(volatile unsigned int *)err != 0u) return;
+    const unsigned int e = *epoch;
+    if (lane >= world) return;
+    const unsigned long long start = global_ns();
+    for (;;) {
+        unsigned int f;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(flags + lane) : "memory");
+        if ((int)(f - e) >= 0) return;
+        if (global_ns() - start > kWaitLimitNs) {
+            atomicCAS(err, 0u, kErrTimeoutPeer);
+            return;
+        }
+        __nanosleep(100);
+    }
+}
+
+// x[b][c] plus the ranks' partial sums of that entry, added in rank order:
+// the all-reduced residual stream (slots [batch][world][cols]).
+__device__ __forceinline__ float reduced_x(const float *x, const float *slots, int world, int cols, int b, int c) {
+    const float *sl = slots + (size_t)b * world * cols + c;
+    float acc = __ldcg(sl);
+    for (int r = 1; r < world; ++r) acc = __fadd_rn(acc, __ldcg(sl + (size_t)r * cols));
+    return __fadd_rn(__ldcg(x + (size_t)b * cols + c), acc);
+}
+
+// J entries of row b at columns c0, c0 + step, ... (zero past the row), each
+// all-reduced as reduced_x does when slots is set: every load of the J
+// entries is issued before any of them is used (one round trip, not J).
+template <int J>
+__device__ __forceinline__ void load_row_entries(float (&v)[J], const float *x, const float *slots, int world, int cols,
+                                                 int b, int c0, int step) {
+    const float *xb = x + (size_t)b * cols;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const int c = c0 + j * step;
+        v[j] = c < cols ? __ldcg(xb + c) : 0.0f;
+    }
+    if (slots == nullptr) return;
+    const float *sb = slots + (size_t)b * world * cols;
+    float acc[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const int c = c0 + j * step;
+        acc[j] = c < cols ? __ldcg(sb + c) : 0.0f;
+    }
+    for (int r = 1; r < world; ++r) {
+        float t[J];
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+            const int c = c0 + j * step;
+            t[j] = c < cols ? __ldcg(sb + (size_t)r * cols + c) : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < J; ++j) acc[j] = __fadd_rn(acc[j], t[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < J; ++j) v[j] = __fadd_rn(v[j], acc[j]);
+}
+
 template <int BITS, int G>
 __global__ void __launch_bounds__(4 * kPrepGroupsPerCta) mma_prep_kernel(const float *x, int cols, int batch,
                                                                          int ngroups_pad, MmaImageView v) {
@@ -260,7 +326,7 @@ __global__ void __launch_bounds__(4 * kPrepGroupsPerCta) mma_prep_kernel(const f
     using S = MmaShape<BITS, G>;
     constexpr int CPL = S::CPL;
     const int b = blockIdx.y;
-    const float *xb = x + (size_t)b * cols;
+    const float *xb = x + (size_t)b * cols;  // the all-reduced x when red_slots is set
     const int tid = threadIdx.x;
     const int ngroups = cols / G;
     const int NB = 2 * batch;
@@ -276,36 +342,17 @@ __global__ void __launch_bounds__(4 * kPrepGroupsPerCta) mma_prep_kernel(const f
     const int g = blockIdx.x * kPrepGroupsPerCta + (tid >> 2), t = tid & 3;
     const bool here = g < ngroups_pad, real = g < ngroups;
     if (v.red_slots != nullptr) {
-        // The ranks' epochs: the first warp acquires them (bounded; after a
-        // wait has run out anywhere, later waits return at once), the CTA
-        // barrier then orders every thread's slot reads after the acquire.
-        if (tid < 32 && *(volatile unsigned int *)v.red_err == 0u) {
-            const unsigned int e = *v.red_epoch;
-            if (tid < v.red_world) {
-                const unsigned long long start = global_ns();
-                for (;;) {
-                    unsigned int f;
-                    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(v.red_flags + tid) : "memory");
-                    if ((int)(f - e) >= 0) break;
-                    if (global_ns() - start > kWaitLimitNs) {
-                        atomicCAS(v.red_err, 0u, kErrTimeoutPeer);
-                        break;
-                    }
-                    __nanosleep(100);
-                }
-            }
-        }
+        // The ranks' epochs: the first warp acquires them, the CTA barrier
+        // then orders every thread's slot reads after the acquire.
+        if (tid < 32) wait_rank_epochs(v.red_flags, v.red_epoch, v.red_world, v.red_err);
         __syncthreads();
         if (real) {
-            float *xl = v.red_x + (size_t)b * cols + (size_t)g * G + t * CPL;
-            const float *sl = v.red_slots + ((size_t)b * v.red_world * cols) + (size_t)g * G + t * CPL;
+            const int c0 = g * G + t * CPL;
 #pragma unroll
-            for (int k = 0; k < CPL; ++k) {
-                float acc = __ldcg(sl + k);
-                for (int r = 1; r < v.red_world; ++r) acc = __fadd_rn(acc, __ldcg(sl + (size_t)r * cols + k));
-                xl[k] = __fadd_rn(xl[k], acc);
-            }
+            for (int k = 0; k < CPL; ++k)
+                v.red_x[(size_t)b * cols + c0 + k] = reduced_x(x, v.red_slots, v.red_world, cols, b, c0 + k);
         }
+        xb = v.red_x + (size_t)b * cols;  // this thread reads back only its own columns
     }
     float v_[CPL];
 #pragma unroll
@@ -366,12 +413,15 @@ __global__ void __launch_bounds__(4 * kPrepGroupsPerCta) mma_prep_kernel(const f
 // the (group, RHS) items in turn.  norm_w (optional): the image holds
 // x * norm_w and rs[b] receives 1 / sqrt(mean(x_b^2) + eps), summed over the
 // whole row in an order that does not depend on the slice, so every CTA of a
-// call gets the same factor.  Every thread of the CTA calls this; the caller
-// synchronises the CTA afterwards.
+// call gets the same factor.  slots (optional): x is first all-reduced with
+// the ranks' partial sums (reduced_x; the caller has waited for the ranks'
+// epochs) and CTA 0 stores the reduced row into x_out.  Every thread of the
+// CTA calls this; the caller synchronises the CTA afterwards.
 template <int BITS, int G, int B, int NW>
 __device__ __forceinline__ void mma_build_image(const float *x, const float *norm_w, float eps, int ngroups,
                                                 int ngroups_pad, int g0, int ng, unsigned char *img_s,
-                                                unsigned char *tab_s, float *red, float *rs) {
+                                                unsigned char *tab_s, float *red, float *rs, const float *slots,
+                                                int world, float *x_out) {
     using S = MmaShape<BITS, G>;
     constexpr int CPL = S::CPL;
     constexpr int NB = 2 * B;
@@ -391,7 +441,9 @@ __device__ __forceinline__ void mma_build_image(const float *x, const float *nor
         float v[CPL];
 #pragma unroll
         for (int k = 0; k < CPL; ++k) v[k] = 0.0f;
-        if (real) {
+        if (real && slots != nullptr) {
+            load_row_entries<CPL>(v, x, slots, world, cols, b, g * G + t * CPL, 1);
+        } else if (real) {
             const float *xl = x + (size_t)b * cols + (size_t)g * G + t * CPL;
             if ((reinterpret_cast<uintptr_t>(xl) & 15) == 0) {
 #pragma unroll
@@ -406,11 +458,11 @@ __device__ __forceinline__ void mma_build_image(const float *x, const float *nor
 #pragma unroll
                 for (int k = 0; k < CPL; ++k) v[k] = __ldcg(xl + k);
             }
-            if (norm_w != nullptr) {
-                const float *wl = norm_w + (size_t)g * G + t * CPL;
+        }
+        if (real && norm_w != nullptr) {
+            const float *wl = norm_w + (size_t)g * G + t * CPL;
 #pragma unroll
-                for (int k = 0; k < CPL; ++k) v[k] = __fmul_rn(v[k], __ldg(wl + k));
-            }
+            for (int k = 0; k < CPL; ++k) v[k] = __fmul_rn(v[k], __ldg(wl + k));
         }
         int E;
         float sum;
@@ -420,20 +472,33 @@ __device__ __forceinline__ void mma_build_image(const float *x, const float *nor
             if (t == 0) tab[(size_t)b * ngroups_pad + g] = act_table_entry(E, sum, !real);
         }
     }
-    if (norm_w != nullptr) {
-        // Sum of squares of the whole row: thread i takes columns i, i + NT,
-        // ... in order, then lanes by xor shuffle, then warps in order.
+    if (norm_w != nullptr || x_out != nullptr) {
+        // The whole row: thread i takes columns i, i + NT, ... in order; the
+        // first CTA stores the all-reduced x (x_out), and the sum of squares
+        // for the RMSNorm factor goes lanes by xor shuffle, then warps in
+        // order.
         constexpr int NT = NW * 32;
+        const bool store = x_out != nullptr && blockIdx.x == 0;
+        constexpr int J = 8;  // columns per thread whose loads are in flight together
 #pragma unroll
         for (int k = 0; k < B; ++k) {
-            const float *xb = x + (size_t)k * cols;
             float sq = 0.0f;
-            for (int c = tid; c < cols; c += NT) {
-                const float xv = __ldcg(xb + c);
-                sq = __fmaf_rn(xv, xv, sq);
+            for (int c0 = tid; c0 < cols; c0 += J * NT) {
+                float xv[J];
+                load_row_entries<J>(xv, x, slots, world, cols, k, c0, NT);
+#pragma unroll
+                for (int j = 0; j < J; ++j) {
+                    const int c = c0 + j * NT;
+                    if (c < cols) {
+                        if (store) x_out[(size_t)k * cols + c] = xv[j];
+                        sq = __fmaf_rn(xv[j], xv[j], sq);
+                    }
+                }
             }
             ss[k] = sq;
         }
+    }
+    if (norm_w != nullptr) {
         const int warp = tid >> 5;
 #pragma unroll
         for (int k = 0; k < B; ++k) {
@@ -559,6 +624,14 @@ struct MmaArgs {
     const float *norm_w;
     float eps;
     int build;
+    // With build: x is first all-reduced with the ranks' partial sums
+    // (red_slots [B][red_world][cols], after waiting for every rank's epoch
+    // *red_epoch in red_flags) and CTA 0 stores the reduced x into x_out.
+    const float *red_slots;
+    const unsigned int *red_flags;
+    const unsigned int *red_epoch;
+    int red_world;
+    float *x_out;
     float *y;
     unsigned long long *keys;              // [B] packed argmax (EPI 2)
     unsigned int *done;                    // CTAs finished (EPI 2)
@@ -700,9 +773,17 @@ __global__ void __launch_bounds__(32 * NW, 1)
     // table); all of them when the CTA built the image itself.
     uint32_t img_ready = 0u;
     if (a.build) {
-        if (U > 0) {  // CTA-uniform
+        // CTA 0 stores the all-reduced x even when it has no units of its own.
+        if (U > 0 || (a.red_slots != nullptr && blockIdx.x == 0)) {  // CTA-uniform
+            if (a.red_slots != nullptr) {
+                // The ranks' epochs: the first warp acquires them, the CTA
+                // barrier orders every thread's slot reads after the acquire.
+                if (warp == 0) wait_rank_epochs(a.red_flags, a.red_epoch, a.red_world, a.err);
+                __syncthreads();
+            }
             mma_build_image<BITS, G, B, NW>(a.x, a.norm_w, a.eps, a.ngroups, a.ngroups_pad, win0 * S::WG,
-                                            nh * S::WG, smem + a.off_image, smem + a.off_table, build_red, build_rs);
+                                            nh * S::WG, smem + a.off_image, smem + a.off_table, build_red, build_rs,
+                                            a.red_slots, a.red_world, a.x_out);
             fence_proxy_async();  // generic-proxy image writes before any later async-proxy use of shared memory
             __syncthreads();
         }

@@ -41,10 +41,15 @@ struct FastCall {
     // stride lets a column slice of a matrix keep 16-byte metadata rows;
     // tensor-core path only.
     uint32_t meta_stride;
-    // An exchange of partial sums to all-reduce into x before it is used
-    // (the prep waits for every rank's epoch and adds the slots [batch]
-    // [world][cols] in rank order, writing x back); tensor-core path only.
+    // An exchange of partial sums to all-reduce into x before it is used:
+    // every rank's epoch is awaited, the slots [batch][world][cols] are
+    // added to x in rank order and the reduced x is written to x_out (which
+    // may be x itself only when the prep kernel runs); tensor-core path only.
     const QmrExchange *reduce;
+    float *x_out;
+    // The caller clears its scratch after any failed call, so calls with
+    // the argmax or exchange epilogue may build their image in-kernel too.
+    bool counted_build;
     // Set by run_fast: the streaming CTAs build the activation image in
     // their prologue from x (no prep kernel, no prepared image).
     bool build;

@@ -139,9 +139,9 @@ def test_synthetic_engine_matches_fp64_oracle_logits_and_greedy_ids(cuda):
     o = synthetic_oracle(cfg, seed, context)
     try:
         with_head, without = eng.step_launches()
-        # embed + per layer (in-proj, mixer, out + residual, gate/up, down + residual; each matrix
-        # one streaming kernel that builds its own activation image) + head (prep + kernel) + advance
-        assert with_head == 1 + 5 * cfg["layers"] + 2 + 1 and without == with_head - 2
+        # embed + per layer (in-proj, mixer, out + residual, gate/up, down + residual) + head
+        # + advance: every matrix one streaming kernel that builds its own activation image
+        assert with_head == 1 + 5 * cfg["layers"] + 1 + 1 and without == with_head - 1
         prompt = prompt_tokens(5, 40, cfg["vocab"])
         worst = 0.0
         for i, t in enumerate(prompt):

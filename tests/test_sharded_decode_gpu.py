@@ -11,8 +11,8 @@ What must hold:
   the single-GPU engine's bound (the all-reduce sums the ranks' partial
   products in rank order, a different order from one GPU's, so the bits
   are not required to equal the unsharded engine's);
-* the step graph holds the one-GPU launches plus the head's key wait: the
-  all-reduces ride in the activation prep of the next matrix that reads x.
+* the step graph holds the one-GPU launches plus the head's key wait: each
+  all-reduce rides in the image build of the next matrix that reads x.
 
 Each world size is skipped when the box has fewer GPUs.  Shapes: the small
 layer graph at 2 ranks (column slices of 4 groups, padded metadata rows),
@@ -142,9 +142,9 @@ def test_sharded_decode_gives_the_oracle_tokens_on_every_rank(name, world):
         scale = np.max(np.abs(want_lgs), axis=1, keepdims=True)
         err = np.max(np.abs(x["lgs"] - want) / scale)
         assert err <= tol, (r, err)
-        # embed + per layer (in-proj, mixer, out, gate/up, down: prep + matmul each, the
-        # all-reduces riding in the next prep; layer 0's in-proj has none to fold and builds
-        # its own image) + head (prep, matmul, key wait) + advance; without the head, the
-        # last all-reduce runs as wait + sum.
+        # embed + per layer (in-proj, mixer, out, gate/up, down: one streaming kernel per
+        # matrix; each all-reduce rides in the image build of the next matrix that reads x)
+        # + head (matmul, key wait) + advance; without the head, the last all-reduce runs as
+        # wait + sum.
         with_head, without = x["launches"].tolist()
-        assert with_head == 1 + 9 * L - 1 + 3 + 1 and without == with_head - 1
+        assert with_head == 1 + 5 * L + 2 + 1 and without == with_head
