@@ -1121,13 +1121,18 @@ __global__ void __launch_bounds__(32 * NW, 1)
                     for (int p = 0; p < a.xworld; ++p) a.xkeys[p][a.xrank * 4 + threadIdx.x] = k;
             }
             if (xchg) {
-                __threadfence_system();
-                __syncthreads();  // flag is the same for the whole CTA
+                __syncthreads();  // the key stores above (flag is the same for the whole CTA)
                 if (threadIdx.x == 0) {
+                    // One system-scope fence, after the CTA barrier and the
+                    // counter that observed every other CTA's stores: it is
+                    // cumulative over all of them, and a fence followed by
+                    // strong (relaxed) stores is a release, so the flag
+                    // stores carry no fence of their own.
+                    __threadfence_system();
                     const unsigned int e = *a.xepoch + 1u;
                     *a.xepoch = e;
                     for (int p = 0; p < a.xworld; ++p)
-                        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.xflags[p] + a.xrank), "r"(e)
+                        asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(a.xflags[p] + a.xrank), "r"(e)
                                      : "memory");
                 }
             }
