@@ -492,8 +492,9 @@ def test_prepared_activations_feed_several_matrices_bit_exactly(cuda):
 def test_in_kernel_image_equals_the_prep_kernel_image(cuda, rows, cols):
     """Device-resident x: every streaming CTA builds its slice of the
     activation image in its prologue (one CTA per row slice at 5120 columns,
-    4-CTA clusters at 17408).  Pinned host x: the prep kernel builds it once.
-    Same image bits, same kernel and plan: the outputs agree bit for bit, for
+    4-CTA clusters at 17408).  Pinned host x and the prepared-activation
+    API: the prep kernel writes the image once and the CTAs copy it.  Same
+    image bits, same kernel and plan: the outputs agree bit for bit, for
     the plain product and for the fused gate/up SwiGLU."""
     g = synth.to_device(synth.affine_matrix(rows, cols, 4, 64, seed=61), rows, cols, 4, 64)
     u = synth.to_device(synth.affine_matrix(rows, cols, 4, 64, seed=62), rows, cols, 4, 64)
@@ -509,8 +510,14 @@ def test_in_kernel_image_equals_the_prep_kernel_image(cuda, rows, cols):
             qmr.ops.gateup_swiglu(g, u, x, a, batch)
             torch.cuda.synchronize()
             outs.append((y.cpu().numpy().view(np.uint32), a.cpu().numpy().view(np.uint32)))
+        prepared = qmr.ops.alloc_prepared(4, cols, batch)
+        qmr.ops.prepare_activations(xd, cols, 4, batch, prepared)
+        yp = torch.empty(batch * rows, dtype=torch.float32, device="cuda")
+        qmr.ops.matmul_prepared(g, prepared, yp, batch)
+        torch.cuda.synchronize()
         assert np.array_equal(outs[0][0], outs[1][0]), batch
         assert np.array_equal(outs[0][1], outs[1][1]), batch
+        assert np.array_equal(outs[0][0], yp.cpu().numpy().view(np.uint32)), batch
 
 
 def test_typed_wrappers_reject_undersized_views_before_launch(cuda):
