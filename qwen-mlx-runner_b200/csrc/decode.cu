@@ -498,7 +498,25 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a) {
                 float acc[8];
 #pragma unroll
                 for (int g = 0; g < 8; ++g) acc[g] = 0.0f;
-                for (int t = t0; t < min(t1, pos + i + 1); ++t) {
+                // Eight positions' value loads in flight before their FMAs (one
+                // cache round trip per eight positions); each accumulator still
+                // adds the positions in ascending order.
+                const int tend = min(t1, pos + i + 1);
+                int t = t0;
+                for (; t + 8 <= tend; t += 8) {
+                    float vv[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        const int tt = t + u;
+                        vv[u] = (tt >= pos) ? vn[(tt - pos) * D + d] : a.vcache[((size_t)tt * NKV + kh) * D + d];
+                    }
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+#pragma unroll
+                        for (int g = 0; g < 8; ++g)
+                            if (g < G) acc[g] = __fmaf_rn(ps[(i * G + g) * kAttnChunk + (t + u - t0)], vv[u], acc[g]);
+                }
+                for (; t < tend; ++t) {
                     const float vv = (t >= pos) ? vn[(t - pos) * D + d] : a.vcache[((size_t)t * NKV + kh) * D + d];
 #pragma unroll
                     for (int g = 0; g < 8; ++g)
