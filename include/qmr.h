@@ -382,8 +382,11 @@ int qmr_model_forward(QmrModel *m, uint32_t token, float *logits, int32_t *next)
 /* Prefill n prompt tokens then greedy-decode: out receives max_new tokens,
  * the first from the prompt's last logits (the reference's prefill + sample +
  * step loop, src/engine.rs:846-935, at temperature 0 and without EOS).  The
- * steps run as graph replays with no host round trip in between;
- * prefill_ms / decode_ms (may be NULL) are device times. */
+ * steps run as graph replays with no host round trip in between; the
+ * prompt's positions before its last token run in blocks of 3 through the
+ * batched path of verify_block (one weight stream per block, results equal
+ * to single steps bit for bit); prefill_ms / decode_ms (may be NULL) are
+ * device times. */
 int qmr_model_generate(QmrModel *m, const uint32_t *prompt, uint32_t n_prompt, uint32_t max_new, uint32_t *out,
                        double *prefill_ms, double *decode_ms);
 /* Engine::verify_block (src/engine/block.rs:296-333): evaluate inputs

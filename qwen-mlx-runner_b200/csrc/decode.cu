@@ -556,19 +556,21 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a) {
     if (tid == 0) a.count[kh] = 0u;
 }
 
-// Embed a verification block: input 0 is the anchor (the last emitted
-// token), input i >= 1 the draft for position pos + i.
+// Embed a block of inputs.  Verification block: input 0 is the anchor (the
+// last emitted token), input i >= 1 the draft for position pos + i.
+// Prefill block (prompt set): input i is the prompt token at pos + i.
 template <bool BF16>
 __global__ void embed_block_kernel(const uint32_t *__restrict__ w, const void *__restrict__ s,
                                    const void *__restrict__ bias, uint32_t cols, uint32_t bits, uint32_t group,
-                                   const DecodeCtrl *ctrl, const int32_t *drafts, BlockCtrl *bctrl,
-                                   float *__restrict__ x) {
+                                   const DecodeCtrl *ctrl, const int32_t *drafts, const int32_t *prompt,
+                                   BlockCtrl *bctrl, float *__restrict__ x) {
     const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
     const int i = blockIdx.y;
     const uint32_t pos = ctrl->pos;
-    if (c == 0 && i == 0) bctrl->pos_base = pos;
+    if (bctrl != nullptr && c == 0 && i == 0) bctrl->pos_base = pos;
     if (c >= cols) return;
-    const uint64_t row = i == 0 ? (uint32_t)ctrl->token : (uint32_t)drafts[pos + i];
+    const uint64_t row = prompt != nullptr ? (uint32_t)prompt[pos + i]
+                                           : (i == 0 ? (uint32_t)ctrl->token : (uint32_t)drafts[pos + i]);
     const uint32_t pack = 32u / bits;
     const uint32_t word = __ldg(w + row * (cols / pack) + c / pack);
     const uint32_t q = (word >> ((c % pack) * bits)) & ((1u << bits) - 1u);
@@ -620,13 +622,13 @@ __global__ void commit_kernel(const BlockCtrl *bctrl, float *const *layer_ptrs, 
 
 // End of a step: append the greedy token (when the step had a head) and
 // advance the position.
-__global__ void advance_kernel(DecodeCtrl *ctrl, int32_t *out, uint32_t cap, int record) {
+__global__ void advance_kernel(DecodeCtrl *ctrl, int32_t *out, uint32_t cap, int record, int step) {
     if (threadIdx.x != 0) return;
     if (record) {
         if (ctrl->n_out < cap) out[ctrl->n_out] = ctrl->token;
         ctrl->n_out += 1;
     }
-    ctrl->pos += 1;
+    ctrl->pos += (uint32_t)step;
 }
 
 int launched(const char *what) {
@@ -696,10 +698,13 @@ int launch_add(float *x, const float *r, uint32_t n, cudaStream_t stream) {
 
 int launch_delta_mixer(const DeltaArgs &a, cudaStream_t stream) {
     if (a.K > 128 || a.K < 1 || a.V < 1 || a.KH < 1 || a.VH % a.KH != 0 || a.W < 1 || a.W > kMaxConvHist + 1 ||
-        a.nq < 1 || a.nq > kMaxTokens || (a.nq > 1 && a.conv_snap == nullptr))
+        a.nq < 1 || a.nq > kMaxTokens || (a.nq % 2 == 0 && a.conv_snap == nullptr))
+        // Without snapshots the block's conv history goes to the ping-pong
+        // buffer of parity pos + 1, which the next step reads only after an
+        // odd number of tokens.
         return fail(QMR_EUNSUPPORTED,
                     "DeltaNet mixer needs key dim <= 128, value heads a multiple of key heads, conv width <= 8 and "
-                    "1..4 tokens (more than one only as a verification block)");
+                    "1..4 tokens (an even number only as a verification block)");
     const int rows = (a.V + kDeltaSplit - 1) / kDeltaSplit;
     const size_t smem = (size_t)(a.nq * (2 * a.K + 2 * rows) + 33) * sizeof(float);
     delta_mixer_kernel<<<a.VH * kDeltaSplit, kDeltaThreads, smem, stream>>>(a);
@@ -725,15 +730,15 @@ int launch_attention(const AttnArgs &a, cudaStream_t stream) {
 }
 
 int launch_embed_block(const void *w, const void *s, const void *b, bool bf16, uint32_t cols, uint32_t bits,
-                       uint32_t group, const DecodeCtrl *ctrl, const int32_t *drafts, BlockCtrl *bctrl, int nq,
-                       float *x, cudaStream_t stream) {
+                       uint32_t group, const DecodeCtrl *ctrl, const int32_t *drafts, const int32_t *prompt,
+                       BlockCtrl *bctrl, int nq, float *x, cudaStream_t stream) {
     const dim3 grid((cols + 255) / 256, (unsigned)nq);
     if (bf16)
         embed_block_kernel<true><<<grid, 256, 0, stream>>>(static_cast<const uint32_t *>(w), s, b, cols, bits, group,
-                                                           ctrl, drafts, bctrl, x);
+                                                           ctrl, drafts, prompt, bctrl, x);
     else
         embed_block_kernel<false><<<grid, 256, 0, stream>>>(static_cast<const uint32_t *>(w), s, b, cols, bits, group,
-                                                            ctrl, drafts, bctrl, x);
+                                                            ctrl, drafts, prompt, bctrl, x);
     return launched("block embed");
 }
 
@@ -750,8 +755,8 @@ int launch_commit(const BlockCtrl *bctrl, float *const *layer_ptrs, int nlayers,
     return launched("commit");
 }
 
-int launch_advance(DecodeCtrl *ctrl, int32_t *out, uint32_t out_cap, bool record, cudaStream_t stream) {
-    advance_kernel<<<1, 32, 0, stream>>>(ctrl, out, out_cap, record ? 1 : 0);
+int launch_advance(DecodeCtrl *ctrl, int32_t *out, uint32_t out_cap, bool record, cudaStream_t stream, int step) {
+    advance_kernel<<<1, 32, 0, stream>>>(ctrl, out, out_cap, record ? 1 : 0, step);
     return launched("advance");
 }
 

@@ -86,11 +86,13 @@ int launch_partial_sum(float *x, const float *slots, int world, int H, int nq, c
 int launch_fill_f32(float *p, uint64_t n, float v, cudaStream_t stream);
 int launch_embed_token(const void *w, const void *s, const void *b, bool bf16, uint32_t cols, uint32_t bits,
                        uint32_t group, const DecodeCtrl *ctrl, const int32_t *prompt, float *x, cudaStream_t stream);
-// Embed a verification block: input 0 = ctrl->token (the anchor), input
-// i >= 1 = drafts[ctrl->pos + i]; records the block's base position.
+// Embed a block.  prompt null (verification block): input 0 = ctrl->token
+// (the anchor), input i >= 1 = drafts[ctrl->pos + i], and the block's base
+// position goes to bctrl.  prompt set (prefill block): input i =
+// prompt[ctrl->pos + i]; bctrl may be null.
 int launch_embed_block(const void *w, const void *s, const void *b, bool bf16, uint32_t cols, uint32_t bits,
-                       uint32_t group, const DecodeCtrl *ctrl, const int32_t *drafts, BlockCtrl *bctrl, int nq,
-                       float *x, cudaStream_t stream);
+                       uint32_t group, const DecodeCtrl *ctrl, const int32_t *drafts, const int32_t *prompt,
+                       BlockCtrl *bctrl, int nq, float *x, cudaStream_t stream);
 // Greedy verification (src/speculative.rs:212-264 at temperature 0): accept
 // drafts while each equals the argmax of the previous row, emit the accepted
 // drafts and the next argmax, advance the position by the inputs consumed.
@@ -105,7 +107,8 @@ int launch_rms_norm(const float *x, const float *w, float *y, uint32_t n, float 
 int launch_add(float *x, const float *r, uint32_t n, cudaStream_t stream);
 int launch_delta_mixer(const DeltaArgs &a, cudaStream_t stream);
 int launch_attention(const AttnArgs &a, cudaStream_t stream);
-// record: append ctrl->token (the step's greedy argmax) to out[].
-int launch_advance(DecodeCtrl *ctrl, int32_t *out, uint32_t out_cap, bool record, cudaStream_t stream);
+// record: append ctrl->token (the step's greedy argmax) to out[]; the
+// position advances by `step` (a prefill block's width).
+int launch_advance(DecodeCtrl *ctrl, int32_t *out, uint32_t out_cap, bool record, cudaStream_t stream, int step = 1);
 
 }  // namespace qmr

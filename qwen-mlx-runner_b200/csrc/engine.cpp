@@ -136,9 +136,11 @@ struct QmrModel {
     uint32_t out_cap = 0;
     int32_t *host_stage = nullptr;  // pinned: [0] token, [1] n_prompt
     cudaStream_t stream = nullptr;
-    cudaGraph_t graph[2] = {nullptr, nullptr};
-    cudaGraphExec_t exec[2] = {nullptr, nullptr};  // [0] no head (prefill), [1] with head
-    uint32_t launches[2] = {0, 0};
+    // [0] one token without the head, [1] one token with the head, [2] a
+    // prefill block of kPrefillBlock prompt tokens without the head.
+    cudaGraph_t graph[3] = {nullptr, nullptr, nullptr};
+    cudaGraphExec_t exec[3] = {nullptr, nullptr, nullptr};
+    uint32_t launches[3] = {0, 0, 0};
     uint32_t pos = 0;
     std::vector<void *> allocs;
     uint64_t compacted = 0, saved_bytes = 0;
@@ -149,9 +151,11 @@ struct QmrModel {
         cudaGetDevice(&prev);
         cudaSetDevice(device);
         if (stream != nullptr) cudaStreamSynchronize(stream);
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < 3; ++i) {
             if (exec[i] != nullptr) cudaGraphExecDestroy(exec[i]);
             if (graph[i] != nullptr) cudaGraphDestroy(graph[i]);
+        }
+        for (int i = 0; i < 2; ++i) {
             for (int b = 0; b <= kMaxBlock; ++b) {
                 if (bexec[i][b] != nullptr) cudaGraphExecDestroy(bexec[i][b]);
                 if (bgraph[i][b] != nullptr) cudaGraphDestroy(bgraph[i][b]);
@@ -541,16 +545,25 @@ int head_call(QmrModel *m, int32_t *argmax, StepCounter *cnt, int nq) {
 // Kinds of recorded step: one token without / with the head, a
 // verification block evaluated, or a full verification round (evaluate,
 // greedy verify, roll back to the consumed prefix).
-enum StepKind { kStepPlain, kStepHead, kStepBlockEval, kStepBlockRound };
+// a prefill block (kPrefillBlock prompt tokens evaluated together, no head).
+enum StepKind { kStepPlain, kStepHead, kStepBlockEval, kStepBlockRound, kStepPrefill };
+
+// Prompt tokens per prefill block.  The matrices stream once for the block
+// and a B-wide call equals B single calls bit for bit, so a block equals as
+// many single steps; an odd width keeps the DeltaNet conv history's
+// ping-pong buffer (chosen by position parity) where the next step reads it.
+constexpr int kPrefillBlock = 3;
 
 int record_step(QmrModel *m, StepKind kind, int nq, StepCounter *cnt) {
     const QmrModelConfig &c = m->lc;
     const bool block = kind == kStepBlockEval || kind == kStepBlockRound;
+    const bool pre = kind == kStepPrefill;
     m->xc = m->x;  // the embedding writes x
     int rc;
-    if (block)
+    if (block || pre)
         rc = launch_embed_block(m->embed.w, m->embed.s, m->embed.b, m->embed.bf16, m->embed.cols, m->embed.bits,
-                                m->embed.group, m->ctrl, m->drafts, m->bctrl, nq, m->x, m->stream);
+                                m->embed.group, m->ctrl, m->drafts, pre ? m->prompt : nullptr,
+                                pre ? nullptr : m->bctrl, nq, m->x, m->stream);
     else
         rc = launch_embed_token(m->embed.w, m->embed.s, m->embed.b, m->embed.bf16, m->embed.cols, m->embed.bits,
                                 m->embed.group, m->ctrl, m->prompt, m->x, m->stream);
@@ -613,11 +626,12 @@ int record_step(QmrModel *m, StepKind kind, int nq, StepCounter *cnt) {
         if (rc == QMR_OK) rc = mat_call(m, L.gate, m->xc, m->act, L.post_norm, nullptr, 1, &L.up, nullptr, cnt, nq);
         if (rc == QMR_OK) rc = mat_reduce(m, L.down, m->act, cnt, nq);
     }
-    if (rc == QMR_OK && kind != kStepPlain) rc = head_call(m, block ? m->block_argmax : &m->ctrl->token, cnt, nq);
+    if (rc == QMR_OK && kind != kStepPlain && !pre)
+        rc = head_call(m, block ? m->block_argmax : &m->ctrl->token, cnt, nq);
     if (rc == QMR_OK) rc = flush_reduce(m, cnt, nq);  // a step without the head: the last down's all-reduce
     m->pending_reduce = nullptr;
     if (rc == QMR_OK && !block) {
-        rc = launch_advance(m->ctrl, m->out, m->out_cap, kind == kStepHead, m->stream);
+        rc = launch_advance(m->ctrl, m->out, m->out_cap, kind == kStepHead, m->stream, pre ? nq : 1);
         ++cnt->n;
     }
     if (rc == QMR_OK && kind == kStepBlockRound) {
@@ -655,19 +669,26 @@ int clear_state(QmrModel *m) {
 }
 
 // One eager step of each kind (per-device kernel attributes and occupancy
-// queries happen outside capture), then the two graphs, then a clean state.
+// queries happen outside capture), then the three graphs, then a clean state.
 int build_graphs(QmrModel *m) {
     int rc = QMR_OK;
-    for (int head = 0; head < 2 && rc == QMR_OK; ++head) {
+    const StepKind kinds[3] = {kStepPlain, kStepHead, kStepPrefill};
+    const int widths[3] = {1, 1, kPrefillBlock};
+    // A context shorter than a prefill block has no prefill graph (its
+    // prompts prefill token by token).
+    const int nkinds = m->context >= (uint32_t)kPrefillBlock ? 3 : 2;
+    for (int head = 0; head < nkinds && rc == QMR_OK; ++head) {
+        // Each warm-up step starts at position 0, inside any context.
         StepCounter cnt;
-        rc = record_step(m, head == 1 ? kStepHead : kStepPlain, 1, &cnt);
+        rc = clear_state(m);
+        if (rc == QMR_OK) rc = record_step(m, kinds[head], widths[head], &cnt);
         if (rc == QMR_OK) rc = cuda_check(cudaStreamSynchronize(m->stream), "warm-up step");
     }
-    for (int head = 0; head < 2 && rc == QMR_OK; ++head) {
+    for (int head = 0; head < nkinds && rc == QMR_OK; ++head) {
         StepCounter cnt;
         rc = cuda_check(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
         if (rc != QMR_OK) break;
-        const int rs = record_step(m, head == 1 ? kStepHead : kStepPlain, 1, &cnt);
+        const int rs = record_step(m, kinds[head], widths[head], &cnt);
         cudaGraph_t g = nullptr;
         const cudaError_t e = cudaStreamEndCapture(m->stream, &g);
         if (rs != QMR_OK) {
@@ -1029,6 +1050,15 @@ int replay(QmrModel *m, int kind, uint32_t times) {
     return QMR_OK;
 }
 
+// Prompt positions without the head: prefill blocks, then single steps for
+// the remainder.
+int prefill(QmrModel *m, uint32_t n) {
+    const uint32_t nb = m->exec[2] != nullptr ? n / (uint32_t)kPrefillBlock : 0u;
+    int rc = replay(m, 2, nb);
+    if (rc == QMR_OK) rc = replay(m, 0, n - nb * (uint32_t)kPrefillBlock);
+    return rc;
+}
+
 }  // namespace
 }  // namespace qmr
 
@@ -1239,7 +1269,7 @@ int qmr_model_generate(QmrModel *m, const uint32_t *prompt, uint32_t n_prompt, u
     cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
     for (int i = 0; i < 3 && rc == QMR_OK; ++i) rc = cuda_check(cudaEventCreate(&ev[i]), "event");
     if (rc == QMR_OK) rc = cuda_check(cudaEventRecord(ev[0], m->stream), "event");
-    if (rc == QMR_OK) rc = replay(m, 0, n_prompt - 1);
+    if (rc == QMR_OK) rc = prefill(m, n_prompt - 1);
     if (rc == QMR_OK) rc = replay(m, 1, 1);
     if (rc == QMR_OK) rc = cuda_check(cudaEventRecord(ev[1], m->stream), "event");
     if (rc == QMR_OK) rc = replay(m, 1, max_new - 1);
@@ -1367,7 +1397,7 @@ int qmr_model_mtp_generate(QmrModel *m, const uint32_t *prompt, uint32_t n_promp
     cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
     for (int i = 0; i < 3 && rc == QMR_OK; ++i) rc = cuda_check(cudaEventCreate(&ev[i]), "event");
     if (rc == QMR_OK) rc = cuda_check(cudaEventRecord(ev[0], m->stream), "event");
-    if (rc == QMR_OK) rc = replay(m, 0, n_prompt - 1);
+    if (rc == QMR_OK) rc = prefill(m, n_prompt - 1);
     if (rc == QMR_OK) rc = replay(m, 1, 1);  // the prompt's last token emits the first output
     if (rc == QMR_OK) rc = cuda_check(cudaEventRecord(ev[1], m->stream), "event");
     // Rounds of verification, replayed in batches; every round emits 1..block

@@ -116,6 +116,39 @@ def test_generate_equals_step_by_step_forward(cuda):
         eng.close()
 
 
+@pytest.mark.parametrize("model", ["tiny-q4", "small"])
+def test_prefill_blocks_equal_single_steps(cuda, model):
+    """generate() runs a long prompt's positions in blocks of 3 through the
+    batched path; the greedy tokens and the recurrent state after them (the
+    next step's logits, bit for bit) equal those of one forward per token."""
+    if model == "tiny-q4":
+        make = lambda: qmr.Engine.load(GOLDEN / "tiny-q4", 32)  # noqa: E731
+        vocab = 64
+    else:
+        make = lambda: qmr.Engine.synthetic(small_config(), 17, 64)  # noqa: E731
+        vocab = small_config()["vocab"]
+    prompt = prompt_tokens(23, 11, vocab)  # 10 positions before the last: 3 blocks and 1 single step
+    eng = make()
+    try:
+        toks, _, _ = eng.generate(prompt, 4)
+        assert eng.position == len(prompt) + 4 - 1
+        lg_blocks, _ = eng.forward(toks[-1])
+        eng.reset()
+        ref = []
+        for t in prompt:
+            _, nxt = eng.forward(t)
+        ref.append(nxt)
+        for _ in range(3):
+            _, nxt = eng.forward(nxt)
+            ref.append(nxt)
+        assert toks == ref
+        lg_steps, _ = eng.forward(ref[-1])
+        assert np.array_equal(lg_blocks.view(np.uint32), lg_steps.view(np.uint32))
+        assert qmr.ops.device_error() == 0
+    finally:
+        eng.close()
+
+
 def small_config():
     """The layer graph at small widths the tensor-core kernel takes (hidden and
     every matrix width a multiple of 512 columns)."""
